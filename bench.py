@@ -1,0 +1,361 @@
+"""Benchmark: decode tok/s at Qwen2-7B shape, INT4 g128, batch 1, on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--ctx C]
+    python bench.py --impl reference ...          # the reference's CPU path
+
+Workload (one "step" = one decode step of the whole model for B sequences):
+a Qwen2-7B-shape decoder (hidden 3584, 28 layers, 28/4 heads, head_dim 128,
+FFN 18944, vocab 152064), random-init N(0, 0.02) weights quantised on the GPU
+to INT4 with group 128 (fp16 scale + zero), lm_head and embeddings included;
+a 2048-token prompt of uniform-random ids is prefilled (untimed), then K
+decode steps run at context 2048.. with the fp16 paged KV cache.
+
+* ``value``: tok/s with token ids and logits resident in HBM (device-side
+  decode graph), CUDA events on the model's stream.  Weights (3.76 GB) exceed
+  L2 (126 MB), so every step streams them from HBM; no L2 flush is needed.
+* ``e2e``: the same through the host C-ABI call ``n730_model_decode`` with host
+  token ids in and host fp32 logits out (copies inside the timed region).
+* ``roofline``: the dequant-GEMV kernel timed alone on the model's gate|up
+  weights (rotating over all 28 layers), algorithmic bytes per launch
+  (codes + fp16 scale/zero + x + y) / average launch time, against the
+  measured HBM peak in MEASURED_PEAKS.json.
+* ``cpu_baseline``: the reference's CPU path for one decoder layer of this
+  shape (its own n730core read+dequant, built from its source, plus numpy
+  fp32 GEMV), extrapolated to a token; per-tensor INT4 stands in for g128
+  (the reference has no group-wise format).
+
+N > 1 (torchrun, one rank per GPU): every rank decodes its own batch
+(independent replicas, weak scaling); time is the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+SHAPE_NAME = "qwen2-7b"
+METRIC = "decode tok/s at Qwen2-7B-shape INT4; dequant-GEMV HBM GB/s vs ~8 TB/s peak"
+
+
+def _args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--ctx", type=int, default=2048, help="prompt length prefilled before decoding")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def _peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi sampling during the timed region (clocks + throttle reasons)."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.p = None
+        return self
+
+    def __exit__(self, *a):
+        self.out = ""
+        if self.p:
+            self.p.terminate()
+            try:
+                self.out, _ = self.p.communicate(timeout=5)
+            except Exception:
+                self.p.kill()
+
+    def summary(self):
+        rows = []
+        for line in (getattr(self, "out", "") or "").splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) >= 9 and f[1].isdigit():
+                rows.append(f)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [int(r[1]) for r in rows]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": int(rows[0][2]), "reasons": reasons,
+                "samples": len(rows)}
+
+
+def _dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's own CPU path on one decoder layer
+# ---------------------------------------------------------------------------
+class CpuLayerSample:
+    """The reference's CPU path on one decoder layer of `shape`.
+
+    Per tensor: the reference core's n730_read_layer (file read + per-tensor
+    INT4 dequant to fp32; the library is built from the reference source by
+    oracle/Makefile) then numpy fp32 ``W @ x`` (inference.py:668,
+    scheduler.py:324).  ``run()`` returns seconds per token: the layer time
+    x layers + lm_head at the same per-parameter rate.
+    """
+
+    def __init__(self, shape, seed=0):
+        import ctypes as C
+        import struct
+        import tempfile
+
+        from oracle import quant as oq
+        core_so = REPO / "oracle" / "_ref" / "n730core.so"
+        if not core_so.exists():
+            raise FileNotFoundError("oracle/_ref/n730core.so missing (built by __graft_entry__.build)")
+        self.C = C
+        core = C.CDLL(str(core_so))
+        core.n730_open.argtypes = [C.c_char_p]
+        core.n730_open.restype = C.c_int64
+        core.n730_read_layer.argtypes = [C.c_int64, C.c_int64, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]
+        core.n730_read_layer.restype = C.c_int32
+        core.n730_close.argtypes = [C.c_int64]
+        self.core = core
+        self.shape = shape
+        h, q, kv, f = shape.hidden, shape.heads * shape.head_dim, shape.kv_heads * shape.head_dim, shape.ffn
+        self.tensors = [(q, h), (kv, h), (kv, h), (h, q), (f, h), (f, h), (h, f)]
+        tmp = tempfile.NamedTemporaryFile(suffix=".n730", delete=False)
+        self.path = tmp.name
+        self.offs = []
+        with open(self.path, "wb") as fo:
+            fo.write(b"N730\x00\x01\x00\x00" + struct.pack(">II", 1, 2) + b"{}")
+            fo.write(bytes(4096 - 18))
+            for i, shp in enumerate(self.tensors):
+                w = np.random.default_rng(seed + i).normal(0, 0.02, shp).astype(np.float32)
+                codes, scale, zp = oq.quantize_int4(w)
+                self.offs.append(fo.tell())
+                blk = struct.pack(">4sIBIIffi", b"LYR\x00", i, 4, shp[0], shp[1], scale, zp, len(codes)) + codes
+                fo.write(blk + bytes((-len(blk)) % 4096))
+        self.h = core.n730_open(self.path.encode())
+        self.x = np.random.default_rng(1).normal(0, 1, h).astype(np.float32)
+        self.xf = np.random.default_rng(2).normal(0, 1, f).astype(np.float32)
+        try:
+            import threadpoolctl
+            self.blas = max(i.get("num_threads", 1) for i in threadpoolctl.threadpool_info())
+        except Exception:
+            self.blas = os.cpu_count() or 1
+
+    def run(self):
+        C = self.C
+        t0 = time.perf_counter()
+        for off, shp in zip(self.offs, self.tensors):
+            buf = np.empty(shp[0] * shp[1], np.float32)
+            r, c, p = C.c_int32(), C.c_int32(), C.c_int32()
+            rc = self.core.n730_read_layer(self.h, off, buf.ctypes.data, C.byref(r), C.byref(c), C.byref(p))
+            assert rc == 0, rc
+            W = buf.reshape(shp)
+            _ = W @ (self.xf if shp[1] == self.shape.ffn else self.x)
+        self.t_layer = time.perf_counter() - t0
+        layer_params = sum(a * b for a, b in self.tensors)
+        lm_params = self.shape.vocab * self.shape.hidden
+        return self.t_layer * self.shape.layers + self.t_layer / layer_params * lm_params
+
+    def close(self):
+        self.core.n730_close(self.h)
+        os.unlink(self.path)
+
+
+def run_reference(a):
+    world, rank, _ = _dist()
+    if rank != 0:
+        return
+    from n730_b200.synthetic import SHAPES
+    shape = SHAPES[SHAPE_NAME]
+    cs = CpuLayerSample(shape)
+    for _ in range(a.warmup):
+        cs.run()
+    times = [cs.run() for _ in range(a.steps)]
+    cs.close()
+    kind, blas = "reference", cs.blas
+    t = statistics.median(times)
+    v = a.batch / t
+    out = {"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tok/s", "n_gpus": a.gpus,
+           "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(t * 1000 * a.batch, 1),
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+           "config": {"workload": "qwen2-7b-shape decoder, INT4 (per-tensor: the reference has no group-wise "
+                                  "format), batch 1 decode step on the host CPU",
+                      "batch": a.batch, "ctx": a.ctx},
+           "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": blas + 1, "kind": kind,
+                            "sample": "one decoder layer per step (n730_read_layer + numpy fp32 GEMV for 7 "
+                                      "tensors), scaled by 28 layers + lm_head params"},
+           "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def run_ours(a):
+    import torch
+    world, rank, local = _dist()
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device(f"cuda:{local}"))
+    else:
+        torch.cuda.set_device(0)
+    from n730_b200.engine import Engine
+    from n730_b200.synthetic import SHAPES, build_on_device
+    shape = SHAPES[SHAPE_NAME]
+    B, ctx = a.batch, a.ctx
+    max_ctx = ctx + a.warmup + a.steps + 64
+    eng = Engine(shape, max_ctx=max_ctx, max_batch=B, max_prefill=512)
+    build_on_device(shape, "int4_g128", eng, seed=rank)
+    eng.finalize()
+    info = eng.info()
+    # prefill every sequence with a 2048-token uniform-random prompt (untimed)
+    rng = np.random.default_rng(100 + rank)
+    for b in range(B):
+        eng.forward(rng.integers(0, shape.vocab, ctx), seq=b)
+    st_ptr = eng.stream
+    st = torch.cuda.ExternalStream(st_ptr)
+    d_tok = torch.from_numpy(rng.integers(0, shape.vocab, B).astype(np.int32)).cuda()
+    d_logits = torch.empty(B, shape.vocab, device="cuda")
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    # ---- value: device-resident decode ----
+    for _ in range(a.warmup):
+        eng.decode_device(d_tok.data_ptr(), B, d_logits.data_ptr(), 0)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        e0.record(st)
+        for _ in range(a.steps):
+            eng.decode_device(0, B, 0, 0)
+        e1.record(st)
+        barrier()
+    t_dev = e0.elapsed_time(e1) / 1000.0
+    # ---- e2e: host ids in, host logits out, through the C ABI ----
+    host_tok = rng.integers(0, shape.vocab, B).astype(np.int32)
+    for _ in range(2):
+        eng.decode(host_tok)
+    barrier()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record(st)
+    for _ in range(a.steps):
+        eng.decode(host_tok)
+    e3.record(st)
+    barrier()
+    t_e2e = e2.elapsed_time(e3) / 1000.0
+    # ---- roofline: the dequant-GEMV alone on the gate|up weights of every layer ----
+    x = torch.randn(B, shape.hidden, device="cuda")
+    y = torch.empty(B, shape.ffn, device="cuda")
+    for l in range(shape.layers):
+        eng.run_linear(l, 2, x.data_ptr(), B, y.data_ptr(), st_ptr)
+    torch.cuda.synchronize()
+    reps = 5
+    e4, e5 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e4.record(st)
+    for _ in range(reps):
+        for l in range(shape.layers):
+            eng.run_linear(l, 2, x.data_ptr(), B, y.data_ptr(), st_ptr)
+    e5.record(st)
+    torch.cuda.synchronize()
+    t_gemv = e4.elapsed_time(e5) / 1000.0 / (reps * shape.layers)
+    gemv_bytes = eng.linear_bytes(0, 2, B)
+
+    # max over ranks
+    if world > 1:
+        tt = torch.tensor([t_dev, t_e2e, t_gemv], device="cuda", dtype=torch.float64)
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+        t_dev, t_e2e, t_gemv = tt.tolist()
+    if rank == 0:
+        peak, peak_kind = _peaks()
+        achieved = gemv_bytes / t_gemv / 1e9
+        traffic = None
+        tf = REPO / "profiles" / "gemv_gateup_traffic.json"
+        if tf.exists():
+            traffic = json.loads(tf.read_text()).get("traffic_bytes_per_launch")
+        toks = B * a.steps * world
+        kv_bytes = info["kv_bytes_per_pos"] * (ctx + a.warmup + a.steps // 2) * B
+        step_bytes = info["weight_bytes"] + kv_bytes
+        out = {
+            "metric": METRIC, "value": round(toks / t_dev, 2), "unit": "tok/s", "n_gpus": world,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(t_dev / a.steps * 1000, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int4 weights, fp32 math",
+            "data": "synthetic (random-init N(0,0.02) weights, uniform-random token ids)",
+            "config": {"workload": "qwen2-7b-shape decoder, all linears INT4 g128 (fp16 scale+zero), batch "
+                                   f"{B} decode after a {ctx}-token prefill, fp16 paged KV",
+                       "batch": B, "ctx_start": ctx, "parallelism": f"replicas x{world}" if world > 1 else "single",
+                       "l2": "no flush: 3.76 GB of weights stream from HBM every step (L2 126 MB)"},
+            "e2e": {"value": round(toks / t_e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
+                    "d2h_bytes_per_step": 4 * B * shape.vocab},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "kernel": "gemv_kernel<4,0,1,R> on gate|up 37888x3584 INT4 g128 (+SwiGLU)",
+                         "peak_source": peak_kind},
+            "step_roofline": {"bytes_per_step": step_bytes,
+                              "achieved_gbs": round(step_bytes / (t_dev / a.steps) / 1e9, 1),
+                              "frac": round(step_bytes / (t_dev / a.steps) / 1e9 / peak, 4)},
+            "clocks": clk.summary(),
+            "gpu_launches": a.steps * (5 * shape.layers + 3),
+        }
+        if not a.no_cpu_baseline:
+            cs = CpuLayerSample(shape)
+            t_token = min(cs.run() for _ in range(3))
+            cs.close()
+            out["cpu_baseline"] = {"value": round(1.0 / t_token, 4), "unit": "tok/s", "cores": cs.blas + 1,
+                                   "kind": "reference",
+                                   "sample": f"one qwen2-7b-shape decoder layer (best of 3, {cs.t_layer:.2f} s: "
+                                             "reference n730_read_layer per-tensor INT4, 1 thread, + numpy fp32 "
+                                             "GEMV on OpenBLAS threads), scaled to 28 layers + lm_head"}
+        print(json.dumps(out), flush=True)
+    eng.close()
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+def main():
+    a = _args()
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_ours(a)
+
+
+if __name__ == "__main__":
+    main()

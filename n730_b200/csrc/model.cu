@@ -1,0 +1,591 @@
+// Whole-model engine: resident packed weights, paged fp16 KV cache, one-call
+// decode step replayed as a CUDA graph, and prefill.
+//
+// Replaces the reference's per-op Python -> ctypes loop of
+// N730CudaTransformer.forward (src-code/inference.py:467-669): per token it
+// re-read every weight from disk, uploaded it synchronously, dequantised it to
+// fp32, ran cuBLAS, and computed the final norm and lm_head on the CPU.  Here
+// a decode step for B sequences is ~5 kernels per layer:
+//   qkv GEMV (RMSNorm prologue, bias) -> RoPE+GQA decode attention (KV append,
+//   split merge) -> o_proj GEMV (+residual) -> gate|up GEMV (RMSNorm, SwiGLU)
+//   -> down GEMV (+residual)
+// then the final-norm + lm_head GEMV and a position update, captured once per
+// batch size into a CUDA graph whose kernels chain with programmatic dependent
+// launch.  Host I/O per step is the token ids in and the logits out.
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <vector>
+
+#include "attention.h"
+#include "n730_cuda.h"
+#include "qweight.h"
+
+namespace n730 {
+
+int qweight_alloc_like(const QWeight& proto, int rows, QWeight** out);
+int qweight_copy_rows(QWeight& dst, const QWeight& src, int dst_row0, int stride, cudaStream_t st);
+void qweight_destroy(QWeight* w);
+
+__global__ void advance_seq_kernel(int* seq_lens, int batch, int by) {
+  pdl_wait();
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b < batch) seq_lens[b] += by;
+}
+
+struct Layer {
+  QWeight* qkv = nullptr;
+  QWeight* o = nullptr;
+  QWeight* gate_up = nullptr;
+  QWeight* down = nullptr;
+  float* ln1 = nullptr;
+  float* ln2 = nullptr;
+  float* qkv_bias = nullptr;
+  float* o_bias = nullptr;
+  float* gate_up_bias = nullptr;
+  float* down_bias = nullptr;
+  KVLayer kv{};
+};
+
+struct Model {
+  N730ModelConfig c{};
+  int qkv_dim = 0;
+  bool finalized = false;
+  std::vector<Layer> L;
+  std::map<std::pair<int, int>, QWeight*> pend_w;
+  std::map<std::pair<int, int>, std::vector<float>> pend_v;
+  QWeight* embed = nullptr;
+  QWeight* lm_head = nullptr;
+  float* final_norm = nullptr;
+  std::vector<void*> allocs;
+  float *cos_t = nullptr, *sin_t = nullptr;
+  __half *k_pool = nullptr, *v_pool = nullptr;
+  int* block_table = nullptr;
+  int* seq_lens = nullptr;
+  std::vector<int> h_seq;
+  int max_pages = 0, n_split = 1;
+  // decode workspace
+  int* d_tokens = nullptr;
+  float *x = nullptr, *qkv = nullptr, *attn = nullptr, *mlp = nullptr, *logits = nullptr;
+  float2* part_ml = nullptr;
+  float* part_acc = nullptr;
+  int* counters = nullptr;
+  // prefill workspace
+  int* p_tokens = nullptr;
+  float *px = nullptr, *pqkv = nullptr, *pattn = nullptr, *pmlp = nullptr;
+  int32_t* h_tok = nullptr;  // pinned
+  float* h_logits = nullptr;  // pinned [max_batch][vocab]
+  cudaStream_t st = nullptr;
+  std::map<int, cudaGraphExec_t> graphs;
+  int device = 0;
+
+  template <typename T>
+  int alloc(T** p, size_t n) {
+    void* q = nullptr;
+    if (cudaMalloc(&q, n * sizeof(T)) != cudaSuccess) {
+      cudaGetLastError();
+      set_error("model: out of device memory allocating %zu bytes", n * sizeof(T));
+      return N730_OOM;
+    }
+    allocs.push_back(q);
+    *p = (T*)q;
+    return N730_OK;
+  }
+};
+
+static int upload_vec(Model* m, const std::vector<float>& v, float** out) {
+  if (int rc = m->alloc(out, v.size())) return rc;
+  N730_CUDA(cudaMemcpyAsync(*out, v.data(), v.size() * 4, cudaMemcpyHostToDevice, m->st));
+  return N730_OK;
+}
+
+static int fuse_rows(Model* m, std::vector<QWeight*> parts, bool interleave, QWeight** out) {
+  for (auto* p : parts) N730_REQUIRE(p, N730_STATE, "model: missing projection weight");
+  int rows = 0;
+  for (auto* p : parts) rows += p->rows;
+  QWeight* f = nullptr;
+  if (int rc = qweight_alloc_like(*parts[0], rows, &f)) return rc;
+  int r0 = 0;
+  for (size_t i = 0; i < parts.size(); ++i) {
+    int rc = interleave ? qweight_copy_rows(*f, *parts[i], (int)i, (int)parts.size(), m->st)
+                        : qweight_copy_rows(*f, *parts[i], r0, 1, m->st);
+    if (rc) { qweight_destroy(f); return rc; }
+    r0 += parts[i]->rows;
+  }
+  *out = f;
+  return N730_OK;
+}
+
+static int finalize(Model* m) {
+  const N730ModelConfig& c = m->c;
+  const int nl = c.layers;
+  m->L.assign(nl, Layer{});
+  auto W = [&](int l, int s) -> QWeight* {
+    auto it = m->pend_w.find({l, s});
+    return it == m->pend_w.end() ? nullptr : it->second;
+  };
+  auto V = [&](int l, int s) -> const std::vector<float>* {
+    auto it = m->pend_v.find({l, s});
+    return it == m->pend_v.end() ? nullptr : &it->second;
+  };
+  m->embed = W(-1, N730_W_EMBED);
+  N730_REQUIRE(m->embed, N730_STATE, "model: embedding weight not set");
+  N730_REQUIRE(m->embed->rows == c.vocab && m->embed->cols == c.hidden, N730_BAD_ARG,
+               "model: embedding is %dx%d, expected %dx%d", m->embed->rows, m->embed->cols, c.vocab, c.hidden);
+  m->lm_head = W(-1, N730_W_LMHEAD);
+  if (!m->lm_head) {
+    N730_REQUIRE(c.tie_embeddings, N730_STATE, "model: lm_head not set and embeddings not tied");
+    m->lm_head = m->embed;
+  }
+  m->qkv_dim = (c.heads + 2 * c.kv_heads) * c.head_dim;
+  for (int l = 0; l < nl; ++l) {
+    Layer& y = m->L[l];
+    QWeight *q = W(l, N730_W_Q), *k = W(l, N730_W_K), *v = W(l, N730_W_V);
+    N730_REQUIRE(q && k && v && W(l, N730_W_O) && W(l, N730_W_GATE) && W(l, N730_W_UP) && W(l, N730_W_DOWN),
+                 N730_STATE, "model: layer %d is missing a projection", l);
+    N730_REQUIRE(q->rows == c.heads * c.head_dim && k->rows == c.kv_heads * c.head_dim &&
+                     v->rows == c.kv_heads * c.head_dim && q->cols == c.hidden,
+                 N730_BAD_ARG, "model: layer %d q/k/v shapes do not match the config", l);
+    if (int rc = fuse_rows(m, {q, k, v}, false, &y.qkv)) return rc;
+    y.o = W(l, N730_W_O);
+    if (int rc = fuse_rows(m, {W(l, N730_W_GATE), W(l, N730_W_UP)}, true, &y.gate_up)) return rc;
+    y.down = W(l, N730_W_DOWN);
+    N730_REQUIRE(y.o->rows == c.hidden && y.o->cols == c.heads * c.head_dim && y.gate_up->rows == 2 * c.ffn &&
+                     y.gate_up->cols == c.hidden && y.down->rows == c.hidden && y.down->cols == c.ffn,
+                 N730_BAD_ARG, "model: layer %d o/gate/up/down shapes do not match the config", l);
+    std::vector<float> ones(c.hidden, 1.f);
+    const std::vector<float>* n1 = V(l, N730_V_INPUT_NORM);
+    const std::vector<float>* n2 = V(l, N730_V_POST_NORM);
+    if (int rc = upload_vec(m, n1 ? *n1 : ones, &y.ln1)) return rc;
+    if (int rc = upload_vec(m, n2 ? *n2 : ones, &y.ln2)) return rc;
+    const auto *bq = V(l, N730_V_Q_BIAS), *bk = V(l, N730_V_K_BIAS), *bv = V(l, N730_V_V_BIAS);
+    if (bq || bk || bv) {
+      std::vector<float> b(m->qkv_dim, 0.f);
+      if (bq) std::copy(bq->begin(), bq->end(), b.begin());
+      if (bk) std::copy(bk->begin(), bk->end(), b.begin() + c.heads * c.head_dim);
+      if (bv) std::copy(bv->begin(), bv->end(), b.begin() + (c.heads + c.kv_heads) * c.head_dim);
+      if (int rc = upload_vec(m, b, &y.qkv_bias)) return rc;
+    }
+    if (const auto* bo = V(l, N730_V_O_BIAS))
+      if (int rc = upload_vec(m, *bo, &y.o_bias)) return rc;
+    if (const auto* bd = V(l, N730_V_DOWN_BIAS))
+      if (int rc = upload_vec(m, *bd, &y.down_bias)) return rc;
+    const auto *bg = V(l, N730_V_GATE_BIAS), *bu = V(l, N730_V_UP_BIAS);
+    if (bg || bu) {
+      std::vector<float> b(2 * c.ffn, 0.f);
+      for (int i = 0; i < c.ffn; ++i) {
+        if (bg) b[2 * i] = (*bg)[i];
+        if (bu) b[2 * i + 1] = (*bu)[i];
+      }
+      if (int rc = upload_vec(m, b, &y.gate_up_bias)) return rc;
+    }
+  }
+  {
+    std::vector<float> ones(c.hidden, 1.f);
+    const std::vector<float>* fn = V(-1, N730_V_FINAL_NORM);
+    if (int rc = upload_vec(m, fn ? *fn : ones, &m->final_norm)) return rc;
+  }
+  N730_CUDA(cudaStreamSynchronize(m->st));
+  for (auto& kv : m->pend_w) {
+    const int s = kv.first.second;
+    if (s == N730_W_Q || s == N730_W_K || s == N730_W_V || s == N730_W_GATE || s == N730_W_UP)
+      qweight_destroy(kv.second);
+  }
+  m->pend_w.clear();
+  m->pend_v.clear();
+
+  // RoPE tables as the reference builds them (n730_cuda.cu:650-661)
+  const int h2 = c.head_dim / 2;
+  {
+    std::vector<float> hc((size_t)c.max_ctx * h2), hs((size_t)c.max_ctx * h2);
+    for (int pos = 0; pos < c.max_ctx; ++pos)
+      for (int i = 0; i < h2; ++i) {
+        const float freq = 1.0f / powf(c.rope_theta, (float)(2 * i) / c.head_dim);
+        const float ang = pos * freq;
+        hc[(size_t)pos * h2 + i] = cosf(ang);
+        hs[(size_t)pos * h2 + i] = sinf(ang);
+      }
+    if (int rc = upload_vec(m, hc, &m->cos_t)) return rc;
+    if (int rc = upload_vec(m, hs, &m->sin_t)) return rc;
+  }
+  // paged KV: sequence b owns pages [b*max_pages, (b+1)*max_pages)
+  m->max_pages = (c.max_ctx + c.page_size - 1) / c.page_size;
+  const size_t pages = (size_t)c.max_batch * m->max_pages;
+  const size_t per_layer = pages * c.kv_heads * c.page_size * c.head_dim;
+  if (int rc = m->alloc(&m->k_pool, per_layer * nl)) return rc;
+  if (int rc = m->alloc(&m->v_pool, per_layer * nl)) return rc;
+  for (int l = 0; l < nl; ++l) m->L[l].kv = KVLayer{m->k_pool + per_layer * l, m->v_pool + per_layer * l};
+  {
+    std::vector<int> bt(pages);
+    for (size_t i = 0; i < pages; ++i) bt[i] = (int)i;
+    if (int rc = m->alloc(&m->block_table, pages)) return rc;
+    N730_CUDA(cudaMemcpyAsync(m->block_table, bt.data(), pages * 4, cudaMemcpyHostToDevice, m->st));
+  }
+  if (int rc = m->alloc(&m->seq_lens, c.max_batch)) return rc;
+  N730_CUDA(cudaMemsetAsync(m->seq_lens, 0, c.max_batch * 4, m->st));
+  m->h_seq.assign(c.max_batch, 0);
+  // decode workspace
+  const int B = c.max_batch;
+  m->n_split = std::max(1, std::min(64, (c.max_ctx + 63) / 64));
+  if (int rc = m->alloc(&m->d_tokens, B)) return rc;
+  if (int rc = m->alloc(&m->x, (size_t)B * c.hidden)) return rc;
+  if (int rc = m->alloc(&m->qkv, (size_t)B * m->qkv_dim)) return rc;
+  if (int rc = m->alloc(&m->attn, (size_t)B * c.heads * c.head_dim)) return rc;
+  if (int rc = m->alloc(&m->mlp, (size_t)B * c.ffn)) return rc;
+  if (int rc = m->alloc(&m->logits, (size_t)B * c.vocab)) return rc;
+  if (int rc = m->alloc(&m->part_ml, (size_t)B * c.heads * m->n_split)) return rc;
+  if (int rc = m->alloc(&m->part_acc, (size_t)B * c.heads * m->n_split * c.head_dim)) return rc;
+  if (int rc = m->alloc(&m->counters, (size_t)B * c.kv_heads)) return rc;
+  N730_CUDA(cudaMemsetAsync(m->counters, 0, (size_t)B * c.kv_heads * 4, m->st));
+  // prefill workspace
+  const int P = c.max_prefill;
+  if (int rc = m->alloc(&m->p_tokens, P)) return rc;
+  if (int rc = m->alloc(&m->px, (size_t)P * c.hidden)) return rc;
+  if (int rc = m->alloc(&m->pqkv, (size_t)P * m->qkv_dim)) return rc;
+  if (int rc = m->alloc(&m->pattn, (size_t)P * c.heads * c.head_dim)) return rc;
+  if (int rc = m->alloc(&m->pmlp, (size_t)P * c.ffn)) return rc;
+  N730_CUDA(cudaMallocHost(&m->h_tok, (size_t)std::max(B, P) * 4));
+  N730_CUDA(cudaMallocHost(&m->h_logits, (size_t)B * c.vocab * 4));
+  N730_CUDA(cudaStreamSynchronize(m->st));
+  m->finalized = true;
+  return N730_OK;
+}
+
+static int gemv(Model* m, const QWeight* w, const float* x, int ldx, int batch, float* y, int ldy,
+                const float* bias, const float* resid, int ldr, const float* norm, int swiglu) {
+  GemvArgs a = {};
+  a.w = w; a.x = x; a.ldx = ldx; a.batch = batch; a.y = y; a.ldy = ldy; a.bias = bias;
+  a.residual = resid; a.ldr = ldr; a.norm_w = norm; a.eps = m->c.rms_eps; a.swiglu = swiglu;
+  a.pdl = m->c.use_pdl;
+  return gemv_launch(a, m->st);
+}
+
+static AttnDims dims(const Model* m) {
+  AttnDims d;
+  d.n_heads = m->c.heads; d.n_kv = m->c.kv_heads; d.head_dim = m->c.head_dim;
+  d.page_size = m->c.page_size; d.max_pages = m->max_pages;
+  d.scale = 1.0f / sqrtf((float)m->c.head_dim);
+  return d;
+}
+
+// Enqueue one decode step for sequences [0, B) on m->st (tokens in m->d_tokens).
+static int enqueue_decode(Model* m, int B) {
+  const N730ModelConfig& c = m->c;
+  const int h = c.hidden, ad = c.heads * c.head_dim;
+  if (int rc = embed_launch(*m->embed, m->d_tokens, B, m->x, m->st)) return rc;
+  for (int l = 0; l < c.layers; ++l) {
+    Layer& y = m->L[l];
+    if (int rc = gemv(m, y.qkv, m->x, h, B, m->qkv, m->qkv_dim, y.qkv_bias, nullptr, 0, y.ln1, 0)) return rc;
+    DecodeAttnArgs a = {};
+    a.qkv = m->qkv; a.ld_qkv = m->qkv_dim; a.cos_t = m->cos_t; a.sin_t = m->sin_t;
+    a.seq_lens = m->seq_lens; a.block_table = m->block_table; a.kv = y.kv; a.d = dims(m);
+    a.out = m->attn; a.batch = B; a.n_split = m->n_split; a.part_ml = m->part_ml; a.part_acc = m->part_acc;
+    a.counters = m->counters; a.pdl = c.use_pdl;
+    if (int rc = attn_decode_launch(a, m->st)) return rc;
+    if (int rc = gemv(m, y.o, m->attn, ad, B, m->x, h, y.o_bias, m->x, h, nullptr, 0)) return rc;
+    if (int rc = gemv(m, y.gate_up, m->x, h, B, m->mlp, c.ffn, y.gate_up_bias, nullptr, 0, y.ln2, 1)) return rc;
+    if (int rc = gemv(m, y.down, m->mlp, c.ffn, B, m->x, h, y.down_bias, m->x, h, nullptr, 0)) return rc;
+  }
+  if (int rc = gemv(m, m->lm_head, m->x, h, B, m->logits, c.vocab, nullptr, nullptr, 0, m->final_norm, 0)) return rc;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((B + 127) / 128);
+  cfg.blockDim = dim3(128);
+  cfg.stream = m->st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = c.use_pdl ? 1 : 0;
+  N730_CUDA(cudaLaunchKernelEx(&cfg, advance_seq_kernel, m->seq_lens, B, 1));
+  return N730_OK;
+}
+
+static int run_decode(Model* m, int B) {
+  if (!m->c.use_graphs) return enqueue_decode(m, B);
+  auto it = m->graphs.find(B);
+  if (it == m->graphs.end()) {
+    cudaGraph_t g = nullptr;
+    N730_CUDA(cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal));
+    int rc = enqueue_decode(m, B);
+    cudaError_t e = cudaStreamEndCapture(m->st, &g);
+    if (rc) { if (g) cudaGraphDestroy(g); return rc; }
+    N730_CUDA(e);
+    cudaGraphExec_t ex = nullptr;
+    e = cudaGraphInstantiate(&ex, g, 0);
+    cudaGraphDestroy(g);
+    N730_CUDA(e);
+    it = m->graphs.emplace(B, ex).first;
+  }
+  N730_CUDA(cudaGraphLaunch(it->second, m->st));
+  return N730_OK;
+}
+
+static int check_capacity(Model* m, int b, int add) {
+  N730_REQUIRE(m->h_seq[b] + add <= m->c.max_ctx, N730_STATE,
+               "KV cache capacity exceeded: %d tokens requested, maximum is %d", m->h_seq[b] + add, m->c.max_ctx);
+  return N730_OK;
+}
+
+static int prefill(Model* m, int seq, const int32_t* d_tok, int T, float* d_logits_row) {
+  const N730ModelConfig& c = m->c;
+  const int h = c.hidden, ad = c.heads * c.head_dim;
+  int done = 0;
+  while (done < T) {
+    const int n = std::min(c.max_prefill, T - done);
+    const int pos0 = m->h_seq[seq] + done;
+    if (int rc = embed_launch(*m->embed, d_tok + done, n, m->px, m->st)) return rc;
+    for (int l = 0; l < c.layers; ++l) {
+      Layer& y = m->L[l];
+      if (int rc = gemv(m, y.qkv, m->px, h, n, m->pqkv, m->qkv_dim, y.qkv_bias, nullptr, 0, y.ln1, 0)) return rc;
+      KVWriteArgs kw = {};
+      kw.qkv = m->pqkv; kw.ld_qkv = m->qkv_dim; kw.cos_t = m->cos_t; kw.sin_t = m->sin_t;
+      kw.block_table = m->block_table + (size_t)seq * m->max_pages; kw.kv = y.kv; kw.d = dims(m);
+      kw.T = n; kw.pos0 = pos0; kw.pdl = c.use_pdl;
+      if (int rc = kv_write_launch(kw, m->st)) return rc;
+      PrefillAttnArgs pa = {};
+      pa.qkv = m->pqkv; pa.ld_qkv = m->qkv_dim; pa.block_table = kw.block_table; pa.kv = y.kv; pa.d = dims(m);
+      pa.T = n; pa.pos0 = pos0; pa.out = m->pattn; pa.pdl = c.use_pdl;
+      if (int rc = attn_prefill_launch(pa, m->st)) return rc;
+      if (int rc = gemv(m, y.o, m->pattn, ad, n, m->px, h, y.o_bias, m->px, h, nullptr, 0)) return rc;
+      if (int rc = gemv(m, y.gate_up, m->px, h, n, m->pmlp, c.ffn, y.gate_up_bias, nullptr, 0, y.ln2, 1)) return rc;
+      if (int rc = gemv(m, y.down, m->pmlp, c.ffn, n, m->px, h, y.down_bias, m->px, h, nullptr, 0)) return rc;
+    }
+    done += n;
+    if (done == T && d_logits_row)
+      if (int rc = gemv(m, m->lm_head, m->px + (size_t)(n - 1) * h, h, 1, d_logits_row, c.vocab, nullptr, nullptr,
+                        0, m->final_norm, 0))
+        return rc;
+  }
+  return N730_OK;
+}
+
+}  // namespace n730
+
+using namespace n730;
+
+#define MODEL(p) Model* m = (Model*)(p); if (!m) return N730_NULL
+
+N730_API int n730_model_create(const N730ModelConfig* cfg, void** out) {
+  if (!cfg || !out) return N730_NULL;
+  *out = nullptr;
+  const N730ModelConfig& c = *cfg;
+  N730_REQUIRE(c.hidden > 0 && c.layers > 0 && c.heads > 0 && c.kv_heads > 0 && c.heads % c.kv_heads == 0 &&
+                   c.head_dim > 0 && c.ffn > 0 && c.vocab > 0 && c.max_ctx > 0 && c.max_batch > 0,
+               N730_BAD_ARG, "model_create: invalid config");
+  N730_REQUIRE(c.head_dim == 64 || c.head_dim == 128, N730_UNSUPPORTED, "model_create: head_dim %d", c.head_dim);
+  Model* m = new Model();
+  m->c = c;
+  if (m->c.page_size <= 0) m->c.page_size = 64;
+  if (m->c.max_prefill <= 0) m->c.max_prefill = 512;
+  if (m->c.tp_size <= 0) m->c.tp_size = 1;
+  cudaGetDevice(&m->device);
+  if (cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking) != cudaSuccess) {
+    delete m;
+    return N730_CUDA_ERR;
+  }
+  *out = m;
+  return N730_OK;
+}
+
+N730_API void n730_model_destroy(void* p) {
+  Model* m = (Model*)p;
+  if (!m) return;
+  cudaStreamSynchronize(m->st);
+  for (auto& g : m->graphs) cudaGraphExecDestroy(g.second);
+  for (auto& kv : m->pend_w) qweight_destroy(kv.second);
+  for (auto& y : m->L) {
+    qweight_destroy(y.qkv); qweight_destroy(y.o); qweight_destroy(y.gate_up); qweight_destroy(y.down);
+  }
+  if (m->lm_head != m->embed) qweight_destroy(m->lm_head);
+  qweight_destroy(m->embed);
+  for (void* a : m->allocs) cudaFree(a);
+  if (m->h_tok) cudaFreeHost(m->h_tok);
+  if (m->h_logits) cudaFreeHost(m->h_logits);
+  cudaStreamDestroy(m->st);
+  delete m;
+}
+
+N730_API int n730_model_set_qweight(void* p, int layer, int slot, void* qw) {
+  MODEL(p);
+  N730_REQUIRE(!m->finalized, N730_STATE, "model: already finalized");
+  N730_REQUIRE(qw, N730_NULL, "model: null weight");
+  const bool global = slot == N730_W_EMBED || slot == N730_W_LMHEAD;
+  N730_REQUIRE(global ? layer == -1 : (layer >= 0 && layer < m->c.layers && slot >= N730_W_Q && slot <= N730_W_DOWN),
+               N730_BAD_ARG, "model: bad weight slot %d for layer %d", slot, layer);
+  auto key = std::make_pair(layer, slot);
+  auto it = m->pend_w.find(key);
+  if (it != m->pend_w.end()) qweight_destroy(it->second);
+  m->pend_w[key] = (QWeight*)qw;
+  return N730_OK;
+}
+
+N730_API int n730_model_set_vector(void* p, int layer, int slot, const float* data, int n, int on_device) {
+  MODEL(p);
+  N730_REQUIRE(!m->finalized, N730_STATE, "model: already finalized");
+  N730_REQUIRE(data && n > 0, N730_NULL, "model: null vector");
+  std::vector<float> v(n);
+  if (on_device) N730_CUDA(cudaMemcpy(v.data(), data, (size_t)n * 4, cudaMemcpyDeviceToHost));
+  else memcpy(v.data(), data, (size_t)n * 4);
+  m->pend_v[{layer, slot}] = std::move(v);
+  return N730_OK;
+}
+
+N730_API int n730_model_finalize(void* p) {
+  MODEL(p);
+  N730_REQUIRE(!m->finalized, N730_STATE, "model: already finalized");
+  return finalize(m);
+}
+
+N730_API int n730_model_reset(void* p) {
+  MODEL(p);
+  N730_REQUIRE(m->finalized, N730_STATE, "model: not finalized");
+  std::fill(m->h_seq.begin(), m->h_seq.end(), 0);
+  N730_CUDA(cudaMemsetAsync(m->seq_lens, 0, m->c.max_batch * 4, m->st));
+  N730_CUDA(cudaStreamSynchronize(m->st));
+  return N730_OK;
+}
+
+N730_API int n730_model_seq_len(void* p, int seq) {
+  MODEL(p);
+  N730_REQUIRE(seq >= 0 && seq < m->c.max_batch && m->finalized, N730_BAD_ARG, "model: bad sequence %d", seq);
+  return m->h_seq[seq];
+}
+
+// Decode one token for each of sequences [0, batch): host token ids in,
+// host logits [batch][vocab] out (pinned staging, copies inside the call).
+N730_API int n730_model_decode(void* p, const int32_t* host_tokens, int batch, float* host_logits) {
+  MODEL(p);
+  N730_REQUIRE(m->finalized, N730_STATE, "model: not finalized");
+  N730_REQUIRE(host_tokens && batch >= 1 && batch <= m->c.max_batch, N730_BAD_ARG, "decode: batch %d", batch);
+  for (int b = 0; b < batch; ++b) {
+    N730_REQUIRE(host_tokens[b] >= 0 && host_tokens[b] < m->c.vocab, N730_BAD_ARG, "decode: token id %d out of range",
+                 host_tokens[b]);
+    if (int rc = check_capacity(m, b, 1)) return rc;
+  }
+  memcpy(m->h_tok, host_tokens, (size_t)batch * 4);
+  N730_CUDA(cudaMemcpyAsync(m->d_tokens, m->h_tok, (size_t)batch * 4, cudaMemcpyHostToDevice, m->st));
+  if (int rc = run_decode(m, batch)) return rc;
+  if (host_logits) {
+    N730_CUDA(cudaMemcpyAsync(m->h_logits, m->logits, (size_t)batch * m->c.vocab * 4, cudaMemcpyDeviceToHost, m->st));
+  }
+  N730_CUDA(cudaStreamSynchronize(m->st));
+  if (host_logits) memcpy(host_logits, m->h_logits, (size_t)batch * m->c.vocab * 4);
+  for (int b = 0; b < batch; ++b) m->h_seq[b] += 1;
+  return gemv_check_error(true);
+}
+
+// Device-resident decode step (no host copies, no synchronisation): d_tokens
+// [batch] int32 and d_logits [batch][vocab] live in device memory; runs on
+// `stream` after the model's own stream work.  Used to time the device path.
+N730_API int n730_model_decode_device(void* p, const int32_t* d_tokens, int batch, float* d_logits, void* stream) {
+  MODEL(p);
+  N730_REQUIRE(m->finalized, N730_STATE, "model: not finalized");
+  N730_REQUIRE(batch >= 1 && batch <= m->c.max_batch, N730_BAD_ARG, "decode: batch %d", batch);
+  for (int b = 0; b < batch; ++b) if (int rc = check_capacity(m, b, 1)) return rc;
+  cudaStream_t us = (cudaStream_t)stream;
+  cudaEvent_t ev;
+  N730_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+  if (us) { N730_CUDA(cudaEventRecord(ev, us)); N730_CUDA(cudaStreamWaitEvent(m->st, ev, 0)); }
+  if (d_tokens) N730_CUDA(cudaMemcpyAsync(m->d_tokens, d_tokens, (size_t)batch * 4, cudaMemcpyDeviceToDevice, m->st));
+  int rc = run_decode(m, batch);
+  if (!rc && d_logits)
+    rc = cuda_rc(cudaMemcpyAsync(d_logits, m->logits, (size_t)batch * m->c.vocab * 4, cudaMemcpyDeviceToDevice, m->st),
+                 __FILE__, __LINE__);
+  if (us) { cudaEventRecord(ev, m->st); cudaStreamWaitEvent(us, ev, 0); }
+  cudaEventDestroy(ev);
+  if (rc) return rc;
+  for (int b = 0; b < batch; ++b) m->h_seq[b] += 1;
+  return N730_OK;
+}
+
+// Append `n` tokens to sequence `seq` (prefill when n > 1, the decode graph
+// when n == 1 and seq == 0) and return the logits of the last position.
+N730_API int n730_model_forward(void* p, int seq, const int32_t* host_tokens, int n, float* host_logits) {
+  MODEL(p);
+  N730_REQUIRE(m->finalized, N730_STATE, "model: not finalized");
+  N730_REQUIRE(host_tokens && n >= 1, N730_BAD_ARG, "forward requires at least one token");
+  N730_REQUIRE(seq >= 0 && seq < m->c.max_batch, N730_BAD_ARG, "forward: bad sequence %d", seq);
+  for (int i = 0; i < n; ++i)
+    N730_REQUIRE(host_tokens[i] >= 0 && host_tokens[i] < m->c.vocab, N730_BAD_ARG, "token id %d out of range",
+                 host_tokens[i]);
+  if (int rc = check_capacity(m, seq, n)) return rc;
+  if (n == 1 && seq == 0) return n730_model_decode(p, host_tokens, 1, host_logits);
+  int done = 0;
+  while (done < n) {  // chunks of the pinned staging size
+    const int k = std::min(n - done, m->c.max_prefill);
+    memcpy(m->h_tok, host_tokens + done, (size_t)k * 4);
+    N730_CUDA(cudaMemcpyAsync(m->p_tokens, m->h_tok, (size_t)k * 4, cudaMemcpyHostToDevice, m->st));
+    if (int rc = prefill(m, seq, m->p_tokens, k, done + k == n ? m->logits : nullptr)) return rc;
+    N730_CUDA(cudaStreamSynchronize(m->st));
+    m->h_seq[seq] += k;
+    // the device copy of the length was written before this chunk's update
+    N730_CUDA(cudaMemcpyAsync(m->seq_lens + seq, &m->h_seq[seq], 4, cudaMemcpyHostToDevice, m->st));
+    done += k;
+  }
+  if (host_logits) N730_CUDA(cudaMemcpyAsync(m->h_logits, m->logits, (size_t)m->c.vocab * 4, cudaMemcpyDeviceToHost, m->st));
+  N730_CUDA(cudaStreamSynchronize(m->st));
+  if (host_logits) memcpy(host_logits, m->h_logits, (size_t)m->c.vocab * 4);
+  return gemv_check_error(true);
+}
+
+// info[16]: weight bytes, kv bytes per position, kv capacity bytes, n_split,
+// qkv_dim, max_pages, finalized
+N730_API int n730_model_info(void* p, int64_t* info) {
+  MODEL(p);
+  if (!info) return N730_NULL;
+  memset(info, 0, 16 * sizeof(int64_t));
+  if (!m->finalized) return N730_OK;
+  auto bytes = [](const QWeight* w) {
+    return w ? w->rows * w->row_bytes + (w->bits == 16 ? 0 : (int64_t)w->rows * w->sz_pitch) : 0;
+  };
+  int64_t wb = bytes(m->embed) + (m->lm_head != m->embed ? bytes(m->lm_head) : 0);
+  for (auto& y : m->L) wb += bytes(y.qkv) + bytes(y.o) + bytes(y.gate_up) + bytes(y.down);
+  info[0] = wb;
+  info[1] = (int64_t)m->c.layers * 2 * m->c.kv_heads * m->c.head_dim * 2;
+  info[2] = info[1] * m->c.max_batch * (int64_t)m->max_pages * m->c.page_size;
+  info[3] = m->n_split;
+  info[4] = m->qkv_dim;
+  info[5] = m->max_pages;
+  info[6] = m->finalized;
+  return N730_OK;
+}
+
+N730_API void* n730_model_stream(void* p) { return p ? ((Model*)p)->st : nullptr; }
+
+// Run one resident linear of the model alone (no norm / bias / residual):
+// which = 0 q|k|v, 1 o_proj, 2 gate|up (SwiGLU), 3 down_proj, 4 lm_head.
+// d_x [batch][cols], d_y [batch][rows] (rows/2 for gate|up).  Used to time
+// the dequant-GEMV kernel on the model's real weights.
+N730_API int n730_model_run_linear(void* p, int layer, int which, const float* d_x, int batch, float* d_y,
+                                   void* stream) {
+  MODEL(p);
+  N730_REQUIRE(m->finalized && d_x && d_y, N730_STATE, "run_linear: model not finalized or null buffers");
+  const QWeight* w = nullptr;
+  if (which == 4) w = m->lm_head;
+  else {
+    N730_REQUIRE(layer >= 0 && layer < m->c.layers, N730_BAD_ARG, "run_linear: layer %d", layer);
+    const Layer& y = m->L[layer];
+    w = which == 0 ? y.qkv : which == 1 ? y.o : which == 2 ? y.gate_up : which == 3 ? y.down : nullptr;
+  }
+  N730_REQUIRE(w, N730_BAD_ARG, "run_linear: which %d", which);
+  GemvArgs a = {};
+  a.w = w; a.x = d_x; a.ldx = w->cols; a.batch = batch; a.y = d_y;
+  a.swiglu = which == 2; a.ldy = which == 2 ? w->rows / 2 : w->rows;
+  return gemv_launch(a, stream ? (cudaStream_t)stream : m->st);
+}
+
+// Algorithmic bytes of one linear: packed codes + scale/zero + x + y.
+N730_API int64_t n730_model_linear_bytes(void* p, int layer, int which, int batch) {
+  Model* m = (Model*)p;
+  if (!m || !m->finalized) return -1;
+  const QWeight* w = which == 4 ? m->lm_head
+                   : (layer < 0 || layer >= m->c.layers) ? nullptr
+                   : which == 0 ? m->L[layer].qkv : which == 1 ? m->L[layer].o
+                   : which == 2 ? m->L[layer].gate_up : which == 3 ? m->L[layer].down : nullptr;
+  if (!w) return -1;
+  const int64_t codes = ((int64_t)w->rows * w->cols * w->bits + 7) / 8;
+  const int64_t sz = w->bits == 16 ? 0 : (w->sz_mode == 0 ? (int64_t)w->rows * w->n_groups * 4 : 8);
+  const int64_t out_rows = which == 2 ? w->rows / 2 : w->rows;
+  return codes + sz + (int64_t)batch * (w->cols + out_rows) * 4;
+}

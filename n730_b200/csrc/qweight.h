@@ -1,0 +1,59 @@
+// Packed weights resident in HBM, and the kernels that consume them.
+#pragma once
+#include "common.cuh"
+
+namespace n730 {
+
+// Device layout of one linear weight W[rows, cols] (out x in).
+//   codes : [rows][row_bytes] packed codes, element 0 of a row in the least
+//           significant bits (the .n730 packing), rows padded to 16 bytes.
+//           For FP16 weights: [rows][cols] fp16.
+//   sz    : sz_mode 0 -> half2 (scale, zero) per (row, group), rows of sz_pitch bytes
+//           sz_mode 1 -> float2 (scale, zero) per row, rows of sz_pitch (16) bytes
+//           (sz_pitch is a multiple of 16 so a run of rows is one bulk copy)
+//           (per-tensor blocks are stored as mode 1 with the tensor's fp32
+//           scale and zero point on every row, so dequant stays bit-exact)
+// Dequantised value: (float(q) - zero) * scale, fp32, no contraction.
+struct QWeight {
+  int prec = 0;
+  int bits = 0;
+  int rows = 0;
+  int cols = 0;
+  int group = 0;      // elements per group (== cols for sz_mode 1)
+  int n_groups = 0;   // groups per row
+  int sz_mode = 0;
+  int64_t row_bytes = 0;
+  int64_t sz_pitch = 0;
+  uint8_t* codes = nullptr;
+  void* sz = nullptr;
+  bool owns = true;
+  int device = 0;
+};
+
+struct GemvArgs {
+  const QWeight* w;
+  const float* x;        // [batch][ldx] fp32 activations
+  int ldx;
+  int batch;
+  float* y;              // [batch][ldy]
+  int ldy;
+  const float* bias;     // [rows] or null
+  const float* residual; // [batch][ldr] or null; y = residual + W x (+ bias); may alias y
+  int ldr;
+  const float* norm_w;   // [cols] RMSNorm weight applied to x first, or null
+  float eps;
+  int swiglu;            // rows interleaved gate/up: y[b][r/2] = silu(g)*u
+  int pdl;               // launched with programmatic dependent launch
+};
+
+int gemv_launch(const GemvArgs& a, cudaStream_t stream);
+int gemv_check_error(bool reset);  // N730_TIMEOUT if a device wait ran out
+int dequant_launch(const QWeight& w, float* out, int64_t ld_out, int row0, int nrows,
+                   cudaStream_t stream);
+int repack_rows_launch(const uint8_t* src, int bits, int rows, int cols, uint8_t* dst,
+                       int64_t row_bytes, cudaStream_t stream);
+int fill_f2_launch(void* out, int64_t pitch, int n, float a, float b, cudaStream_t stream);
+int64_t sz_pitch_for(int sz_mode, int n_groups);
+int embed_launch(const QWeight& w, const int32_t* tokens, int n, float* out, cudaStream_t stream);
+
+}  // namespace n730

@@ -1,0 +1,229 @@
+"""Python wrapper of the C model engine (include/n730_cuda.h, "whole-model engine").
+
+Weights enter as packed ``QWeight`` handles (``qweight_from_block`` for
+``.n730`` blocks, ``qweight_from_device`` for device buffers); the engine
+fuses q|k|v and gate/up, owns the paged KV cache, and runs prefill and the
+graph-replayed decode step.  Torch is not required here.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import _lib
+from .formats import RawBlock, GROUPED
+
+W_Q, W_K, W_V, W_O, W_GATE, W_UP, W_DOWN, W_EMBED, W_LMHEAD = range(9)
+V_INPUT_NORM, V_POST_NORM, V_Q_BIAS, V_K_BIAS, V_V_BIAS, V_O_BIAS, V_GATE_BIAS, V_UP_BIAS, V_DOWN_BIAS, \
+    V_FINAL_NORM = range(10)
+
+PROJ_SLOTS = {"self_attn.q_proj": W_Q, "self_attn.k_proj": W_K, "self_attn.v_proj": W_V,
+              "self_attn.o_proj": W_O, "mlp.gate_proj": W_GATE, "mlp.up_proj": W_UP,
+              "mlp.down_proj": W_DOWN}
+BIAS_SLOTS = {"self_attn.q_proj": V_Q_BIAS, "self_attn.k_proj": V_K_BIAS, "self_attn.v_proj": V_V_BIAS,
+              "self_attn.o_proj": V_O_BIAS, "mlp.gate_proj": V_GATE_BIAS, "mlp.up_proj": V_UP_BIAS,
+              "mlp.down_proj": V_DOWN_BIAS}
+
+
+class N730ModelConfig(C.Structure):
+    _fields_ = [(n, C.c_int32) for n in ("hidden", "layers", "heads", "kv_heads", "head_dim", "ffn", "vocab")] + \
+               [("rms_eps", C.c_float), ("rope_theta", C.c_float)] + \
+               [(n, C.c_int32) for n in ("max_ctx", "max_batch", "page_size", "max_prefill", "tie_embeddings",
+                                         "tp_rank", "tp_size", "use_graphs", "use_pdl")]
+
+
+def _sigs(lib):
+    if getattr(lib, "_model_sigs", False):
+        return lib
+    vp, i32, i64p = C.c_void_p, C.c_int32, C.POINTER(C.c_int64)
+    lib.n730_model_create.argtypes = [C.POINTER(N730ModelConfig), C.POINTER(vp)]
+    lib.n730_model_create.restype = i32
+    lib.n730_model_destroy.argtypes = [vp]
+    lib.n730_model_destroy.restype = None
+    lib.n730_model_set_qweight.argtypes = [vp, i32, i32, vp]
+    lib.n730_model_set_qweight.restype = i32
+    lib.n730_model_set_vector.argtypes = [vp, i32, i32, vp, i32, i32]
+    lib.n730_model_set_vector.restype = i32
+    for f in ("n730_model_finalize", "n730_model_reset"):
+        getattr(lib, f).argtypes = [vp]
+        getattr(lib, f).restype = i32
+    lib.n730_model_seq_len.argtypes = [vp, i32]
+    lib.n730_model_seq_len.restype = i32
+    lib.n730_model_forward.argtypes = [vp, i32, vp, i32, vp]
+    lib.n730_model_forward.restype = i32
+    lib.n730_model_decode.argtypes = [vp, vp, i32, vp]
+    lib.n730_model_decode.restype = i32
+    lib.n730_model_decode_device.argtypes = [vp, vp, i32, vp, vp]
+    lib.n730_model_decode_device.restype = i32
+    lib.n730_model_info.argtypes = [vp, i64p]
+    lib.n730_model_info.restype = i32
+    lib.n730_model_stream.argtypes = [vp]
+    lib.n730_model_stream.restype = vp
+    lib.n730_model_run_linear.argtypes = [vp, i32, i32, vp, i32, vp, vp]
+    lib.n730_model_run_linear.restype = i32
+    lib.n730_model_linear_bytes.argtypes = [vp, i32, i32, i32]
+    lib.n730_model_linear_bytes.restype = C.c_int64
+    lib._model_sigs = True
+    return lib
+
+
+def qweight_from_block(b: RawBlock):
+    """Register a .n730 block's packed codes on the current device."""
+    lib = _lib.cuda()
+    out = C.c_void_p()
+    payload = np.frombuffer(b.payload, np.uint8)
+    if b.prec_id in GROUPED:
+        s16 = np.ascontiguousarray(b.scales16)
+        z16 = np.ascontiguousarray(b.zeros16)
+        rc = lib.n730_qweight_create(b.prec_id, b.rows, b.cols, b.group_size, 1.0, 0.0,
+                                     payload.ctypes.data_as(C.c_void_p), s16.ctypes.data_as(C.c_void_p),
+                                     z16.ctypes.data_as(C.c_void_p), 0, None, C.byref(out))
+    else:
+        rc = lib.n730_qweight_create(b.prec_id, b.rows, b.cols, 0, b.scale, b.zero_point,
+                                     payload.ctypes.data_as(C.c_void_p), None, None, 0, None, C.byref(out))
+    _lib.check(rc, "qweight_create")
+    return out
+
+
+def qweight_from_device(prec_id, rows, cols, group, d_codes, d_s16=None, d_z16=None, scale=1.0, zero=0.0,
+                        stream=None):
+    lib = _lib.cuda()
+    out = C.c_void_p()
+    _lib.check(lib.n730_qweight_create(prec_id, rows, cols, group, scale, zero, C.c_void_p(d_codes),
+                                       C.c_void_p(d_s16) if d_s16 else None, C.c_void_p(d_z16) if d_z16 else None,
+                                       1, C.c_void_p(stream) if stream else None, C.byref(out)),
+               "qweight_create")
+    return out
+
+
+@dataclass
+class ModelShape:
+    hidden: int
+    layers: int
+    heads: int
+    kv_heads: int
+    head_dim: int
+    ffn: int
+    vocab: int
+    rope_theta: float = 1e6
+    rms_eps: float = 1e-6
+    tie_embeddings: bool = False
+
+
+class Engine:
+    """Owns one C model; all methods raise ``N730Error`` on a negative code."""
+
+    def __init__(self, shape: ModelShape, max_ctx: int = 4096, max_batch: int = 1, page_size: int = 64,
+                 max_prefill: int = 512, use_graphs: bool = True, use_pdl: bool = True,
+                 tp_rank: int = 0, tp_size: int = 1):
+        self.lib = _sigs(_lib.cuda())
+        self.shape = shape
+        c = N730ModelConfig(shape.hidden, shape.layers, shape.heads, shape.kv_heads, shape.head_dim, shape.ffn,
+                            shape.vocab, shape.rms_eps, shape.rope_theta, max_ctx, max_batch, page_size,
+                            max_prefill, int(shape.tie_embeddings), tp_rank, tp_size, int(use_graphs),
+                            int(use_pdl))
+        self.cfg = c
+        self.h = C.c_void_p()
+        _lib.check(self.lib.n730_model_create(C.byref(c), C.byref(self.h)), "model_create")
+        self.max_batch = max_batch
+        self._logits = np.zeros((max_batch, shape.vocab), np.float32)
+
+    def set_qweight(self, layer: int, slot: int, qw):
+        _lib.check(self.lib.n730_model_set_qweight(self.h, layer, slot, qw), "model_set_qweight")
+
+    def set_vector(self, layer: int, slot: int, v):
+        v = np.ascontiguousarray(v, np.float32)
+        _lib.check(self.lib.n730_model_set_vector(self.h, layer, slot, v.ctypes.data_as(C.c_void_p), v.size, 0),
+                   "model_set_vector")
+
+    def finalize(self):
+        _lib.check(self.lib.n730_model_finalize(self.h), "model_finalize")
+
+    def reset(self):
+        _lib.check(self.lib.n730_model_reset(self.h), "model_reset")
+
+    def seq_len(self, seq: int = 0) -> int:
+        return _lib.check(self.lib.n730_model_seq_len(self.h, seq), "model_seq_len")
+
+    def forward(self, token_ids, seq: int = 0) -> np.ndarray:
+        ids = np.ascontiguousarray(token_ids, np.int32).reshape(-1)
+        out = np.empty(self.shape.vocab, np.float32)
+        _lib.check(self.lib.n730_model_forward(self.h, seq, ids.ctypes.data_as(C.c_void_p), ids.size,
+                                               out.ctypes.data_as(C.c_void_p)), "model_forward")
+        return out
+
+    def decode(self, tokens) -> np.ndarray:
+        ids = np.ascontiguousarray(tokens, np.int32).reshape(-1)
+        B = ids.size
+        _lib.check(self.lib.n730_model_decode(self.h, ids.ctypes.data_as(C.c_void_p), B,
+                                              self._logits.ctypes.data_as(C.c_void_p)), "model_decode")
+        return self._logits[:B]
+
+    def decode_device(self, d_tokens: int, batch: int, d_logits: int, stream: int = 0):
+        _lib.check(self.lib.n730_model_decode_device(self.h, C.c_void_p(d_tokens) if d_tokens else None, batch,
+                                                     C.c_void_p(d_logits) if d_logits else None,
+                                                     C.c_void_p(stream) if stream else None), "model_decode_device")
+
+    def info(self) -> dict:
+        a = (C.c_int64 * 16)()
+        _lib.check(self.lib.n730_model_info(self.h, a), "model_info")
+        return {"weight_bytes": a[0], "kv_bytes_per_pos": a[1], "kv_capacity_bytes": a[2], "n_split": a[3],
+                "qkv_dim": a[4], "pages_per_seq": a[5]}
+
+    def run_linear(self, layer: int, which: int, d_x: int, batch: int, d_y: int, stream: int = 0):
+        _lib.check(self.lib.n730_model_run_linear(self.h, layer, which, C.c_void_p(d_x), batch, C.c_void_p(d_y),
+                                                  C.c_void_p(stream) if stream else None), "model_run_linear")
+
+    def linear_bytes(self, layer: int, which: int, batch: int = 1) -> int:
+        return int(self.lib.n730_model_linear_bytes(self.h, layer, which, batch))
+
+    @property
+    def stream(self) -> int:
+        return self.lib.n730_model_stream(self.h) or 0
+
+    def close(self):
+        if self.h:
+            self.lib.n730_model_destroy(self.h)
+            self.h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def load_tensors(engine: Engine, named_blocks, norms: dict | None = None):
+    """Hand a model's tensors to the engine by HF name.
+
+    ``named_blocks``: iterable of (name, RawBlock) for every 2-D weight and 1-D
+    bias; ``norms``: name -> fp32 vector (absent norms default to ones, as
+    the reference's identity fallback, inference.py:398-406).
+    """
+    for name, b in named_blocks:
+        if name == "model.embed_tokens.weight":
+            engine.set_qweight(-1, W_EMBED, qweight_from_block(b))
+        elif name == "lm_head.weight":
+            engine.set_qweight(-1, W_LMHEAD, qweight_from_block(b))
+        elif name.startswith("model.layers."):
+            rest = name[len("model.layers."):]
+            i, _, tail = rest.partition(".")
+            layer = int(i)
+            base, _, kind = tail.rpartition(".")
+            if kind == "weight" and base in PROJ_SLOTS:
+                engine.set_qweight(layer, PROJ_SLOTS[base], qweight_from_block(b))
+            elif kind == "bias" and base in BIAS_SLOTS:
+                v = np.frombuffer(b.payload, np.float16).astype(np.float32) if b.prec_id == 16 else None
+                if v is None:
+                    from .converter import read_layer  # non-FP16 bias: host dequant
+                    raise ValueError(f"bias {name} must be FP16")
+                engine.set_vector(layer, BIAS_SLOTS[base], v)
+    for name, v in (norms or {}).items():
+        if name == "model.norm.weight":
+            engine.set_vector(-1, V_FINAL_NORM, v)
+        elif name.startswith("model.layers.") and name.endswith("input_layernorm.weight"):
+            engine.set_vector(int(name.split(".")[2]), V_INPUT_NORM, v)
+        elif name.startswith("model.layers.") and name.endswith("post_attention_layernorm.weight"):
+            engine.set_vector(int(name.split(".")[2]), V_POST_NORM, v)

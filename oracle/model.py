@@ -80,6 +80,21 @@ def swiglu(g: np.ndarray, u: np.ndarray) -> np.ndarray:
     return (g / (np.float32(1.0) + np.exp(-g)) * u).astype(np.float32)
 
 
+class _Cfg:
+    """Reads either the reference ModelConfig names (inference.py:145-208) or
+    the engine's shape names."""
+
+    def __init__(self, c):
+        g = lambda *names: next(getattr(c, n) for n in names if hasattr(c, n))
+        self.hidden_size = g("hidden_size", "hidden")
+        self.num_hidden_layers = g("num_hidden_layers", "layers")
+        self.num_attention_heads = g("num_attention_heads", "heads")
+        self.num_kv_heads = g("num_kv_heads", "kv_heads")
+        self.head_dim = g("head_dim")
+        self.rms_norm_eps = g("rms_norm_eps", "rms_eps")
+        self.rope_theta = g("rope_theta")
+
+
 class OracleDecoder:
     """Whole-model numpy forward with an fp32 KV cache (the reference keeps fp32 KV).
 
@@ -89,6 +104,7 @@ class OracleDecoder:
     """
 
     def __init__(self, cfg, weights: dict, max_pos: int = 4096):
+        cfg = _Cfg(cfg)
         self.cfg = cfg
         self.w = weights
         self.cos, self.sin = rope_table(max_pos, cfg.head_dim, cfg.rope_theta)

@@ -1,0 +1,104 @@
+"""Whole-model parity: the engine (prefill + graph-replayed decode over the
+paged fp16 KV cache) against the oracle decoder on the same .n730 file.
+
+Bar (from the benchmark spec): logits within max|y - y_ref| / max|y_ref| <= 1e-2.
+"""
+import numpy as np
+import pytest
+
+from gpu_util import rel_err
+from oracle import quant as oq
+from oracle.model import OracleDecoder
+from n730_b200 import synthetic
+from n730_b200.engine import Engine, load_tensors
+from n730_b200.formats import read_block, read_header, GROUPED
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-2
+
+
+def _blocks(path):
+    hdr = read_header(path)
+    return [(e["layer_name"], read_block(path, e["file_offset"])) for e in hdr["seek_table"]]
+
+
+def _oracle_weights(blocks):
+    w = {}
+    for name, b in blocks:
+        if b.prec_id in GROUPED:
+            bits = {0x42: 2, 0x44: 4, 0x48: 8}[b.prec_id]
+            w[name] = oq.dequant_grouped(b.codes, b.scales16, b.zeros16, bits, b.rows, b.cols)
+        else:
+            w[name] = oq.dequant_tensor(b.payload, b.prec_id, b.rows * b.cols, b.scale,
+                                        b.zero_point).reshape(b.rows, b.cols)
+            if b.cols == 1:
+                w[name] = w[name].reshape(-1)
+    return w
+
+
+@pytest.fixture(scope="module", params=[("tiny", "int4_g128"), ("tiny-gqa7", "mixed_05b"),
+                                        ("tiny-128", "aggressive")])
+def model(request, tmp_path_factory):
+    shape_name, pmap = request.param
+    shape = synthetic.SHAPES[shape_name]
+    path = tmp_path_factory.mktemp("m") / f"{shape_name}.n730"
+    synthetic.write_n730(path, shape, pmap, seed=3)
+    blocks = _blocks(path)
+    return shape, blocks, _oracle_weights(blocks)
+
+
+def _engine(shape, blocks, **kw):
+    e = Engine(shape, max_ctx=kw.pop("max_ctx", 512), max_batch=kw.pop("max_batch", 4), max_prefill=64, **kw)
+    load_tensors(e, blocks)
+    e.finalize()
+    return e
+
+
+@pytest.mark.parametrize("graphs", [True, False])
+def test_prefill_then_decode(model, graphs):
+    shape, blocks, w = model
+    e = _engine(shape, blocks, use_graphs=graphs)
+    orc = OracleDecoder(shape, w, max_pos=512)
+    rng = np.random.default_rng(11)
+    prompt = rng.integers(0, shape.vocab, 100)          # crosses a 64-token prefill chunk
+    assert rel_err(e.forward(prompt), orc.forward(prompt)) <= TOL
+    tok = int(rng.integers(0, shape.vocab))
+    for step in range(12):
+        y, yr = e.forward([tok]), orc.forward([tok])
+        assert rel_err(y, yr) <= TOL, f"step {step}"
+        tok = int(np.argmax(yr))
+    assert e.seq_len(0) == 112
+    e.close()
+
+
+def test_batched_decode(model):
+    shape, blocks, w = model
+    e = _engine(shape, blocks)
+    rng = np.random.default_rng(5)
+    B = 3
+    oracles = [OracleDecoder(shape, w, max_pos=512) for _ in range(B)]
+    for b in range(B):  # ragged prompt lengths
+        p = rng.integers(0, shape.vocab, 7 + 13 * b)
+        assert rel_err(e.forward(p, seq=b), oracles[b].forward(p)) <= TOL
+    toks = rng.integers(0, shape.vocab, B)
+    for step in range(6):
+        y = e.decode(toks)
+        for b in range(B):
+            assert rel_err(y[b], oracles[b].forward([toks[b]])) <= TOL, (step, b)
+        toks = np.argmax(y, axis=1)
+    e.close()
+
+
+def test_capacity_and_reset(model):
+    shape, blocks, w = model
+    e = _engine(shape, blocks, max_ctx=64, max_batch=1)
+    e.forward(np.arange(60) % shape.vocab)
+    with pytest.raises(RuntimeError, match="capacity"):
+        e.forward(np.arange(10))
+    e.reset()
+    assert e.seq_len(0) == 0
+    orc = OracleDecoder(shape, w, max_pos=64)
+    assert rel_err(e.forward([1, 2, 3]), orc.forward([1, 2, 3])) <= TOL
+    with pytest.raises(RuntimeError):
+        e.forward([shape.vocab + 5])
+    e.close()
