@@ -446,8 +446,10 @@ static int dispatch(int nb, int r, const GemvParams& p, int grid, size_t smem, c
   if (nb == 1 && r == 1) return launch_t<BITS, SZM, 1, 1>(p, grid, smem, st, pdl);
   if (nb == 2 && r == 2) return launch_t<BITS, SZM, 2, 2>(p, grid, smem, st, pdl);
   if (nb == 2 && r == 1) return launch_t<BITS, SZM, 2, 1>(p, grid, smem, st, pdl);
-  if (nb == 3) return launch_t<BITS, SZM, 3, 1>(p, grid, smem, st, pdl);
-  if (nb == 4) return launch_t<BITS, SZM, 4, 1>(p, grid, smem, st, pdl);
+  if (nb == 3 && r == 2) return launch_t<BITS, SZM, 3, 2>(p, grid, smem, st, pdl);
+  if (nb == 3 && r == 1) return launch_t<BITS, SZM, 3, 1>(p, grid, smem, st, pdl);
+  if (nb == 4 && r == 2) return launch_t<BITS, SZM, 4, 2>(p, grid, smem, st, pdl);
+  if (nb == 4 && r == 1) return launch_t<BITS, SZM, 4, 1>(p, grid, smem, st, pdl);
   set_error("gemv: no kernel for batch chunk %d, rows/warp %d", nb, r);
   return N730_BAD_ARG;
 }
@@ -461,14 +463,15 @@ struct Plan {
   size_t smem;
 };
 
-static bool plan_for(const QWeight& w, int nb, int rows_per_cta, int C, Plan& out) {
+// SwiGLU pairs rows 2i (gate) and 2i+1 (up) inside one warp, so it needs an even R.
+static bool plan_for(const QWeight& w, int nb, int rows_per_cta, int C, bool swiglu, Plan& out) {
   const int E = w.bits == 16 ? 8 : 128 / w.bits;
   const int Cx = (C + 31 + 31) / 32 * 32;
   const size_t fixed = 128 + (size_t)nb * Cx * E * 4 + (size_t)nb * Cx * 4;
   double best = -1;
   for (int R : {4, 2, 1}) {
-    if (nb >= 3 && R != 1) continue;
-    if (nb == 2 && R == 4) continue;
+    if (nb >= 2 && R == 4) continue;
+    if (swiglu && (R & 1)) continue;
     for (int WK = 1; WK <= GEMV_WARPS; WK *= 2) {
       const int WR = GEMV_WARPS / WK;
       const int stage_rows = WR * R;
@@ -544,7 +547,7 @@ int gemv_launch(const GemvArgs& a, cudaStream_t stream) {
   while (b0 < a.batch) {
     int nb = std::min(GEMV_MAX_NB, a.batch - b0);
     Plan pl;
-    while (nb >= 1 && !plan_for(w, nb, rpc, p.C, pl)) --nb;
+    while (nb >= 1 && !plan_for(w, nb, rpc, p.C, a.swiglu != 0, pl)) --nb;
     N730_REQUIRE(nb >= 1, N730_BAD_ARG, "gemv: K=%d too large for one CTA's shared memory", w.cols);
     p.WK = pl.WK; p.Ck = pl.Ck; p.Cx = pl.Cx; p.stage_rows = pl.stage_rows; p.n_stages = pl.S;
     p.stage_off = pl.stage_off; p.stage_stride = pl.stage_stride;

@@ -137,11 +137,12 @@ def test_qlinear_per_tensor(lib, prec, rows, cols, batch):
     lib.n730_qweight_destroy(qw)
 
 
-def test_qlinear_epilogues(lib):
+@pytest.mark.parametrize("B", [1, 2, 3, 4, 7])
+def test_qlinear_epilogues(lib, B):
     """Fused RMSNorm prologue, bias, residual, and SwiGLU on interleaved gate/up rows."""
     from oracle.model import rms_norm, swiglu
-    rng = np.random.default_rng(9)
-    K, N, B = 896, 640, 2
+    rng = np.random.default_rng(9 + B)
+    K, N = 896, 640
     w = rng.normal(0, 0.02, (N, K)).astype(np.float32)
     x = rng.normal(0, 1, (B, K)).astype(np.float32)
     nw = rng.uniform(0.5, 1.5, K).astype(np.float32)
