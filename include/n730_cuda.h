@@ -102,6 +102,9 @@ int n730_qweight_create(int prec_id, int rows, int cols, int group_size, float s
                         const void* codes, const void* scales16, const void* zeros16, int src_on_device,
                         void* stream, void** out_qw);
 void n730_qweight_destroy(void* qw);
+/* Device layout: 0 row-major (all formats), 1 tensor-core fragment tiles (INT4 group-wise,
+ * group % 64 == 0), used by the tensor-core GEMV; dequant and gather read either. */
+int n730_qweight_set_layout(void* qw, int layout, void* stream);
 /* info[8] = prec, bits, rows, cols, group, n_groups, row_bytes, device bytes. */
 int n730_qweight_info(void* qw, int64_t* info);
 /* Bit-exact dequant of the whole weight to fp32 d_out[rows, cols]:
@@ -135,6 +138,8 @@ typedef struct N730ModelConfig {
   int32_t tp_rank, tp_size;  /* tensor parallel position (0, 1 for one GPU) */
   int32_t use_graphs;   /* replay the decode step as a CUDA graph */
   int32_t use_pdl;      /* programmatic dependent launch between kernels */
+  int32_t exact_gemv;   /* 1: fp32 CUDA-core GEMV everywhere; 0: INT4 g%64 weights use the
+                           tensor-core GEMV (x rounded to fp16) */
 } N730ModelConfig;
 
 /* weight slots (n730_model_set_qweight); EMBED/LMHEAD take layer = -1 */
@@ -154,6 +159,8 @@ int n730_model_finalize(void* model);
 /* Clear every sequence's KV (the reference's kv.clear(), inference.py:251-252). */
 int n730_model_reset(void* model);
 int n730_model_seq_len(void* model, int seq);
+/* Take positions [0, len) of sequence seq as already cached (resume / benchmark positioning). */
+int n730_model_set_seq_len(void* model, int seq, int len);
 /* Append n tokens to sequence seq; logits [vocab] of the last position to host.
  * Same contract as N730CudaTransformer.forward (inference.py:467-669). */
 int n730_model_forward(void* model, int seq, const int32_t* host_tokens, int n, float* host_logits);

@@ -52,6 +52,7 @@ _CUDA_SIGS = {
     "n730_qweight_create": ([i32, i32, i32, i32, f32, f32, vp, vp, vp, i32, vp, pp], i32),
     "n730_qweight_destroy": ([vp], None),
     "n730_qweight_info": ([vp, i64p], i32),
+    "n730_qweight_set_layout": ([vp, i32, vp], i32),
     "n730_dequant_to_f32": ([vp, vp, vp], i32),
     "n730_embed": ([vp, vp, i32, vp, vp], i32),
     "n730_qlinear": ([vp, vp, i32, i32, vp, i32, vp, vp, i32, vp, f32, i32, vp], i32),

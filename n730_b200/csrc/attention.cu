@@ -5,29 +5,31 @@
 // n730_attention_forward (n730_cuda.cu:709-845: whole-cache repack, 2*n_heads
 // cuBLAS calls, materialised fp32 scores, mask and softmax kernels).
 //
-// Decode (one token per sequence) is a single kernel: each CTA owns one
-// (sequence, KV head, split of the context).  It applies rotate_half RoPE to
-// the group's n_heads/n_kv query heads in shared memory, the CTA whose split
-// holds the new position RoPEs and appends k/v to the cache, then streams its
-// pages once for all query heads of the group (flash-decoding with an online
-// softmax).  The last CTA of a (sequence, KV head) to finish, found with an
-// atomic ticket, merges the splits: out = sum_s e^(m_s-M) acc_s /
-// (sum_s e^(m_s-M) l_s + 1e-9), the reference's normalisation
-// (n730_cuda.cu:236-257).  Scores are scaled by 1/sqrt(head_dim).  The
-// reference's exp(max(s - m, -50)) floor changes weights by at most e^-50 and
-// is not reproduced.
+// Decode (one token per sequence) is a single kernel: a cluster of 8 CTAs per
+// (sequence, KV head), each CTA one split of the context.  A CTA applies
+// rotate_half RoPE to the group's n_heads/n_kv query heads in shared memory;
+// the CTA whose split holds the new position RoPEs and appends k/v to the
+// cache; then each CTA streams its pages once for all query heads of the
+// group (flash-decoding with an online softmax).  The splits merge through
+// distributed shared memory (cluster rank 0 reads every rank's partials):
+// out = sum_s e^(m_s-M) acc_s / (sum_s e^(m_s-M) l_s + 1e-9), the reference's
+// normalisation (n730_cuda.cu:236-257).  Scores are scaled by 1/sqrt(head_dim).
+// The reference's exp(max(s - m, -50)) floor changes weights by at most e^-50
+// and is not reproduced.
 //
 // Prefill uses kv_write (RoPE + cache append for T tokens) and a causal
 // CUDA-core flash-attention kernel; masked keys get weight 0 (the reference
 // uses -1e4 scores, weight <= e^-50).
 #include <cfloat>
 
+#include <cooperative_groups.h>
+
 #include "attention.h"
+
+namespace cg = cooperative_groups;
 
 namespace n730 {
 
-constexpr int ATT_THREADS = 128;
-constexpr int ATT_TILE = 64;
 constexpr int MAX_G = 8;
 
 __device__ __forceinline__ const __half* page_ptr(const __half* pages, const int* bt, int p, const AttnDims& d,
@@ -36,182 +38,258 @@ __device__ __forceinline__ const __half* page_ptr(const __half* pages, const int
   return pages + (((int64_t)page * d.n_kv + kvh) * d.page_size + (p % d.page_size)) * d.head_dim;
 }
 
-template <int HD>
-__global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(const DecodeAttnArgs a) {
-  constexpr int H2 = HD / 2;
-  constexpr int QST = H2 + 4;            // padded half-row stride of q in smem
-  constexpr int PH = ATT_THREADS / HD;   // position groups in the PV phase
-  __shared__ float q_s[MAX_G][2][QST];
-  __shared__ float s_s[MAX_G][ATT_TILE];
-  __shared__ float m_s[MAX_G], l_s[MAX_G], al_s[MAX_G];
-  __shared__ float acc_s[PH > 1 ? PH : 1][MAX_G][HD];
-  __shared__ int last_s;
+// Decode attention, one thread-block cluster per (sequence, KV head): CTA r
+// of the cluster owns context positions [r*chunk, (r+1)*chunk).  Per tile of
+// DEC_TILE positions the CTA stages K and V with cp.async into XOR-swizzled
+// shared memory; each of its 8 warps takes 16 positions and computes
+//   S = Q K^T   with mma.m16n8k16 (f16 in, f32 accumulate): the G <= 8 query
+//               heads of the group are rows 0..G-1 of the A tile, K feeds B
+//               through ldmatrix,
+//   online softmax on the S fragments (per warp running max / sum),
+//   O += P V    with P re-packed from the S fragments as the A operand and V
+//               through ldmatrix.trans.
+// Warps merge in shared memory, then the cluster's CTAs merge through
+// distributed shared memory (rank 0 reads every rank's m, l, O).
+constexpr int DEC_THREADS = 256;
+constexpr int DEC_WARPS = DEC_THREADS / 32;
+constexpr int DEC_TILE = 16 * DEC_WARPS;  // 128 positions per tile
 
-  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ void mma_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+               "{%0,%1,%2,%3};"
+               : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+               : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool pred) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" :: "r"(dst), "l"(src), "r"(pred ? 16 : 0));
+}
+// byte offset of 16-byte chunk c of row r in a swizzled [rows][HD] fp16 tile
+template <int HD>
+__device__ __forceinline__ uint32_t swz(int r, int c) {
+  return (uint32_t)(r * HD * 2 + ((c ^ (r & 7)) << 4));
+}
+
+template <int HD>
+struct DecSmem {
+  __half k[DEC_TILE * HD];
+  __half v[DEC_TILE * HD];
+  float q[MAX_G][HD];                 // RoPE'd, scaled queries (fp32)
+  float wm[DEC_WARPS][MAX_G], wl[DEC_WARPS][MAX_G];
+  float wo[DEC_WARPS][MAX_G][HD];     // per-warp unnormalised outputs
+  float m[MAX_G], l[MAX_G];           // this CTA's split
+  float o[MAX_G][HD];
+};
+
+template <int HD>
+__global__ void __launch_bounds__(DEC_THREADS) attn_decode_kernel(const DecodeAttnArgs a) {
+  using SM = DecSmem<HD>;
+  constexpr int H2 = HD / 2, KS = HD / 16, NCH = HD / 8;  // k-steps, 16-B chunks per row
+  extern __shared__ __align__(128) uint8_t dsm[];
+  SM& sm = *reinterpret_cast<SM*>(dsm);
+
+  cg::cluster_group cluster = cg::this_cluster();
+  const int S = (int)cluster.num_blocks();
+  const int split = (int)cluster.block_rank();
+  const int kvh = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const AttnDims& d = a.d;
   const int G = d.n_heads / d.n_kv;
   pdl_wait();
   const int pos = a.seq_lens[b];
   const int L = pos + 1;
-  const int chunk = ((L + a.n_split - 1) / a.n_split + ATT_TILE - 1) / ATT_TILE * ATT_TILE;
+  const int chunk = ((L + S - 1) / S + DEC_TILE - 1) / DEC_TILE * DEC_TILE;
   const int t0 = split * chunk, t1 = min(L, t0 + chunk);
   const int* bt = a.block_table + (int64_t)b * d.max_pages;
   const float* qkv = a.qkv + (int64_t)b * a.ld_qkv;
   const float* cs = a.cos_t + (int64_t)pos * H2;
   const float* sn = a.sin_t + (int64_t)pos * H2;
 
-  if (tid < MAX_G) { m_s[tid] = -INFINITY; l_s[tid] = 0.f; }
-  // RoPE'd, pre-scaled queries of the group
-  for (int i = tid; i < G * H2; i += ATT_THREADS) {
-    const int g = i / H2, j = i % H2;
-    const float* qh = qkv + (int64_t)(kvh * G + g) * HD;
-    const float x0 = qh[j], x1 = qh[j + H2], c = cs[j], s = sn[j];
-    q_s[g][0][j] = (x0 * c - x1 * s) * d.scale;
-    q_s[g][1][j] = (x1 * c + x0 * s) * d.scale;
+  for (int i = tid; i < MAX_G * HD; i += DEC_THREADS) {  // RoPE'd, pre-scaled queries
+    const int g = i / HD, j = i % HD;
+    float v = 0.f;
+    if (g < G) {
+      const float* qh = qkv + (int64_t)(kvh * G + g) * HD;
+      const int j0 = j < H2 ? j : j - H2;
+      const float x0 = qh[j0], x1 = qh[j0 + H2], c = cs[j0], s = sn[j0];
+      v = (j < H2 ? x0 * c - x1 * s : x1 * c + x0 * s) * d.scale;
+    }
+    sm.q[g][j] = v;
   }
-  // the split that holds the new position appends k, v
-  if (t0 <= pos && pos < t1) {
+  // the new position's k (RoPE'd) and v, rounded to fp16 as stored
+  const bool owns_new = t0 <= pos && pos < t1;
+  if (owns_new) {
     const float* kh = qkv + (int64_t)(d.n_heads + kvh) * HD;
     const float* vh = qkv + (int64_t)(d.n_heads + d.n_kv + kvh) * HD;
     __half* kd = const_cast<__half*>(page_ptr(a.kv.k_pages, bt, pos, d, kvh));
     __half* vd = const_cast<__half*>(page_ptr(a.kv.v_pages, bt, pos, d, kvh));
-    for (int j = tid; j < H2; j += ATT_THREADS) {
+    for (int j = tid; j < H2; j += DEC_THREADS) {
       const float x0 = kh[j], x1 = kh[j + H2], c = cs[j], s = sn[j];
       kd[j] = __float2half_rn(x0 * c - x1 * s);
       kd[j + H2] = __float2half_rn(x1 * c + x0 * s);
     }
-    for (int j = tid; j < HD; j += ATT_THREADS) vd[j] = __float2half_rn(vh[j]);
+    for (int j = tid; j < HD; j += DEC_THREADS) vd[j] = __float2half_rn(vh[j]);
   }
   __syncthreads();
   pdl_launch_dependents();
 
-  float acc[MAX_G];
+  // Q as the A operand: rows 0..7 = query heads (>= G are zero), rows 8..15 zero
+  uint32_t qa[KS][2];
+  {
+    const int r = lane >> 2, c = (lane & 3) * 2;
 #pragma unroll
-  for (int g = 0; g < MAX_G; ++g) acc[g] = 0.f;
-  const int pd = tid % HD, pg = tid / HD;
+    for (int ks = 0; ks < KS; ++ks) {
+      qa[ks][0] = pack_half2(sm.q[r][ks * 16 + c], sm.q[r][ks * 16 + c + 1]);
+      qa[ks][1] = pack_half2(sm.q[r][ks * 16 + c + 8], sm.q[r][ks * 16 + c + 9]);
+    }
+  }
+  float o[HD / 8][4];
+#pragma unroll
+  for (int n = 0; n < HD / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float m_run = -INFINITY, l_run = 0.f;  // for head row lane>>2 (replicated over the 4 lanes of a row)
+  const uint32_t ks_base = smem_u32(sm.k), vs_base = smem_u32(sm.v);
 
-  for (int tile = t0; tile < t1; tile += ATT_TILE) {
-    // scores: two threads per position, one half of head_dim each
-    {
-      const int pi = tid >> 1, half = tid & 1;
-      const int p = tile + pi;
-      float dot[MAX_G];
-#pragma unroll
-      for (int g = 0; g < MAX_G; ++g) dot[g] = 0.f;
-      if (p < t1) {
-        const uint4* kr = reinterpret_cast<const uint4*>(page_ptr(a.kv.k_pages, bt, p, d, kvh) + half * H2);
-#pragma unroll
-        for (int v4 = 0; v4 < H2 / 8; ++v4) {
-          const uint4 u = kr[v4];
-          const __half2* h2 = reinterpret_cast<const __half2*>(&u);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 kf = __half22float2(h2[e]);
-            const int j = v4 * 8 + e * 2;
-#pragma unroll
-            for (int g = 0; g < MAX_G; ++g) {
-              if (g < G) dot[g] = fmaf(q_s[g][half][j], kf.x, fmaf(q_s[g][half][j + 1], kf.y, dot[g]));
-            }
-          }
-        }
+  for (int tile = t0; tile < t1; tile += DEC_TILE) {
+    const int np = min(DEC_TILE, t1 - tile);
+    // ---- stage K and V rows [tile, tile+np) into swizzled smem ----
+    for (int i = tid; i < DEC_TILE * NCH; i += DEC_THREADS) {
+      const int r = i / NCH, c = i % NCH;
+      const bool ok = r < np;
+      const int p = ok ? tile + r : tile;
+      cp_async16(ks_base + swz<HD>(r, c), page_ptr(a.kv.k_pages, bt, p, d, kvh) + c * 8, ok);
+      cp_async16(vs_base + swz<HD>(r, c), page_ptr(a.kv.v_pages, bt, p, d, kvh) + c * 8, ok);
+    }
+    asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+    if (owns_new && pos >= tile && pos < tile + DEC_TILE) {  // the row just appended, from registers' values
+      const int r = pos - tile;
+      const float* kh = qkv + (int64_t)(d.n_heads + kvh) * HD;
+      const float* vh = qkv + (int64_t)(d.n_heads + d.n_kv + kvh) * HD;
+      for (int j = tid; j < HD; j += DEC_THREADS) {
+        const int j0 = j < H2 ? j : j - H2;
+        const float x0 = kh[j0], x1 = kh[j0 + H2], c = cs[j0], s = sn[j0];
+        const float kv = j < H2 ? x0 * c - x1 * s : x1 * c + x0 * s;
+        const uint32_t off = swz<HD>(r, j / 8) + (j % 8) * 2;
+        *reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(sm.k) + off) = __float2half_rn(kv);
+        *reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(sm.v) + off) = __float2half_rn(vh[j]);
       }
+      __syncthreads();
+    }
+    const int w0 = warp * 16;  // this warp's 16 positions of the tile
+    if (w0 < np) {
+      // ---- S = Q K^T for 16 positions (two n-tiles of 8) ----
+      float sacc[2][4];
 #pragma unroll
-      for (int g = 0; g < MAX_G; ++g) {
-        dot[g] += __shfl_xor_sync(0xffffffffu, dot[g], 1);
-        if (half == 0 && g < G) s_s[g][pi] = p < t1 ? dot[g] : -INFINITY;
+      for (int n = 0; n < 2; ++n) sacc[n][0] = sacc[n][1] = sacc[n][2] = sacc[n][3] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks) {
+        // matrices: (n-tile 0, k lo), (n-tile 0, k hi), (n-tile 1, k lo), (n-tile 1, k hi)
+        const int mi = lane >> 3, rr = lane & 7;
+        const int row = w0 + (mi >> 1) * 8 + rr;
+        const int chk = ks * 2 + (mi & 1);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(ks_base + swz<HD>(row, chk), b0, b1, b2, b3);
+        const uint32_t af[4] = {qa[ks][0], 0u, qa[ks][1], 0u};
+        mma_16816(sacc[0], af, b0, b1);
+        mma_16816(sacc[1], af, b2, b3);
+      }
+      // ---- online softmax on rows 0..7 (c0, c1 of each n-tile) ----
+      float sv[4];
+      sv[0] = sacc[0][0]; sv[1] = sacc[0][1]; sv[2] = sacc[1][0]; sv[3] = sacc[1][1];
+      const int cb = (lane & 3) * 2;
+      float mt = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int pcol = w0 + (j >> 1) * 8 + cb + (j & 1);
+        if (pcol >= np) sv[j] = -INFINITY;
+        mt = fmaxf(mt, sv[j]);
+      }
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 1));
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 2));
+      const float mn = fmaxf(m_run, mt);
+      const float al = m_run == -INFINITY ? 0.f : __expf(m_run - mn);
+      float pe[4], ts = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) { pe[j] = sv[j] == -INFINITY ? 0.f : __expf(sv[j] - mn); ts += pe[j]; }
+      ts += __shfl_xor_sync(0xffffffffu, ts, 1);
+      ts += __shfl_xor_sync(0xffffffffu, ts, 2);
+      l_run = l_run * al + ts;
+      m_run = mn;
+#pragma unroll
+      for (int n = 0; n < HD / 8; ++n) { o[n][0] *= al; o[n][1] *= al; }
+      // ---- O += P V (P: rows = heads, k = this warp's 16 positions) ----
+      const uint32_t pa[4] = {pack_half2(pe[0], pe[1]), 0u, pack_half2(pe[2], pe[3]), 0u};
+#pragma unroll
+      for (int n2 = 0; n2 < HD / 16; ++n2) {
+        // matrices (trans): (k lo, n-tile 2*n2), (k hi, n-tile 2*n2), (k lo, 2*n2+1), (k hi, 2*n2+1)
+        const int mi = lane >> 3, rr = lane & 7;
+        const int row = w0 + (mi & 1) * 8 + rr;
+        const int chk = n2 * 2 + (mi >> 1);
+        uint32_t v0, v1, v2, v3;
+        ldsm_x4_t(vs_base + swz<HD>(row, chk), v0, v1, v2, v3);
+        mma_16816(o[2 * n2], pa, v0, v1);
+        mma_16816(o[2 * n2 + 1], pa, v2, v3);
       }
     }
-    __syncthreads();
-    // online softmax update, one warp per head
-    for (int g = warp; g < G; g += ATT_THREADS / 32) {
-      const float s0 = s_s[g][lane], s1 = s_s[g][lane + 32];
-      const float mt = warp_max(fmaxf(s0, s1));
-      const float mo = m_s[g];
-      const float mn = fmaxf(mo, mt);
-      const float e0 = s0 == -INFINITY ? 0.f : __expf(s0 - mn);
-      const float e1 = s1 == -INFINITY ? 0.f : __expf(s1 - mn);
-      s_s[g][lane] = e0;
-      s_s[g][lane + 32] = e1;
-      const float ts = warp_sum(e0 + e1);
-      if (lane == 0) {
-        const float al = mo == -INFINITY ? 0.f : __expf(mo - mn);
-        al_s[g] = al;
-        l_s[g] = l_s[g] * al + ts;
-        m_s[g] = mn;
-      }
-    }
-    __syncthreads();
-    // P.V: thread = one dim (and one position group when head_dim < 128)
-    {
-#pragma unroll
-      for (int g = 0; g < MAX_G; ++g) if (g < G) acc[g] *= al_s[g];
-      const int np = min(ATT_TILE, t1 - tile);
-      for (int pi = pg; pi < np; pi += PH) {
-        const float v = __half2float(page_ptr(a.kv.v_pages, bt, tile + pi, d, kvh)[pd]);
-#pragma unroll
-        for (int g = 0; g < MAX_G; ++g) if (g < G) acc[g] = fmaf(s_s[g][pi], v, acc[g]);
-      }
-    }
-    __syncthreads();
+    __syncthreads();  // tile buffers are reused
   }
 
-  // partials of this split
-  const int S = a.n_split;
-  if (PH > 1) {
+  // ---- merge the 8 warps of this CTA ----
+  {
+    const int r = lane >> 2, cb = (lane & 3) * 2;
+    if ((lane & 3) == 0 && r < MAX_G) { sm.wm[warp][r] = m_run; sm.wl[warp][r] = l_run; }
+    if (r < MAX_G)
 #pragma unroll
-    for (int g = 0; g < MAX_G; ++g) if (g < G) acc_s[pg][g][pd] = acc[g];
-    __syncthreads();
-  }
-  if (pg == 0) {
-#pragma unroll
-    for (int g = 0; g < MAX_G; ++g) {
-      if (g >= G) continue;
-      float v = acc[g];
-      if (PH > 1) { v = 0.f; for (int k = 0; k < PH; ++k) v += acc_s[k][g][pd]; }
-      const int h = kvh * G + g;
-      a.part_acc[(((int64_t)b * d.n_heads + h) * S + split) * HD + pd] = v;
-    }
-  }
-  if (tid < G) {
-    const int h = kvh * G + tid;
-    a.part_ml[((int64_t)b * d.n_heads + h) * S + split] = make_float2(m_s[tid], l_s[tid]);
-  }
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) {
-    const int ticket = atomicAdd(&a.counters[b * d.n_kv + kvh], 1);
-    last_s = ticket == S - 1;
+      for (int n = 0; n < HD / 8; ++n) { sm.wo[warp][r][n * 8 + cb] = o[n][0]; sm.wo[warp][r][n * 8 + cb + 1] = o[n][1]; }
   }
   __syncthreads();
-  if (!last_s) return;
-  __threadfence();
-  // merge the splits of this (sequence, KV head)
-  for (int g = 0; g < G; ++g) {
-    const int h = kvh * G + g;
-    const float2* ml = a.part_ml + ((int64_t)b * d.n_heads + h) * S;
+  for (int i = tid; i < G * HD; i += DEC_THREADS) {
+    const int g = i / HD, dd = i % HD;
     float M = -INFINITY;
-    for (int s = 0; s < S; ++s) M = fmaxf(M, __ldcg(&ml[s].x));
-    for (int dd = tid; dd < HD; dd += ATT_THREADS) {
+#pragma unroll
+    for (int w = 0; w < DEC_WARPS; ++w) M = fmaxf(M, sm.wm[w][g]);
+    float num = 0.f, den = 0.f;
+#pragma unroll
+    for (int w = 0; w < DEC_WARPS; ++w) {
+      const float mw = sm.wm[w][g];
+      if (mw == -INFINITY) continue;
+      const float e = __expf(mw - M);
+      num = fmaf(e, sm.wo[w][g][dd], num);
+      den = fmaf(e, sm.wl[w][g], den);
+    }
+    sm.o[g][dd] = num;
+    if (dd == 0) { sm.m[g] = M; sm.l[g] = den; }
+  }
+  cluster.sync();  // every split's (m, l, o) is visible cluster-wide
+  if (split == 0) {
+    for (int i = tid; i < G * HD; i += DEC_THREADS) {
+      const int g = i / HD, dd = i % HD;
+      float M = -INFINITY;
+      for (int r = 0; r < S; ++r) M = fmaxf(M, cluster.map_shared_rank(&sm, r)->m[g]);
       float num = 0.f, den = 0.f;
-      for (int s = 0; s < S; ++s) {
-        const float2 v = __ldcg(&ml[s]);
-        if (v.x == -INFINITY) continue;
-        const float w = __expf(v.x - M);
-        den = fmaf(w, v.y, den);
-        num = fmaf(w, __ldcg(&a.part_acc[(((int64_t)b * d.n_heads + h) * S + s) * HD + dd]), num);
+      for (int r = 0; r < S; ++r) {
+        const SM* rs = cluster.map_shared_rank(&sm, r);
+        const float mr = rs->m[g];
+        if (mr == -INFINITY) continue;
+        const float w = __expf(mr - M);
+        den = fmaf(w, rs->l[g], den);
+        num = fmaf(w, rs->o[g][dd], num);
       }
-      a.out[(int64_t)b * d.n_heads * HD + (int64_t)h * HD + dd] = num / (den + 1e-9f);
+      a.out[(int64_t)b * d.n_heads * HD + (int64_t)(kvh * G + g) * HD + dd] = num / (den + 1e-9f);
     }
   }
-  if (tid == 0) a.counters[b * d.n_kv + kvh] = 0;
-}
-
-size_t attn_decode_workspace(int batch, int n_heads, int n_kv, int head_dim, int n_split) {
-  const size_t ml = (size_t)batch * n_heads * n_split * sizeof(float2);
-  const size_t acc = (size_t)batch * n_heads * n_split * head_dim * sizeof(float);
-  const size_t cnt = (size_t)batch * n_kv * sizeof(int);
-  return ml + acc + cnt + 3 * 256;
+  cluster.sync();  // keep every CTA's shared memory alive until rank 0 is done
 }
 
 template <typename KernelT, typename ArgT>
@@ -230,16 +308,57 @@ static int launch_pdl(KernelT k, dim3 grid, dim3 block, size_t smem, cudaStream_
   return N730_OK;
 }
 
+template <int HD>
+static int decode_cluster_size() {
+  const size_t smem = sizeof(DecSmem<HD>);
+  N730_CUDA(cudaFuncSetAttribute(attn_decode_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  N730_CUDA(cudaFuncSetAttribute(attn_decode_kernel<HD>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+  for (int cl : {16, 8}) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(cl, 1, 1);
+    cfg.blockDim = dim3(DEC_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cl;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, attn_decode_kernel<HD>, &cfg) == cudaSuccess && n > 0) return cl;
+    cudaGetLastError();
+  }
+  return 8;
+}
+
 int attn_decode_launch(const DecodeAttnArgs& a, cudaStream_t st) {
   const AttnDims& d = a.d;
   N730_REQUIRE(d.n_kv > 0 && d.n_heads % d.n_kv == 0 && d.n_heads / d.n_kv <= MAX_G, N730_BAD_ARG,
                "attention: n_heads/n_kv must be an integer <= %d", MAX_G);
   N730_REQUIRE(d.head_dim == 64 || d.head_dim == 128, N730_UNSUPPORTED, "attention: head_dim %d", d.head_dim);
-  N730_REQUIRE(a.n_split >= 1 && a.batch >= 1, N730_BAD_ARG, "attention: bad split/batch");
-  N730_REQUIRE(a.part_ml && a.part_acc && a.counters, N730_NULL, "attention: workspace is null");
-  dim3 grid(a.n_split, d.n_kv, a.batch);
-  if (d.head_dim == 128) return launch_pdl(attn_decode_kernel<128>, grid, dim3(ATT_THREADS), 0, st, a.pdl, a);
-  return launch_pdl(attn_decode_kernel<64>, grid, dim3(ATT_THREADS), 0, st, a.pdl, a);
+  N730_REQUIRE(a.batch >= 1, N730_BAD_ARG, "attention: bad batch");
+  static int cl128 = 0, cl64 = 0;
+  int& cl = d.head_dim == 128 ? cl128 : cl64;
+  if (!cl) cl = d.head_dim == 128 ? decode_cluster_size<128>() : decode_cluster_size<64>();
+  if (cl < 0) return cl;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(cl, d.n_kv, a.batch);
+  cfg.blockDim = dim3(DEC_THREADS);
+  cfg.stream = st;
+  cfg.dynamicSmemBytes = d.head_dim == 128 ? sizeof(DecSmem<128>) : sizeof(DecSmem<64>);
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cl;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = a.pdl ? 2 : 1;
+  if (d.head_dim == 128) N730_CUDA(cudaLaunchKernelEx(&cfg, attn_decode_kernel<128>, a));
+  else N730_CUDA(cudaLaunchKernelEx(&cfg, attn_decode_kernel<64>, a));
+  return N730_OK;
 }
 
 // ---------------------------------------------------------------------------

@@ -20,10 +20,9 @@ struct AttnDims {
 
 // Decode: one new token per sequence.  qkv [B][ld_qkv] holds q|k|v (biases
 // added, RoPE not yet applied); positions are seq_lens[b].  Writes the RoPE'd
-// k and v into the cache and attn_out [B][n_heads*head_dim].
-// Workspace: part_ml [B][n_heads][n_split] float2 (max, sum),
-// part_acc [B][n_heads][n_split][head_dim] fp32, counters [B][n_kv] int (zero
-// on entry; left zero on exit).
+// k and v into the cache and attn_out [B][n_heads*head_dim].  No global
+// workspace: the context splits of a (sequence, KV head) form one thread-block
+// cluster and merge through distributed shared memory.
 struct DecodeAttnArgs {
   const float* qkv; int ld_qkv;
   const float* cos_t; const float* sin_t;   // [max_pos][head_dim/2]
@@ -32,12 +31,10 @@ struct DecodeAttnArgs {
   KVLayer kv;
   AttnDims d;
   float* out;
-  int batch, n_split;
-  float2* part_ml; float* part_acc; int* counters;
+  int batch;
   int pdl;
 };
 int attn_decode_launch(const DecodeAttnArgs& a, cudaStream_t st);
-size_t attn_decode_workspace(int batch, int n_heads, int n_kv, int head_dim, int n_split);
 
 // Prefill of T tokens of sequence b at positions [pos0, pos0+T): applies RoPE
 // to q (in place in qkv) and k, writes k/v into the cache.

@@ -502,8 +502,11 @@ static bool plan_for(const QWeight& w, int nb, int rows_per_cta, int C, bool swi
   return best > 0;
 }
 
+int* gemv_err_word() { return device_err_word(); }
+
 int gemv_launch(const GemvArgs& a, cudaStream_t stream) {
   const QWeight& w = *a.w;
+  if (w.layout == 1) return gemv_mma_launch(a, stream);
   N730_REQUIRE(w.codes && a.x && a.y, N730_NULL, "gemv: null pointer");
   N730_REQUIRE(a.batch >= 1, N730_BAD_ARG, "gemv: batch %d", a.batch);
   const int bits = w.bits;
@@ -568,6 +571,12 @@ int gemv_launch(const GemvArgs& a, cudaStream_t stream) {
     if (rc) return rc;
     b0 += nb;
   }
+  return N730_OK;
+}
+
+// Allocate the per-device error word outside any stream capture.
+int gemv_prepare() {
+  N730_REQUIRE(device_err_word(), N730_OOM, "gemv: error word allocation failed");
   return N730_OK;
 }
 

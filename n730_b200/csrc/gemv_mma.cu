@@ -1,0 +1,546 @@
+// Tensor-core decode GEMV for INT4 group-wise weights (batch <= 16).
+//
+// The fp32 CUDA-core kernel (gemv.cu) needs ~2.4 issue slots per INT4 weight
+// at best, which caps it well below the HBM roofline on B200.  This kernel
+// moves the multiply-adds onto the tensor cores with mma.m16n8k16 (f16 in, f32
+// accumulate) and leaves ~5 integer instructions per 8 codes per lane:
+//  * Weights use a fragment-ordered layout built once at registration: for
+//    row tile t (16 rows) and k-step s (16 columns), lane l's 32-bit word holds
+//    exactly the 8 codes of its A fragment.  One LOP3 per two codes ORs them
+//    into the mantissa of fp16 1024: A = 1024 + q (rows g) or 1024 + 16 q
+//    (rows g+8, the high nibbles), both exact in fp16.
+//  * x (RMS-normalised in the prologue) is the B operand, rounded to fp16;
+//    batch rows are the n dimension (n-tiles of 8).  The prologue also forms
+//    Sx = sum of the fp16 x over each group, in fp32.
+//  * Each group accumulates C = sum (1024 + q) x in fresh fp32 fragments; the
+//    group epilogue removes the offset and zero point and applies the scale in
+//    fp32:  y += s C - s (1024 + z) Sx   (rows g+8: (s/16) C - s (64 + z) Sx),
+//    which equals s sum (q - z) x.
+//  * Every warp streams its own work units (row tile, K-part) through a private
+//    ring of TMA bulk copies; a unit's groups are contiguous in the layout, so
+//    each chunk (codes plus the groups' scale/zero blocks) is one copy.
+// Numerics: exact codes, scales and zero points; x rounded to fp16 (relative
+// 2^-11 per element); the offset cancellation costs ~7 of fp32's 24 bits - the
+// decoder's 1e-2 logit bar holds with a wide margin.  The bit-exact fp32 path
+// stays available (gemv.cu).
+#include <algorithm>
+#include <cstdlib>
+
+#include "qweight.h"
+
+namespace n730 {
+
+
+// ---------------------------------------------------------------------------
+// layout, per row tile and group (kpg = group/16 k-steps):
+//   codes [kpg/4][32 lanes][4] u32  (a lane's 4 consecutive k-step words are
+//                                    contiguous: one LDS.128)
+//   sz    [8] x {s_g, s_g8, z_g, z_g8} fp16 (64 B; g = lane/4, rows g and g+8)
+// so any run of whole groups of a tile is one contiguous bulk copy.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int64_t mma_group_bytes(int kpg) { return (int64_t)kpg * 128 + 64; }
+
+__global__ void to_mma_layout_kernel(const uint8_t* codes, int64_t row_bytes, const uint8_t* sz, int64_t sz_pitch,
+                                     int rows, int cols, int group, uint8_t* out) {
+  const int ks_n = cols / 16, tiles = (rows + 15) / 16, G = cols / group, kpg = group / 16;
+  const int64_t gb = mma_group_bytes(kpg);
+  const int64_t nwords = (int64_t)tiles * ks_n * 32;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nwords;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    // i enumerates [t][s4][lane][j]
+    const int j = (int)(i & 3), lane = (int)((i >> 2) & 31);
+    const int64_t ts4 = i >> 7;
+    const int s4 = (int)(ts4 % (ks_n / 4)), t = (int)(ts4 / (ks_n / 4));
+    const int s = s4 * 4 + j;
+    const int gi = s / kpg, sl = s % kpg;  // group, k-step within the group
+    const int g = lane >> 2, tq = lane & 3;
+    const int r0 = t * 16 + g, r1 = r0 + 8;
+    const int k0 = s * 16 + 2 * tq;
+    auto q = [&](int r, int k) -> uint32_t {
+      if (r >= rows) return 0u;
+      const uint8_t byte = codes[(int64_t)r * row_bytes + (k >> 1)];
+      return (k & 1) ? (byte >> 4) : (byte & 15u);
+    };
+    const uint32_t w = q(r0, k0) | q(r1, k0) << 4 | q(r0, k0 + 8) << 8 | q(r1, k0 + 8) << 12 |
+                       q(r0, k0 + 1) << 16 | q(r1, k0 + 1) << 20 | q(r0, k0 + 9) << 24 | q(r1, k0 + 9) << 28;
+    uint32_t* dst = reinterpret_cast<uint32_t*>(out + ((int64_t)t * G + gi) * gb);
+    dst[((sl >> 2) * 32 + lane) * 4 + (sl & 3)] = w;
+  }
+  const int64_t nsz = (int64_t)tiles * G * 8;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nsz; i += (int64_t)gridDim.x * blockDim.x) {
+    const int g = (int)(i & 7);
+    const int64_t tg = i >> 3;
+    const int gi = (int)(tg % G), t = (int)(tg / G);
+    const int r0 = t * 16 + g, r1 = r0 + 8;
+    auto get = [&](int r) -> __half2 {
+      if (r >= rows) return __halves2half2(__float2half(0.f), __float2half(0.f));
+      return reinterpret_cast<const __half2*>(sz + (int64_t)r * sz_pitch)[gi];
+    };
+    const __half2 a = get(r0), b = get(r1);  // (scale, zero)
+    const __half s0 = __low2half(a), z0 = __high2half(a), s1 = __low2half(b), z1 = __high2half(b);
+    const __half2 lo = __halves2half2(s0, s1);
+    const __half2 hi = __halves2half2(z0, z1);
+    uint2 v;
+    v.x = *reinterpret_cast<const uint32_t*>(&lo);
+    v.y = *reinterpret_cast<const uint32_t*>(&hi);
+    reinterpret_cast<uint2*>(out + ((int64_t)t * G + gi) * gb + (int64_t)kpg * 128)[g] = v;
+  }
+}
+
+int qweight_to_mma_layout(QWeight& w, cudaStream_t st) {
+  if (w.layout == 1) return N730_OK;
+  N730_REQUIRE(w.bits == 4 && w.sz_mode == 0 && w.group % 64 == 0 && w.cols % 64 == 0, N730_UNSUPPORTED,
+               "mma layout: needs INT4 group-wise weights with group %% 64 == 0");
+  const int tiles = (w.rows + 15) / 16, ks_n = w.cols / 16, G = w.n_groups, kpg = w.group / 16;
+  uint8_t* blob = nullptr;
+  if (cudaMalloc(&blob, (size_t)tiles * G * ((size_t)kpg * 128 + 64)) != cudaSuccess) {
+    cudaGetLastError();
+    set_error("mma layout: out of device memory");
+    return N730_OOM;
+  }
+  const int64_t work = std::max<int64_t>((int64_t)tiles * ks_n * 32, (int64_t)tiles * G * 8);
+  const int grid = (int)std::min<int64_t>((work + 255) / 256, num_sms() * 16);
+  to_mma_layout_kernel<<<grid, 256, 0, st>>>(w.codes, w.row_bytes, (const uint8_t*)w.sz, w.sz_pitch, w.rows, w.cols,
+                                             w.group, blob);
+  if (int rc = cuda_rc(cudaGetLastError(), __FILE__, __LINE__)) { cudaFree(blob); return rc; }
+  N730_CUDA(cudaStreamSynchronize(st));
+  if (w.owns) { cudaFree(w.codes); cudaFree(w.sz); }
+  w.codes = blob;
+  w.sz = nullptr;
+  w.owns = true;
+  w.layout = 1;
+  w.row_bytes = (int64_t)w.cols / 2;  // logical bytes per row (16 rows share a tile)
+  w.sz_pitch = 0;
+  return N730_OK;
+}
+
+// ---------------------------------------------------------------------------
+// kernel
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+__device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+               "{%0,%1,%2,%3};"
+               : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+               : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+struct MmaParams {
+  const uint8_t* blob;     // [tiles][G] x (codes kpg*128 B, sz 64 B)
+  int rows, cols, ks_n, G;
+  int tiles_per_cta;
+  int parts;               // K-parts per row tile
+  int xf_off, sx_off, acc_off, ring_off, ring_stride;  // smem byte offsets / per-buffer bytes
+  int ring;                // chunks in flight per warp (<= MG2_RING)
+  const float* x; int ldx; int batch;
+  float* y; int ldy;
+  const float* bias;
+  const float* residual; int ldr;
+  const float* norm_w; float eps;
+  int swiglu;
+  int* err;
+};
+
+__device__ __forceinline__ uint64_t gtimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = gtimer();
+  while (!mbar_try_wait(bar, parity))
+    if (gtimer() - t0 > 2000000000ull) return false;
+  return true;
+}
+
+constexpr int MG2_RING = 3;   // chunks in flight per warp (fewer when shared memory is short)
+constexpr int MG2_CHUNK = 32; // k-steps per chunk: a whole number of groups, ~4.3 KB with their scales
+
+// Groups [0, NG) of one chunk in shared memory: straight-line code, so the NG
+// groups' accumulator chains interleave.  xb[nn] points at the chunk's first
+// k-step pair of x fragments (n-tile nn); sxg at the chunk's first group of Sx.
+template <int KPG, int NT, int NG>
+__device__ __forceinline__ void mma_chunk(const uint8_t* buf, int lane, const uint4* const (&xb)[NT],
+                                          const float* sxg, float (&acc)[NT][4]) {
+  constexpr int GB = KPG * 128 + 64;
+  constexpr uint32_t MAGIC = 0x64006400u;
+  const int g = lane >> 2, tq = lane & 3;
+#pragma unroll
+  for (int gr = 0; gr < NG; ++gr) {
+    const uint32_t* cw = reinterpret_cast<const uint32_t*>(buf + gr * GB) + lane * 4;
+    // two accumulator chains (even / odd k-steps) per n-tile
+    float ca[NT][4], cb[NT][4];
+#pragma unroll
+    for (int nn = 0; nn < NT; ++nn)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) ca[nn][e] = cb[nn][e] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < KPG; kk += 4) {
+      const int kl = gr * KPG + kk;  // k-step within the chunk
+      const uint4 w4 = *reinterpret_cast<const uint4*>(cw + (kk >> 2) * 128);
+      const uint32_t wv[4] = {w4.x, w4.y, w4.z, w4.w};
+      uint4 bx[NT][2];
+#pragma unroll
+      for (int nn = 0; nn < NT; ++nn) {
+        bx[nn][0] = xb[nn][(kl >> 1) * 4];
+        bx[nn][1] = xb[nn][((kl >> 1) + 1) * 4];
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t w = wv[j], ws = w >> 8;
+        const uint32_t a0 = lop3_and_or(w, 0x000F000Fu, MAGIC);   // rows g,   k 2tq..+1:  1024 + q
+        const uint32_t a1 = lop3_and_or(w, 0x00F000F0u, MAGIC);   // rows g+8, k 2tq..+1:  1024 + 16 q
+        const uint32_t a2 = lop3_and_or(ws, 0x000F000Fu, MAGIC);  // rows g,   k 2tq+8..+9
+        const uint32_t a3 = lop3_and_or(ws, 0x00F000F0u, MAGIC);  // rows g+8, k 2tq+8..+9
+#pragma unroll
+        for (int nn = 0; nn < NT; ++nn) {
+          const uint4 v = bx[nn][j >> 1];
+          if (j & 1) mma16816(cb[nn], a0, a1, a2, a3, v.z, v.w);
+          else       mma16816(ca[nn], a0, a1, a2, a3, v.x, v.y);
+        }
+      }
+    }
+    // group epilogue: y += s C - s (1024 + z) Sx ; rows g+8: (s/16) C - s (64 + z) Sx
+    const uint2 szv = *reinterpret_cast<const uint2*>(buf + gr * GB + KPG * 128 + g * 8);
+    const float2 sf = __half22float2(u2h(szv.x)), zf = __half22float2(u2h(szv.y));
+    const float m0 = sf.x, m1 = sf.y * 0.0625f;
+    const float o0 = -sf.x * (1024.f + zf.x), o1 = -sf.y * (64.f + zf.y);
+#pragma unroll
+    for (int nn = 0; nn < NT; ++nn) {
+      const float2 xs = *reinterpret_cast<const float2*>(sxg + gr * (NT * 8) + nn * 8 + 2 * tq);
+      acc[nn][0] = fmaf(m0, ca[nn][0] + cb[nn][0], fmaf(o0, xs.x, acc[nn][0]));
+      acc[nn][1] = fmaf(m0, ca[nn][1] + cb[nn][1], fmaf(o0, xs.y, acc[nn][1]));
+      acc[nn][2] = fmaf(m1, ca[nn][2] + cb[nn][2], fmaf(o1, xs.x, acc[nn][2]));
+      acc[nn][3] = fmaf(m1, ca[nn][3] + cb[nn][3], fmaf(o1, xs.y, acc[nn][3]));
+    }
+  }
+}
+
+// Work of one warp: units u = warp, warp+WARPS, ... of the CTA; unit -> (row
+// tile, K-part).  Each warp streams its units' chunks through its own bulk-copy
+// ring, so warps never wait for one another; K-parts of a tile merge with
+// shared-memory atomics and the warp that completes a tile writes it out.
+// WARPS = 8 fits two CTAs per SM, so the next kernel of a PDL chain can start
+// its weight copies while this one finishes.
+template <int KPG, int NT, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) gemv_mma2_kernel(const MmaParams p) {
+  constexpr int THREADS = WARPS * 32;
+  constexpr int GPC = MG2_CHUNK / KPG;       // groups per chunk
+  constexpr int GB = KPG * 128 + 64;         // bytes per group: codes + scale/zero block
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);                   // [WARPS][MG2_RING]
+  int* tile_cnt = reinterpret_cast<int*>(smem + WARPS * MG2_RING * 8);  // [tiles_per_cta]
+  uint4* xf = reinterpret_cast<uint4*>(smem + p.xf_off);                // [batch][ks_n/2][4 tq] x 2 k-steps
+  float* sx = reinterpret_cast<float*>(smem + p.sx_off);                // [G][NT*8]
+  float* accs = reinterpret_cast<float*>(smem + p.acc_off);             // [tiles_per_cta][16][NT*8]
+  float* red = accs + p.tiles_per_cta * 16 * NT * 8;                    // [WARPS][16] + [16]
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int n_tiles = (p.rows + 15) / 16;
+  const int tile0 = blockIdx.x * p.tiles_per_cta;
+  if (tile0 >= n_tiles) return;
+  const int ntc = min(p.tiles_per_cta, n_tiles - tile0);
+  const int P = p.parts;
+  const int n_units = ntc * P;
+  uint64_t* wb = bars + warp * MG2_RING;
+  uint8_t* ring = smem + p.ring_off + (size_t)warp * p.ring * p.ring_stride;
+
+  for (int i = tid; i < ntc * 16 * NT * 8; i += THREADS) accs[i] = 0.f;
+  for (int i = tid; i < ntc; i += THREADS) tile_cnt[i] = 0;
+  if (lane == 0) {
+    for (int r = 0; r < p.ring; ++r) mbar_init(&wb[r], 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+
+  // chunk cursor over this warp's units; unit u -> (row tile, K-part)
+  struct Cursor { int u, t, ks, ks_end; };
+  auto start_unit = [&](Cursor& c) {
+    if (c.u >= n_units) return;
+    c.t = tile0 + c.u / P;
+    const int part = c.u % P;
+    c.ks = (part * p.G / P) * KPG;
+    c.ks_end = ((part + 1) * p.G / P) * KPG;
+  };
+  auto issue = [&](const Cursor& c, int slot) {
+    const int ng = min(MG2_CHUNK, c.ks_end - c.ks) / KPG;
+    const uint32_t bytes = (uint32_t)(ng * GB);
+    mbar_arrive_expect_tx(&wb[slot], bytes);
+    bulk_g2s(ring + (size_t)slot * p.ring_stride, p.blob + ((int64_t)c.t * p.G + c.ks / KPG) * GB, bytes, &wb[slot]);
+  };
+  auto advance = [&](Cursor& c) {
+    c.ks += MG2_CHUNK;
+    if (c.ks >= c.ks_end) { c.u += WARPS; start_unit(c); }
+  };
+
+  // weights do not depend on the previous kernel: start streaming before the
+  // grid dependency wait
+  Cursor prod{warp, 0, 0, 0};
+  start_unit(prod);
+  if (lane == 0)
+    for (int r = 0; r < p.ring && prod.u < n_units; ++r) { issue(prod, r); advance(prod); }
+  pdl_wait();
+
+  // ---- prologue: per-row inverse RMS (all batch rows in one pass) ----
+  const int K = p.cols, nb = p.batch;
+  float* inv = red + WARPS * 16;
+  if (p.norm_w) {
+    float ss[16];
+#pragma unroll
+    for (int b = 0; b < 16; ++b) ss[b] = 0.f;
+    for (int i = tid; i < (K >> 2); i += THREADS) {
+#pragma unroll
+      for (int b = 0; b < 16; ++b) {
+        if (b < nb) {
+          const float4 v = reinterpret_cast<const float4*>(p.x + (int64_t)b * p.ldx)[i];
+          ss[b] += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        }
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < 16; ++b) {
+      if (b < nb) {
+        const float v = warp_sum(ss[b]);
+        if (lane == 0) red[warp * 16 + b] = v;
+      }
+    }
+    __syncthreads();
+    if (tid < nb) {
+      float v = 0.f;
+      for (int w = 0; w < WARPS; ++w) v += red[w * 16 + tid];
+      inv[tid] = rsqrtf(v / K + p.eps);
+    }
+    __syncthreads();
+  }
+  // ---- x -> (RMS-normalised) fp16 B fragments: xf[b][s][tq] = {x[2tq], x[2tq+1], x[2tq+8], x[2tq+9]} ----
+  uint2* xf2 = reinterpret_cast<uint2*>(xf);
+  const int per_row = p.ks_n * 4;
+#pragma unroll 4
+  for (int i = tid; i < nb * per_row; i += THREADS) {
+    const int b = i / per_row, r = i - b * per_row;
+    const int s = r >> 2, tq = r & 3, k = s * 16 + 2 * tq;
+    const float* xb = p.x + (int64_t)b * p.ldx;
+    float2 v0 = *reinterpret_cast<const float2*>(xb + k), v1 = *reinterpret_cast<const float2*>(xb + k + 8);
+    if (p.norm_w) {
+      const float iv = inv[b];
+      const float2 n0 = *reinterpret_cast<const float2*>(p.norm_w + k);
+      const float2 n1 = *reinterpret_cast<const float2*>(p.norm_w + k + 8);
+      v0.x = v0.x * iv * n0.x; v0.y = v0.y * iv * n0.y;
+      v1.x = v1.x * iv * n1.x; v1.y = v1.y * iv * n1.y;
+    }
+    // element (b, s, tq) at uint2 index ((b * ks_n/2 + s/2) * 4 + tq) * 2 + (s & 1)
+    xf2[(((size_t)b * (p.ks_n >> 1) + (s >> 1)) * 4 + tq) * 2 + (s & 1)] =
+        make_uint2(h2u(__floats2half2_rn(v0.x, v0.y)), h2u(__floats2half2_rn(v1.x, v1.y)));
+  }
+  __syncthreads();
+  // Sx[grp][col]: sum of the fp16 x of group grp, batch row col (0 beyond the
+  // batch); one thread per (group, col), sequential order
+  for (int pr = tid; pr < p.G * NT * 8; pr += THREADS) {
+    const int grp = pr / (NT * 8), col = pr - grp * (NT * 8);
+    float v = 0.f;
+    if (col < nb) {
+      const uint4* src = xf + ((size_t)col * (p.ks_n >> 1) + grp * (KPG >> 1)) * 4;
+#pragma unroll 4
+      for (int e = 0; e < KPG * 2; ++e) {  // KPG/2 k-step pairs x 4 tq
+        const uint4 u = src[e];
+        const float2 f0 = __half22float2(u2h(u.x)), f1 = __half22float2(u2h(u.y));
+        const float2 f2 = __half22float2(u2h(u.z)), f3 = __half22float2(u2h(u.w));
+        v += ((f0.x + f0.y) + (f1.x + f1.y)) + ((f2.x + f2.y) + (f3.x + f3.y));
+      }
+    }
+    sx[pr] = v;
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+
+  const int g = lane >> 2, tq = lane & 3;
+  const int ks_half = p.ks_n >> 1;
+  bool aborted = false;
+  Cursor cons{warp, 0, 0, 0};
+  start_unit(cons);
+  int q = 0;  // chunks consumed by this warp
+  while (cons.u < n_units) {
+    const int t = cons.t, ks0 = cons.ks, nks = cons.ks_end - cons.ks;
+    float acc[NT][4];
+#pragma unroll
+    for (int n = 0; n < NT; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+    for (int off = 0; off < nks; off += MG2_CHUNK, ++q) {
+      const int slot = q % p.ring;
+      int okl = 0;
+      if (lane == 0) okl = !aborted && wait_bar(&wb[slot], (uint32_t)((q / p.ring) & 1));
+      if (!__shfl_sync(0xffffffffu, okl, 0)) {
+        if (lane == 0 && !aborted) atomicExch(p.err, DEV_ERR_TIMEOUT);
+        aborted = true;
+        break;
+      }
+      const uint8_t* buf = ring + (size_t)slot * p.ring_stride;
+      const int ngr = min(MG2_CHUNK, nks - off) / KPG;
+      const int grp0 = (ks0 + off) / KPG;
+      // x fragments of this chunk: row min(g, batch-1) (columns >= batch are never read)
+      const uint4* xb[NT];
+#pragma unroll
+      for (int nn = 0; nn < NT; ++nn)
+        xb[nn] = xf + ((size_t)min(nn * 8 + g, nb - 1) * ks_half + ((ks0 + off) >> 1)) * 4 + tq;
+      const float* sxg = sx + grp0 * (NT * 8);
+      if (ngr == GPC) {
+        mma_chunk<KPG, NT, GPC>(buf, lane, xb, sxg, acc);
+      } else {
+        for (int gr = 0; gr < ngr; ++gr) {
+          const uint4* xg[NT];
+#pragma unroll
+          for (int nn = 0; nn < NT; ++nn) xg[nn] = xb[nn] + gr * (KPG >> 1) * 4;
+          mma_chunk<KPG, NT, 1>(buf + gr * GB, lane, xg, sxg + gr * (NT * 8), acc);
+        }
+      }
+      // this chunk's buffer is free: issue the chunk RING positions ahead
+      __syncwarp();
+      if (lane == 0 && prod.u < n_units) { issue(prod, slot); advance(prod); }
+    }
+    if (aborted) break;
+    // merge this K-part into the tile; the warp completing the tile writes it out
+    const int tl = t - tile0;
+    float* ta = accs + (size_t)tl * 16 * NT * 8;
+#pragma unroll
+    for (int nn = 0; nn < NT; ++nn) {
+      const int c = nn * 8 + 2 * tq;
+      if (c < nb) { atomicAdd(&ta[g * NT * 8 + c], acc[nn][0]); atomicAdd(&ta[(g + 8) * NT * 8 + c], acc[nn][2]); }
+      if (c + 1 < nb) { atomicAdd(&ta[g * NT * 8 + c + 1], acc[nn][1]); atomicAdd(&ta[(g + 8) * NT * 8 + c + 1], acc[nn][3]); }
+    }
+    __threadfence_block();
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) last = atomicAdd(&tile_cnt[tl], 1) == P - 1;
+    if (__shfl_sync(0xffffffffu, last, 0)) {
+      __threadfence_block();
+      for (int i = lane; i < 16 * NT * 8; i += 32) {
+        const int r = i / (NT * 8), bc = i % (NT * 8);
+        const int row = t * 16 + r;
+        if (bc >= nb || row >= p.rows) continue;
+        if (p.swiglu && (r & 1)) continue;
+        float v = ta[i] + (p.bias ? p.bias[row] : 0.f);
+        if (p.swiglu) {
+          const float u = ta[i + NT * 8] + (p.bias ? p.bias[row + 1] : 0.f);
+          p.y[(int64_t)bc * p.ldy + row / 2] = (v / (1.0f + expf(-v))) * u;
+        } else {
+          if (p.residual) v += p.residual[(int64_t)bc * p.ldr + row];
+          p.y[(int64_t)bc * p.ldy + row] = v;
+        }
+      }
+    }
+    cons.u += WARPS;
+    start_unit(cons);
+  }
+  // a timed-out warp waits (bounded) for the copies it issued before exiting
+  if (aborted && lane == 0)
+    for (int r = 0; r < p.ring; ++r) wait_bar(&wb[r], 0), wait_bar(&wb[r], 1);
+}
+
+int* gemv_err_word();
+
+template <int KPG, int NT, int WARPS>
+static int launch_mma2(const MmaParams& p, int grid, size_t smem, cudaStream_t st, bool pdl) {
+  static bool configured = false;
+  if (!configured) {
+    N730_CUDA(cudaFuncSetAttribute(gemv_mma2_kernel<KPG, NT, WARPS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   227 * 1024));
+    configured = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(WARPS * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  N730_CUDA(cudaLaunchKernelEx(&cfg, gemv_mma2_kernel<KPG, NT, WARPS>, p));
+  return N730_OK;
+}
+
+template <int WARPS>
+static int launch_mma2_w(int kpg, int NT, const MmaParams& p, int grid, size_t smem, cudaStream_t st, bool pdl) {
+  if (kpg == 8) return NT == 1 ? launch_mma2<8, 1, WARPS>(p, grid, smem, st, pdl) : launch_mma2<8, 2, WARPS>(p, grid, smem, st, pdl);
+  if (kpg == 4) return NT == 1 ? launch_mma2<4, 1, WARPS>(p, grid, smem, st, pdl) : launch_mma2<4, 2, WARPS>(p, grid, smem, st, pdl);
+  return NT == 1 ? launch_mma2<16, 1, WARPS>(p, grid, smem, st, pdl) : launch_mma2<16, 2, WARPS>(p, grid, smem, st, pdl);
+}
+
+// Warps per CTA: 16 (one CTA per SM, the most bytes in flight) unless
+// N730_GEMV_WARPS=8 asks for two 8-warp CTAs per SM.
+static int mma_warps() {
+  static int w = [] {
+    const char* e = getenv("N730_GEMV_WARPS");
+    return (e && atoi(e) == 8) ? 8 : 16;
+  }();
+  return w;
+}
+
+int gemv_mma_launch(const GemvArgs& a, cudaStream_t st) {
+  const QWeight& w = *a.w;
+  N730_REQUIRE(w.layout == 1, N730_BAD_ARG, "gemv_mma: weight not in mma layout");
+  N730_REQUIRE(!a.swiglu || w.rows % 2 == 0, N730_BAD_ARG, "gemv_mma: swiglu needs even rows");
+  int* err = gemv_err_word();
+  N730_REQUIRE(err, N730_OOM, "gemv_mma: error word allocation failed");
+  const int kpg = w.group / 16;
+  N730_REQUIRE(kpg == 4 || kpg == 8 || kpg == 16, N730_UNSUPPORTED, "gemv_mma: group %d", w.group);
+  N730_REQUIRE(((uintptr_t)a.x & 15) == 0 && a.ldx % 4 == 0 && (!a.norm_w || ((uintptr_t)a.norm_w & 7) == 0),
+               N730_BAD_ARG, "gemv_mma: x must be 16-byte aligned with ldx %% 4 == 0");
+  const int WARPS = mma_warps();
+  MmaParams p = {};
+  p.blob = w.codes;
+  p.rows = w.rows; p.cols = w.cols; p.ks_n = w.cols / 16; p.G = w.n_groups;
+  p.ldy = a.ldy; p.bias = a.bias; p.ldr = a.ldr; p.norm_w = a.norm_w; p.eps = a.eps; p.swiglu = a.swiglu;
+  p.err = err;
+  const int n_tiles = (w.rows + 15) / 16;
+  // one CTA per SM: with 8 warps the other half of the SM stays free for the
+  // next kernel's CTA, which streams its weights while this one finishes
+  const int ctas = num_sms();
+  p.tiles_per_cta = (n_tiles + ctas - 1) / ctas;
+  const int grid = (n_tiles + p.tiles_per_cta - 1) / p.tiles_per_cta;
+  // K-parts so every warp has a unit; each part a whole number of groups
+  p.parts = std::max(1, std::min(p.G, (WARPS + p.tiles_per_cta - 1) / p.tiles_per_cta));
+  p.ring_stride = ((MG2_CHUNK / kpg) * (kpg * 128 + 64) + 127) / 128 * 128;
+  const size_t cap = WARPS == 16 ? 227 * 1024 : 113 * 1024;
+  int b0 = 0;
+  while (b0 < a.batch) {
+    int nb = std::min(16, a.batch - b0);
+    p.ring = MG2_RING;
+    auto layout = [&](int nb_) {
+      const int NT = nb_ > 8 ? 2 : 1;
+      size_t off = 128 + (size_t)WARPS * MG2_RING * 8 + (size_t)p.tiles_per_cta * 4;
+      off = (off + 127) / 128 * 128;
+      p.xf_off = (int)off;
+      off += (size_t)nb_ * p.ks_n * 4 * sizeof(uint2);  // ks_n is even (cols % 64 == 0)
+      off = (off + 127) / 128 * 128;
+      p.sx_off = (int)off;
+      off += (size_t)p.G * NT * 8 * 4;
+      off = (off + 127) / 128 * 128;
+      p.acc_off = (int)off;
+      off += ((size_t)p.tiles_per_cta * 16 * NT * 8 + (WARPS + 1) * 16) * 4;
+      off = (off + 127) / 128 * 128;
+      p.ring_off = (int)off;
+      return off + (size_t)WARPS * p.ring * p.ring_stride;
+    };
+    while (nb > 1 && layout(nb) > cap) --nb;
+    while (p.ring > 2 && layout(nb) > cap) --p.ring;
+    const size_t smem = layout(nb);
+    N730_REQUIRE(smem <= cap, N730_BAD_ARG, "gemv_mma: K=%d too large for shared memory", w.cols);
+    const int NT = nb > 8 ? 2 : 1;
+    p.x = a.x + (int64_t)b0 * a.ldx; p.ldx = a.ldx; p.batch = nb;
+    p.y = a.y + (int64_t)b0 * a.ldy;
+    p.residual = a.residual ? a.residual + (int64_t)b0 * a.ldr : nullptr;
+    const bool pdl = a.pdl != 0;
+    const int rc = WARPS == 16 ? launch_mma2_w<16>(kpg, NT, p, grid, smem, st, pdl)
+                               : launch_mma2_w<8>(kpg, NT, p, grid, smem, st, pdl);
+    if (rc) return rc;
+    b0 += nb;
+  }
+  return N730_OK;
+}
+
+}  // namespace n730

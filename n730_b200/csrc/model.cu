@@ -68,9 +68,6 @@ struct Model {
   // decode workspace
   int* d_tokens = nullptr;
   float *x = nullptr, *qkv = nullptr, *attn = nullptr, *mlp = nullptr, *logits = nullptr;
-  float2* part_ml = nullptr;
-  float* part_acc = nullptr;
-  int* counters = nullptr;
   // prefill workspace
   int* p_tokens = nullptr;
   float *px = nullptr, *pqkv = nullptr, *pattn = nullptr, *pmlp = nullptr;
@@ -119,6 +116,7 @@ static int fuse_rows(Model* m, std::vector<QWeight*> parts, bool interleave, QWe
 
 static int finalize(Model* m) {
   const N730ModelConfig& c = m->c;
+  if (int rc = gemv_prepare()) return rc;
   const int nl = c.layers;
   m->L.assign(nl, Layer{});
   auto W = [&](int l, int s) -> QWeight* {
@@ -187,6 +185,19 @@ static int finalize(Model* m) {
     if (int rc = upload_vec(m, fn ? *fn : ones, &m->final_norm)) return rc;
   }
   N730_CUDA(cudaStreamSynchronize(m->st));
+  if (!c.exact_gemv) {  // INT4 group-wise weights -> tensor-core fragment tiles
+    auto conv = [&](QWeight* w) -> int {
+      if (w && w->bits == 4 && w->sz_mode == 0 && w->group % 64 == 0 && w->cols % 64 == 0 && w->layout == 0)
+        return qweight_to_mma_layout(*w, m->st);
+      return N730_OK;
+    };
+    for (auto& y : m->L)
+      for (QWeight* w : {y.qkv, y.o, y.gate_up, y.down})
+        if (int rc = conv(w)) return rc;
+    if (int rc = conv(m->embed)) return rc;
+    if (m->lm_head != m->embed)
+      if (int rc = conv(m->lm_head)) return rc;
+  }
   for (auto& kv : m->pend_w) {
     const int s = kv.first.second;
     if (s == N730_W_Q || s == N730_W_K || s == N730_W_V || s == N730_W_GATE || s == N730_W_UP)
@@ -227,17 +238,13 @@ static int finalize(Model* m) {
   m->h_seq.assign(c.max_batch, 0);
   // decode workspace
   const int B = c.max_batch;
-  m->n_split = std::max(1, std::min(64, (c.max_ctx + 63) / 64));
+  m->n_split = 8;  // context splits per (sequence, KV head): one 8-CTA cluster
   if (int rc = m->alloc(&m->d_tokens, B)) return rc;
   if (int rc = m->alloc(&m->x, (size_t)B * c.hidden)) return rc;
   if (int rc = m->alloc(&m->qkv, (size_t)B * m->qkv_dim)) return rc;
   if (int rc = m->alloc(&m->attn, (size_t)B * c.heads * c.head_dim)) return rc;
   if (int rc = m->alloc(&m->mlp, (size_t)B * c.ffn)) return rc;
   if (int rc = m->alloc(&m->logits, (size_t)B * c.vocab)) return rc;
-  if (int rc = m->alloc(&m->part_ml, (size_t)B * c.heads * m->n_split)) return rc;
-  if (int rc = m->alloc(&m->part_acc, (size_t)B * c.heads * m->n_split * c.head_dim)) return rc;
-  if (int rc = m->alloc(&m->counters, (size_t)B * c.kv_heads)) return rc;
-  N730_CUDA(cudaMemsetAsync(m->counters, 0, (size_t)B * c.kv_heads * 4, m->st));
   // prefill workspace
   const int P = c.max_prefill;
   if (int rc = m->alloc(&m->p_tokens, P)) return rc;
@@ -280,8 +287,7 @@ static int enqueue_decode(Model* m, int B) {
     DecodeAttnArgs a = {};
     a.qkv = m->qkv; a.ld_qkv = m->qkv_dim; a.cos_t = m->cos_t; a.sin_t = m->sin_t;
     a.seq_lens = m->seq_lens; a.block_table = m->block_table; a.kv = y.kv; a.d = dims(m);
-    a.out = m->attn; a.batch = B; a.n_split = m->n_split; a.part_ml = m->part_ml; a.part_acc = m->part_acc;
-    a.counters = m->counters; a.pdl = c.use_pdl;
+    a.out = m->attn; a.batch = B; a.pdl = c.use_pdl;
     if (int rc = attn_decode_launch(a, m->st)) return rc;
     if (int rc = gemv(m, y.o, m->attn, ad, B, m->x, h, y.o_bias, m->x, h, nullptr, 0)) return rc;
     if (int rc = gemv(m, y.gate_up, m->x, h, B, m->mlp, c.ffn, y.gate_up_bias, nullptr, 0, y.ln2, 1)) return rc;
@@ -446,6 +452,19 @@ N730_API int n730_model_reset(void* p) {
   return N730_OK;
 }
 
+// Set a sequence's cached length (positions [0, len) are taken as already in
+// the KV cache).  Used to resume a sequence whose cache was filled earlier
+// and to position decode benchmarks at a given context.
+N730_API int n730_model_set_seq_len(void* p, int seq, int len) {
+  MODEL(p);
+  N730_REQUIRE(m->finalized && seq >= 0 && seq < m->c.max_batch && len >= 0 && len <= m->c.max_ctx,
+               N730_BAD_ARG, "set_seq_len: bad sequence %d or length %d", seq, len);
+  m->h_seq[seq] = len;
+  N730_CUDA(cudaMemcpyAsync(m->seq_lens + seq, &m->h_seq[seq], 4, cudaMemcpyHostToDevice, m->st));
+  N730_CUDA(cudaStreamSynchronize(m->st));
+  return N730_OK;
+}
+
 N730_API int n730_model_seq_len(void* p, int seq) {
   MODEL(p);
   N730_REQUIRE(seq >= 0 && seq < m->c.max_batch && m->finalized, N730_BAD_ARG, "model: bad sequence %d", seq);
@@ -536,8 +555,10 @@ N730_API int n730_model_info(void* p, int64_t* info) {
   if (!info) return N730_NULL;
   memset(info, 0, 16 * sizeof(int64_t));
   if (!m->finalized) return N730_OK;
-  auto bytes = [](const QWeight* w) {
-    return w ? w->rows * w->row_bytes + (w->bits == 16 ? 0 : (int64_t)w->rows * w->sz_pitch) : 0;
+  auto bytes = [](const QWeight* w) -> int64_t {
+    if (!w) return 0;
+    if (w->layout == 1) return (int64_t)((w->rows + 15) / 16) * w->n_groups * ((int64_t)(w->group / 16) * 128 + 64);
+    return w->rows * w->row_bytes + (w->bits == 16 ? 0 : (int64_t)w->rows * w->sz_pitch);
   };
   int64_t wb = bytes(m->embed) + (m->lm_head != m->embed ? bytes(m->lm_head) : 0);
   for (auto& y : m->L) wb += bytes(y.qkv) + bytes(y.o) + bytes(y.gate_up) + bytes(y.down);
@@ -585,7 +606,7 @@ N730_API int64_t n730_model_linear_bytes(void* p, int layer, int which, int batc
                    : which == 2 ? m->L[layer].gate_up : which == 3 ? m->L[layer].down : nullptr;
   if (!w) return -1;
   const int64_t codes = ((int64_t)w->rows * w->cols * w->bits + 7) / 8;
-  const int64_t sz = w->bits == 16 ? 0 : (w->sz_mode == 0 ? (int64_t)w->rows * w->n_groups * 4 : 8);
+  const int64_t sz = w->bits == 16 ? 0 : (w->sz_mode == 0 ? (int64_t)w->rows * w->n_groups * 4 : 8);  // fp16 s + z
   const int64_t out_rows = which == 2 ? w->rows / 2 : w->rows;
   return codes + sz + (int64_t)batch * (w->cols + out_rows) * 4;
 }

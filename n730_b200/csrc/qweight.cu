@@ -37,9 +37,30 @@ __device__ __forceinline__ float dq(uint32_t q, float s, float z) {
 }
 
 __device__ __forceinline__ float2 load_sz(const QWeight& w, int r, int c) {
+  if (w.layout == 1) {  // fragment tiles: per (tile, group) codes then {s_g, s_g8, z_g, z_g8} x 8
+    const int t = r >> 4, rr = r & 15, g = rr & 7, kpg = w.group >> 4;
+    const uint8_t* grp = w.codes + ((int64_t)t * w.n_groups + c / w.group) * ((int64_t)kpg * 128 + 64);
+    const uint2 v = reinterpret_cast<const uint2*>(grp + kpg * 128)[g];
+    const __half2 sc = *reinterpret_cast<const __half2*>(&v.x), zp = *reinterpret_cast<const __half2*>(&v.y);
+    return rr < 8 ? make_float2(__low2float(sc), __low2float(zp)) : make_float2(__high2float(sc), __high2float(zp));
+  }
   const uint8_t* row = reinterpret_cast<const uint8_t*>(w.sz) + (int64_t)r * w.sz_pitch;
   if (w.sz_mode == 0) return __half22float2(reinterpret_cast<const __half2*>(row)[c / w.group]);
   return *reinterpret_cast<const float2*>(row);
+}
+
+// code of element (r, c); layout 1 inverts the fragment packing of gemv_mma.cu
+__device__ __forceinline__ uint32_t code_rc(const QWeight& w, int r, int c) {
+  if (w.layout == 1) {
+    const int t = r >> 4, rr = r & 15, kpg = w.group >> 4;
+    const int s = (c % w.group) >> 4, kc = c & 15;  // k-step within the group, column within the k-step
+    const int lane = (rr & 7) * 4 + ((kc & 7) >> 1);
+    const int nib = (rr >> 3) + 2 * (kc >> 3) + 4 * (kc & 1);
+    const uint8_t* grp = w.codes + ((int64_t)t * w.n_groups + c / w.group) * ((int64_t)kpg * 128 + 64);
+    const uint32_t word = reinterpret_cast<const uint32_t*>(grp)[((s >> 2) * 32 + lane) * 4 + (s & 3)];
+    return (word >> (4 * nib)) & 15u;
+  }
+  return code_at(w.codes + (int64_t)r * w.row_bytes, w.bits, c);
 }
 
 __global__ void dequant_kernel(const QWeight w, float* out, int64_t ld, int row0, int nrows) {
@@ -47,13 +68,12 @@ __global__ void dequant_kernel(const QWeight w, float* out, int64_t ld, int row0
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int r = row0 + (int)(i / w.cols), c = (int)(i % w.cols);
-    const uint8_t* row = w.codes + (int64_t)r * w.row_bytes;
     float v;
     if (w.bits == 16) {
-      v = __half2float(reinterpret_cast<const __half*>(row)[c]);
+      v = __half2float(reinterpret_cast<const __half*>(w.codes + (int64_t)r * w.row_bytes)[c]);
     } else {
       const float2 sz = load_sz(w, r, c);
-      v = dq(code_at(row, w.bits, c), sz.x, sz.y);
+      v = dq(code_rc(w, r, c), sz.x, sz.y);
     }
     out[(int64_t)(r - row0) * ld + c] = v;
   }
@@ -68,11 +88,10 @@ __global__ void embed_kernel(const QWeight w, const int32_t* tokens, int n, floa
       out[(int64_t)t * w.cols + c] = 0.f;
     return;
   }
-  const uint8_t* row = w.codes + (int64_t)r * w.row_bytes;
   for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < w.cols; c += gridDim.x * blockDim.x) {
     float v;
-    if (w.bits == 16) v = __half2float(reinterpret_cast<const __half*>(row)[c]);
-    else { const float2 sz = load_sz(w, r, c); v = dq(code_at(row, w.bits, c), sz.x, sz.y); }
+    if (w.bits == 16) v = __half2float(reinterpret_cast<const __half*>(w.codes + (int64_t)r * w.row_bytes)[c]);
+    else { const float2 sz = load_sz(w, r, c); v = dq(code_rc(w, r, c), sz.x, sz.y); }
     out[(int64_t)t * w.cols + c] = v;
   }
 }
@@ -329,6 +348,7 @@ int qweight_alloc_like(const QWeight& proto, int rows, QWeight** out) {
 }
 
 int qweight_copy_rows(QWeight& dst, const QWeight& src, int dst_row0, int stride, cudaStream_t st) {
+  N730_REQUIRE(dst.layout == 0 && src.layout == 0, N730_BAD_ARG, "qweight_copy_rows: row layout required");
   N730_REQUIRE(dst.bits == src.bits && dst.row_bytes == src.row_bytes && dst.sz_mode == src.sz_mode &&
                dst.cols == src.cols && (dst.sz_mode != 0 || dst.n_groups == src.n_groups),
                N730_BAD_ARG, "qweight_copy_rows: layouts differ");
@@ -371,8 +391,19 @@ N730_API int n730_qweight_info(void* qw, int64_t* info) {
   const QWeight* w = (const QWeight*)qw;
   info[0] = w->prec; info[1] = w->bits; info[2] = w->rows; info[3] = w->cols;
   info[4] = w->group; info[5] = w->n_groups; info[6] = w->row_bytes;
-  info[7] = w->rows * w->row_bytes + (w->bits == 16 ? 0 : (int64_t)w->rows * w->sz_pitch);
+  info[7] = w->layout == 1 ? (int64_t)((w->rows + 15) / 16) * w->n_groups * ((int64_t)(w->group / 16) * 128 + 64)
+                           : w->rows * w->row_bytes + (w->bits == 16 ? 0 : (int64_t)w->rows * w->sz_pitch);
   return N730_OK;
+}
+
+// Convert a weight to a device layout: 0 row-major (any format), 1 tensor-core
+// fragment tiles (INT4 group-wise, group % 64 == 0; used by the mma GEMV).
+N730_API int n730_qweight_set_layout(void* qw, int layout, void* stream) {
+  if (!qw) return N730_NULL;
+  QWeight* w = (QWeight*)qw;
+  if (layout == w->layout) return N730_OK;
+  N730_REQUIRE(layout == 1, N730_UNSUPPORTED, "qweight_set_layout: only row -> fragment tiles is supported");
+  return qweight_to_mma_layout(*w, (cudaStream_t)stream);
 }
 
 N730_API int n730_dequant_to_f32(void* qw, float* d_out, void* stream) {

@@ -22,6 +22,7 @@ struct QWeight {
   int group = 0;      // elements per group (== cols for sz_mode 1)
   int n_groups = 0;   // groups per row
   int sz_mode = 0;
+  int layout = 0;     // 0 row-major padded rows; 1 mma fragment tiles (INT4 grouped)
   int64_t row_bytes = 0;
   int64_t sz_pitch = 0;
   uint8_t* codes = nullptr;
@@ -47,7 +48,11 @@ struct GemvArgs {
 };
 
 int gemv_launch(const GemvArgs& a, cudaStream_t stream);
-int gemv_check_error(bool reset);  // N730_TIMEOUT if a device wait ran out
+int gemv_mma_launch(const GemvArgs& a, cudaStream_t stream);
+int qweight_to_mma_layout(QWeight& w, cudaStream_t stream);
+int* gemv_err_word();
+int gemv_check_error(bool reset);
+int gemv_prepare();  // allocate device state before any graph capture  // N730_TIMEOUT if a device wait ran out
 int dequant_launch(const QWeight& w, float* out, int64_t ld_out, int row0, int nrows,
                    cudaStream_t stream);
 int repack_rows_launch(const uint8_t* src, int bits, int rows, int cols, uint8_t* dst,

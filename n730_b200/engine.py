@@ -31,7 +31,7 @@ class N730ModelConfig(C.Structure):
     _fields_ = [(n, C.c_int32) for n in ("hidden", "layers", "heads", "kv_heads", "head_dim", "ffn", "vocab")] + \
                [("rms_eps", C.c_float), ("rope_theta", C.c_float)] + \
                [(n, C.c_int32) for n in ("max_ctx", "max_batch", "page_size", "max_prefill", "tie_embeddings",
-                                         "tp_rank", "tp_size", "use_graphs", "use_pdl")]
+                                         "tp_rank", "tp_size", "use_graphs", "use_pdl", "exact_gemv")]
 
 
 def _sigs(lib):
@@ -51,6 +51,8 @@ def _sigs(lib):
         getattr(lib, f).restype = i32
     lib.n730_model_seq_len.argtypes = [vp, i32]
     lib.n730_model_seq_len.restype = i32
+    lib.n730_model_set_seq_len.argtypes = [vp, i32, i32]
+    lib.n730_model_set_seq_len.restype = i32
     lib.n730_model_forward.argtypes = [vp, i32, vp, i32, vp]
     lib.n730_model_forward.restype = i32
     lib.n730_model_decode.argtypes = [vp, vp, i32, vp]
@@ -117,13 +119,13 @@ class Engine:
 
     def __init__(self, shape: ModelShape, max_ctx: int = 4096, max_batch: int = 1, page_size: int = 64,
                  max_prefill: int = 512, use_graphs: bool = True, use_pdl: bool = True,
-                 tp_rank: int = 0, tp_size: int = 1):
+                 tp_rank: int = 0, tp_size: int = 1, exact_gemv: bool = False):
         self.lib = _sigs(_lib.cuda())
         self.shape = shape
         c = N730ModelConfig(shape.hidden, shape.layers, shape.heads, shape.kv_heads, shape.head_dim, shape.ffn,
                             shape.vocab, shape.rms_eps, shape.rope_theta, max_ctx, max_batch, page_size,
                             max_prefill, int(shape.tie_embeddings), tp_rank, tp_size, int(use_graphs),
-                            int(use_pdl))
+                            int(use_pdl), int(exact_gemv))
         self.cfg = c
         self.h = C.c_void_p()
         _lib.check(self.lib.n730_model_create(C.byref(c), C.byref(self.h)), "model_create")
@@ -146,6 +148,9 @@ class Engine:
 
     def seq_len(self, seq: int = 0) -> int:
         return _lib.check(self.lib.n730_model_seq_len(self.h, seq), "model_seq_len")
+
+    def set_seq_len(self, seq: int, n: int):
+        _lib.check(self.lib.n730_model_set_seq_len(self.h, seq, n), "model_set_seq_len")
 
     def forward(self, token_ids, seq: int = 0) -> np.ndarray:
         ids = np.ascontiguousarray(token_ids, np.int32).reshape(-1)

@@ -170,3 +170,44 @@ def test_bad_group_rejected(lib):
                                  s.ctypes.data_as(C.c_void_p), s.ctypes.data_as(C.c_void_p), 0, None,
                                  C.byref(out))
     assert rc == -13 and b"group" in lib.n730_last_error()
+
+
+@pytest.mark.parametrize("rows,cols,group,batch", [(4096, 4096, 128, 1), (4608, 3584, 128, 1), (3584, 18944, 128, 1),
+                                                   (40, 256, 64, 3), (37, 512, 128, 9), (300, 1024, 256, 16),
+                                                   (64, 3584, 128, 20)])
+def test_qlinear_tensor_core_layout(lib, rows, cols, group, batch):
+    """INT4 group-wise weights in the tensor-core fragment layout: dequant stays
+    bit-exact; the GEMV (x rounded to fp16, fp32 accumulation) is within 2e-3."""
+    rng = np.random.default_rng(rows * 7 + batch)
+    w = rng.normal(0, 0.02, (rows, cols)).astype(np.float32)
+    x = rng.normal(0, 1, (batch, cols)).astype(np.float32)
+    codes, s16, z16 = oq.quantize_grouped(w, 4, group)
+    wd = oq.dequant_grouped(codes, s16, z16, 4, rows, cols)
+    qw = qweight_from_oracle(0x44, rows, cols, codes, s16=s16, z16=z16, group=group)
+    _lib.check(lib.n730_qweight_set_layout(qw, 1, None), "set_layout")
+    assert np.array_equal(_dequant(lib, qw, rows, cols).view(np.uint32), wd.view(np.uint32))
+    y = _qlinear(lib, qw, x, rows)
+    assert rel_err(y, oq.gemv(wd, x)) <= 2e-3
+    lib.n730_qweight_destroy(qw)
+
+
+@pytest.mark.parametrize("B", [1, 2, 5])
+def test_tensor_core_epilogues(lib, B):
+    from oracle.model import rms_norm, swiglu
+    rng = np.random.default_rng(90 + B)
+    K, N = 1024, 640
+    w = rng.normal(0, 0.02, (N, K)).astype(np.float32)
+    x = rng.normal(0, 1, (B, K)).astype(np.float32)
+    nw = rng.uniform(0.5, 1.5, K).astype(np.float32)
+    bias = rng.normal(0, 0.02, N).astype(np.float32)
+    res = rng.normal(0, 1, (B, N)).astype(np.float32)
+    codes, s16, z16 = oq.quantize_grouped(w, 4, 128)
+    wd = oq.dequant_grouped(codes, s16, z16, 4, N, K)
+    qw = qweight_from_oracle(0x44, N, K, codes, s16=s16, z16=z16, group=128)
+    _lib.check(lib.n730_qweight_set_layout(qw, 1, None), "set_layout")
+    xn = rms_norm(x, nw, 1e-6)
+    assert rel_err(_qlinear(lib, qw, x, N, bias=bias, resid=res, norm=nw), res + xn @ wd.T + bias) <= 2e-3
+    full = xn @ wd.T + bias
+    assert rel_err(_qlinear(lib, qw, x, N // 2, bias=bias, norm=nw, swiglu=1),
+                   swiglu(full[:, 0::2], full[:, 1::2])) <= 2e-3
+    lib.n730_qweight_destroy(qw)
