@@ -140,6 +140,8 @@ typedef struct N730ModelConfig {
   int32_t use_pdl;      /* programmatic dependent launch between kernels */
   int32_t exact_gemv;   /* 1: fp32 CUDA-core GEMV everywhere; 0: INT4 g%64 weights use the
                            tensor-core GEMV (x rounded to fp16) */
+  int32_t per_op_decode; /* 1: batch-1 decode as one kernel per op; 0: one persistent
+                            cooperative kernel for the whole step when the model allows it */
 } N730ModelConfig;
 
 /* weight slots (n730_model_set_qweight); EMBED/LMHEAD take layer = -1 */

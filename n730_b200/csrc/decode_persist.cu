@@ -1,0 +1,662 @@
+// Persistent decode step: the whole batch-1 forward pass (every layer's qkv
+// GEMV, RoPE + GQA attention, o_proj, gate|up + SwiGLU, down_proj, then the
+// final-norm lm_head) in ONE cooperative launch of one 16-warp CTA per SM.
+//
+// Why: a decode step is ~140 dependent GEMVs that each stream a few MB of
+// packed weights.  As separate kernels every op pays a launch, a prologue that
+// re-reads x behind its own weight prefetch, and a pipeline fill.  Here:
+//  * Each CTA owns a fixed run of whole row tiles of every GEMV, split evenly
+//    over its 16 warps by [tile][group] units; lane 0 of each warp streams the
+//    warp's chunks through a private TMA bulk-copy ring whose cursor runs
+//    ACROSS ops and layers.  Weights never depend on activations, so while the
+//    CTA waits at an op boundary its ring already holds the next op's weights.
+//  * Ops are separated by a grid barrier (one arrival counter, bounded spin on
+//    %globaltimer; an expired wait raises the abort flag that releases every
+//    CTA and sets the device error word).  Each op then costs few dependent
+//    global round trips: the barrier, one batch of loads (x, norm weights,
+//    residual and bias rows), and fire-and-forget stores.
+//  * After the barrier each CTA builds the op's fp16 x fragments and per-group
+//    x sums (RMSNorm folded in) in shared memory; warps run the tensor-core
+//    INT4 GEMV of mma_gemv.cuh on their chunks; a tile split between warps is
+//    merged by the last contributor in warp order (deterministic) and written
+//    with its epilogue (store, residual add in place, or SwiGLU of interleaved
+//    gate/up rows).
+//  * Attention: each split is one KV page (64 positions) of one KV head.  The
+//    page's K and V are bulk-copied into shared memory a whole layer ahead (the
+//    cached positions do not depend on this step); the split holding the new
+//    position RoPEs and appends k/v; scores and P V on CUDA cores with an
+//    online softmax; the last split of a head merges all splits with one batch
+//    of loads:  out = sum_s e^(m_s-M) o_s / (sum_s e^(m_s-M) l_s + 1e-9)
+//    (the reference normalisation, n730_cuda.cu:236-257).
+// Data written by other CTAs during the launch is read with ld.global.cg (L2),
+// never through a possibly stale L1 line.
+#include <algorithm>
+#include <cmath>
+
+#include "decode_persist.h"
+#include "mma_gemv.cuh"
+#include "qweight.h"
+
+namespace n730 {
+
+constexpr int PD_WARPS = 16;
+constexpr int PD_THREADS = PD_WARPS * 32;
+constexpr int PD_RING = 2;         // chunks in flight per warp
+constexpr int PD_NREG = 4;         // normalised x items (4 values) per thread: K <= 4 * 512 * 4
+constexpr int PD_KNORM = 4 * PD_THREADS * PD_NREG;
+constexpr int PD_MAXG = 8;         // query heads per KV head
+constexpr int PD_MAXSPLIT = 64;    // context splits per KV head
+constexpr int PD_ADDMAX = 512;     // epilogue addend rows (bias / residual) per CTA
+constexpr uint64_t PD_WAIT_NS = 200000000ull;  // grid-barrier wait limit (0.2 s)
+
+// groups per chunk: ~4.2-4.6 KB per bulk copy
+__host__ __device__ constexpr int pd_gpc(int kpg) { return kpg == 4 ? 8 : kpg == 8 ? 4 : 2; }
+
+// [lo, hi) split into n near-equal parts: start of part i
+__device__ __forceinline__ int pd_rng(int lo, int hi, int i, int n) {
+  return lo + (int)((int64_t)(hi - lo) * i / n);
+}
+// the part of [lo, hi) (split into n) that holds unit u
+__device__ __forceinline__ int pd_owner(int u, int lo, int hi, int n) {
+  int i = (int)((int64_t)(u - lo) * n / (hi - lo));
+  i = min(max(i, 0), n - 1);
+  while (i > 0 && pd_rng(lo, hi, i, n) > u) --i;
+  while (i < n - 1 && pd_rng(lo, hi, i + 1, n) <= u) ++i;
+  return i;
+}
+
+__device__ __forceinline__ int ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ int ld_relaxed(const int* p) {
+  int v;
+  asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Grid barrier number k (all CTAs call it in the same order).  False when the
+// launch is being aborted.
+__device__ bool pd_barrier(const PdArgs& a, int k, int* flag) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    atomicAdd(&a.sync[0], 1);
+    const int target = (int)gridDim.x * k;
+    int ok = 1;
+    if (ld_acquire(&a.sync[0]) < target) {
+      const uint64_t t0 = gtimer();
+      while (ld_acquire(&a.sync[0]) < target) {
+        if (ld_relaxed(&a.sync[2])) { ok = 0; break; }
+        if (gtimer() - t0 > PD_WAIT_NS) {
+          atomicExch(&a.sync[2], 1);
+          atomicExch(a.err, DEV_ERR_TIMEOUT);
+          ok = 0;
+          break;
+        }
+      }
+    }
+    if (ld_relaxed(&a.sync[2])) ok = 0;
+    __threadfence();
+    *flag = ok;
+  }
+  __syncthreads();
+  return *flag != 0;
+}
+
+// KV split geometry of this step (batch 1): ns splits per KV head of ppi pages.
+struct PdSplits { int pos, L, npages, ppi, ns, items; };
+__device__ __forceinline__ PdSplits pd_splits(const PdArgs& a) {
+  PdSplits s;
+  s.pos = a.seq_lens[0];
+  s.L = s.pos + 1;
+  s.npages = (s.L + PD_PAGE - 1) / PD_PAGE;
+  const int ns0 = min(s.npages, a.max_split);
+  s.ppi = (s.npages + ns0 - 1) / ns0;
+  s.ns = (s.npages + s.ppi - 1) / s.ppi;
+  s.items = a.d.n_kv * s.ns;
+  return s;
+}
+
+template <int KPG, int HD>
+__global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdArgs a) {
+  constexpr int GPC = pd_gpc(KPG);
+  constexpr int GB = KPG * 128 + 64;  // bytes per group
+  constexpr int H2 = HD / 2;
+  constexpr int CH = HD / 8;          // 16-byte chunks per K/V row
+  constexpr uint32_t PAGE_BYTES = PD_PAGE * HD * 2;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int NC = gridDim.x, cta = blockIdx.x;
+  const int g = lane >> 2, tq = lane & 3;
+  uint64_t* wb = reinterpret_cast<uint64_t*>(smem) + warp * PD_RING;
+  uint64_t* kvbar = reinterpret_cast<uint64_t*>(smem) + PD_WARPS * PD_RING;
+  uint8_t* ring = smem + a.ring_off + (size_t)warp * PD_RING * a.ring_stride;
+  uint8_t* work = smem + a.work_off;
+  __half* Ks = reinterpret_cast<__half*>(smem + a.kv_off);      // [PD_PAGE][HD]
+  __half* Vs = Ks + PD_PAGE * HD;                               // [PD_PAGE][HD]
+  float* addv = reinterpret_cast<float*>(smem + a.add_off);      // [PD_ADDMAX]
+  float* wpart = reinterpret_cast<float*>(smem + a.wpart_off);  // [16 warps][2][16 rows]
+  int* wcnt = reinterpret_cast<int*>(smem + a.misc_off);         // [16]
+  int* flag = wcnt + 16;                                         // [16]
+  float* red = reinterpret_cast<float*>(wcnt + 32);              // [32]
+
+  const PdSplits sp = pd_splits(a);
+  const AttnDims& d = a.d;
+  const int GQ = d.n_heads / d.n_kv;
+  const bool has_item = cta < sp.items;
+  const int kvh = has_item ? cta / sp.ns : 0, split = has_item ? cta % sp.ns : 0;
+  const int pg0 = split * sp.ppi, pg1 = min(sp.npages, pg0 + sp.ppi);
+
+  if (tid < 16) wcnt[tid] = 0;
+  if (lane == 0) {
+    for (int r = 0; r < PD_RING; ++r) mbar_init(&wb[r], 1);
+    if (warp == 0) mbar_init(kvbar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  // ---- KV page copies (thread 0): page p of this CTA's KV head, layer of phase ph ----
+  int kv_uses = 0;      // copies issued (thread 0)
+  int kv_waited = 0;    // copies waited for (thread 0)
+  auto kv_issue = [&](int ph, int p) {
+    const PdPhase& P = a.phases[ph];
+    const int page = a.block_table[p];
+    const int64_t off = ((int64_t)page * d.n_kv + kvh) * PD_PAGE * HD;
+    mbar_arrive_expect_tx(kvbar, 2 * PAGE_BYTES);
+    bulk_g2s(Ks, P.kv.k_pages + off, PAGE_BYTES, kvbar);
+    bulk_g2s(Vs, P.kv.v_pages + off, PAGE_BYTES, kvbar);
+    ++kv_uses;
+  };
+  auto next_attn = [&](int ph) {
+    for (; ph < a.n_phases; ++ph)
+      if (a.phases[ph].kind == PD_ATTN) return ph;
+    return a.n_phases;
+  };
+
+  // ---- weight stream: this warp's chunks of every GEMV op, in op order ----
+  struct Cursor { int ph, u, end, gi, G; const uint8_t* blob; };
+  auto set_phase = [&](Cursor& c, int ph) {
+    for (; ph < a.n_phases; ++ph) {
+      const PdPhase& P = a.phases[ph];
+      if (P.kind != PD_GEMV) continue;
+      const int T = (P.rows + 15) >> 4;
+      const int c0 = pd_rng(0, T, cta, NC) * P.G, c1 = pd_rng(0, T, cta + 1, NC) * P.G;
+      const int w0 = pd_rng(c0, c1, warp, PD_WARPS), w1 = pd_rng(c0, c1, warp + 1, PD_WARPS);
+      if (w0 < w1) { c.ph = ph; c.u = w0; c.end = w1; c.gi = w0 % P.G; c.G = P.G; c.blob = P.blob; return; }
+    }
+    c.ph = a.n_phases;
+  };
+  int issued = 0, consumed = 0;
+  Cursor prod{0, 0, 0, 0, 1, nullptr};
+  auto issue_next = [&](int slot) {  // lane 0
+    if (prod.ph >= a.n_phases) return;
+    const int n = min(min(GPC, prod.end - prod.u), prod.G - prod.gi);  // never crosses a row tile
+    mbar_arrive_expect_tx(&wb[slot], (uint32_t)(n * GB));
+    bulk_g2s(ring + (size_t)slot * a.ring_stride, prod.blob + (int64_t)prod.u * GB, (uint32_t)(n * GB), &wb[slot]);
+    ++issued;
+    prod.u += n;
+    prod.gi += n;
+    if (prod.gi == prod.G) prod.gi = 0;
+    if (prod.u >= prod.end) set_phase(prod, prod.ph + 1);
+  };
+  if (lane == 0) {
+    set_phase(prod, 0);
+    for (int r = 0; r < PD_RING; ++r) issue_next(r);
+  }
+  if (tid == 0 && has_item) {
+    const int ph = next_attn(0);
+    if (ph < a.n_phases) kv_issue(ph, pg0);
+  }
+
+  // A warp whose copy wait runs out stops consuming and raises the abort flag;
+  // every CTA then leaves at its next grid barrier (a CTA-uniform decision).
+  bool wfail = false;
+  int bar_k = 0, attn_idx = 0;
+  for (int ph = 0; ph < a.n_phases; ++ph) {
+    const PdPhase& P = a.phases[ph];
+    if (P.kind == PD_GEMV && P.norm_w)  // constant: pull this thread's norm weights into L1 before the wait
+      for (int i = tid; i < (P.cols >> 2); i += PD_THREADS) {
+        const float* p = P.norm_w + (i >> 2) * 16 + 2 * (i & 3);
+        asm volatile("prefetch.global.L1 [%0];" :: "l"(p));
+        asm volatile("prefetch.global.L1 [%0];" :: "l"(p + 8));
+      }
+    if (ph > 0 && !pd_barrier(a, ++bar_k, flag)) break;
+
+    if (P.kind == PD_ATTN) {
+      // ============================ attention ============================
+      if (has_item) {
+        __half* q_h = reinterpret_cast<__half*>(work);                              // [PD_MAXG][HD + 8]
+        float* sc = reinterpret_cast<float*>(work + (size_t)PD_MAXG * (HD + 8) * 2);  // [PD_MAXG][PD_PAGE]
+        float* ml = sc + PD_MAXG * PD_PAGE;           // [PD_MAXG][4]: m, l, alpha, den
+        const float* cs = a.cos_t + (int64_t)sp.pos * H2;
+        const float* sn = a.sin_t + (int64_t)sp.pos * H2;
+        // O accumulator fragment: warp w < HD/8 owns dims [8w, 8w+8); row g = query head g
+        float oc[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int pg = pg0; pg < pg1; ++pg) {
+          if (tid == 0) {
+            if (pg > pg0) kv_issue(ph, pg);
+            const bool okw = wait_bar(kvbar, (uint32_t)(kv_waited & 1));
+            ++kv_waited;
+            if (!okw) { atomicExch(&a.sync[2], 1); atomicExch(a.err, DEV_ERR_TIMEOUT); }
+          }
+          __syncthreads();
+          const int t0 = pg * PD_PAGE, n = min(PD_PAGE, sp.L - t0);
+          // one batch of loads: the RoPE'd, pre-scaled queries (fp16, rows >= GQ zero) and,
+          // in the split holding it, the new token's k (RoPE'd) and v, to the page and the cache
+          if (pg == pg0) {
+            for (int i = tid; i < PD_MAXG * HD; i += PD_THREADS) {
+              const int j = i / HD, dd = i - j * HD;
+              float v = 0.f;
+              if (j < GQ) {
+                const float* qh = a.qkv + (int64_t)(kvh * GQ + j) * HD;
+                const int j0 = dd < H2 ? dd : dd - H2;
+                const float x0 = __ldcg(qh + j0), x1 = __ldcg(qh + j0 + H2), c = cs[j0], sv = sn[j0];
+                v = (dd < H2 ? x0 * c - x1 * sv : x1 * c + x0 * sv) * d.scale;
+              }
+              q_h[j * (HD + 8) + dd] = __float2half_rn(v);
+            }
+            if (tid < GQ) { ml[tid * 4 + 0] = -INFINITY; ml[tid * 4 + 1] = 0.f; }
+          }
+          if (t0 <= sp.pos && sp.pos < t0 + PD_PAGE) {
+            const int r = sp.pos - t0;
+            const float* kh = a.qkv + (int64_t)(d.n_heads + kvh) * HD;
+            const float* vh = a.qkv + (int64_t)(d.n_heads + d.n_kv + kvh) * HD;
+            const int64_t off = (((int64_t)a.block_table[pg] * d.n_kv + kvh) * PD_PAGE + r) * HD;
+            for (int dd = tid; dd < HD; dd += PD_THREADS) {
+              const int j0 = dd < H2 ? dd : dd - H2;
+              const float x0 = __ldcg(kh + j0), x1 = __ldcg(kh + j0 + H2), c = cs[j0], sv = sn[j0];
+              const __half kq = __float2half_rn(dd < H2 ? x0 * c - x1 * sv : x1 * c + x0 * sv);
+              const __half vq = __float2half_rn(__ldcg(vh + dd));
+              Ks[r * HD + dd] = kq;
+              Vs[r * HD + dd] = vq;
+              P.kv.k_pages[off + dd] = kq;
+              P.kv.v_pages[off + dd] = vq;
+            }
+          }
+          for (int i = tid; i < (PD_PAGE - n) * (HD / 8); i += PD_THREADS)  // V rows past the context: 0
+            reinterpret_cast<uint4*>(Vs + n * HD)[i] = make_uint4(0u, 0u, 0u, 0u);
+          __syncthreads();
+          if (warp < PD_PAGE / 8) {  // S = Q K^T on the tensor cores: warp w scores positions [8w, 8w+8)
+            float c4[4] = {0.f, 0.f, 0.f, 0.f};
+            const uint32_t* q32 = reinterpret_cast<const uint32_t*>(q_h + g * (HD + 8));
+            const uint32_t* k32 = reinterpret_cast<const uint32_t*>(Ks + (warp * 8 + g) * HD);
+#pragma unroll
+            for (int ks = 0; ks < HD / 16; ++ks)
+              mma16816(c4, q32[ks * 8 + tq], 0u, q32[ks * 8 + 4 + tq], 0u, k32[ks * 8 + tq], k32[ks * 8 + 4 + tq]);
+            if (g < GQ) *reinterpret_cast<float2*>(sc + g * PD_PAGE + warp * 8 + 2 * tq) = make_float2(c4[0], c4[1]);
+          }
+          __syncthreads();
+          if (warp < GQ) {  // online softmax, one warp per query head
+            const int j = warp;
+            const float v0 = lane < n ? sc[j * PD_PAGE + lane] : -INFINITY;
+            const float v1 = lane + 32 < n ? sc[j * PD_PAGE + lane + 32] : -INFINITY;
+            const float m_old = ml[j * 4 + 0];
+            const float m_new = fmaxf(m_old, warp_max(fmaxf(v0, v1)));
+            const float e0 = lane < n ? __expf(v0 - m_new) : 0.f;
+            const float e1 = lane + 32 < n ? __expf(v1 - m_new) : 0.f;
+            const float sum = warp_sum(e0 + e1);
+            const float alpha = m_old == -INFINITY ? 0.f : __expf(m_old - m_new);
+            sc[j * PD_PAGE + lane] = e0;
+            sc[j * PD_PAGE + lane + 32] = e1;
+            __syncwarp();
+            if (lane == 0) { ml[j * 4 + 0] = m_new; ml[j * 4 + 1] = ml[j * 4 + 1] * alpha + sum; ml[j * 4 + 2] = alpha; }
+          }
+          __syncthreads();
+          if (warp < HD / 8) {  // O = alpha O + P V on the tensor cores (P in fp16, rows >= GQ zero)
+            const bool row = g < GQ;
+            const float al = row ? ml[g * 4 + 2] : 0.f;
+            oc[0] *= al; oc[1] *= al;
+            const float* pr = sc + (row ? g : 0) * PD_PAGE;
+            const __half* vc = Vs + warp * 8 + g;
+#pragma unroll
+            for (int ks = 0; ks < PD_PAGE / 16; ++ks) {
+              const int k0 = ks * 16 + 2 * tq;
+              const float2 p0 = *reinterpret_cast<const float2*>(pr + k0);
+              const float2 p1 = *reinterpret_cast<const float2*>(pr + k0 + 8);
+              const uint32_t a0 = row ? h2u(__floats2half2_rn(p0.x, p0.y)) : 0u;
+              const uint32_t a2 = row ? h2u(__floats2half2_rn(p1.x, p1.y)) : 0u;
+              const uint32_t b0 = h2u(__halves2half2(vc[k0 * HD], vc[(k0 + 1) * HD]));
+              const uint32_t b1 = h2u(__halves2half2(vc[(k0 + 8) * HD], vc[(k0 + 9) * HD]));
+              mma16816(oc, a0, 0u, a2, 0u, b0, b1);
+            }
+          }
+          __syncthreads();
+        }
+        // the page buffer is free: start copying this CTA's page of the next layer
+        if (tid == 0) {
+          const int nph = next_attn(ph + 1);
+          if (nph < a.n_phases) kv_issue(nph, pg0);
+        }
+        // this split's partial: o [GQ][HD] and (m, l) per query head
+        const int item = kvh * sp.ns + split;
+        float* part_o = a.attn_part + (size_t)item * GQ * HD;
+        float* part_ml = a.attn_part + (size_t)d.n_kv * a.max_split * GQ * HD + (size_t)item * GQ * 2;
+        if (warp < HD / 8 && g < GQ) *reinterpret_cast<float2*>(part_o + g * HD + warp * 8 + 2 * tq) = make_float2(oc[0], oc[1]);
+        if (tid < GQ) *reinterpret_cast<float2*>(part_ml + tid * 2) = make_float2(ml[tid * 4 + 0], ml[tid * 4 + 1]);
+        // wait for every split of this KV head (co-resident CTAs, bounded wait)
+        __syncthreads();
+        if (tid == 0) {
+          asm volatile("red.release.gpu.global.add.s32 [%0], 1;" :: "l"(a.attn_cnt + kvh) : "memory");
+          const int target = sp.ns * (attn_idx + 1);
+          int okw = 1;
+          if (ld_acquire(a.attn_cnt + kvh) < target) {
+            const uint64_t tw = gtimer();
+            while (ld_acquire(a.attn_cnt + kvh) < target) {
+              if (ld_relaxed(&a.sync[2])) { okw = 0; break; }
+              if (gtimer() - tw > PD_WAIT_NS) { atomicExch(&a.sync[2], 1); atomicExch(a.err, DEV_ERR_TIMEOUT); okw = 0; break; }
+            }
+          }
+          flag[1] = okw;
+        }
+        __syncthreads();
+        if (flag[1]) {
+          // this split merges outputs [o_lo, o_hi) of its head group (GQ*HD values): one batch of loads
+          const int no = GQ * HD, o_lo = split * no / sp.ns, o_hi = (split + 1) * no / sp.ns;
+          const int nout = o_hi - o_lo, j_lo = o_lo / HD, nj = (o_hi - 1) / HD - j_lo + 1;
+          float* mv = ml + PD_MAXG * 4;                 // [nj][ns] (nj*ns <= GQ + 2 ns): m, then weight
+          float* lv = mv + 4 * PD_MAXSPLIT;             // [nj][ns]
+          float* ov = lv + 4 * PD_MAXSPLIT;             // [nout][ns] (<= GQ*HD + ns)
+          const float* base_o = a.attn_part + (size_t)kvh * sp.ns * GQ * HD;
+          const float* base_ml = a.attn_part + (size_t)d.n_kv * a.max_split * GQ * HD + (size_t)kvh * sp.ns * GQ * 2;
+          for (int i = tid; i < nj * sp.ns; i += PD_THREADS) {
+            const int jj = i / sp.ns, s2 = i - jj * sp.ns;
+            const float2 v = __ldcg(reinterpret_cast<const float2*>(base_ml + ((size_t)s2 * GQ + j_lo + jj) * 2));
+            mv[i] = v.x; lv[i] = v.y;
+          }
+          for (int i = tid; i < nout * sp.ns; i += PD_THREADS) {
+            const int oo = i / sp.ns, s2 = i - oo * sp.ns, o = o_lo + oo;
+            ov[i] = __ldcg(base_o + (size_t)s2 * GQ * HD + o);
+          }
+          __syncthreads();
+          if (tid < nj) {
+            float M = -INFINITY;
+            for (int s2 = 0; s2 < sp.ns; ++s2) M = fmaxf(M, mv[tid * sp.ns + s2]);
+            float den = 0.f;
+            for (int s2 = 0; s2 < sp.ns; ++s2) {
+              const float m = mv[tid * sp.ns + s2];
+              const float w = m == -INFINITY ? 0.f : __expf(m - M);
+              mv[tid * sp.ns + s2] = w;
+              den = fmaf(w, lv[tid * sp.ns + s2], den);
+            }
+            ml[tid * 4 + 3] = den;
+          }
+          __syncthreads();
+          for (int oo = tid; oo < nout; oo += PD_THREADS) {
+            const int o = o_lo + oo, jj = o / HD - j_lo;
+            float num = 0.f;
+            for (int s2 = 0; s2 < sp.ns; ++s2) num = fmaf(mv[jj * sp.ns + s2], ov[oo * sp.ns + s2], num);
+            a.attn_out[(int64_t)kvh * no + o] = num / (ml[jj * 4 + 3] + 1e-9f);
+          }
+        }
+      }
+      ++attn_idx;
+      continue;
+    }
+
+    // ============================== GEMV ==============================
+    const int K = P.cols, G = P.G;
+    const int T = (P.rows + 15) >> 4;
+    const int t0 = pd_rng(0, T, cta, NC), t1 = pd_rng(0, T, cta + 1, NC);
+    const int c0 = t0 * G, c1 = t1 * G;
+    const bool has_add = P.epi == PD_EPI_RESID || P.bias;
+    uint4* xf = reinterpret_cast<uint4*>(work);                     // [ks_n/2][4 tq] x 2 k-steps
+    float* sx = reinterpret_cast<float*>(work + (size_t)K * 2);     // [G] (+8 pad)
+    {
+      // one batch of loads: x (and norm weights), this CTA's residual / bias rows
+      if (has_add) {
+        const int r0 = t0 * 16, r1 = min(t1 * 16, P.rows);
+        for (int r = r0 + tid; r < r1; r += PD_THREADS)
+          addv[r - r0] = (P.epi == PD_EPI_RESID ? __ldcg(P.y + r) : 0.f) + (P.bias ? P.bias[r] : 0.f);
+      }
+      // x -> (RMS-normalised) fp16 B fragments and per-group sums of the fp16 x
+      const int items = K >> 2;  // (k-step, tq) items of 4 values: k, k+1, k+8, k+9
+      uint2* xf2 = reinterpret_cast<uint2*>(xf);
+      auto put = [&](int i, float v0, float v1, float v2, float v3) {
+        const int s = i >> 2, tqi = i & 3;
+        xf2[(((s >> 1) * 4 + tqi) << 1) + (s & 1)] =
+            make_uint2(h2u(__floats2half2_rn(v0, v1)), h2u(__floats2half2_rn(v2, v3)));
+      };
+      if (P.norm_w) {  // K <= PD_KNORM: the row stays in registers across the reduction
+        float xv[PD_NREG][4];
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < PD_NREG; ++j) {
+          const int i = tid + j * PD_THREADS;
+          if (i < items) {
+            const int k = (i >> 2) * 16 + 2 * (i & 3);
+            const float2 v0 = __ldcg(reinterpret_cast<const float2*>(P.x + k));
+            const float2 v1 = __ldcg(reinterpret_cast<const float2*>(P.x + k + 8));
+            xv[j][0] = v0.x; xv[j][1] = v0.y; xv[j][2] = v1.x; xv[j][3] = v1.y;
+            ss += v0.x * v0.x + v0.y * v0.y + v1.x * v1.x + v1.y * v1.y;
+          }
+        }
+        const float inv = rsqrtf(block_sum(ss, red) / K + a.eps);
+#pragma unroll
+        for (int j = 0; j < PD_NREG; ++j) {
+          const int i = tid + j * PD_THREADS;
+          if (i < items) {  // norm weights were prefetched into L1 before the barrier
+            const int k = (i >> 2) * 16 + 2 * (i & 3);
+            const float2 n0 = *reinterpret_cast<const float2*>(P.norm_w + k);
+            const float2 n1 = *reinterpret_cast<const float2*>(P.norm_w + k + 8);
+            put(i, xv[j][0] * inv * n0.x, xv[j][1] * inv * n0.y, xv[j][2] * inv * n1.x, xv[j][3] * inv * n1.y);
+          }
+        }
+      } else {
+#pragma unroll 4
+        for (int i = tid; i < items; i += PD_THREADS) {
+          const int k = (i >> 2) * 16 + 2 * (i & 3);
+          const float2 v0 = __ldcg(reinterpret_cast<const float2*>(P.x + k));
+          const float2 v1 = __ldcg(reinterpret_cast<const float2*>(P.x + k + 8));
+          put(i, v0.x, v0.y, v1.x, v1.y);
+        }
+      }
+      __syncthreads();
+      for (int grp = tid; grp < G; grp += PD_THREADS) {
+        const uint4* src = xf + (size_t)grp * (KPG >> 1) * 4;
+        float v = 0.f;
+#pragma unroll 4
+        for (int e = 0; e < KPG * 2; ++e) {
+          const uint4 u = src[e];
+          const float2 f0 = __half22float2(u2h(u.x)), f1 = __half22float2(u2h(u.y));
+          const float2 f2 = __half22float2(u2h(u.z)), f3 = __half22float2(u2h(u.w));
+          v += ((f0.x + f0.y) + (f1.x + f1.y)) + ((f2.x + f2.y) + (f3.x + f3.y));
+        }
+        sx[grp] = v;
+      }
+      __syncthreads();
+    }
+
+    // epilogue of the 16 rows of tile t (all 32 lanes; lane r < 16 holds row t*16 + r)
+    auto tile_out = [&](int t, float v) {
+      const int row = t * 16 + lane;
+      const bool in = lane < 16 && row < P.rows;
+      if (in && has_add) v += addv[row - t0 * 16];
+      if (P.epi == PD_EPI_SWIGLU) {
+        const float up = __shfl_down_sync(0xffffffffu, v, 1);
+        if (in && !(lane & 1)) P.y[row >> 1] = (v / (1.0f + expf(-v))) * up;
+      } else if (in) {
+        P.y[row] = v;
+      }
+    };
+
+    const int w0 = pd_rng(c0, c1, warp, PD_WARPS), w1 = pd_rng(c0, c1, warp + 1, PD_WARPS);
+    float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
+    int t = w0 / G, gi = w0 - t * G;  // current row tile, group within it
+    for (int u = w0; u < w1 && !wfail;) {
+      const int n = min(min(GPC, w1 - u), G - gi);
+      const int slot = consumed % PD_RING;
+      int okl = 0;
+      if (lane == 0) okl = wait_bar(&wb[slot], (uint32_t)((consumed / PD_RING) & 1));
+      if (!__shfl_sync(0xffffffffu, okl, 0)) {
+        if (lane == 0) { atomicExch(&a.sync[2], 1); atomicExch(a.err, DEV_ERR_TIMEOUT); }
+        wfail = true;
+        break;
+      }
+      const uint8_t* buf = ring + (size_t)slot * a.ring_stride;
+      const uint4* xb[1] = {xf + gi * KPG * 2 + tq};
+      const float* sxg = sx + gi;
+      if (n == GPC) {
+        mma_chunk<KPG, 1, GPC, true, 1>(buf, lane, xb, sxg, acc);
+      } else {
+        for (int gr = 0; gr < n; ++gr) {
+          const uint4* xg[1] = {xb[0] + gr * KPG * 2};
+          mma_chunk<KPG, 1, 1, true, 1>(buf + gr * GB, lane, xg, sxg + gr, acc);
+        }
+      }
+      ++consumed;
+      __syncwarp();
+      if (lane == 0) issue_next(slot);
+      u += n;
+      gi += n;
+      if (u < w1 && gi < G) continue;
+      // ---- this warp's part of row tile tt is complete ----
+      const int tt = t;
+      if (gi == G) { gi = 0; ++t; }
+      const int tu0 = tt * G, tu1 = tu0 + G;
+      const int side = (tt == w0 / G) ? 0 : 1;
+      float* mine = wpart + (warp * 2 + side) * 16;
+      if (tq == 0) { mine[g] = acc[0][0]; mine[g + 8] = acc[0][2]; }
+      acc[0][0] = acc[0][1] = acc[0][2] = acc[0][3] = 0.f;
+      __syncwarp();
+      if (w0 <= tu0 && tu1 <= w1) {  // the warp owns the whole tile
+        tile_out(tt, lane < 16 ? mine[lane] : 0.f);
+        __syncwarp();
+        continue;
+      }
+      // shared with other warps of the CTA: the last contributor sums them in warp order
+      const int wa = pd_owner(tu0, c0, c1, PD_WARPS), wz = pd_owner(tu1 - 1, c0, c1, PD_WARPS);
+      int contrib = 0;
+      for (int w = wa; w <= wz; ++w) contrib += pd_rng(c0, c1, w, PD_WARPS) < pd_rng(c0, c1, w + 1, PD_WARPS);
+      __threadfence_block();
+      int last = 0;
+      if (lane == 0) last = atomicAdd(&wcnt[wa], 1) == contrib - 1;
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (!last) continue;
+      if (lane == 0) wcnt[wa] = 0;
+      __threadfence_block();
+      float v = 0.f;
+      if (lane < 16)
+        for (int w = wa; w <= wz; ++w) {
+          const int ws0 = pd_rng(c0, c1, w, PD_WARPS);
+          if (ws0 == pd_rng(c0, c1, w + 1, PD_WARPS)) continue;
+          const int sd = (tt == ws0 / G) ? 0 : 1;
+          v += *reinterpret_cast<volatile float*>(wpart + (w * 2 + sd) * 16 + lane);
+        }
+      tile_out(tt, v);
+    }
+  }
+
+  // copies still in flight (abort path) are waited for, bounded, before exit
+  if (lane == 0)
+    for (int q = consumed; q < issued; ++q) wait_bar(&wb[q % PD_RING], (uint32_t)((q / PD_RING) & 1));
+  if (tid == 0)
+    for (; kv_waited < kv_uses; ++kv_waited) wait_bar(kvbar, (uint32_t)(kv_waited & 1));
+  __syncthreads();
+  if (tid == 0) {  // the last CTA out resets the counters for the next launch
+    __threadfence();
+    if (atomicAdd(&a.sync[1], 1) == NC - 1) {
+      for (int h = 0; h < d.n_kv; ++h) a.attn_cnt[h] = 0;
+      a.sync[0] = 0;
+      a.sync[2] = 0;
+      __threadfence();
+      a.sync[1] = 0;
+    }
+  }
+}
+
+template <int KPG, int HD>
+static int persist_setup(const PdPlan& plan, bool launch, cudaStream_t st, int* max_blocks) {
+  auto kern = persist_decode_kernel<KPG, HD>;
+  static bool configured = false;
+  if (!configured) {
+    N730_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+    configured = true;
+  }
+  if (max_blocks) N730_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(max_blocks, kern, PD_THREADS, plan.smem));
+  if (!launch) return N730_OK;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(plan.grid);
+  cfg.blockDim = dim3(PD_THREADS);
+  cfg.dynamicSmemBytes = plan.smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  N730_CUDA(cudaLaunchKernelEx(&cfg, kern, plan.a));
+  return N730_OK;
+}
+
+static int persist_dispatch(const PdPlan& plan, int head_dim, bool launch, cudaStream_t st, int* max_blocks) {
+  const int kpg = plan.a.kpg;
+  if (head_dim == 128) {
+    if (kpg == 8) return persist_setup<8, 128>(plan, launch, st, max_blocks);
+    if (kpg == 4) return persist_setup<4, 128>(plan, launch, st, max_blocks);
+    return persist_setup<16, 128>(plan, launch, st, max_blocks);
+  }
+  if (kpg == 8) return persist_setup<8, 64>(plan, launch, st, max_blocks);
+  if (kpg == 4) return persist_setup<4, 64>(plan, launch, st, max_blocks);
+  return persist_setup<16, 64>(plan, launch, st, max_blocks);
+}
+
+int persist_plan(const PdPhase* ph, int n, int head_dim, int group_q, int page_size, PdPlan* plan) {
+  auto round = [](size_t v) { return (v + 127) / 128 * 128; };
+  if (!(head_dim == 64 || head_dim == 128) || group_q < 1 || group_q > PD_MAXG || page_size != PD_PAGE)
+    return N730_UNSUPPORTED;
+  int dev = 0, sms = 0, coop = 0, maxb = 0;
+  N730_CUDA(cudaGetDevice(&dev));
+  N730_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  N730_CUDA(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev));
+  if (!coop) return N730_UNSUPPORTED;
+  int kpg = 0, kmax = 0, gmax = 0;
+  for (int i = 0; i < n; ++i) {
+    if (ph[i].kind != PD_GEMV) continue;
+    const int k = ph[i].cols / ph[i].G / 16;
+    if (ph[i].cols % 64 || (ph[i].norm_w && ph[i].cols > PD_KNORM) || (kpg && k != kpg) ||
+        !(k == 4 || k == 8 || k == 16))
+      return N730_UNSUPPORTED;
+    if (ph[i].epi == PD_EPI_SWIGLU && ph[i].rows % 2) return N730_UNSUPPORTED;
+    const int tiles_per_cta = ((ph[i].rows + 15) / 16 + sms - 1) / sms;
+    if ((ph[i].epi == PD_EPI_RESID || ph[i].bias) && tiles_per_cta * 16 > PD_ADDMAX) return N730_UNSUPPORTED;
+    kpg = k;
+    kmax = std::max(kmax, ph[i].cols);
+    gmax = std::max(gmax, ph[i].G);
+  }
+  if (!kpg) return N730_UNSUPPORTED;
+  PdArgs& a = plan->a;
+  a.kpg = kpg;
+  const int gb = kpg * 128 + 64;
+  a.ring_stride = (int)round((size_t)pd_gpc(kpg) * gb);
+  size_t off = round((size_t)(PD_WARPS * PD_RING + 1) * 8);
+  a.ring_off = (int)off;
+  off += (size_t)PD_WARPS * PD_RING * a.ring_stride;
+  a.work_off = (int)round(off);
+  const size_t gemv_work = round((size_t)kmax * 2) + (size_t)(gmax + 8) * 4;
+  const size_t attn_work = ((size_t)PD_MAXG * head_dim + PD_MAXG * PD_PAGE + PD_MAXG * 4 + 8 * PD_MAXSPLIT +
+                            (size_t)PD_MAXG * head_dim + PD_MAXSPLIT) * 4;
+  off = a.work_off + round(std::max(gemv_work, attn_work));
+  a.kv_off = (int)off;
+  off += round((size_t)2 * PD_PAGE * head_dim * 2);
+  a.add_off = (int)off;
+  off += round((size_t)PD_ADDMAX * 4);
+  a.wpart_off = (int)off;
+  off += round((size_t)PD_WARPS * 2 * 16 * 4);
+  a.misc_off = (int)off;
+  off += 64 * 4;
+  plan->smem = round(off);
+  if (plan->smem > 227 * 1024) return N730_UNSUPPORTED;
+  a.d.head_dim = head_dim;
+  if (int rc = persist_dispatch(*plan, head_dim, false, nullptr, &maxb)) return rc;
+  if (maxb < 1) return N730_UNSUPPORTED;
+  plan->grid = sms;
+  return N730_OK;
+}
+
+int persist_launch(const PdPlan& plan, cudaStream_t st) {
+  return persist_dispatch(plan, plan.a.d.head_dim, true, st, nullptr);
+}
+
+}  // namespace n730

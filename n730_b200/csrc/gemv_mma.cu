@@ -26,6 +26,7 @@
 #include <algorithm>
 #include <cstdlib>
 
+#include "mma_gemv.cuh"
 #include "qweight.h"
 
 namespace n730 {
@@ -117,17 +118,6 @@ int qweight_to_mma_layout(QWeight& w, cudaStream_t st) {
 // ---------------------------------------------------------------------------
 // kernel
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
-__device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
-
-__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                         uint32_t b0, uint32_t b1) {
-  asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-               "{%0,%1,%2,%3};"
-               : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-               : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
 struct MmaParams {
   const uint8_t* blob;     // [tiles][G] x (codes kpg*128 B, sz 64 B)
   int rows, cols, ks_n, G;
@@ -144,81 +134,8 @@ struct MmaParams {
   int* err;
 };
 
-__device__ __forceinline__ uint64_t gtimer() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = gtimer();
-  while (!mbar_try_wait(bar, parity))
-    if (gtimer() - t0 > 2000000000ull) return false;
-  return true;
-}
-
 constexpr int MG2_RING = 3;   // chunks in flight per warp (fewer when shared memory is short)
 constexpr int MG2_CHUNK = 32; // k-steps per chunk: a whole number of groups, ~4.3 KB with their scales
-
-// Groups [0, NG) of one chunk in shared memory: straight-line code, so the NG
-// groups' accumulator chains interleave.  xb[nn] points at the chunk's first
-// k-step pair of x fragments (n-tile nn); sxg at the chunk's first group of Sx.
-template <int KPG, int NT, int NG>
-__device__ __forceinline__ void mma_chunk(const uint8_t* buf, int lane, const uint4* const (&xb)[NT],
-                                          const float* sxg, float (&acc)[NT][4]) {
-  constexpr int GB = KPG * 128 + 64;
-  constexpr uint32_t MAGIC = 0x64006400u;
-  const int g = lane >> 2, tq = lane & 3;
-#pragma unroll
-  for (int gr = 0; gr < NG; ++gr) {
-    const uint32_t* cw = reinterpret_cast<const uint32_t*>(buf + gr * GB) + lane * 4;
-    // two accumulator chains (even / odd k-steps) per n-tile
-    float ca[NT][4], cb[NT][4];
-#pragma unroll
-    for (int nn = 0; nn < NT; ++nn)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) ca[nn][e] = cb[nn][e] = 0.f;
-#pragma unroll
-    for (int kk = 0; kk < KPG; kk += 4) {
-      const int kl = gr * KPG + kk;  // k-step within the chunk
-      const uint4 w4 = *reinterpret_cast<const uint4*>(cw + (kk >> 2) * 128);
-      const uint32_t wv[4] = {w4.x, w4.y, w4.z, w4.w};
-      uint4 bx[NT][2];
-#pragma unroll
-      for (int nn = 0; nn < NT; ++nn) {
-        bx[nn][0] = xb[nn][(kl >> 1) * 4];
-        bx[nn][1] = xb[nn][((kl >> 1) + 1) * 4];
-      }
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint32_t w = wv[j], ws = w >> 8;
-        const uint32_t a0 = lop3_and_or(w, 0x000F000Fu, MAGIC);   // rows g,   k 2tq..+1:  1024 + q
-        const uint32_t a1 = lop3_and_or(w, 0x00F000F0u, MAGIC);   // rows g+8, k 2tq..+1:  1024 + 16 q
-        const uint32_t a2 = lop3_and_or(ws, 0x000F000Fu, MAGIC);  // rows g,   k 2tq+8..+9
-        const uint32_t a3 = lop3_and_or(ws, 0x00F000F0u, MAGIC);  // rows g+8, k 2tq+8..+9
-#pragma unroll
-        for (int nn = 0; nn < NT; ++nn) {
-          const uint4 v = bx[nn][j >> 1];
-          if (j & 1) mma16816(cb[nn], a0, a1, a2, a3, v.z, v.w);
-          else       mma16816(ca[nn], a0, a1, a2, a3, v.x, v.y);
-        }
-      }
-    }
-    // group epilogue: y += s C - s (1024 + z) Sx ; rows g+8: (s/16) C - s (64 + z) Sx
-    const uint2 szv = *reinterpret_cast<const uint2*>(buf + gr * GB + KPG * 128 + g * 8);
-    const float2 sf = __half22float2(u2h(szv.x)), zf = __half22float2(u2h(szv.y));
-    const float m0 = sf.x, m1 = sf.y * 0.0625f;
-    const float o0 = -sf.x * (1024.f + zf.x), o1 = -sf.y * (64.f + zf.y);
-#pragma unroll
-    for (int nn = 0; nn < NT; ++nn) {
-      const float2 xs = *reinterpret_cast<const float2*>(sxg + gr * (NT * 8) + nn * 8 + 2 * tq);
-      acc[nn][0] = fmaf(m0, ca[nn][0] + cb[nn][0], fmaf(o0, xs.x, acc[nn][0]));
-      acc[nn][1] = fmaf(m0, ca[nn][1] + cb[nn][1], fmaf(o0, xs.y, acc[nn][1]));
-      acc[nn][2] = fmaf(m1, ca[nn][2] + cb[nn][2], fmaf(o1, xs.x, acc[nn][2]));
-      acc[nn][3] = fmaf(m1, ca[nn][3] + cb[nn][3], fmaf(o1, xs.y, acc[nn][3]));
-    }
-  }
-}
 
 // Work of one warp: units u = warp, warp+WARPS, ... of the CTA; unit -> (row
 // tile, K-part).  Each warp streams its units' chunks through its own bulk-copy

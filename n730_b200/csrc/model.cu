@@ -19,6 +19,7 @@
 #include <vector>
 
 #include "attention.h"
+#include "decode_persist.h"
 #include "n730_cuda.h"
 #include "qweight.h"
 
@@ -76,6 +77,9 @@ struct Model {
   cudaStream_t st = nullptr;
   std::map<int, cudaGraphExec_t> graphs;
   int device = 0;
+  // persistent batch-1 decode (decode_persist.cu)
+  bool pd_ok = false;
+  PdPlan pd;
 
   template <typename T>
   int alloc(T** p, size_t n) {
@@ -111,6 +115,63 @@ static int fuse_rows(Model* m, std::vector<QWeight*> parts, bool interleave, QWe
     r0 += parts[i]->rows;
   }
   *out = f;
+  return N730_OK;
+}
+
+static AttnDims dims(const Model* m);
+
+// Phase table + scratch for the persistent batch-1 decode kernel.  Leaves
+// pd_ok false (per-op kernels) when a weight is not in fragment tiles, groups
+// differ, or the shapes exceed the kernel's limits.
+static int plan_persistent(Model* m) {
+  const N730ModelConfig& c = m->c;
+  auto tiled = [](const QWeight* w) { return w && w->layout == 1; };
+  for (auto& y : m->L)
+    if (!tiled(y.qkv) || !tiled(y.o) || !tiled(y.gate_up) || !tiled(y.down)) return N730_OK;
+  if (!tiled(m->lm_head)) return N730_OK;
+  std::vector<PdPhase> ph;
+  auto gemv_phase = [&](const QWeight* w, const float* x, const float* norm, const float* bias, float* y, int epi) {
+    PdPhase p = {};
+    p.kind = PD_GEMV; p.epi = epi; p.blob = w->codes; p.rows = w->rows; p.cols = w->cols; p.G = w->n_groups;
+    p.x = x; p.norm_w = norm; p.bias = bias; p.y = y;
+    ph.push_back(p);
+  };
+  for (auto& y : m->L) {
+    gemv_phase(y.qkv, m->x, y.ln1, y.qkv_bias, m->qkv, PD_EPI_STORE);
+    PdPhase at = {};
+    at.kind = PD_ATTN; at.kv = y.kv;
+    ph.push_back(at);
+    gemv_phase(y.o, m->attn, nullptr, y.o_bias, m->x, PD_EPI_RESID);
+    gemv_phase(y.gate_up, m->x, y.ln2, y.gate_up_bias, m->mlp, PD_EPI_SWIGLU);
+    gemv_phase(y.down, m->mlp, nullptr, y.down_bias, m->x, PD_EPI_RESID);
+  }
+  gemv_phase(m->lm_head, m->x, m->final_norm, nullptr, m->logits, PD_EPI_STORE);
+  PdPlan plan;
+  const int rc = persist_plan(ph.data(), (int)ph.size(), c.head_dim, c.heads / c.kv_heads, c.page_size, &plan);
+  if (rc == N730_UNSUPPORTED) return N730_OK;
+  if (rc) return rc;
+  const int GQ = c.heads / c.kv_heads;
+  const int max_split = std::min(64, plan.grid / c.kv_heads);
+  if (max_split < 1) return N730_OK;
+  PdArgs& a = plan.a;
+  PdPhase* d_ph = nullptr;
+  if (int r = m->alloc(&d_ph, ph.size())) return r;
+  N730_CUDA(cudaMemcpyAsync(d_ph, ph.data(), ph.size() * sizeof(PdPhase), cudaMemcpyHostToDevice, m->st));
+  a.phases = d_ph;
+  a.n_phases = (int)ph.size();
+  a.eps = c.rms_eps;
+  a.qkv = m->qkv; a.attn_out = m->attn; a.cos_t = m->cos_t; a.sin_t = m->sin_t;
+  a.seq_lens = m->seq_lens; a.block_table = m->block_table; a.d = dims(m);
+  a.max_split = max_split;
+  if (int r = m->alloc(&a.attn_part, (size_t)c.kv_heads * max_split * GQ * (c.head_dim + 2))) return r;
+  if (int r = m->alloc(&a.attn_cnt, (size_t)c.kv_heads)) return r;
+  if (int r = m->alloc(&a.sync, 4)) return r;
+  N730_CUDA(cudaMemsetAsync(a.attn_cnt, 0, c.kv_heads * 4, m->st));
+  N730_CUDA(cudaMemsetAsync(a.sync, 0, 16, m->st));
+  a.err = gemv_err_word();
+  N730_REQUIRE(a.err, N730_OOM, "model: error word allocation failed");
+  m->pd = plan;
+  m->pd_ok = true;
   return N730_OK;
 }
 
@@ -226,6 +287,8 @@ static int finalize(Model* m) {
   const size_t per_layer = pages * c.kv_heads * c.page_size * c.head_dim;
   if (int rc = m->alloc(&m->k_pool, per_layer * nl)) return rc;
   if (int rc = m->alloc(&m->v_pool, per_layer * nl)) return rc;
+  N730_CUDA(cudaMemsetAsync(m->k_pool, 0, per_layer * nl * sizeof(__half), m->st));
+  N730_CUDA(cudaMemsetAsync(m->v_pool, 0, per_layer * nl * sizeof(__half), m->st));
   for (int l = 0; l < nl; ++l) m->L[l].kv = KVLayer{m->k_pool + per_layer * l, m->v_pool + per_layer * l};
   {
     std::vector<int> bt(pages);
@@ -254,6 +317,8 @@ static int finalize(Model* m) {
   if (int rc = m->alloc(&m->pmlp, (size_t)P * c.ffn)) return rc;
   N730_CUDA(cudaMallocHost(&m->h_tok, (size_t)std::max(B, P) * 4));
   N730_CUDA(cudaMallocHost(&m->h_logits, (size_t)B * c.vocab * 4));
+  if (!c.per_op_decode)
+    if (int rc = plan_persistent(m)) return rc;
   N730_CUDA(cudaStreamSynchronize(m->st));
   m->finalized = true;
   return N730_OK;
@@ -269,7 +334,7 @@ static int gemv(Model* m, const QWeight* w, const float* x, int ldx, int batch, 
 }
 
 static AttnDims dims(const Model* m) {
-  AttnDims d;
+  AttnDims d{};
   d.n_heads = m->c.heads; d.n_kv = m->c.kv_heads; d.head_dim = m->c.head_dim;
   d.page_size = m->c.page_size; d.max_pages = m->max_pages;
   d.scale = 1.0f / sqrtf((float)m->c.head_dim);
@@ -281,7 +346,10 @@ static int enqueue_decode(Model* m, int B) {
   const N730ModelConfig& c = m->c;
   const int h = c.hidden, ad = c.heads * c.head_dim;
   if (int rc = embed_launch(*m->embed, m->d_tokens, B, m->x, m->st)) return rc;
-  for (int l = 0; l < c.layers; ++l) {
+  const bool persistent = B == 1 && m->pd_ok;
+  if (persistent)
+    if (int rc = persist_launch(m->pd, m->st)) return rc;
+  for (int l = 0; l < c.layers && !persistent; ++l) {
     Layer& y = m->L[l];
     if (int rc = gemv(m, y.qkv, m->x, h, B, m->qkv, m->qkv_dim, y.qkv_bias, nullptr, 0, y.ln1, 0)) return rc;
     DecodeAttnArgs a = {};
@@ -293,7 +361,9 @@ static int enqueue_decode(Model* m, int B) {
     if (int rc = gemv(m, y.gate_up, m->x, h, B, m->mlp, c.ffn, y.gate_up_bias, nullptr, 0, y.ln2, 1)) return rc;
     if (int rc = gemv(m, y.down, m->mlp, c.ffn, B, m->x, h, y.down_bias, m->x, h, nullptr, 0)) return rc;
   }
-  if (int rc = gemv(m, m->lm_head, m->x, h, B, m->logits, c.vocab, nullptr, nullptr, 0, m->final_norm, 0)) return rc;
+  if (!persistent)
+    if (int rc = gemv(m, m->lm_head, m->x, h, B, m->logits, c.vocab, nullptr, nullptr, 0, m->final_norm, 0))
+      return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((B + 127) / 128);
   cfg.blockDim = dim3(128);
@@ -569,6 +639,7 @@ N730_API int n730_model_info(void* p, int64_t* info) {
   info[4] = m->qkv_dim;
   info[5] = m->max_pages;
   info[6] = m->finalized;
+  info[7] = m->pd_ok;
   return N730_OK;
 }
 

@@ -31,7 +31,8 @@ class N730ModelConfig(C.Structure):
     _fields_ = [(n, C.c_int32) for n in ("hidden", "layers", "heads", "kv_heads", "head_dim", "ffn", "vocab")] + \
                [("rms_eps", C.c_float), ("rope_theta", C.c_float)] + \
                [(n, C.c_int32) for n in ("max_ctx", "max_batch", "page_size", "max_prefill", "tie_embeddings",
-                                         "tp_rank", "tp_size", "use_graphs", "use_pdl", "exact_gemv")]
+                                         "tp_rank", "tp_size", "use_graphs", "use_pdl", "exact_gemv",
+                                         "per_op_decode")]
 
 
 def _sigs(lib):
@@ -119,13 +120,13 @@ class Engine:
 
     def __init__(self, shape: ModelShape, max_ctx: int = 4096, max_batch: int = 1, page_size: int = 64,
                  max_prefill: int = 512, use_graphs: bool = True, use_pdl: bool = True,
-                 tp_rank: int = 0, tp_size: int = 1, exact_gemv: bool = False):
+                 tp_rank: int = 0, tp_size: int = 1, exact_gemv: bool = False, per_op_decode: bool = False):
         self.lib = _sigs(_lib.cuda())
         self.shape = shape
         c = N730ModelConfig(shape.hidden, shape.layers, shape.heads, shape.kv_heads, shape.head_dim, shape.ffn,
                             shape.vocab, shape.rms_eps, shape.rope_theta, max_ctx, max_batch, page_size,
                             max_prefill, int(shape.tie_embeddings), tp_rank, tp_size, int(use_graphs),
-                            int(use_pdl), int(exact_gemv))
+                            int(use_pdl), int(exact_gemv), int(per_op_decode))
         self.cfg = c
         self.h = C.c_void_p()
         _lib.check(self.lib.n730_model_create(C.byref(c), C.byref(self.h)), "model_create")
@@ -175,7 +176,7 @@ class Engine:
         a = (C.c_int64 * 16)()
         _lib.check(self.lib.n730_model_info(self.h, a), "model_info")
         return {"weight_bytes": a[0], "kv_bytes_per_pos": a[1], "kv_capacity_bytes": a[2], "n_split": a[3],
-                "qkv_dim": a[4], "pages_per_seq": a[5]}
+                "qkv_dim": a[4], "pages_per_seq": a[5], "persistent_decode": bool(a[7])}
 
     def run_linear(self, layer: int, which: int, d_x: int, batch: int, d_y: int, stream: int = 0):
         _lib.check(self.lib.n730_model_run_linear(self.h, layer, which, C.c_void_p(d_x), batch, C.c_void_p(d_y),

@@ -37,7 +37,8 @@ def _oracle_weights(blocks):
 
 
 @pytest.fixture(scope="module", params=[("tiny", "int4_g128"), ("tiny-gqa7", "mixed_05b"),
-                                        ("tiny-128", "aggressive")])
+                                        ("tiny-128", "aggressive"), ("tiny-gqa7", "int4_g128"),
+                                        ("tiny-128", "int4_g128")])
 def model(request, tmp_path_factory):
     shape_name, pmap = request.param
     shape = synthetic.SHAPES[shape_name]
@@ -102,3 +103,45 @@ def test_capacity_and_reset(model):
     with pytest.raises(RuntimeError):
         e.forward([shape.vocab + 5])
     e.close()
+
+
+def test_persistent_decode_matches_per_op(model):
+    """Batch-1 decode through the persistent kernel (all-INT4 models) and through
+    one kernel per op: both within the bar of the oracle, and close to each other."""
+    shape, blocks, w = model
+    ep = _engine(shape, blocks, max_batch=1)
+    eo = _engine(shape, blocks, max_batch=1, per_op_decode=True)
+    all_int4 = all(b.prec_id == 0x44 for _, b in blocks if b.cols > 1)
+    assert ep.info()["persistent_decode"] == all_int4
+    assert not eo.info()["persistent_decode"]
+    orc = OracleDecoder(shape, w, max_pos=512)
+    rng = np.random.default_rng(21)
+    prompt = rng.integers(0, shape.vocab, 70)
+    yp, yo, yr = ep.forward(prompt), eo.forward(prompt), orc.forward(prompt)
+    assert rel_err(yp, yr) <= TOL and rel_err(yo, yr) <= TOL
+    tok = int(rng.integers(0, shape.vocab))
+    for step in range(10):
+        yp, yo, yr = ep.forward([tok]), eo.forward([tok]), orc.forward([tok])
+        assert rel_err(yp, yr) <= TOL, f"persistent, step {step}"
+        assert rel_err(yp, yo) <= 2e-3, f"persistent vs per-op, step {step}"
+        tok = int(np.argmax(yr))
+    ep.close()
+    eo.close()
+
+
+def test_persistent_decode_deterministic(model):
+    """Re-running decode steps from the same cached state gives bit-identical
+    logits: split tiles and attention splits are merged in a fixed order."""
+    shape, blocks, _ = model
+    e = _engine(shape, blocks, max_batch=1)
+    if not e.info()["persistent_decode"]:
+        e.close()
+        pytest.skip("per-op GEMVs merge K-parts with shared-memory atomics (order not fixed)")
+    e.forward(np.arange(40) % shape.vocab)
+    L = e.seq_len(0)
+    first = [e.forward([t]) for t in (3, 5, 7)]
+    e.set_seq_len(0, L)
+    again = [e.forward([t]) for t in (3, 5, 7)]
+    e.close()
+    for a, b in zip(first, again):
+        assert np.array_equal(a, b)
