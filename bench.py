@@ -15,10 +15,14 @@ decode steps run at context 2048.. with the fp16 paged KV cache.
   L2 (126 MB), so every step streams them from HBM; no L2 flush is needed.
 * ``e2e``: the same through the host C-ABI call ``n730_model_decode`` with host
   token ids in and host fp32 logits out (copies inside the timed region).
-* ``roofline``: the dequant-GEMV kernel timed alone on the model's gate|up
-  weights (rotating over all 28 layers), algorithmic bytes per launch
-  (codes + fp16 scale/zero + x + y) / average launch time, against the
-  measured HBM peak in MEASURED_PEAKS.json.
+* ``roofline``: the dominant kernel, the persistent decode kernel (one
+  cooperative launch runs all 28 layers and the lm_head of a batch-1 step),
+  timed alone with CUDA events on the model's stream; algorithmic bytes per
+  launch = every packed weight it streams (q|k|v, o, gate|up, down per layer
+  and the lm_head: INT4 codes + fp16 scale/zero) + the fp16 K/V it reads
+  (28 layers x 4 KV heads x 128 x 2 x 2 B per cached position), against the
+  measured HBM peak in MEASURED_PEAKS.json.  For batch > 1 (per-op kernels)
+  the gate|up dequant-GEMV is timed alone instead.
 * ``cpu_baseline``: the reference's CPU path for one decoder layer of this
   shape (its own n730core read+dequant, built from its source, plus numpy
   fp32 GEMV), extrapolated to a token; per-tensor INT4 stands in for g128
@@ -30,6 +34,7 @@ N > 1 (torchrun, one rank per GPU): every rank decodes its own batch
 from __future__ import annotations
 
 import argparse
+import dataclasses
 import json
 import os
 import statistics
@@ -50,12 +55,13 @@ METRIC = "decode tok/s at Qwen2-7B-shape INT4; dequant-GEMV HBM GB/s vs ~8 TB/s 
 def _args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--ctx", type=int, default=2048, help="prompt length prefilled before decoding")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=0, help="override the layer count (small profiling cases)")
     return ap.parse_args()
 
 
@@ -68,7 +74,8 @@ def _peaks():
 
 
 class ClockSampler:
-    """nvidia-smi sampling during the timed region (clocks + throttle reasons)."""
+    """nvidia-smi sampling (every 20 ms) of clocks and throttle reasons; only the
+    samples that arrive inside the timed region are summarised."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -77,30 +84,41 @@ class ClockSampler:
     def __init__(self, index: int):
         self.index = index
         self.p = None
+        self.lines = []
+
+    def _read(self):
+        for line in self.p.stdout:
+            self.lines.append((time.time(), line))
 
     def __enter__(self):
+        import threading
         try:
             self.p = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                       "--format=csv,noheader,nounits", "-lms", "20"],
                                       stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.th = threading.Thread(target=self._read, daemon=True)
+            self.th.start()
+            time.sleep(0.3)  # let the sampler start before the timed region
         except Exception:
             self.p = None
+        self.t_start = time.time()
         return self
 
     def __exit__(self, *a):
-        self.out = ""
+        self.t_end = time.time()
         if self.p:
             self.p.terminate()
             try:
-                self.out, _ = self.p.communicate(timeout=5)
+                self.p.wait(timeout=5)
             except Exception:
                 self.p.kill()
+            self.th.join(timeout=2)
 
     def summary(self):
         rows = []
-        for line in (getattr(self, "out", "") or "").splitlines():
+        for t, line in self.lines:
             f = [x.strip() for x in line.split(",")]
-            if len(f) >= 9 and f[1].isdigit():
+            if self.t_start <= t <= self.t_end and len(f) >= 9 and f[1].isdigit():
                 rows.append(f)
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
@@ -235,6 +253,8 @@ def run_ours(a):
     from n730_b200.engine import Engine
     from n730_b200.synthetic import SHAPES, build_on_device
     shape = SHAPES[SHAPE_NAME]
+    if a.layers:
+        shape = dataclasses.replace(shape, layers=a.layers)
     B, ctx = a.batch, a.ctx
     max_ctx = ctx + a.warmup + a.steps + 64
     eng = Engine(shape, max_ctx=max_ctx, max_batch=B, max_prefill=512)
@@ -280,58 +300,81 @@ def run_ours(a):
     e3.record(st)
     barrier()
     t_e2e = e2.elapsed_time(e3) / 1000.0
-    # ---- roofline: the dequant-GEMV alone on the gate|up weights of every layer ----
-    x = torch.randn(B, shape.hidden, device="cuda")
-    y = torch.empty(B, shape.ffn, device="cuda")
-    for l in range(shape.layers):
-        eng.run_linear(l, 2, x.data_ptr(), B, y.data_ptr(), st_ptr)
-    torch.cuda.synchronize()
-    reps = 5
-    e4, e5 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e4.record(st)
-    for _ in range(reps):
+    # ---- roofline: the dominant kernel alone ----
+    persistent = B == 1 and info["persistent_decode"]
+    kv_read = info["kv_bytes_per_pos"] * (eng.seq_len(0) + 1)  # K and V of every layer, cached + new position
+    if persistent:
+        reps = max(3, a.steps // 2)
+        for _ in range(2):
+            eng.run_step_kernel(st_ptr)
+        torch.cuda.synchronize()
+        e4, e5 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e4.record(st)
+        for _ in range(reps):
+            eng.run_step_kernel(st_ptr)
+        e5.record(st)
+        torch.cuda.synchronize()
+        t_kern = e4.elapsed_time(e5) / 1000.0 / reps
+        kern_bytes = info["weight_bytes"] - info["embed_bytes"] + kv_read
+        kern_name = "persist_decode_kernel<8,128> (whole batch-1 step, 148 CTAs x 512 threads)"
+        traffic_file = "decode_persist_7b_traffic.txt"
+    else:
+        x = torch.randn(B, shape.hidden, device="cuda")
+        y = torch.empty(B, shape.ffn, device="cuda")
         for l in range(shape.layers):
             eng.run_linear(l, 2, x.data_ptr(), B, y.data_ptr(), st_ptr)
-    e5.record(st)
-    torch.cuda.synchronize()
-    t_gemv = e4.elapsed_time(e5) / 1000.0 / (reps * shape.layers)
-    gemv_bytes = eng.linear_bytes(0, 2, B)
+        torch.cuda.synchronize()
+        reps = 5
+        e4, e5 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e4.record(st)
+        for _ in range(reps):
+            for l in range(shape.layers):
+                eng.run_linear(l, 2, x.data_ptr(), B, y.data_ptr(), st_ptr)
+        e5.record(st)
+        torch.cuda.synchronize()
+        t_kern = e4.elapsed_time(e5) / 1000.0 / (reps * shape.layers)
+        kern_bytes = eng.linear_bytes(0, 2, B)
+        kern_name = "gemv_mma2_kernel on gate|up 37888x3584 INT4 g128 (+SwiGLU)"
+        traffic_file = "gemv_gateup_traffic.txt"
 
     # max over ranks
     if world > 1:
-        tt = torch.tensor([t_dev, t_e2e, t_gemv], device="cuda", dtype=torch.float64)
+        tt = torch.tensor([t_dev, t_e2e, t_kern], device="cuda", dtype=torch.float64)
         torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
-        t_dev, t_e2e, t_gemv = tt.tolist()
+        t_dev, t_e2e, t_kern = tt.tolist()
     if rank == 0:
         peak, peak_kind = _peaks()
-        achieved = gemv_bytes / t_gemv / 1e9
+        achieved = kern_bytes / t_kern / 1e9
         traffic = None
-        tf = REPO / "profiles" / "gemv_gateup_traffic.json"
-        if tf.exists():
-            traffic = json.loads(tf.read_text()).get("traffic_bytes_per_launch")
+        tf = REPO / "profiles" / traffic_file
+        if tf.exists() and not a.layers:
+            for line in tf.read_text().splitlines():
+                if line.startswith("traffic_bytes_per_launch:"):
+                    traffic = int(line.split(":", 1)[1])
         toks = B * a.steps * world
         kv_bytes = info["kv_bytes_per_pos"] * (ctx + a.warmup + a.steps // 2) * B
         step_bytes = info["weight_bytes"] + kv_bytes
         out = {
             "metric": METRIC, "value": round(toks / t_dev, 2), "unit": "tok/s", "n_gpus": world,
             "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(t_dev / a.steps * 1000, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int4 weights, fp32 math",
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int4 weights (exact dequant); fp16 x, f32 accumulate",
             "data": "synthetic (random-init N(0,0.02) weights, uniform-random token ids)",
-            "config": {"workload": "qwen2-7b-shape decoder, all linears INT4 g128 (fp16 scale+zero), batch "
-                                   f"{B} decode after a {ctx}-token prefill, fp16 paged KV",
+            "config": {"workload": f"qwen2-7b-shape decoder ({shape.layers} layers), all linears INT4 g128 "
+                                   f"(fp16 scale+zero), batch {B} decode after a {ctx}-token prefill, fp16 paged KV",
                        "batch": B, "ctx_start": ctx, "parallelism": f"replicas x{world}" if world > 1 else "single",
                        "l2": "no flush: 3.76 GB of weights stream from HBM every step (L2 126 MB)"},
             "e2e": {"value": round(toks / t_e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
                     "d2h_bytes_per_step": 4 * B * shape.vocab},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": traffic,
-                         "kernel": "gemv_kernel<4,0,1,R> on gate|up 37888x3584 INT4 g128 (+SwiGLU)",
+                         "frac": round(achieved / peak, 4), "traffic": traffic, "kernel": kern_name,
+                         "bytes_per_launch": kern_bytes, "ms_per_launch": round(t_kern * 1000, 4),
                          "peak_source": peak_kind},
             "step_roofline": {"bytes_per_step": step_bytes,
                               "achieved_gbs": round(step_bytes / (t_dev / a.steps) / 1e9, 1),
                               "frac": round(step_bytes / (t_dev / a.steps) / 1e9 / peak, 4)},
             "clocks": clk.summary(),
-            "gpu_launches": a.steps * (5 * shape.layers + 3),
+            "gpu_launches": a.steps * (3 if persistent else 5 * shape.layers + 3),
         }
         if not a.no_cpu_baseline:
             cs = CpuLayerSample(shape)

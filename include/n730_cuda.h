@@ -175,6 +175,10 @@ int n730_model_info(void* model, int64_t* info);
 void* n730_model_stream(void* model);
 /* One resident linear alone (which: 0 q|k|v, 1 o, 2 gate|up + SwiGLU, 3 down, 4 lm_head),
  * no norm/bias/residual; used to time the dequant-GEMV on the model's weights. */
+/* Launch only the persistent kernel of a batch-1 decode step (no embedding, no
+ * position update; repeated calls recompute the same position).  Timing hook;
+ * N730_UNSUPPORTED (-14) when the model decodes with one kernel per op. */
+int n730_model_run_step_kernel(void* model, void* stream);
 int n730_model_run_linear(void* model, int layer, int which, const float* d_x, int batch, float* d_y,
                           void* stream);
 /* Algorithmic bytes of that linear for `batch` rows: codes + fp16 scale/zero + x + y. */

@@ -588,6 +588,17 @@ N730_API int n730_model_decode_device(void* p, const int32_t* d_tokens, int batc
   return N730_OK;
 }
 
+// Launch only the persistent decode kernel of a batch-1 step on `stream` (the
+// embedding and the position update are not run, so repeated calls recompute
+// the same position).  Used to time that kernel alone.
+N730_API int n730_model_run_step_kernel(void* p, void* stream) {
+  MODEL(p);
+  N730_REQUIRE(m->finalized, N730_STATE, "model: not finalized");
+  N730_REQUIRE(m->pd_ok, N730_UNSUPPORTED, "model: batch-1 decode does not use the persistent kernel");
+  N730_REQUIRE(m->h_seq[0] < m->c.max_ctx, N730_STATE, "KV cache capacity exceeded");
+  return persist_launch(m->pd, stream ? (cudaStream_t)stream : m->st);
+}
+
 // Append `n` tokens to sequence `seq` (prefill when n > 1, the decode graph
 // when n == 1 and seq == 0) and return the logits of the last position.
 N730_API int n730_model_forward(void* p, int seq, const int32_t* host_tokens, int n, float* host_logits) {
@@ -619,7 +630,7 @@ N730_API int n730_model_forward(void* p, int seq, const int32_t* host_tokens, in
 }
 
 // info[16]: weight bytes, kv bytes per position, kv capacity bytes, n_split,
-// qkv_dim, max_pages, finalized
+// qkv_dim, max_pages, finalized, persistent batch-1 decode, untied embedding bytes
 N730_API int n730_model_info(void* p, int64_t* info) {
   MODEL(p);
   if (!info) return N730_NULL;
@@ -640,6 +651,7 @@ N730_API int n730_model_info(void* p, int64_t* info) {
   info[5] = m->max_pages;
   info[6] = m->finalized;
   info[7] = m->pd_ok;
+  info[8] = m->lm_head != m->embed ? bytes(m->embed) : 0;  // read one row per token, not streamed
   return N730_OK;
 }
 

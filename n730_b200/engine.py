@@ -64,6 +64,8 @@ def _sigs(lib):
     lib.n730_model_info.restype = i32
     lib.n730_model_stream.argtypes = [vp]
     lib.n730_model_stream.restype = vp
+    lib.n730_model_run_step_kernel.argtypes = [vp, vp]
+    lib.n730_model_run_step_kernel.restype = i32
     lib.n730_model_run_linear.argtypes = [vp, i32, i32, vp, i32, vp, vp]
     lib.n730_model_run_linear.restype = i32
     lib.n730_model_linear_bytes.argtypes = [vp, i32, i32, i32]
@@ -176,7 +178,13 @@ class Engine:
         a = (C.c_int64 * 16)()
         _lib.check(self.lib.n730_model_info(self.h, a), "model_info")
         return {"weight_bytes": a[0], "kv_bytes_per_pos": a[1], "kv_capacity_bytes": a[2], "n_split": a[3],
-                "qkv_dim": a[4], "pages_per_seq": a[5], "persistent_decode": bool(a[7])}
+                "qkv_dim": a[4], "pages_per_seq": a[5], "persistent_decode": bool(a[7]),
+                "embed_bytes": a[8]}
+
+    def run_step_kernel(self, stream: int = 0):
+        """Launch only the persistent decode kernel of a batch-1 step (timing hook)."""
+        _lib.check(self.lib.n730_model_run_step_kernel(self.h, C.c_void_p(stream) if stream else None),
+                   "model_run_step_kernel")
 
     def run_linear(self, layer: int, which: int, d_x: int, batch: int, d_y: int, stream: int = 0):
         _lib.check(self.lib.n730_model_run_linear(self.h, layer, which, C.c_void_p(d_x), batch, C.c_void_p(d_y),
