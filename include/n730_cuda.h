@@ -68,6 +68,14 @@ int n730_softmax_scores(float* d_scores, int n_heads, int seq_q, int seq_total, 
 int n730_attention_forward(void* ctx, const float* d_q, const float* d_k_cache, const float* d_v_cache,
                            float* d_out, int seq_q, int seq_total, int n_heads, int n_kv_heads,
                            int head_dim, int cache_offset);
+/* No counterpart in the reference: n730_attention_forward without a context
+ * and without allocating.  The [n_heads, seq_q, seq_total] scores live in a
+ * fixed 4 MiB device array (heads * seq_q * seq_total <= 1 Mi floats, else
+ * N730_BAD_ARG); first call per device resolves it (make it outside stream
+ * capture); calls that overlap in time race on it.  Runs on `stream`. */
+int n730_attention_forward_noalloc(const float* d_q, const float* d_k_cache, const float* d_v_cache,
+                                   float* d_out, int seq_q, int seq_total, int n_heads, int n_kv_heads,
+                                   int head_dim, int cache_offset, void* stream);
 /* Replaces n730_cuda.cu:887-950. */
 int n730_attention_qk_only(void* ctx, const float* d_q, const float* d_k_cache, int seq_q,
                            int seq_total, int n_heads, int n_kv_heads, int head_dim);

@@ -13,6 +13,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <mutex>
 
 #include "qweight.h"
 
@@ -380,6 +381,70 @@ N730_API int n730_attention_forward(void* ctx, const float* d_q, const float* d_
   N730_CHECK_LAUNCH();
   pv_kernel<<<dim3(seq_q, n_heads), std::min(head_dim, 256)>>>(c->d_scores, d_v_cache, d_out, seq_q,
                                                                seq_total, n_heads, n_kv_heads, head_dim);
+  N730_CHECK_LAUNCH();
+  return N730_OK;
+}
+
+// ---------------------------------------------------------------------------
+// No-allocation variant of n730_attention_forward (no counterpart in the
+// reference).  Same kernels and results, but the [heads, seq_q, seq_total]
+// score matrix lives in a fixed file-scope device array instead of the
+// context's heads x max_seq^2 buffer, so the call needs no context, performs
+// no cudaMalloc / cudaFree and cannot fail for lack of memory after start-up.
+// For callers that must not allocate: a context sized for long contexts does
+// not fit (64 heads x 8192^2 positions is 17 GB of scores), and cudaMalloc /
+// cudaFree per call would synchronise the device under work on other streams.
+//  * Limit: heads * seq_q * seq_total <= N730_ATTN_SCRATCH_FLOATS (1 Mi floats,
+//    4 MiB; e.g. decode of 64 heads over 16384 positions); larger requests
+//    return N730_BAD_ARG before any GPU work.
+//  * The scratch address is resolved with cudaGetSymbolAddress once per device,
+//    on that device's first call; make that first call outside stream capture.
+//  * Nothing in the scratch must start at zero: scores_kernel writes every
+//    element that the softmax and P V kernels read.
+//  * One scratch per device: calls that overlap in time (other streams, other
+//    host threads) race on it; serialise them.
+// ---------------------------------------------------------------------------
+constexpr int64_t N730_ATTN_SCRATCH_FLOATS = int64_t(1) << 20;
+static __device__ __align__(256) float g_attn_scratch[N730_ATTN_SCRATCH_FLOATS];
+
+static float* attn_scratch(int dev) {
+  static std::mutex mu;
+  static float* addr[128] = {};
+  std::lock_guard<std::mutex> lk(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_attn_scratch) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    addr[dev] = static_cast<float*>(p);
+  }
+  return addr[dev];
+}
+
+N730_API int n730_attention_forward_noalloc(const float* d_q, const float* d_k_cache, const float* d_v_cache,
+                                            float* d_out, int seq_q, int seq_total, int n_heads, int n_kv_heads,
+                                            int head_dim, int cache_offset, void* stream) {
+  if (!d_q || !d_k_cache || !d_v_cache || !d_out) return N730_NULL;
+  if (seq_q <= 0 || seq_total <= 0) return N730_OK;
+  N730_REQUIRE(n_heads > 0 && n_kv_heads > 0 && n_heads % n_kv_heads == 0 && head_dim > 0 && head_dim <= 4096,
+               N730_BAD_ARG, "attention_noalloc: bad heads / head_dim");
+  N730_REQUIRE((int64_t)n_heads * seq_q * seq_total <= N730_ATTN_SCRATCH_FLOATS, N730_BAD_ARG,
+               "attention_noalloc: %d heads x %d x %d scores exceed the %lld-float scratch", n_heads, seq_q,
+               seq_total, (long long)N730_ATTN_SCRATCH_FLOATS);
+  int dev = 0;
+  N730_CUDA(cudaGetDevice(&dev));
+  N730_REQUIRE(dev >= 0 && dev < 128, N730_BAD_ARG, "attention_noalloc: device %d", dev);
+  float* sc = attn_scratch(dev);
+  N730_REQUIRE(sc, N730_CUDA_ERR, "attention_noalloc: scratch address unavailable");
+  cudaStream_t st = (cudaStream_t)stream;
+  scores_kernel<<<dim3((seq_total + 127) / 128, seq_q, n_heads), 128, head_dim * 4, st>>>(
+      d_q, d_k_cache, sc, seq_q, seq_total, n_heads, n_kv_heads, head_dim, 1.0f / sqrtf((float)head_dim));
+  N730_CHECK_LAUNCH();
+  mask_softmax_kernel<<<n_heads * seq_q, 128, 0, st>>>(sc, seq_q, seq_total, cache_offset, seq_q > 1);
+  N730_CHECK_LAUNCH();
+  pv_kernel<<<dim3(seq_q, n_heads), std::min(head_dim, 256), 0, st>>>(sc, d_v_cache, d_out, seq_q, seq_total,
+                                                                     n_heads, n_kv_heads, head_dim);
   N730_CHECK_LAUNCH();
   return N730_OK;
 }
