@@ -150,6 +150,10 @@ typedef struct N730ModelConfig {
                            tensor-core GEMV (x rounded to fp16) */
   int32_t per_op_decode; /* 1: batch-1 decode as one kernel per op; 0: one persistent
                             cooperative kernel for the whole step when the model allows it */
+  int32_t stream_depth;  /* 0: all layer weights resident in HBM.  d > 0: per-layer weights live
+                            in pinned host memory and are copied into d + 1 HBM slots on a copy
+                            stream, d layers ahead of the layer being computed (the reference's
+                            N730Scheduler prefetch, scheduler.py:236-287, as host->HBM copies) */
 } N730ModelConfig;
 
 /* weight slots (n730_model_set_qweight); EMBED/LMHEAD take layer = -1 */

@@ -153,8 +153,8 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) gemv_mma2_kernel(const
   int* tile_cnt = reinterpret_cast<int*>(smem + WARPS * MG2_RING * 8);  // [tiles_per_cta]
   uint4* xf = reinterpret_cast<uint4*>(smem + p.xf_off);                // [batch][ks_n/2][4 tq] x 2 k-steps
   float* sx = reinterpret_cast<float*>(smem + p.sx_off);                // [G][NT*8]
-  float* accs = reinterpret_cast<float*>(smem + p.acc_off);             // [tiles_per_cta][16][NT*8]
-  float* red = accs + p.tiles_per_cta * 16 * NT * 8;                    // [WARPS][16] + [16]
+  float* accs = reinterpret_cast<float*>(smem + p.acc_off);             // [tiles_per_cta][parts][16][NT*8]
+  float* red = accs + p.tiles_per_cta * p.parts * 16 * NT * 8;          // [WARPS][16] + [16]
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int n_tiles = (p.rows + 15) / 16;
@@ -166,7 +166,6 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) gemv_mma2_kernel(const
   uint64_t* wb = bars + warp * MG2_RING;
   uint8_t* ring = smem + p.ring_off + (size_t)warp * p.ring * p.ring_stride;
 
-  for (int i = tid; i < ntc * 16 * NT * 8; i += THREADS) accs[i] = 0.f;
   for (int i = tid; i < ntc; i += THREADS) tile_cnt[i] = 0;
   if (lane == 0) {
     for (int r = 0; r < p.ring; ++r) mbar_init(&wb[r], 1);
@@ -318,14 +317,16 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) gemv_mma2_kernel(const
       if (lane == 0 && prod.u < n_units) { issue(prod, slot); advance(prod); }
     }
     if (aborted) break;
-    // merge this K-part into the tile; the warp completing the tile writes it out
-    const int tl = t - tile0;
-    float* ta = accs + (size_t)tl * 16 * NT * 8;
+    // this K-part's partial goes to its own slot; the warp completing the tile
+    // sums the slots in part order (deterministic) and writes the tile out
+    const int tl = t - tile0, part = (cons.u - (cons.u / P) * P);
+    constexpr int TS = 16 * NT * 8;  // floats per slot
+    float* ta = accs + ((size_t)tl * P + part) * TS;
 #pragma unroll
     for (int nn = 0; nn < NT; ++nn) {
       const int c = nn * 8 + 2 * tq;
-      if (c < nb) { atomicAdd(&ta[g * NT * 8 + c], acc[nn][0]); atomicAdd(&ta[(g + 8) * NT * 8 + c], acc[nn][2]); }
-      if (c + 1 < nb) { atomicAdd(&ta[g * NT * 8 + c + 1], acc[nn][1]); atomicAdd(&ta[(g + 8) * NT * 8 + c + 1], acc[nn][3]); }
+      ta[g * NT * 8 + c] = acc[nn][0]; ta[(g + 8) * NT * 8 + c] = acc[nn][2];
+      ta[g * NT * 8 + c + 1] = acc[nn][1]; ta[(g + 8) * NT * 8 + c + 1] = acc[nn][3];
     }
     __threadfence_block();
     __syncwarp();
@@ -333,14 +334,20 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) gemv_mma2_kernel(const
     if (lane == 0) last = atomicAdd(&tile_cnt[tl], 1) == P - 1;
     if (__shfl_sync(0xffffffffu, last, 0)) {
       __threadfence_block();
-      for (int i = lane; i < 16 * NT * 8; i += 32) {
+      const volatile float* tb = accs + (size_t)tl * P * TS;
+      auto tile_sum = [&](int i) {
+        float v = 0.f;
+        for (int q2 = 0; q2 < P; ++q2) v += tb[q2 * TS + i];
+        return v;
+      };
+      for (int i = lane; i < TS; i += 32) {
         const int r = i / (NT * 8), bc = i % (NT * 8);
         const int row = t * 16 + r;
         if (bc >= nb || row >= p.rows) continue;
         if (p.swiglu && (r & 1)) continue;
-        float v = ta[i] + (p.bias ? p.bias[row] : 0.f);
+        float v = tile_sum(i) + (p.bias ? p.bias[row] : 0.f);
         if (p.swiglu) {
-          const float u = ta[i + NT * 8] + (p.bias ? p.bias[row + 1] : 0.f);
+          const float u = tile_sum(i + NT * 8) + (p.bias ? p.bias[row + 1] : 0.f);
           p.y[(int64_t)bc * p.ldy + row / 2] = (v / (1.0f + expf(-v))) * u;
         } else {
           if (p.residual) v += p.residual[(int64_t)bc * p.ldr + row];
@@ -438,7 +445,7 @@ int gemv_mma_launch(const GemvArgs& a, cudaStream_t st) {
       off += (size_t)p.G * NT * 8 * 4;
       off = (off + 127) / 128 * 128;
       p.acc_off = (int)off;
-      off += ((size_t)p.tiles_per_cta * 16 * NT * 8 + (WARPS + 1) * 16) * 4;
+      off += ((size_t)p.tiles_per_cta * p.parts * 16 * NT * 8 + (WARPS + 1) * 16) * 4;
       off = (off + 127) / 128 * 128;
       p.ring_off = (int)off;
       return off + (size_t)WARPS * p.ring * p.ring_stride;

@@ -12,6 +12,7 @@
 // then the final-norm + lm_head GEMV and a position update, captured once per
 // batch size into a CUDA graph whose kernels chain with programmatic dependent
 // launch.  Host I/O per step is the token ids in and the logits out.
+#include <array>
 #include <cmath>
 #include <cstring>
 #include <map>
@@ -80,6 +81,17 @@ struct Model {
   // persistent batch-1 decode (decode_persist.cu)
   bool pd_ok = false;
   PdPlan pd;
+  // layer streaming (stream_depth > 0): per-layer weight images in pinned host
+  // memory, copied into HBM slots on `cst` ahead of use
+  struct WOff { int64_t codes, sz; };
+  std::vector<uint8_t*> img;                 // [layers] pinned host images
+  std::vector<int64_t> img_bytes;            // [layers]
+  std::vector<std::array<WOff, 4>> img_off;  // [layers][qkv, o, gate_up, down]
+  std::vector<uint8_t*> slot;                // [depth + 1] HBM slots
+  std::vector<std::array<QWeight, 4>> slot_w;  // weights bound to a slot
+  std::vector<cudaEvent_t> ev_ready, ev_free;  // per slot
+  cudaStream_t cst = nullptr;
+  int64_t streamed_bytes = 0;                // host->HBM bytes per forward pass
 
   template <typename T>
   int alloc(T** p, size_t n) {
@@ -120,11 +132,113 @@ static int fuse_rows(Model* m, std::vector<QWeight*> parts, bool interleave, QWe
 
 static AttnDims dims(const Model* m);
 
+static int64_t dev_code_bytes(const QWeight* w) {
+  if (w->layout == 1) return (int64_t)((w->rows + 15) / 16) * w->n_groups * ((int64_t)(w->group / 16) * 128 + 64);
+  return (int64_t)w->rows * w->row_bytes;
+}
+static int64_t dev_sz_bytes(const QWeight* w) {
+  return (w->layout == 1 || w->bits == 16) ? 0 : (int64_t)w->rows * w->sz_pitch;
+}
+
+// Move every layer's weights into a pinned host image (after fusion and layout
+// conversion, so an image is the exact device bytes) and set up the HBM slots.
+static int setup_streaming(Model* m) {
+  const int nl = m->c.layers, ns = m->c.stream_depth + 1;
+  m->img.assign(nl, nullptr);
+  m->img_bytes.assign(nl, 0);
+  m->img_off.assign(nl, {});
+  int64_t slot_bytes = 0;
+  for (int l = 0; l < nl; ++l) {
+    Layer& y = m->L[l];
+    QWeight* ws[4] = {y.qkv, y.o, y.gate_up, y.down};
+    int64_t off = 0;
+    for (int k = 0; k < 4; ++k) {
+      m->img_off[l][k].codes = off;
+      off += (dev_code_bytes(ws[k]) + 255) / 256 * 256;
+      m->img_off[l][k].sz = off;
+      off += (dev_sz_bytes(ws[k]) + 255) / 256 * 256;
+    }
+    m->img_bytes[l] = off;
+    slot_bytes = std::max(slot_bytes, off);
+    N730_CUDA(cudaMallocHost(&m->img[l], off));
+    for (int k = 0; k < 4; ++k) {
+      QWeight* w = ws[k];
+      N730_CUDA(cudaMemcpy(m->img[l] + m->img_off[l][k].codes, w->codes, dev_code_bytes(w), cudaMemcpyDeviceToHost));
+      if (dev_sz_bytes(w))
+        N730_CUDA(cudaMemcpy(m->img[l] + m->img_off[l][k].sz, w->sz, dev_sz_bytes(w), cudaMemcpyDeviceToHost));
+      if (w->owns) { cudaFree(w->codes); cudaFree(w->sz); }
+      w->codes = nullptr;  // metadata only from here on
+      w->sz = nullptr;
+      w->owns = false;
+    }
+    m->streamed_bytes += off;
+  }
+  m->slot.assign(ns, nullptr);
+  m->slot_w.assign(ns, {});
+  m->ev_ready.assign(ns, nullptr);
+  m->ev_free.assign(ns, nullptr);
+  for (int s = 0; s < ns; ++s) {
+    if (int rc = m->alloc(&m->slot[s], (size_t)slot_bytes)) return rc;
+    N730_CUDA(cudaEventCreateWithFlags(&m->ev_ready[s], cudaEventDisableTiming));
+    N730_CUDA(cudaEventCreateWithFlags(&m->ev_free[s], cudaEventDisableTiming));
+    N730_CUDA(cudaEventRecord(m->ev_free[s], m->st));
+  }
+  N730_CUDA(cudaStreamCreateWithFlags(&m->cst, cudaStreamNonBlocking));
+  return N730_OK;
+}
+
+// Copy layer l's image into its slot on the copy stream, after the slot's
+// previous layer has finished computing.
+static int stream_issue(Model* m, int l) {
+  const int s = l % (int)m->slot.size();
+  N730_CUDA(cudaStreamWaitEvent(m->cst, m->ev_free[s], 0));
+  N730_CUDA(cudaMemcpyAsync(m->slot[s], m->img[l], (size_t)m->img_bytes[l], cudaMemcpyHostToDevice, m->cst));
+  N730_CUDA(cudaEventRecord(m->ev_ready[s], m->cst));
+  return N730_OK;
+}
+
+struct LayerW { const QWeight *qkv, *o, *gate_up, *down; };
+
+// Start of a pass over the layers: prefetch the first `depth` layers.
+static int stream_begin(Model* m) {
+  if (!m->c.stream_depth) return N730_OK;
+  for (int l = 0; l < std::min(m->c.stream_depth, m->c.layers); ++l)
+    if (int rc = stream_issue(m, l)) return rc;
+  return N730_OK;
+}
+
+// Weights of layer l, ready to use on m->st (streamed: wait for its copy).
+static int stream_acquire(Model* m, int l, LayerW* out) {
+  Layer& y = m->L[l];
+  if (!m->c.stream_depth) { *out = LayerW{y.qkv, y.o, y.gate_up, y.down}; return N730_OK; }
+  const int s = l % (int)m->slot.size();
+  N730_CUDA(cudaStreamWaitEvent(m->st, m->ev_ready[s], 0));
+  const QWeight* meta[4] = {y.qkv, y.o, y.gate_up, y.down};
+  for (int k = 0; k < 4; ++k) {
+    QWeight& w = m->slot_w[s][k];
+    w = *meta[k];
+    w.codes = m->slot[s] + m->img_off[l][k].codes;
+    w.sz = dev_sz_bytes(meta[k]) ? m->slot[s] + m->img_off[l][k].sz : nullptr;
+    w.owns = false;
+  }
+  *out = LayerW{&m->slot_w[s][0], &m->slot_w[s][1], &m->slot_w[s][2], &m->slot_w[s][3]};
+  return N730_OK;
+}
+
+// Layer l's kernels are enqueued: free its slot and start the copy `depth` layers ahead.
+static int stream_release(Model* m, int l) {
+  if (!m->c.stream_depth) return N730_OK;
+  N730_CUDA(cudaEventRecord(m->ev_free[l % (int)m->slot.size()], m->st));
+  if (l + m->c.stream_depth < m->c.layers) return stream_issue(m, l + m->c.stream_depth);
+  return N730_OK;
+}
+
 // Phase table + scratch for the persistent batch-1 decode kernel.  Leaves
 // pd_ok false (per-op kernels) when a weight is not in fragment tiles, groups
 // differ, or the shapes exceed the kernel's limits.
 static int plan_persistent(Model* m) {
   const N730ModelConfig& c = m->c;
+  if (c.stream_depth > 0) return N730_OK;  // weights are not resident
   auto tiled = [](const QWeight* w) { return w && w->layout == 1; };
   for (auto& y : m->L)
     if (!tiled(y.qkv) || !tiled(y.o) || !tiled(y.gate_up) || !tiled(y.down)) return N730_OK;
@@ -259,6 +373,8 @@ static int finalize(Model* m) {
     if (m->lm_head != m->embed)
       if (int rc = conv(m->lm_head)) return rc;
   }
+  if (c.stream_depth > 0)
+    if (int rc = setup_streaming(m)) return rc;
   for (auto& kv : m->pend_w) {
     const int s = kv.first.second;
     if (s == N730_W_Q || s == N730_W_K || s == N730_W_V || s == N730_W_GATE || s == N730_W_UP)
@@ -349,17 +465,22 @@ static int enqueue_decode(Model* m, int B) {
   const bool persistent = B == 1 && m->pd_ok;
   if (persistent)
     if (int rc = persist_launch(m->pd, m->st)) return rc;
+  if (!persistent)
+    if (int rc = stream_begin(m)) return rc;
   for (int l = 0; l < c.layers && !persistent; ++l) {
     Layer& y = m->L[l];
-    if (int rc = gemv(m, y.qkv, m->x, h, B, m->qkv, m->qkv_dim, y.qkv_bias, nullptr, 0, y.ln1, 0)) return rc;
+    LayerW lw;
+    if (int rc = stream_acquire(m, l, &lw)) return rc;
+    if (int rc = gemv(m, lw.qkv, m->x, h, B, m->qkv, m->qkv_dim, y.qkv_bias, nullptr, 0, y.ln1, 0)) return rc;
     DecodeAttnArgs a = {};
     a.qkv = m->qkv; a.ld_qkv = m->qkv_dim; a.cos_t = m->cos_t; a.sin_t = m->sin_t;
     a.seq_lens = m->seq_lens; a.block_table = m->block_table; a.kv = y.kv; a.d = dims(m);
     a.out = m->attn; a.batch = B; a.pdl = c.use_pdl;
     if (int rc = attn_decode_launch(a, m->st)) return rc;
-    if (int rc = gemv(m, y.o, m->attn, ad, B, m->x, h, y.o_bias, m->x, h, nullptr, 0)) return rc;
-    if (int rc = gemv(m, y.gate_up, m->x, h, B, m->mlp, c.ffn, y.gate_up_bias, nullptr, 0, y.ln2, 1)) return rc;
-    if (int rc = gemv(m, y.down, m->mlp, c.ffn, B, m->x, h, y.down_bias, m->x, h, nullptr, 0)) return rc;
+    if (int rc = gemv(m, lw.o, m->attn, ad, B, m->x, h, y.o_bias, m->x, h, nullptr, 0)) return rc;
+    if (int rc = gemv(m, lw.gate_up, m->x, h, B, m->mlp, c.ffn, y.gate_up_bias, nullptr, 0, y.ln2, 1)) return rc;
+    if (int rc = gemv(m, lw.down, m->mlp, c.ffn, B, m->x, h, y.down_bias, m->x, h, nullptr, 0)) return rc;
+    if (int rc = stream_release(m, l)) return rc;
   }
   if (!persistent)
     if (int rc = gemv(m, m->lm_head, m->x, h, B, m->logits, c.vocab, nullptr, nullptr, 0, m->final_norm, 0))
@@ -378,7 +499,7 @@ static int enqueue_decode(Model* m, int B) {
 }
 
 static int run_decode(Model* m, int B) {
-  if (!m->c.use_graphs) return enqueue_decode(m, B);
+  if (!m->c.use_graphs || m->c.stream_depth > 0) return enqueue_decode(m, B);
   auto it = m->graphs.find(B);
   if (it == m->graphs.end()) {
     cudaGraph_t g = nullptr;
@@ -411,9 +532,12 @@ static int prefill(Model* m, int seq, const int32_t* d_tok, int T, float* d_logi
     const int n = std::min(c.max_prefill, T - done);
     const int pos0 = m->h_seq[seq] + done;
     if (int rc = embed_launch(*m->embed, d_tok + done, n, m->px, m->st)) return rc;
+    if (int rc = stream_begin(m)) return rc;
     for (int l = 0; l < c.layers; ++l) {
       Layer& y = m->L[l];
-      if (int rc = gemv(m, y.qkv, m->px, h, n, m->pqkv, m->qkv_dim, y.qkv_bias, nullptr, 0, y.ln1, 0)) return rc;
+      LayerW lw;
+      if (int rc = stream_acquire(m, l, &lw)) return rc;
+      if (int rc = gemv(m, lw.qkv, m->px, h, n, m->pqkv, m->qkv_dim, y.qkv_bias, nullptr, 0, y.ln1, 0)) return rc;
       KVWriteArgs kw = {};
       kw.qkv = m->pqkv; kw.ld_qkv = m->qkv_dim; kw.cos_t = m->cos_t; kw.sin_t = m->sin_t;
       kw.block_table = m->block_table + (size_t)seq * m->max_pages; kw.kv = y.kv; kw.d = dims(m);
@@ -423,9 +547,10 @@ static int prefill(Model* m, int seq, const int32_t* d_tok, int T, float* d_logi
       pa.qkv = m->pqkv; pa.ld_qkv = m->qkv_dim; pa.block_table = kw.block_table; pa.kv = y.kv; pa.d = dims(m);
       pa.T = n; pa.pos0 = pos0; pa.out = m->pattn; pa.pdl = c.use_pdl;
       if (int rc = attn_prefill_launch(pa, m->st)) return rc;
-      if (int rc = gemv(m, y.o, m->pattn, ad, n, m->px, h, y.o_bias, m->px, h, nullptr, 0)) return rc;
-      if (int rc = gemv(m, y.gate_up, m->px, h, n, m->pmlp, c.ffn, y.gate_up_bias, nullptr, 0, y.ln2, 1)) return rc;
-      if (int rc = gemv(m, y.down, m->pmlp, c.ffn, n, m->px, h, y.down_bias, m->px, h, nullptr, 0)) return rc;
+      if (int rc = gemv(m, lw.o, m->pattn, ad, n, m->px, h, y.o_bias, m->px, h, nullptr, 0)) return rc;
+      if (int rc = gemv(m, lw.gate_up, m->px, h, n, m->pmlp, c.ffn, y.gate_up_bias, nullptr, 0, y.ln2, 1)) return rc;
+      if (int rc = gemv(m, lw.down, m->pmlp, c.ffn, n, m->px, h, y.down_bias, m->px, h, nullptr, 0)) return rc;
+      if (int rc = stream_release(m, l)) return rc;
     }
     done += n;
     if (done == T && d_logits_row)
@@ -450,6 +575,8 @@ N730_API int n730_model_create(const N730ModelConfig* cfg, void** out) {
                    c.head_dim > 0 && c.ffn > 0 && c.vocab > 0 && c.max_ctx > 0 && c.max_batch > 0,
                N730_BAD_ARG, "model_create: invalid config");
   N730_REQUIRE(c.head_dim == 64 || c.head_dim == 128, N730_UNSUPPORTED, "model_create: head_dim %d", c.head_dim);
+  N730_REQUIRE(c.stream_depth >= 0 && c.stream_depth <= 16, N730_BAD_ARG, "model_create: stream_depth %d",
+               c.stream_depth);
   Model* m = new Model();
   m->c = c;
   if (m->c.page_size <= 0) m->c.page_size = 64;
@@ -476,6 +603,10 @@ N730_API void n730_model_destroy(void* p) {
   if (m->lm_head != m->embed) qweight_destroy(m->lm_head);
   qweight_destroy(m->embed);
   for (void* a : m->allocs) cudaFree(a);
+  for (uint8_t* im : m->img) if (im) cudaFreeHost(im);
+  for (auto e : m->ev_ready) if (e) cudaEventDestroy(e);
+  for (auto e : m->ev_free) if (e) cudaEventDestroy(e);
+  if (m->cst) cudaStreamDestroy(m->cst);
   if (m->h_tok) cudaFreeHost(m->h_tok);
   if (m->h_logits) cudaFreeHost(m->h_logits);
   cudaStreamDestroy(m->st);
@@ -630,7 +761,8 @@ N730_API int n730_model_forward(void* p, int seq, const int32_t* host_tokens, in
 }
 
 // info[16]: weight bytes, kv bytes per position, kv capacity bytes, n_split,
-// qkv_dim, max_pages, finalized, persistent batch-1 decode, untied embedding bytes
+// qkv_dim, max_pages, finalized, persistent batch-1 decode, untied embedding bytes,
+// streamed layer bytes per pass
 N730_API int n730_model_info(void* p, int64_t* info) {
   MODEL(p);
   if (!info) return N730_NULL;
@@ -652,6 +784,7 @@ N730_API int n730_model_info(void* p, int64_t* info) {
   info[6] = m->finalized;
   info[7] = m->pd_ok;
   info[8] = m->lm_head != m->embed ? bytes(m->embed) : 0;  // read one row per token, not streamed
+  info[9] = m->streamed_bytes;                                // host->HBM bytes per forward pass
   return N730_OK;
 }
 
@@ -665,6 +798,7 @@ N730_API int n730_model_run_linear(void* p, int layer, int which, const float* d
                                    void* stream) {
   MODEL(p);
   N730_REQUIRE(m->finalized && d_x && d_y, N730_STATE, "run_linear: model not finalized or null buffers");
+  N730_REQUIRE(which == 4 || !m->c.stream_depth, N730_STATE, "run_linear: layer weights are host-resident (streamed)");
   const QWeight* w = nullptr;
   if (which == 4) w = m->lm_head;
   else {

@@ -32,7 +32,7 @@ class N730ModelConfig(C.Structure):
                [("rms_eps", C.c_float), ("rope_theta", C.c_float)] + \
                [(n, C.c_int32) for n in ("max_ctx", "max_batch", "page_size", "max_prefill", "tie_embeddings",
                                          "tp_rank", "tp_size", "use_graphs", "use_pdl", "exact_gemv",
-                                         "per_op_decode")]
+                                         "per_op_decode", "stream_depth")]
 
 
 def _sigs(lib):
@@ -122,17 +122,19 @@ class Engine:
 
     def __init__(self, shape: ModelShape, max_ctx: int = 4096, max_batch: int = 1, page_size: int = 64,
                  max_prefill: int = 512, use_graphs: bool = True, use_pdl: bool = True,
-                 tp_rank: int = 0, tp_size: int = 1, exact_gemv: bool = False, per_op_decode: bool = False):
+                 tp_rank: int = 0, tp_size: int = 1, exact_gemv: bool = False, per_op_decode: bool = False,
+                 stream_depth: int = 0):
         self.lib = _sigs(_lib.cuda())
         self.shape = shape
         c = N730ModelConfig(shape.hidden, shape.layers, shape.heads, shape.kv_heads, shape.head_dim, shape.ffn,
                             shape.vocab, shape.rms_eps, shape.rope_theta, max_ctx, max_batch, page_size,
                             max_prefill, int(shape.tie_embeddings), tp_rank, tp_size, int(use_graphs),
-                            int(use_pdl), int(exact_gemv), int(per_op_decode))
+                            int(use_pdl), int(exact_gemv), int(per_op_decode), int(stream_depth))
         self.cfg = c
         self.h = C.c_void_p()
         _lib.check(self.lib.n730_model_create(C.byref(c), C.byref(self.h)), "model_create")
         self.max_batch = max_batch
+        self.max_ctx = max_ctx
         self._logits = np.zeros((max_batch, shape.vocab), np.float32)
 
     def set_qweight(self, layer: int, slot: int, qw):
@@ -179,7 +181,7 @@ class Engine:
         _lib.check(self.lib.n730_model_info(self.h, a), "model_info")
         return {"weight_bytes": a[0], "kv_bytes_per_pos": a[1], "kv_capacity_bytes": a[2], "n_split": a[3],
                 "qkv_dim": a[4], "pages_per_seq": a[5], "persistent_decode": bool(a[7]),
-                "embed_bytes": a[8]}
+                "embed_bytes": a[8], "streamed_bytes": a[9]}
 
     def run_step_kernel(self, stream: int = 0):
         """Launch only the persistent decode kernel of a batch-1 step (timing hook)."""
@@ -212,15 +214,19 @@ class Engine:
 def load_tensors(engine: Engine, named_blocks, norms: dict | None = None):
     """Hand a model's tensors to the engine by HF name.
 
-    ``named_blocks``: iterable of (name, RawBlock) for every 2-D weight and 1-D
-    bias; ``norms``: name -> fp32 vector (absent norms default to ones, as
-    the reference's identity fallback, inference.py:398-406).
+    ``named_blocks``: iterable of (name, RawBlock) for every 2-D weight and
+    1-D FP16 bias / norm vector; ``norms``: name -> fp32 vector, overriding
+    norm blocks of the file (absent norms default to ones, the reference's
+    identity fallback, inference.py:398-406).
     """
+    norms = dict(norms or {})
     for name, b in named_blocks:
         if name == "model.embed_tokens.weight":
             engine.set_qweight(-1, W_EMBED, qweight_from_block(b))
         elif name == "lm_head.weight":
             engine.set_qweight(-1, W_LMHEAD, qweight_from_block(b))
+        elif name.endswith("norm.weight") and b.prec_id == 16 and name not in norms:
+            norms[name] = np.frombuffer(b.payload, np.float16).astype(np.float32)
         elif name.startswith("model.layers."):
             rest = name[len("model.layers."):]
             i, _, tail = rest.partition(".")
@@ -229,12 +235,10 @@ def load_tensors(engine: Engine, named_blocks, norms: dict | None = None):
             if kind == "weight" and base in PROJ_SLOTS:
                 engine.set_qweight(layer, PROJ_SLOTS[base], qweight_from_block(b))
             elif kind == "bias" and base in BIAS_SLOTS:
-                v = np.frombuffer(b.payload, np.float16).astype(np.float32) if b.prec_id == 16 else None
-                if v is None:
-                    from .converter import read_layer  # non-FP16 bias: host dequant
-                    raise ValueError(f"bias {name} must be FP16")
-                engine.set_vector(layer, BIAS_SLOTS[base], v)
-    for name, v in (norms or {}).items():
+                if b.prec_id != 16:
+                    raise ValueError(f"bias {name} must be stored FP16 (as the reference converter writes it)")
+                engine.set_vector(layer, BIAS_SLOTS[base], np.frombuffer(b.payload, np.float16).astype(np.float32))
+    for name, v in norms.items():
         if name == "model.norm.weight":
             engine.set_vector(-1, V_FINAL_NORM, v)
         elif name.startswith("model.layers.") and name.endswith("input_layernorm.weight"):

@@ -129,14 +129,16 @@ def test_persistent_decode_matches_per_op(model):
     eo.close()
 
 
-def test_persistent_decode_deterministic(model):
+def test_decode_deterministic(model):
     """Re-running decode steps from the same cached state gives bit-identical
-    logits: split tiles and attention splits are merged in a fixed order."""
+    logits on both decode paths: split tiles, K-parts and attention splits are
+    merged in a fixed order."""
     shape, blocks, _ = model
-    e = _engine(shape, blocks, max_batch=1)
-    if not e.info()["persistent_decode"]:
-        e.close()
-        pytest.skip("per-op GEMVs merge K-parts with shared-memory atomics (order not fixed)")
+    for per_op in (False, True):
+        _deterministic(_engine(shape, blocks, max_batch=1, per_op_decode=per_op), shape)
+
+
+def _deterministic(e, shape):
     e.forward(np.arange(40) % shape.vocab)
     L = e.seq_len(0)
     first = [e.forward([t]) for t in (3, 5, 7)]
@@ -145,3 +147,28 @@ def test_persistent_decode_deterministic(model):
     e.close()
     for a, b in zip(first, again):
         assert np.array_equal(a, b)
+
+
+@pytest.mark.parametrize("depth", [1, 2])
+def test_streamed_layers_match_resident(model, depth):
+    """Weights held in pinned host memory and copied into depth + 1 HBM slots
+    ahead of use give the same logits as resident weights (same kernels)."""
+    shape, blocks, w = model
+    er = _engine(shape, blocks, max_batch=1, per_op_decode=True)
+    es = _engine(shape, blocks, max_batch=1, stream_depth=depth)
+    assert es.info()["streamed_bytes"] > 0 and not es.info()["persistent_decode"]
+    orc = OracleDecoder(shape, w, max_pos=512)
+    rng = np.random.default_rng(31)
+    prompt = rng.integers(0, shape.vocab, 70)   # two prefill chunks of 64
+    ys, yr = es.forward(prompt), er.forward(prompt)
+    assert np.array_equal(ys, yr)
+    assert rel_err(ys, orc.forward(prompt)) <= TOL
+    tok = 11
+    for _ in range(4):
+        ys, yr = es.forward([tok]), er.forward([tok])
+        assert np.array_equal(ys, yr)
+        tok = int(np.argmax(ys))
+    with pytest.raises(RuntimeError, match="host-resident"):
+        es.run_linear(0, 0, 16, 1, 16)  # rejected before any pointer is used
+    es.close()
+    er.close()
