@@ -187,6 +187,13 @@ int n730_model_info(void* model, int64_t* info);
 void* n730_model_stream(void* model);
 /* One resident linear alone (which: 0 q|k|v, 1 o, 2 gate|up + SwiGLU, 3 down, 4 lm_head),
  * no norm/bias/residual; used to time the dequant-GEMV on the model's weights. */
+/* Tensor parallelism (config tp_rank / tp_size > 1; no counterpart in the reference): every
+ * rank holds a shard - q/k/v by heads, gate/up by FFN rows in whole quant groups, o/down by
+ * the matching input columns, lm_head by vocabulary rows (or replicated) - and the row-split
+ * projections' partial sums are allreduced (NCCL) before the residual add.  Rank 0 makes the
+ * id, the host shares it, every rank calls tp_init before finalize. */
+int n730_tp_unique_id(uint8_t* out_128_bytes);
+int n730_model_tp_init(void* model, const uint8_t* id_128_bytes, int rank, int size);
 /* Launch only the persistent kernel of a batch-1 decode step (no embedding, no
  * position update; repeated calls recompute the same position).  Timing hook;
  * N730_UNSUPPORTED (-14) when the model decodes with one kernel per op. */

@@ -19,6 +19,8 @@
 #include <mutex>
 #include <vector>
 
+#include <nccl.h>
+
 #include "attention.h"
 #include "decode_persist.h"
 #include "n730_cuda.h"
@@ -29,6 +31,24 @@ namespace n730 {
 int qweight_alloc_like(const QWeight& proto, int rows, QWeight** out);
 int qweight_copy_rows(QWeight& dst, const QWeight& src, int dst_row0, int stride, cudaStream_t st);
 void qweight_destroy(QWeight* w);
+
+// x += d (the residual add after a tensor-parallel allreduce of the partial sums)
+__global__ void add_inplace_kernel(float* x, const float* d, int64_t n) {
+  pdl_wait();
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    x[i] += d[i];
+}
+
+// all-gathered vocab shards [T][B][vl] -> logits [B][T * vl]
+__global__ void gather_logits_kernel(const float* all, float* out, int T, int B, int vl) {
+  const int64_t n = (int64_t)T * B * vl;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int v = (int)(i % vl);
+    const int64_t tb = i / vl;
+    const int b = (int)(tb % B), t = (int)(tb / B);
+    out[(int64_t)b * T * vl + (int64_t)t * vl + v] = all[i];
+  }
+}
 
 __global__ void advance_seq_kernel(int* seq_lens, int batch, int by) {
   pdl_wait();
@@ -92,6 +112,13 @@ struct Model {
   std::vector<cudaEvent_t> ev_ready, ev_free;  // per slot
   cudaStream_t cst = nullptr;
   int64_t streamed_bytes = 0;                // host->HBM bytes per forward pass
+  // tensor parallel (tp_size > 1): partial sums of the row-split o/down
+  // projections are allreduced before the residual add; the lm_head is split
+  // by vocabulary and its logits all-gathered
+  ncclComm_t comm = nullptr;
+  float* delta = nullptr;        // [max(max_batch, max_prefill)][hidden]
+  float* logits_all = nullptr;   // [tp][max_batch][vocab / tp]
+  int vocab_l = 0;               // lm_head rows on this rank
 
   template <typename T>
   int alloc(T** p, size_t n) {
@@ -238,7 +265,7 @@ static int stream_release(Model* m, int l) {
 // differ, or the shapes exceed the kernel's limits.
 static int plan_persistent(Model* m) {
   const N730ModelConfig& c = m->c;
-  if (c.stream_depth > 0) return N730_OK;  // weights are not resident
+  if (c.stream_depth > 0 || c.tp_size > 1) return N730_OK;  // weights not resident / collectives between ops
   auto tiled = [](const QWeight* w) { return w && w->layout == 1; };
   for (auto& y : m->L)
     if (!tiled(y.qkv) || !tiled(y.o) || !tiled(y.gate_up) || !tiled(y.down)) return N730_OK;
@@ -310,6 +337,16 @@ static int finalize(Model* m) {
   if (!m->lm_head) {
     N730_REQUIRE(c.tie_embeddings, N730_STATE, "model: lm_head not set and embeddings not tied");
     m->lm_head = m->embed;
+  }
+  m->vocab_l = m->lm_head->rows;
+  if (c.tp_size > 1) {
+    N730_REQUIRE(m->comm, N730_STATE, "model: tensor parallel needs n730_model_tp_init before finalize");
+    N730_REQUIRE(m->lm_head->rows == c.vocab || (long long)m->lm_head->rows * c.tp_size == c.vocab, N730_BAD_ARG,
+                 "model: lm_head has %d rows: expected %d (replicated) or %d (vocab split)", m->lm_head->rows,
+                 c.vocab, c.vocab / c.tp_size);
+  } else {
+    N730_REQUIRE(m->lm_head->rows == c.vocab && m->lm_head->cols == c.hidden, N730_BAD_ARG,
+                 "model: lm_head is %dx%d, expected %dx%d", m->lm_head->rows, m->lm_head->cols, c.vocab, c.hidden);
   }
   m->qkv_dim = (c.heads + 2 * c.kv_heads) * c.head_dim;
   for (int l = 0; l < nl; ++l) {
@@ -424,6 +461,11 @@ static int finalize(Model* m) {
   if (int rc = m->alloc(&m->attn, (size_t)B * c.heads * c.head_dim)) return rc;
   if (int rc = m->alloc(&m->mlp, (size_t)B * c.ffn)) return rc;
   if (int rc = m->alloc(&m->logits, (size_t)B * c.vocab)) return rc;
+  if (c.tp_size > 1) {
+    if (int rc = m->alloc(&m->delta, (size_t)std::max(B, c.max_prefill) * c.hidden)) return rc;
+    if (m->vocab_l != c.vocab)
+      if (int rc = m->alloc(&m->logits_all, (size_t)c.tp_size * B * m->vocab_l)) return rc;
+  }
   // prefill workspace
   const int P = c.max_prefill;
   if (int rc = m->alloc(&m->p_tokens, P)) return rc;
@@ -447,6 +489,55 @@ static int gemv(Model* m, const QWeight* w, const float* x, int ldx, int batch, 
   a.residual = resid; a.ldr = ldr; a.norm_w = norm; a.eps = m->c.rms_eps; a.swiglu = swiglu;
   a.pdl = m->c.use_pdl;
   return gemv_launch(a, m->st);
+}
+
+static int launch_add(Model* m, float* x, const float* d, int64_t n) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)std::min<int64_t>((n + 255) / 256, 4 * num_sms()));
+  cfg.blockDim = dim3(256);
+  cfg.stream = m->st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = m->c.use_pdl ? 1 : 0;
+  N730_CUDA(cudaLaunchKernelEx(&cfg, add_inplace_kernel, x, d, n));
+  return N730_OK;
+}
+
+// y = x_res + W a (+ bias): the row-split projections o_proj / down_proj.  With
+// tensor parallelism W holds this rank's K columns: the partial products are
+// summed across ranks by one allreduce, then added to the residual stream.
+static int rowsplit_linear(Model* m, const QWeight* w, const float* a, int lda, int B, float* x, int ldx,
+                           const float* bias) {
+  if (m->c.tp_size <= 1) return gemv(m, w, a, lda, B, x, ldx, bias, x, ldx, nullptr, 0);
+  const int h = m->c.hidden;
+  if (int rc = gemv(m, w, a, lda, B, m->delta, h, bias, nullptr, 0, nullptr, 0)) return rc;
+  if (ncclAllReduce(m->delta, m->delta, (size_t)B * h, ncclFloat, ncclSum, m->comm, m->st) != ncclSuccess) {
+    set_error("model: ncclAllReduce failed");
+    return N730_COMM;
+  }
+  N730_REQUIRE(ldx == h, N730_BAD_ARG, "model: residual stride");
+  return launch_add(m, x, m->delta, (int64_t)B * h);
+}
+
+// logits [B][vocab] = lm_head(final_norm(x)); vocab-split lm_head: gather the shards
+static int lm_head_logits(Model* m, const float* x, int B, float* logits) {
+  const N730ModelConfig& c = m->c;
+  if (m->vocab_l == c.vocab)
+    return gemv(m, m->lm_head, x, c.hidden, B, logits, c.vocab, nullptr, nullptr, 0, m->final_norm, 0);
+  float* part = m->logits_all + (size_t)c.tp_rank * B * m->vocab_l;
+  if (int rc = gemv(m, m->lm_head, x, c.hidden, B, part, m->vocab_l, nullptr, nullptr, 0, m->final_norm, 0))
+    return rc;
+  if (ncclAllGather(part, m->logits_all, (size_t)B * m->vocab_l, ncclFloat, m->comm, m->st) != ncclSuccess) {
+    set_error("model: ncclAllGather failed");
+    return N730_COMM;
+  }
+  const int64_t n = (int64_t)c.tp_size * B * m->vocab_l;
+  gather_logits_kernel<<<(unsigned)std::min<int64_t>((n + 255) / 256, 4 * num_sms()), 256, 0, m->st>>>(
+      m->logits_all, logits, c.tp_size, B, m->vocab_l);
+  N730_CHECK_LAUNCH();
+  return N730_OK;
 }
 
 static AttnDims dims(const Model* m) {
@@ -477,14 +568,13 @@ static int enqueue_decode(Model* m, int B) {
     a.seq_lens = m->seq_lens; a.block_table = m->block_table; a.kv = y.kv; a.d = dims(m);
     a.out = m->attn; a.batch = B; a.pdl = c.use_pdl;
     if (int rc = attn_decode_launch(a, m->st)) return rc;
-    if (int rc = gemv(m, lw.o, m->attn, ad, B, m->x, h, y.o_bias, m->x, h, nullptr, 0)) return rc;
+    if (int rc = rowsplit_linear(m, lw.o, m->attn, ad, B, m->x, h, y.o_bias)) return rc;
     if (int rc = gemv(m, lw.gate_up, m->x, h, B, m->mlp, c.ffn, y.gate_up_bias, nullptr, 0, y.ln2, 1)) return rc;
-    if (int rc = gemv(m, lw.down, m->mlp, c.ffn, B, m->x, h, y.down_bias, m->x, h, nullptr, 0)) return rc;
+    if (int rc = rowsplit_linear(m, lw.down, m->mlp, c.ffn, B, m->x, h, y.down_bias)) return rc;
     if (int rc = stream_release(m, l)) return rc;
   }
   if (!persistent)
-    if (int rc = gemv(m, m->lm_head, m->x, h, B, m->logits, c.vocab, nullptr, nullptr, 0, m->final_norm, 0))
-      return rc;
+    if (int rc = lm_head_logits(m, m->x, B, m->logits)) return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((B + 127) / 128);
   cfg.blockDim = dim3(128);
@@ -547,16 +637,14 @@ static int prefill(Model* m, int seq, const int32_t* d_tok, int T, float* d_logi
       pa.qkv = m->pqkv; pa.ld_qkv = m->qkv_dim; pa.block_table = kw.block_table; pa.kv = y.kv; pa.d = dims(m);
       pa.T = n; pa.pos0 = pos0; pa.out = m->pattn; pa.pdl = c.use_pdl;
       if (int rc = attn_prefill_launch(pa, m->st)) return rc;
-      if (int rc = gemv(m, lw.o, m->pattn, ad, n, m->px, h, y.o_bias, m->px, h, nullptr, 0)) return rc;
+      if (int rc = rowsplit_linear(m, lw.o, m->pattn, ad, n, m->px, h, y.o_bias)) return rc;
       if (int rc = gemv(m, lw.gate_up, m->px, h, n, m->pmlp, c.ffn, y.gate_up_bias, nullptr, 0, y.ln2, 1)) return rc;
-      if (int rc = gemv(m, lw.down, m->pmlp, c.ffn, n, m->px, h, y.down_bias, m->px, h, nullptr, 0)) return rc;
+      if (int rc = rowsplit_linear(m, lw.down, m->pmlp, c.ffn, n, m->px, h, y.down_bias)) return rc;
       if (int rc = stream_release(m, l)) return rc;
     }
     done += n;
     if (done == T && d_logits_row)
-      if (int rc = gemv(m, m->lm_head, m->px + (size_t)(n - 1) * h, h, 1, d_logits_row, c.vocab, nullptr, nullptr,
-                        0, m->final_norm, 0))
-        return rc;
+      if (int rc = lm_head_logits(m, m->px + (size_t)(n - 1) * h, 1, d_logits_row)) return rc;
   }
   return N730_OK;
 }
@@ -591,11 +679,41 @@ N730_API int n730_model_create(const N730ModelConfig* cfg, void** out) {
   return N730_OK;
 }
 
+N730_API int n730_tp_unique_id(uint8_t* out) {
+  if (!out) return N730_NULL;
+  ncclUniqueId id;
+  if (ncclGetUniqueId(&id) != ncclSuccess) {
+    set_error("ncclGetUniqueId failed");
+    return N730_COMM;
+  }
+  memcpy(out, &id, sizeof id);
+  return N730_OK;
+}
+
+N730_API int n730_model_tp_init(void* p, const uint8_t* id_bytes, int rank, int size) {
+  MODEL(p);
+  N730_REQUIRE(id_bytes, N730_NULL, "tp_init: null id");
+  N730_REQUIRE(!m->finalized && !m->comm, N730_STATE, "tp_init: call once, before finalize");
+  N730_REQUIRE(size == m->c.tp_size && rank == m->c.tp_rank && size > 1, N730_BAD_ARG,
+               "tp_init: rank %d of %d does not match the config (%d of %d)", rank, size, m->c.tp_rank,
+               m->c.tp_size);
+  ncclUniqueId id;
+  memcpy(&id, id_bytes, sizeof id);
+  N730_CUDA(cudaSetDevice(m->device));
+  if (ncclCommInitRank(&m->comm, size, id, rank) != ncclSuccess) {
+    m->comm = nullptr;
+    set_error("ncclCommInitRank failed (rank %d of %d)", rank, size);
+    return N730_COMM;
+  }
+  return N730_OK;
+}
+
 N730_API void n730_model_destroy(void* p) {
   Model* m = (Model*)p;
   if (!m) return;
   cudaStreamSynchronize(m->st);
-  for (auto& g : m->graphs) cudaGraphExecDestroy(g.second);
+  for (auto& g : m->graphs) cudaGraphExecDestroy(g.second);  // graphs holding NCCL calls go before the comm
+  if (m->comm) ncclCommDestroy(m->comm);
   for (auto& kv : m->pend_w) qweight_destroy(kv.second);
   for (auto& y : m->L) {
     qweight_destroy(y.qkv); qweight_destroy(y.o); qweight_destroy(y.gate_up); qweight_destroy(y.down);

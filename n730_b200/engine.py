@@ -64,6 +64,10 @@ def _sigs(lib):
     lib.n730_model_info.restype = i32
     lib.n730_model_stream.argtypes = [vp]
     lib.n730_model_stream.restype = vp
+    lib.n730_tp_unique_id.argtypes = [vp]
+    lib.n730_tp_unique_id.restype = i32
+    lib.n730_model_tp_init.argtypes = [vp, vp, i32, i32]
+    lib.n730_model_tp_init.restype = i32
     lib.n730_model_run_step_kernel.argtypes = [vp, vp]
     lib.n730_model_run_step_kernel.restype = i32
     lib.n730_model_run_linear.argtypes = [vp, i32, i32, vp, i32, vp, vp]
@@ -182,6 +186,17 @@ class Engine:
         return {"weight_bytes": a[0], "kv_bytes_per_pos": a[1], "kv_capacity_bytes": a[2], "n_split": a[3],
                 "qkv_dim": a[4], "pages_per_seq": a[5], "persistent_decode": bool(a[7]),
                 "embed_bytes": a[8], "streamed_bytes": a[9]}
+
+    @staticmethod
+    def tp_unique_id() -> bytes:
+        """128-byte NCCL unique id (rank 0 makes it, every rank passes it to tp_init)."""
+        buf = (C.c_uint8 * 128)()
+        _lib.check(_sigs(_lib.cuda()).n730_tp_unique_id(buf), "tp_unique_id")
+        return bytes(buf)
+
+    def tp_init(self, id_bytes: bytes, rank: int, size: int):
+        buf = (C.c_uint8 * 128).from_buffer_copy(id_bytes)
+        _lib.check(self.lib.n730_model_tp_init(self.h, buf, rank, size), "model_tp_init")
 
     def run_step_kernel(self, stream: int = 0):
         """Launch only the persistent decode kernel of a batch-1 step (timing hook)."""

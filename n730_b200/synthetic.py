@@ -96,11 +96,14 @@ def write_n730(path, shape: ModelShape, pmap: str, seed: int = 0, biases: bool =
 
 
 def build_on_device(shape: ModelShape, pmap: str, engine: Engine, seed: int = 0, std: float = 0.02,
-                    biases: bool = True):
+                    biases: bool = True, tp_rank: int = 0, tp_size: int = 1):
     """Draw every tensor on the GPU and quantise it there; hand the packed weights
     to ``engine``.  Group-wise precisions use the library's GPU quantiser;
     per-tensor INT8 and FP16 (small tensors in the mixed map) are packed on
-    the host by the converter's quantisers."""
+    the host by the converter's quantisers.  With ``tp_size > 1`` every rank
+    draws the same full tensors and keeps its tensor-parallel shard
+    (``n730_b200.tp.shard``); ``shape`` is the global shape."""
+    from . import tp as tpmod
     import ctypes as C
 
     import torch
@@ -111,10 +114,17 @@ def build_on_device(shape: ModelShape, pmap: str, engine: Engine, seed: int = 0,
     lib = _lib.cuda()
     f = precision_map(pmap)
     stream = torch.cuda.current_stream().cuda_stream
+    ffn_group = tpmod.ffn_group_of(f, "model.layers.0.mlp.down_proj.weight")
     for i, (name, shp) in enumerate(tensor_names(shape, biases)):
         g = torch.Generator(device="cuda")
         g.manual_seed(seed * 100003 + i)
         w = torch.randn(shp, generator=g, device="cuda", dtype=torch.float32) * std
+        if tp_size > 1:
+            w = tpmod.shard(name, w, shape, tp_size, tp_rank, ffn_group)
+            if w is None:
+                continue
+            w = w.contiguous()
+            shp = tuple(w.shape)
         if len(shp) == 1:
             layer = int(name.split(".")[2])
             base = name.split(".", 3)[3].rsplit(".", 1)[0]
