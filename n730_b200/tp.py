@@ -26,9 +26,15 @@ def span(n: int, size: int, rank: int, unit: int = 1):
     return lo * unit, hi * unit
 
 
-def check_shape(shape, size: int, ffn_group: int):
+def check_shape(shape, size: int, ffn_group: int, attn_group: int = 128):
+    """Raise unless the shape splits over ``size`` ranks: whole heads and KV heads per
+    rank, o_proj's per-rank input columns a whole number of its quant groups, and
+    at least one FFN group per rank."""
     if shape.heads % size or shape.kv_heads % size:
         raise ValueError(f"{shape.heads} heads / {shape.kv_heads} KV heads do not split over {size} ranks")
+    if size > 1 and (shape.heads // size * shape.head_dim) % attn_group:
+        raise ValueError(f"o_proj input columns per rank ({shape.heads // size * shape.head_dim}) are not whole "
+                         f"groups of {attn_group}")
     if (shape.ffn // ffn_group) < size:
         raise ValueError(f"FFN {shape.ffn} has fewer than {size} groups of {ffn_group}")
 

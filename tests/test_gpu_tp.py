@@ -48,6 +48,7 @@ def _worker(rank, size, port, shape_name, path, out):
                             timeout=timedelta(seconds=60))
     try:
         shape = synthetic.SHAPES[shape_name]
+        tp.check_shape(shape, size, FFN_GROUP)
         eng = Engine(tp.local_shape(shape, size, rank, FFN_GROUP), max_ctx=256, max_batch=2, max_prefill=32,
                      tp_rank=rank, tp_size=size)
         tp.init_engine_comm(eng, rank, size)
@@ -65,11 +66,14 @@ def _worker(rank, size, port, shape_name, path, out):
         if rank == 0:
             out.put((ys, yb.copy()))
         eng.close()
+    except Exception as e:  # report instead of leaving the parent waiting
+        out.put(repr(e))
+        raise
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("shape_name", ["tiny", "tiny-gqa7"])
+@pytest.mark.parametrize("shape_name", ["tiny", "tiny-128"])
 def test_tp2_engine(shape_name, tmp_path):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
@@ -85,6 +89,7 @@ def test_tp2_engine(shape_name, tmp_path):
     res = q.get(timeout=300)
     for p in procs:
         p.join(timeout=120)
+    assert not isinstance(res, str), res
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     ys, yb = res
     w = _oracle_weights(_blocks(path))

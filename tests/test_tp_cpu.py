@@ -113,6 +113,9 @@ def test_shard_geometry():
     assert tp.lm_head_split(s72, 8) and not tp.lm_head_split(synthetic.SHAPES["qwen2-0.5b"], 2)
     with pytest.raises(ValueError):
         tp.check_shape(synthetic.SHAPES["qwen2-7b"], 8, 128)  # 4 KV heads over 8 ranks
+    with pytest.raises(ValueError, match="o_proj"):
+        tp.check_shape(synthetic.SHAPES["tiny-gqa7"], 2, 128)  # 7 heads x 64 = 448 columns per rank
+    tp.check_shape(synthetic.SHAPES["qwen2-72b"], 8, 128)
 
 
 @pytest.mark.parametrize("name,rows,cols", [("model.layers.0.mlp.down_proj.weight", 256, 512),
