@@ -128,6 +128,13 @@ int n730_embed(void* qw, const int32_t* d_tokens, int n, float* d_out, void* str
 int n730_qlinear(void* qw, const float* d_x, int ldx, int batch, float* d_y, int ldy, const float* d_bias,
                  const float* d_residual, int ldr, const float* d_norm_w, float eps, int swiglu,
                  void* stream);
+/* Many-token linear on the tcgen05 tensor cores (TMEM accumulators): the same epilogues as
+ * n730_qlinear for `tokens` rows of x; weights must be INT4 in tensor-core fragment tiles
+ * (n730_qweight_set_layout 1).  d_ws: `tokens` floats of device workspace when d_norm_w is set.
+ * Replaces the per-layer cuBLAS Sgemm of prefill (n730_cuda.cu:549-579, 847-870). */
+int n730_qgemm(void* qw, const float* d_x, int ldx, int tokens, float* d_y, int ldy, const float* d_bias,
+               const float* d_residual, int ldr, const float* d_norm_w, float eps, int swiglu, float* d_ws,
+               void* stream);
 /* Group-wise quantiser on the GPU (the converter's per-group rule):
  * d_w fp32 [rows, cols] -> packed codes, fp16 scales and zeros [rows, cols/group]. */
 int n730_quantize_grouped(const float* d_w, int rows, int cols, int bits, int group, uint8_t* d_codes,

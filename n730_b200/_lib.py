@@ -57,6 +57,7 @@ _CUDA_SIGS = {
     "n730_embed": ([vp, vp, i32, vp, vp], i32),
     "n730_qlinear": ([vp, vp, i32, i32, vp, i32, vp, vp, i32, vp, f32, i32, vp], i32),
     "n730_quantize_grouped": ([vp, i32, i32, i32, i32, vp, vp, vp, vp], i32),
+    "n730_qgemm": ([vp, vp, i32, i32, vp, i32, vp, vp, i32, vp, f32, i32, vp, vp], i32),
     "n730_attention_forward_noalloc": ([vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, vp], i32),
 }
 

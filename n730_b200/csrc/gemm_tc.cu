@@ -1,0 +1,323 @@
+// Prefill / batched GEMM on the 5th-generation tensor cores (tcgen05 + TMEM).
+//
+// Y[T x N] = X[T x K] . dequant(W)[N x K]^T for INT4 group-wise weights held in
+// the fragment-tiled layout of the decode GEMV (no second copy of the weights),
+// with the decoder's epilogues: bias, residual add (in place), SwiGLU of
+// interleaved gate/up rows, and RMSNorm folded into the A operand.
+//
+// One CTA computes a 128-token x 128-row output tile over K in steps of 64:
+//  * all 8 warps stage the step's A tile (x, normalised, rounded to fp16) and
+//    B tile (codes -> (q - z) * s in fp32 -> fp16) into shared memory in the
+//    K-major, 128-byte-swizzled layout the UMMA shared-memory descriptors
+//    read (8-row x 128-byte atoms, 16-byte chunk c of row r at c ^ (r % 8));
+//  * one thread issues four tcgen05.mma.kind::f16 (M 128, N 128, K 16, fp32
+//    accumulate in tensor memory) and a tcgen05.commit that frees the stage
+//    when those MMAs have read it; the next step's staging overlaps them
+//    (2 stages);
+//  * after the last step the accumulator is read back with tcgen05.ld
+//    (32 lanes x 32 columns per warp and instruction) and written with the
+//    epilogue.
+// Every mbarrier wait is bounded (%globaltimer, 2 s); a wait that runs out sets
+// the device error word, stops issuing, waits (bounded) for the MMAs in
+// flight, and still frees the tensor memory.
+// Numerics: dequantised weights and x rounded to fp16 (relative 2^-11 each),
+// fp32 accumulation.
+#include <algorithm>
+
+#include "mma_gemv.cuh"
+#include "qweight.h"
+
+namespace n730 {
+
+constexpr int TC_BM = 128, TC_BN = 128, TC_BK = 64, TC_STAGES = 2, TC_THREADS = 256;
+constexpr int TC_TILE = TC_BM * TC_BK * 2;  // bytes of one fp16 operand tile (A or B)
+constexpr uint32_t TC_TMEM_COLS = 128;      // fp32 accumulator columns (N)
+
+struct TcArgs {
+  const uint8_t* blob;  // fragment tiles: group u = tile*G + g at u * (kpg*128 + 64)
+  int rows, cols, G, kpg;
+  const float* x; int ldx; int T;
+  const float* inv_rms;  // [T] per-token 1/rms, or null (no norm)
+  const float* norm_w;   // [cols]
+  float* y; int ldy;
+  const float* bias;
+  const float* residual; int ldr;
+  int swiglu;
+  int* err;
+};
+
+// UMMA shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row x 128 B
+// atoms stacked every 1024 B along M/N.
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);  // start address, 16-byte units
+  d |= (uint64_t)1 << 16;                            // leading byte offset (not used by swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;                  // stride byte offset: next 8-row atom
+  d |= (uint64_t)1 << 46;                            // descriptor version
+  d |= (uint64_t)2 << 61;                            // swizzle: 128 B
+  return d;
+}
+
+// kind::f16 instruction descriptor: D fp32, A = B = fp16, both K-major, N = 128, M = 128.
+constexpr uint32_t TC_IDESC = (1u << 4) | ((uint32_t)(TC_BN >> 3) << 17) | ((uint32_t)(TC_BM >> 4) << 24);
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+  asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+               " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}"
+               :: "r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(TC_IDESC), "r"(accumulate) : "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+               :: "r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void tc_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+               "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                 "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+                 "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+                 "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+                 "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+               : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// byte offset of element (row r, column k) in a K-major 128B-swizzled tile (64 fp16 per row)
+__device__ __forceinline__ uint32_t sw128(int r, int k) {
+  return (uint32_t)(r * 128 + ((((k >> 3) ^ (r & 7)) & 7) << 4) + ((k & 7) << 1));
+}
+
+__global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_kernel(const TcArgs p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* As = smem;                                 // [STAGES][TC_TILE]
+  uint8_t* Bs = smem + TC_STAGES * TC_TILE;           // [STAGES][TC_TILE]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(Bs + TC_STAGES * TC_TILE);  // empty[STAGES], done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + TC_STAGES + 1);
+  int* flag = reinterpret_cast<int*>(tmem_slot + 1);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int n0 = blockIdx.x * TC_BN, m0 = blockIdx.y * TC_BM;
+  const int GB = p.kpg * 128 + 64;
+  const int n_tiles = (p.rows + 15) >> 4;
+
+  if (tid == 0) {
+    for (int s = 0; s <= TC_STAGES; ++s) mbar_init(&bars[s], 1);
+    fence_mbar_init();
+    *flag = 0;
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                 :: "r"(smem_u32(tmem_slot)), "r"(TC_TMEM_COLS) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  const int KT = p.cols / TC_BK;
+  int issued = 0;  // k-steps whose MMAs were issued (thread 0)
+  for (int kt = 0; kt < KT; ++kt) {
+    const int s = kt % TC_STAGES;
+    if (kt >= TC_STAGES) {  // the MMAs that read this stage last must be done
+      if (tid == 0 && !wait_bar(&bars[s], (uint32_t)(((kt / TC_STAGES) - 1) & 1))) {
+        atomicExch(p.err, DEV_ERR_TIMEOUT);
+        *flag = 1;
+      }
+      __syncthreads();
+      if (*flag) break;
+    }
+    uint8_t* as = As + s * TC_TILE;
+    uint8_t* bs = Bs + s * TC_TILE;
+    // ---- A: x rows m0.., columns kt*64.., (RMS-normalised) to fp16 ----
+    for (int i = tid; i < TC_BM * 8; i += TC_THREADS) {
+      const int r = i >> 3, c8 = i & 7, tok = m0 + r, k = kt * TC_BK + c8 * 8;
+      uint4 pk = make_uint4(0u, 0u, 0u, 0u);
+      if (tok < p.T) {
+        const float4* src = reinterpret_cast<const float4*>(p.x + (int64_t)tok * p.ldx + k);
+        float4 a = src[0], b = src[1];
+        if (p.inv_rms) {
+          const float iv = p.inv_rms[tok];
+          const float4* nw = reinterpret_cast<const float4*>(p.norm_w + k);
+          const float4 na = nw[0], nb = nw[1];
+          a.x *= iv * na.x; a.y *= iv * na.y; a.z *= iv * na.z; a.w *= iv * na.w;
+          b.x *= iv * nb.x; b.y *= iv * nb.y; b.z *= iv * nb.z; b.w *= iv * nb.w;
+        }
+        pk = make_uint4(h2u(__floats2half2_rn(a.x, a.y)), h2u(__floats2half2_rn(a.z, a.w)),
+                        h2u(__floats2half2_rn(b.x, b.y)), h2u(__floats2half2_rn(b.z, b.w)));
+      }
+      *reinterpret_cast<uint4*>(as + r * 128 + ((c8 ^ (r & 7)) << 4)) = pk;
+    }
+    // ---- B: rows n0.. from the fragment tiles: warp w = row tile, lane = fragment lane ----
+    {
+      const int tile = (n0 >> 4) + warp;
+      const int s0 = kt * 4, gi = s0 / p.kpg, s4 = (s0 % p.kpg) >> 2;
+      const int r0 = warp * 16 + (lane >> 2), r1 = r0 + 8;  // rows within the B tile
+      const int kb = 2 * (lane & 3);
+      if (tile < n_tiles) {
+        const uint8_t* grp = p.blob + ((int64_t)tile * p.G + gi) * GB;
+        const uint4 w4 = __ldg(reinterpret_cast<const uint4*>(grp + s4 * 512 + lane * 16));
+        const uint2 szv = __ldg(reinterpret_cast<const uint2*>(grp + p.kpg * 128 + (lane >> 2) * 8));
+        const float2 sc = __half22float2(u2h(szv.x)), zp = __half22float2(u2h(szv.y));
+        const uint32_t wv[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t w = wv[j];
+          const int k0 = j * 16 + kb;
+          auto q = [&](int sh) { return (float)((w >> sh) & 15u); };
+          *reinterpret_cast<uint32_t*>(bs + sw128(r0, k0)) =
+              h2u(__floats2half2_rn((q(0) - zp.x) * sc.x, (q(16) - zp.x) * sc.x));
+          *reinterpret_cast<uint32_t*>(bs + sw128(r1, k0)) =
+              h2u(__floats2half2_rn((q(4) - zp.y) * sc.y, (q(20) - zp.y) * sc.y));
+          *reinterpret_cast<uint32_t*>(bs + sw128(r0, k0 + 8)) =
+              h2u(__floats2half2_rn((q(8) - zp.x) * sc.x, (q(24) - zp.x) * sc.x));
+          *reinterpret_cast<uint32_t*>(bs + sw128(r1, k0 + 8)) =
+              h2u(__floats2half2_rn((q(12) - zp.y) * sc.y, (q(28) - zp.y) * sc.y));
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int k0 = j * 16 + kb;
+          *reinterpret_cast<uint32_t*>(bs + sw128(r0, k0)) = 0u;
+          *reinterpret_cast<uint32_t*>(bs + sw128(r1, k0)) = 0u;
+          *reinterpret_cast<uint32_t*>(bs + sw128(r0, k0 + 8)) = 0u;
+          *reinterpret_cast<uint32_t*>(bs + sw128(r1, k0 + 8)) = 0u;
+        }
+      }
+    }
+    // generic-proxy shared-memory writes -> visible to the tensor core's (async proxy) reads
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t a0 = smem_u32(as), b0 = smem_u32(bs);
+#pragma unroll
+      for (int j = 0; j < TC_BK / 16; ++j)  // K = 16 per MMA: 32 bytes along the swizzled row
+        tc_mma(tmem, umma_desc_sw128(a0 + j * 32), umma_desc_sw128(b0 + j * 32), (kt > 0 || j > 0) ? 1u : 0u);
+      tc_commit(&bars[s]);
+      ++issued;
+    }
+  }
+  // all MMAs issued so far complete -> done barrier
+  if (tid == 0) {
+    if (issued > 0) {
+      tc_commit(&bars[TC_STAGES]);
+      if (!wait_bar(&bars[TC_STAGES], 0)) {
+        atomicExch(p.err, DEV_ERR_TIMEOUT);
+        *flag = 1;
+      }
+    } else {
+      *flag = 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (!*flag) {
+    // ---- epilogue: warp w reads TMEM lanes 32*(w%4).. (tokens), columns 64*(w/4).. (rows) ----
+    const int qd = warp & 3, half = warp >> 2;
+    const int m = qd * 32 + lane, tok = m0 + m;
+#pragma unroll 1
+    for (int c = 0; c < 2; ++c) {
+      const int col0 = half * 64 + c * 32;
+      float v[32];
+      tc_ld32(tmem + ((uint32_t)(qd * 32) << 16) + (uint32_t)col0, v);
+      if (tok < p.T) {
+        if (p.swiglu) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            const int n = n0 + col0 + i;
+            if (n + 1 < p.rows) {
+              const float gt = v[i] + (p.bias ? p.bias[n] : 0.f);
+              const float up = v[i + 1] + (p.bias ? p.bias[n + 1] : 0.f);
+              p.y[(int64_t)tok * p.ldy + (n >> 1)] = (gt / (1.0f + expf(-gt))) * up;
+            }
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int n = n0 + col0 + i;
+            if (n < p.rows) {
+              float o = v[i] + (p.bias ? p.bias[n] : 0.f);
+              if (p.residual) o += p.residual[(int64_t)tok * p.ldr + n];
+              p.y[(int64_t)tok * p.ldy + n] = o;
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(TC_TMEM_COLS) : "memory");
+}
+
+// per-token 1/rms of x [T][ldx] over K columns: one warp per token
+__global__ void inv_rms_kernel(const float* x, int ldx, int T, int K, float eps, float* out) {
+  const int tok = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (tok >= T) return;
+  const float* r = x + (int64_t)tok * ldx;
+  float ss = 0.f;
+  for (int k = lane * 4; k < K; k += 128) {
+    const float4 v = *reinterpret_cast<const float4*>(r + k);
+    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+  }
+  ss = warp_sum(ss);
+  if (lane == 0) out[tok] = rsqrtf(ss / K + eps);
+}
+
+int* gemv_err_word();
+
+constexpr size_t TC_SMEM = 1024 + 2 * TC_STAGES * TC_TILE + 64;
+
+// One-time kernel attribute set-up (call before any stream capture).
+int gemm_tc_prepare() {
+  static bool configured = false;
+  if (!configured) {
+    N730_CUDA(cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM));
+    configured = true;
+  }
+  return N730_OK;
+}
+
+bool gemm_tc_supported(const QWeight& w, int T) {
+  return w.layout == 1 && w.bits == 4 && w.cols % TC_BK == 0 && (w.group / 16) % 4 == 0 && T >= 1;
+}
+
+int gemm_tc_launch(const GemvArgs& a, float* inv_ws, cudaStream_t st) {
+  const QWeight& w = *a.w;
+  N730_REQUIRE(gemm_tc_supported(w, a.batch), N730_UNSUPPORTED, "gemm_tc: needs INT4 fragment tiles, K %% 64 == 0");
+  N730_REQUIRE(!a.swiglu || w.rows % 2 == 0, N730_BAD_ARG, "gemm_tc: swiglu needs even rows");
+  N730_REQUIRE(((uintptr_t)a.x & 15) == 0 && a.ldx % 4 == 0, N730_BAD_ARG, "gemm_tc: x must be 16-byte aligned");
+  N730_REQUIRE(!a.norm_w || (inv_ws && ((uintptr_t)a.norm_w & 15) == 0), N730_BAD_ARG,
+               "gemm_tc: RMSNorm needs a workspace of batch floats and 16-byte aligned weights");
+  int* err = gemv_err_word();
+  N730_REQUIRE(err, N730_OOM, "gemm_tc: error word allocation failed");
+  if (a.norm_w) {
+    inv_rms_kernel<<<(a.batch + 7) / 8, 256, 0, st>>>(a.x, a.ldx, a.batch, w.cols, a.eps, inv_ws);
+    N730_CHECK_LAUNCH();
+  }
+  TcArgs p = {};
+  p.blob = w.codes; p.rows = w.rows; p.cols = w.cols; p.G = w.n_groups; p.kpg = w.group / 16;
+  p.x = a.x; p.ldx = a.ldx; p.T = a.batch;
+  p.inv_rms = a.norm_w ? inv_ws : nullptr; p.norm_w = a.norm_w;
+  p.y = a.y; p.ldy = a.ldy; p.bias = a.bias; p.residual = a.residual; p.ldr = a.ldr; p.swiglu = a.swiglu;
+  p.err = err;
+  if (int rc = gemm_tc_prepare()) return rc;
+  const dim3 grid((w.rows + TC_BN - 1) / TC_BN, (a.batch + TC_BM - 1) / TC_BM);
+  gemm_tc_kernel<<<grid, TC_THREADS, TC_SMEM, st>>>(p);
+  N730_CHECK_LAUNCH();
+  return N730_OK;
+}
+
+}  // namespace n730

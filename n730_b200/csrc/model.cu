@@ -119,6 +119,7 @@ struct Model {
   float* delta = nullptr;        // [max(max_batch, max_prefill)][hidden]
   float* logits_all = nullptr;   // [tp][max_batch][vocab / tp]
   int vocab_l = 0;               // lm_head rows on this rank
+  float* rms_ws = nullptr;       // [max(max_batch, max_prefill)] per-token 1/rms for the tcgen05 GEMM
 
   template <typename T>
   int alloc(T** p, size_t n) {
@@ -319,6 +320,7 @@ static int plan_persistent(Model* m) {
 static int finalize(Model* m) {
   const N730ModelConfig& c = m->c;
   if (int rc = gemv_prepare()) return rc;
+  if (int rc = gemm_tc_prepare()) return rc;
   const int nl = c.layers;
   m->L.assign(nl, Layer{});
   auto W = [&](int l, int s) -> QWeight* {
@@ -461,6 +463,7 @@ static int finalize(Model* m) {
   if (int rc = m->alloc(&m->attn, (size_t)B * c.heads * c.head_dim)) return rc;
   if (int rc = m->alloc(&m->mlp, (size_t)B * c.ffn)) return rc;
   if (int rc = m->alloc(&m->logits, (size_t)B * c.vocab)) return rc;
+  if (int rc = m->alloc(&m->rms_ws, (size_t)std::max(B, c.max_prefill))) return rc;
   if (c.tp_size > 1) {
     if (int rc = m->alloc(&m->delta, (size_t)std::max(B, c.max_prefill) * c.hidden)) return rc;
     if (m->vocab_l != c.vocab)
@@ -482,12 +485,16 @@ static int finalize(Model* m) {
   return N730_OK;
 }
 
+// One linear for `batch` rows of x: the tcgen05 GEMM from GEMM_TC_MIN_TOKENS
+// rows on (weights read once per 128 rows), else the dequant-GEMV.
 static int gemv(Model* m, const QWeight* w, const float* x, int ldx, int batch, float* y, int ldy,
                 const float* bias, const float* resid, int ldr, const float* norm, int swiglu) {
   GemvArgs a = {};
   a.w = w; a.x = x; a.ldx = ldx; a.batch = batch; a.y = y; a.ldy = ldy; a.bias = bias;
   a.residual = resid; a.ldr = ldr; a.norm_w = norm; a.eps = m->c.rms_eps; a.swiglu = swiglu;
   a.pdl = m->c.use_pdl;
+  if (batch >= GEMM_TC_MIN_TOKENS && gemm_tc_supported(*w, batch) && !m->c.exact_gemv)
+    return gemm_tc_launch(a, m->rms_ws, m->st);
   return gemv_launch(a, m->st);
 }
 

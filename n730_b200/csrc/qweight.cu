@@ -429,6 +429,17 @@ N730_API int n730_qlinear(void* qw, const float* d_x, int ldx, int batch, float*
   return gemv_launch(a, (cudaStream_t)stream);
 }
 
+N730_API int n730_qgemm(void* qw, const float* d_x, int ldx, int tokens, float* d_y, int ldy, const float* d_bias,
+                        const float* d_residual, int ldr, const float* d_norm_w, float eps, int swiglu, float* d_ws,
+                        void* stream) {
+  if (!qw || !d_x || !d_y) return N730_NULL;
+  N730_REQUIRE(tokens >= 1, N730_BAD_ARG, "qgemm: tokens %d", tokens);
+  GemvArgs a = {};
+  a.w = (const QWeight*)qw; a.x = d_x; a.ldx = ldx; a.batch = tokens; a.y = d_y; a.ldy = ldy;
+  a.bias = d_bias; a.residual = d_residual; a.ldr = ldr; a.norm_w = d_norm_w; a.eps = eps; a.swiglu = swiglu;
+  return gemm_tc_launch(a, d_ws, (cudaStream_t)stream);
+}
+
 N730_API int n730_quantize_grouped(const float* d_w, int rows, int cols, int bits, int group,
                                    uint8_t* d_codes, uint16_t* d_scales16, uint16_t* d_zeros16,
                                    void* stream) {
