@@ -62,6 +62,8 @@ def _args():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (small profiling cases)")
+    ap.add_argument("--ffn-fuse", type=int, default=0, choices=[-1, 0, 1],
+                    help="persistent decode FFN: 0 auto, 1 one fused phase, -1 two GEMV phases")
     ap.add_argument("--workload", default="resident", choices=["resident", "streamed", "tp72b"],
                     help="streamed: 7B aggressive mixed quant (FFN INT2 g64, attention INT4 g128, lm_head INT8 "
                          "per channel), layer weights in pinned host memory, 2-layer prefetch, 1024-token prompt; "
@@ -261,7 +263,7 @@ def run_ours(a):
         shape = dataclasses.replace(shape, layers=a.layers)
     B, ctx = a.batch, a.ctx
     max_ctx = ctx + 2 * (a.warmup + a.steps) + 64  # device-side steps, then the e2e steps
-    eng = Engine(shape, max_ctx=max_ctx, max_batch=B, max_prefill=512)
+    eng = Engine(shape, max_ctx=max_ctx, max_batch=B, max_prefill=512, ffn_fuse=a.ffn_fuse)
     build_on_device(shape, "int4_g128", eng, seed=rank)
     eng.finalize()
     info = eng.info()
@@ -372,6 +374,8 @@ def run_ours(a):
             "config": {"workload": f"qwen2-7b-shape decoder ({shape.layers} layers), all linears INT4 g128 "
                                    f"(fp16 scale+zero), batch {B} decode after a {ctx}-token prefill, fp16 paged KV",
                        "batch": B, "ctx_start": ctx, "parallelism": f"replicas x{world}" if world > 1 else "single",
+                       "decode_path": ("persistent kernel" + (", FFN fused" if info["ffn_fused"] else "")
+                                       if persistent else "per-op kernels (graph)"),
                        "l2": "no flush: 3.76 GB of weights stream from HBM every step (L2 126 MB)"},
             "e2e": {"value": round(toks / t_e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
                     "d2h_bytes_per_step": 4 * B * shape.vocab},

@@ -161,6 +161,10 @@ typedef struct N730ModelConfig {
                             in pinned host memory and are copied into d + 1 HBM slots on a copy
                             stream, d layers ahead of the layer being computed (the reference's
                             N730Scheduler prefetch, scheduler.py:236-287, as host->HBM copies) */
+  int32_t ffn_fuse;      /* persistent decode: 0 runs gate|up and down_proj as ONE phase (each CTA owns
+                            whole FFN quant groups, down_proj partial sums reduced in a fixed order)
+                            when the down groups divide evenly over the SMs; 1 whenever the shapes
+                            allow it; -1 never (two GEMV phases) */
 } N730ModelConfig;
 
 /* weight slots (n730_model_set_qweight); EMBED/LMHEAD take layer = -1 */

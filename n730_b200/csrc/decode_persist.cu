@@ -48,6 +48,8 @@ constexpr int PD_MAXG = 8;         // query heads per KV head
 constexpr int PD_MAXSPLIT = 64;    // context splits per KV head
 constexpr int PD_ADDMAX = 512;     // epilogue addend rows (bias / residual) per CTA
 constexpr uint64_t PD_WAIT_NS = 200000000ull;  // grid-barrier wait limit (0.2 s)
+constexpr float PD_FIX = 4294967296.0f;          // 32.32 fixed point of the FFN accumulator
+constexpr float PD_UNFIX = 2.3283064365386963e-10f;
 
 // groups per chunk: ~4.2-4.6 KB per bulk copy
 __host__ __device__ constexpr int pd_gpc(int kpg) { return kpg == 4 ? 8 : kpg == 8 ? 4 : 2; }
@@ -105,6 +107,20 @@ __device__ bool pd_barrier(const PdArgs& a, int k, int* flag) {
   return *flag != 0;
 }
 
+// This CTA's row tiles [t0, t1) of weight-streaming phase P: an even share of
+// a GEMV's tiles, or for an FFN phase the gate|up tiles of the CTA's FFN
+// groups (2 kpg tiles of 8 interleaved gate/up channel pairs per group).
+__device__ __forceinline__ void pd_tiles(const PdPhase& P, int cta, int NC, int kpg, int& t0, int& t1) {
+  if (P.kind == PD_FFN) {
+    t0 = pd_rng(0, P.G2, cta, NC) * 2 * kpg;
+    t1 = pd_rng(0, P.G2, cta + 1, NC) * 2 * kpg;
+  } else {
+    const int T = (P.rows + 15) >> 4;
+    t0 = pd_rng(0, T, cta, NC);
+    t1 = pd_rng(0, T, cta + 1, NC);
+  }
+}
+
 // KV split geometry of this step (batch 1): ns splits per KV head of ppi pages.
 struct PdSplits { int pos, L, npages, ppi, ns, items; };
 __device__ __forceinline__ PdSplits pd_splits(const PdArgs& a) {
@@ -141,6 +157,7 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
   int* wcnt = reinterpret_cast<int*>(smem + a.misc_off);         // [16]
   int* flag = wcnt + 16;                                         // [16]
   float* red = reinterpret_cast<float*>(wcnt + 32);              // [32]
+  float* mloc = reinterpret_cast<float*>(smem + a.ffn_off);      // FFN: this CTA's SwiGLU channels
 
   const PdSplits sp = pd_splits(a);
   const AttnDims& d = a.d;
@@ -175,31 +192,63 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
     return a.n_phases;
   };
 
-  // ---- weight stream: this warp's chunks of every GEMV op, in op order ----
-  struct Cursor { int ph, u, end, gi, G; const uint8_t* blob; };
+  // ---- weight stream: this warp's chunks of every GEMV / FFN op, in op order ----
+  // sub 0: [tile][group] units of the phase's (gate|up) GEMV; sub 1: an FFN
+  // phase's down_proj units, whole row tiles [u, end) of the warp, each the
+  // CTA's nj groups from j0 (one bulk copy per tile).
+  struct Cursor { int ph, sub, u, end, gi, G, j0, nj; const uint8_t* blob; };
+  auto set_down = [&](Cursor& c, int ph) {
+    const PdPhase& P = a.phases[ph];
+    const int j0 = pd_rng(0, P.G2, cta, NC), j1 = pd_rng(0, P.G2, cta + 1, NC);
+    const int Td = (P.rows2 + 15) >> 4;
+    const int w0 = pd_rng(0, Td, warp, PD_WARPS), w1 = pd_rng(0, Td, warp + 1, PD_WARPS);
+    if (j0 == j1 || w0 == w1) return false;
+    c.ph = ph; c.sub = 1; c.u = w0; c.end = w1; c.gi = 0; c.G = P.G2; c.j0 = j0; c.nj = j1 - j0; c.blob = P.blob2;
+    return true;
+  };
   auto set_phase = [&](Cursor& c, int ph) {
     for (; ph < a.n_phases; ++ph) {
       const PdPhase& P = a.phases[ph];
-      if (P.kind != PD_GEMV) continue;
-      const int T = (P.rows + 15) >> 4;
-      const int c0 = pd_rng(0, T, cta, NC) * P.G, c1 = pd_rng(0, T, cta + 1, NC) * P.G;
+      if (P.kind != PD_GEMV && P.kind != PD_FFN) continue;
+      int t0, t1;
+      pd_tiles(P, cta, NC, KPG, t0, t1);
+      const int c0 = t0 * P.G, c1 = t1 * P.G;
       const int w0 = pd_rng(c0, c1, warp, PD_WARPS), w1 = pd_rng(c0, c1, warp + 1, PD_WARPS);
-      if (w0 < w1) { c.ph = ph; c.u = w0; c.end = w1; c.gi = w0 % P.G; c.G = P.G; c.blob = P.blob; return; }
+      if (w0 < w1) {
+        c.ph = ph; c.sub = 0; c.u = w0; c.end = w1; c.gi = w0 % P.G; c.G = P.G; c.j0 = 0; c.nj = 0; c.blob = P.blob;
+        return;
+      }
+      if (P.kind == PD_FFN && set_down(c, ph)) return;
     }
     c.ph = a.n_phases;
   };
   int issued = 0, consumed = 0;
-  Cursor prod{0, 0, 0, 0, 1, nullptr};
+  Cursor prod{0, 0, 0, 0, 0, 1, 0, 0, nullptr};
   auto issue_next = [&](int slot) {  // lane 0
     if (prod.ph >= a.n_phases) return;
+    uint8_t* dst = ring + (size_t)slot * a.ring_stride;
+    if (prod.sub == 1) {  // whole down tiles, nj groups each
+      const int n = min(max(1, GPC / prod.nj), prod.end - prod.u);
+      const uint32_t tb = (uint32_t)(prod.nj * GB);
+      mbar_arrive_expect_tx(&wb[slot], (uint32_t)n * tb);
+      for (int i = 0; i < n; ++i)
+        bulk_g2s(dst + (size_t)i * tb, prod.blob + ((int64_t)(prod.u + i) * prod.G + prod.j0) * GB, tb, &wb[slot]);
+      ++issued;
+      prod.u += n;
+      if (prod.u >= prod.end) set_phase(prod, prod.ph + 1);
+      return;
+    }
     const int n = min(min(GPC, prod.end - prod.u), prod.G - prod.gi);  // never crosses a row tile
     mbar_arrive_expect_tx(&wb[slot], (uint32_t)(n * GB));
-    bulk_g2s(ring + (size_t)slot * a.ring_stride, prod.blob + (int64_t)prod.u * GB, (uint32_t)(n * GB), &wb[slot]);
+    bulk_g2s(dst, prod.blob + (int64_t)prod.u * GB, (uint32_t)(n * GB), &wb[slot]);
     ++issued;
     prod.u += n;
     prod.gi += n;
     if (prod.gi == prod.G) prod.gi = 0;
-    if (prod.u >= prod.end) set_phase(prod, prod.ph + 1);
+    if (prod.u >= prod.end) {
+      if (a.phases[prod.ph].kind == PD_FFN && set_down(prod, prod.ph)) return;
+      set_phase(prod, prod.ph + 1);
+    }
   };
   if (lane == 0) {
     set_phase(prod, 0);
@@ -216,7 +265,7 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
   int bar_k = 0, attn_idx = 0;
   for (int ph = 0; ph < a.n_phases; ++ph) {
     const PdPhase& P = a.phases[ph];
-    if (P.kind == PD_GEMV && P.norm_w)  // constant: pull this thread's norm weights into L1 before the wait
+    if ((P.kind == PD_GEMV || P.kind == PD_FFN) && P.norm_w)  // constant: pull this thread's norm weights into L1 before the wait
       for (int i = tid; i < (P.cols >> 2); i += PD_THREADS) {
         const float* p = P.norm_w + (i >> 2) * 16 + 2 * (i & 3);
         asm volatile("prefetch.global.L1 [%0];" :: "l"(p));
@@ -395,10 +444,10 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
       continue;
     }
 
-    // ============================== GEMV ==============================
+    // ========================= GEMV (FFN: gate|up part) =========================
     const int K = P.cols, G = P.G;
-    const int T = (P.rows + 15) >> 4;
-    const int t0 = pd_rng(0, T, cta, NC), t1 = pd_rng(0, T, cta + 1, NC);
+    int t0, t1;
+    pd_tiles(P, cta, NC, KPG, t0, t1);
     const int c0 = t0 * G, c1 = t1 * G;
     const bool has_add = P.epi == PD_EPI_RESID || P.bias;
     uint4* xf = reinterpret_cast<uint4*>(work);                     // [ks_n/2][4 tq] x 2 k-steps
@@ -407,16 +456,35 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
       // one batch of loads: x (and norm weights), this CTA's residual / bias rows
       if (has_add) {
         const int r0 = t0 * 16, r1 = min(t1 * 16, P.rows);
-        for (int r = r0 + tid; r < r1; r += PD_THREADS)
-          addv[r - r0] = (P.epi == PD_EPI_RESID ? __ldcg(P.y + r) : 0.f) + (P.bias ? P.bias[r] : 0.f);
+        const bool fold = P.epi == PD_EPI_RESID && P.acc;  // h + acc is the residual; clear acc
+        for (int r = r0 + tid; r < r1; r += PD_THREADS) {
+          float h = P.epi == PD_EPI_RESID ? __ldcg(P.y + r) : 0.f;
+          if (fold) {
+            h += __ll2float_rn((long long)__ldcg(P.acc + r)) * PD_UNFIX;
+            P.acc[r] = 0ull;
+          }
+          addv[r - r0] = h + (P.bias ? P.bias[r] : 0.f);
+        }
       }
-      // x -> (RMS-normalised) fp16 B fragments and per-group sums of the fp16 x
+      // x = h + acc (an FFN phase's acc is its own output, not an input)
+      const unsigned long long* xacc = P.kind == PD_GEMV && P.epi != PD_EPI_RESID ? P.acc : nullptr;
+      // x -> (RMS-normalised) fp16 B fragments and per-group sums of the fp16 x.
+      // A group's KPG*4 items are consecutive, so for KPG <= 8 they sit in one
+      // warp (or half-warp) and Sx is a shuffle reduction of the rounded values.
       const int items = K >> 2;  // (k-step, tq) items of 4 values: k, k+1, k+8, k+9
       uint2* xf2 = reinterpret_cast<uint2*>(xf);
       auto put = [&](int i, float v0, float v1, float v2, float v3) {
         const int s = i >> 2, tqi = i & 3;
-        xf2[(((s >> 1) * 4 + tqi) << 1) + (s & 1)] =
-            make_uint2(h2u(__floats2half2_rn(v0, v1)), h2u(__floats2half2_rn(v2, v3)));
+        const __half2 h01 = __floats2half2_rn(v0, v1), h23 = __floats2half2_rn(v2, v3);
+        xf2[(((s >> 1) * 4 + tqi) << 1) + (s & 1)] = make_uint2(h2u(h01), h2u(h23));
+        const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+        return (f01.x + f01.y) + (f23.x + f23.y);
+      };
+      auto group_sum = [&](int i, float v) {  // all 32 lanes; lane 0 of the group writes
+        if (KPG > 8) return;
+#pragma unroll
+        for (int o = KPG * 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if ((lane & (KPG * 4 - 1)) == 0 && i < items) sx[i / (KPG * 4)] = v;
       };
       if (P.norm_w) {  // K <= PD_KNORM: the row stays in registers across the reduction
         float xv[PD_NREG][4];
@@ -429,43 +497,68 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
             const float2 v0 = __ldcg(reinterpret_cast<const float2*>(P.x + k));
             const float2 v1 = __ldcg(reinterpret_cast<const float2*>(P.x + k + 8));
             xv[j][0] = v0.x; xv[j][1] = v0.y; xv[j][2] = v1.x; xv[j][3] = v1.y;
-            ss += v0.x * v0.x + v0.y * v0.y + v1.x * v1.x + v1.y * v1.y;
+            if (xacc) {
+              const ulonglong2 a0 = __ldcg(reinterpret_cast<const ulonglong2*>(xacc + k));
+              const ulonglong2 a1 = __ldcg(reinterpret_cast<const ulonglong2*>(xacc + k + 8));
+              xv[j][0] += __ll2float_rn((long long)a0.x) * PD_UNFIX;
+              xv[j][1] += __ll2float_rn((long long)a0.y) * PD_UNFIX;
+              xv[j][2] += __ll2float_rn((long long)a1.x) * PD_UNFIX;
+              xv[j][3] += __ll2float_rn((long long)a1.y) * PD_UNFIX;
+            }
+            ss += xv[j][0] * xv[j][0] + xv[j][1] * xv[j][1] + xv[j][2] * xv[j][2] + xv[j][3] * xv[j][3];
           }
         }
         const float inv = rsqrtf(block_sum(ss, red) / K + a.eps);
 #pragma unroll
         for (int j = 0; j < PD_NREG; ++j) {
           const int i = tid + j * PD_THREADS;
+          float sv = 0.f;
           if (i < items) {  // norm weights were prefetched into L1 before the barrier
             const int k = (i >> 2) * 16 + 2 * (i & 3);
             const float2 n0 = *reinterpret_cast<const float2*>(P.norm_w + k);
             const float2 n1 = *reinterpret_cast<const float2*>(P.norm_w + k + 8);
-            put(i, xv[j][0] * inv * n0.x, xv[j][1] * inv * n0.y, xv[j][2] * inv * n1.x, xv[j][3] * inv * n1.y);
+            sv = put(i, xv[j][0] * inv * n0.x, xv[j][1] * inv * n0.y, xv[j][2] * inv * n1.x, xv[j][3] * inv * n1.y);
           }
+          if (j * PD_THREADS < items) group_sum(i, sv);
         }
       } else {
 #pragma unroll 4
-        for (int i = tid; i < items; i += PD_THREADS) {
-          const int k = (i >> 2) * 16 + 2 * (i & 3);
-          const float2 v0 = __ldcg(reinterpret_cast<const float2*>(P.x + k));
-          const float2 v1 = __ldcg(reinterpret_cast<const float2*>(P.x + k + 8));
-          put(i, v0.x, v0.y, v1.x, v1.y);
+        for (int b = 0; b < items; b += PD_THREADS) {
+          const int i = b + tid;
+          float sv = 0.f;
+          if (i < items) {
+            const int k = (i >> 2) * 16 + 2 * (i & 3);
+            float2 v0 = __ldcg(reinterpret_cast<const float2*>(P.x + k));
+            float2 v1 = __ldcg(reinterpret_cast<const float2*>(P.x + k + 8));
+            if (xacc) {
+              const ulonglong2 a0 = __ldcg(reinterpret_cast<const ulonglong2*>(xacc + k));
+              const ulonglong2 a1 = __ldcg(reinterpret_cast<const ulonglong2*>(xacc + k + 8));
+              v0.x += __ll2float_rn((long long)a0.x) * PD_UNFIX;
+              v0.y += __ll2float_rn((long long)a0.y) * PD_UNFIX;
+              v1.x += __ll2float_rn((long long)a1.x) * PD_UNFIX;
+              v1.y += __ll2float_rn((long long)a1.y) * PD_UNFIX;
+            }
+            sv = put(i, v0.x, v0.y, v1.x, v1.y);
+          }
+          group_sum(i, sv);
         }
       }
       __syncthreads();
-      for (int grp = tid; grp < G; grp += PD_THREADS) {
-        const uint4* src = xf + (size_t)grp * (KPG >> 1) * 4;
-        float v = 0.f;
+      if (KPG > 8) {  // a group spans two warps: sum its fp16 x from shared memory
+        for (int grp = tid; grp < G; grp += PD_THREADS) {
+          const uint4* src = xf + (size_t)grp * (KPG >> 1) * 4;
+          float v = 0.f;
 #pragma unroll 4
-        for (int e = 0; e < KPG * 2; ++e) {
-          const uint4 u = src[e];
-          const float2 f0 = __half22float2(u2h(u.x)), f1 = __half22float2(u2h(u.y));
-          const float2 f2 = __half22float2(u2h(u.z)), f3 = __half22float2(u2h(u.w));
-          v += ((f0.x + f0.y) + (f1.x + f1.y)) + ((f2.x + f2.y) + (f3.x + f3.y));
+          for (int e = 0; e < KPG * 2; ++e) {
+            const uint4 u = src[e];
+            const float2 f0 = __half22float2(u2h(u.x)), f1 = __half22float2(u2h(u.y));
+            const float2 f2 = __half22float2(u2h(u.z)), f3 = __half22float2(u2h(u.w));
+            v += ((f0.x + f0.y) + (f1.x + f1.y)) + ((f2.x + f2.y) + (f3.x + f3.y));
+          }
+          sx[grp] = v;
         }
-        sx[grp] = v;
+        __syncthreads();
       }
-      __syncthreads();
     }
 
     // epilogue of the 16 rows of tile t (all 32 lanes; lane r < 16 holds row t*16 + r)
@@ -475,7 +568,11 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
       if (in && has_add) v += addv[row - t0 * 16];
       if (P.epi == PD_EPI_SWIGLU) {
         const float up = __shfl_down_sync(0xffffffffu, v, 1);
-        if (in && !(lane & 1)) P.y[row >> 1] = (v / (1.0f + expf(-v))) * up;
+        if (in && !(lane & 1)) {
+          const float m = (v / (1.0f + expf(-v))) * up;
+          if (P.kind == PD_FFN) mloc[(row >> 1) - t0 * 8] = m;
+          else P.y[row >> 1] = m;
+        }
       } else if (in) {
         P.y[row] = v;
       }
@@ -546,6 +643,77 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
         }
       tile_out(tt, v);
     }
+    if (P.kind != PD_FFN) continue;
+
+    // ============ FFN: down_proj partial sums over this CTA's channels ============
+    __syncthreads();  // every SwiGLU channel of the CTA is in mloc
+    const int j0 = pd_rng(0, P.G2, cta, NC), nj = pd_rng(0, P.G2, cta + 1, NC) - j0;
+    if (nj == 0) continue;
+    {
+      const int items = nj * KPG * 4;  // (k-step, tq) items of the nj groups
+      uint2* xf2 = reinterpret_cast<uint2*>(xf);
+      for (int i = tid; i < items; i += PD_THREADS) {
+        const int s = i >> 2, tqi = i & 3, k = s * 16 + 2 * tqi;
+        xf2[(((s >> 1) * 4 + tqi) << 1) + (s & 1)] =
+            make_uint2(h2u(__floats2half2_rn(mloc[k], mloc[k + 1])), h2u(__floats2half2_rn(mloc[k + 8], mloc[k + 9])));
+      }
+      __syncthreads();
+      for (int grp = tid; grp < nj; grp += PD_THREADS) {
+        const uint4* src = xf + (size_t)grp * (KPG >> 1) * 4;
+        float v = 0.f;
+        for (int e = 0; e < KPG * 2; ++e) {
+          const uint4 u = src[e];
+          const float2 f0 = __half22float2(u2h(u.x)), f1 = __half22float2(u2h(u.y));
+          const float2 f2 = __half22float2(u2h(u.z)), f3 = __half22float2(u2h(u.w));
+          v += ((f0.x + f0.y) + (f1.x + f1.y)) + ((f2.x + f2.y) + (f3.x + f3.y));
+        }
+        sx[grp] = v;
+      }
+      __syncthreads();
+    }
+    const int Td = (P.rows2 + 15) >> 4;
+    const int d0 = pd_rng(0, Td, warp, PD_WARPS), d1 = pd_rng(0, Td, warp + 1, PD_WARPS);
+    const int per = max(1, GPC / nj);  // whole tiles per chunk
+    auto put_rows = [&](int t, float r_g, float r_g8) {  // fixed-point sums: order-independent
+      const int r = t * 16 + g;
+      if (tq == 0) {
+        if (r < P.rows2) atomicAdd(P.acc + r, (unsigned long long)__float2ll_rn(r_g * PD_FIX));
+        if (r + 8 < P.rows2) atomicAdd(P.acc + r + 8, (unsigned long long)__float2ll_rn(r_g8 * PD_FIX));
+      }
+    };
+    for (int u = d0; u < d1 && !wfail;) {
+      const int n = min(per, d1 - u);
+      const int slot = consumed % PD_RING;
+      int okl = 0;
+      if (lane == 0) okl = wait_bar(&wb[slot], (uint32_t)((consumed / PD_RING) & 1));
+      if (!__shfl_sync(0xffffffffu, okl, 0)) {
+        if (lane == 0) { atomicExch(&a.sync[2], 1); atomicExch(a.err, DEV_ERR_TIMEOUT); }
+        wfail = true;
+        break;
+      }
+      const uint8_t* buf = ring + (size_t)slot * a.ring_stride;
+      if (nj == 1 && n == GPC) {
+        float acc4[GPC][4];
+#pragma unroll
+        for (int i = 0; i < GPC; ++i) acc4[i][0] = acc4[i][1] = acc4[i][2] = acc4[i][3] = 0.f;
+        mma_units<KPG, GPC>(buf, lane, xf + tq, sx[0], acc4);
+#pragma unroll
+        for (int i = 0; i < GPC; ++i) put_rows(u + i, acc4[i][0], acc4[i][2]);
+      } else {
+        for (int i = 0; i < n; ++i) {
+          float acc1[1][4] = {{0.f, 0.f, 0.f, 0.f}};
+          for (int jj = 0; jj < nj; ++jj) {
+            const uint4* xg[1] = {xf + jj * KPG * 2 + tq};
+            mma_chunk<KPG, 1, 1, true, 1>(buf + (size_t)(i * nj + jj) * GB, lane, xg, sx + jj, acc1);
+          }
+          put_rows(u + i, acc1[0][0], acc1[0][2]);
+        }
+      }
+      ++consumed;
+      __syncwarp();
+      if (lane == 0) issue_next(slot);
+      u += n;
+    }
   }
 
   // copies still in flight (abort path) are waited for, bounded, before exit
@@ -554,9 +722,14 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
   if (tid == 0)
     for (; kv_waited < kv_uses; ++kv_waited) wait_bar(kvbar, (uint32_t)(kv_waited & 1));
   __syncthreads();
-  if (tid == 0) {  // the last CTA out resets the counters for the next launch
+  if (tid == 0) {  // the last CTA out resets the counters and the FFN accumulator for the next launch
     __threadfence();
-    if (atomicAdd(&a.sync[1], 1) == NC - 1) {
+    flag[2] = atomicAdd(&a.sync[1], 1) == NC - 1;
+  }
+  __syncthreads();
+  if (flag[2]) {
+    for (int i = tid; i < a.acc_n; i += PD_THREADS) a.acc[i] = 0ull;
+    if (tid == 0) {
       for (int h = 0; h < d.n_kv; ++h) a.attn_cnt[h] = 0;
       a.sync[0] = 0;
       a.sync[2] = 0;
@@ -611,15 +784,26 @@ int persist_plan(const PdPhase* ph, int n, int head_dim, int group_q, int page_s
   N730_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   N730_CUDA(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev));
   if (!coop) return N730_UNSUPPORTED;
-  int kpg = 0, kmax = 0, gmax = 0;
+  int kpg = 0, kmax = 0, gmax = 0, ffn_floats = 0;
   for (int i = 0; i < n; ++i) {
-    if (ph[i].kind != PD_GEMV) continue;
+    if (ph[i].kind != PD_GEMV && ph[i].kind != PD_FFN) continue;
     const int k = ph[i].cols / ph[i].G / 16;
     if (ph[i].cols % 64 || (ph[i].norm_w && ph[i].cols > PD_KNORM) || (kpg && k != kpg) ||
         !(k == 4 || k == 8 || k == 16))
       return N730_UNSUPPORTED;
     if (ph[i].epi == PD_EPI_SWIGLU && ph[i].rows % 2) return N730_UNSUPPORTED;
-    const int tiles_per_cta = ((ph[i].rows + 15) / 16 + sms - 1) / sms;
+    int tiles_per_cta = ((ph[i].rows + 15) / 16 + sms - 1) / sms;
+    if (ph[i].kind == PD_FFN) {
+      // gate|up rows interleave the down_proj input channels; whole down groups per CTA
+      const int nj = (ph[i].G2 + sms - 1) / sms;
+      if (ph[i].epi != PD_EPI_SWIGLU || ph[i].rows != 2 * ph[i].cols2 || ph[i].cols2 != ph[i].G2 * 16 * k ||
+          nj > PD_FFN_MAXG || nj > pd_gpc(k) || nj * 16 * k > ph[i].cols || !ph[i].acc)
+        return N730_UNSUPPORTED;
+      tiles_per_cta = nj * 2 * k;
+      kmax = std::max(kmax, nj * 16 * k);
+      gmax = std::max(gmax, nj);
+      ffn_floats = std::max(ffn_floats, nj * 16 * k);
+    }
     if ((ph[i].epi == PD_EPI_RESID || ph[i].bias) && tiles_per_cta * 16 > PD_ADDMAX) return N730_UNSUPPORTED;
     kpg = k;
     kmax = std::max(kmax, ph[i].cols);
@@ -646,12 +830,21 @@ int persist_plan(const PdPhase* ph, int n, int head_dim, int group_q, int page_s
   off += round((size_t)PD_WARPS * 2 * 16 * 4);
   a.misc_off = (int)off;
   off += 64 * 4;
+  a.ffn_off = (int)round(off);
+  off = a.ffn_off + (size_t)ffn_floats * 4;
   plan->smem = round(off);
   if (plan->smem > 227 * 1024) return N730_UNSUPPORTED;
   a.d.head_dim = head_dim;
   if (int rc = persist_dispatch(*plan, head_dim, false, nullptr, &maxb)) return rc;
   if (maxb < 1) return N730_UNSUPPORTED;
   plan->grid = sms;
+  return N730_OK;
+}
+
+int persist_grid(int* grid) {
+  int dev = 0;
+  N730_CUDA(cudaGetDevice(&dev));
+  N730_CUDA(cudaDeviceGetAttribute(grid, cudaDevAttrMultiProcessorCount, dev));
   return N730_OK;
 }
 

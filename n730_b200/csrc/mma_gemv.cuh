@@ -114,4 +114,47 @@ __device__ __forceinline__ void mma_chunk(const uint8_t* buf, int lane, const ui
   }
 }
 
+// NU independent units (row tiles) of ONE group each, all against the same x
+// group (xb, xs): unit i sits at buf + i * GB and accumulates into acc[i]
+// (batch column 0 only: acc[i][0] row g, acc[i][2] row g+8).  The x
+// fragments are loaded once per k-step pair and shared by the NU chains.
+template <int KPG, int NU>
+__device__ __forceinline__ void mma_units(const uint8_t* buf, int lane, const uint4* xb, float xs,
+                                          float (&acc)[NU][4]) {
+  constexpr int GB = KPG * 128 + 64;
+  constexpr uint32_t MAGIC = 0x64006400u;
+  const int g = lane >> 2;
+  float cg[NU][4];
+#pragma unroll
+  for (int kk = 0; kk < KPG; kk += 4) {
+    const uint4 bx0 = xb[(kk >> 1) * 4], bx1 = xb[((kk >> 1) + 1) * 4];
+    uint4 w4[NU];
+#pragma unroll
+    for (int i = 0; i < NU; ++i)
+      w4[i] = *reinterpret_cast<const uint4*>(buf + i * GB + lane * 16 + (kk >> 2) * 512);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint4 v = (j >> 1) ? bx1 : bx0;
+      const uint32_t b0 = (j & 1) ? v.z : v.x, b1 = (j & 1) ? v.w : v.y;
+#pragma unroll
+      for (int i = 0; i < NU; ++i) {
+        const uint32_t w = j == 0 ? w4[i].x : j == 1 ? w4[i].y : j == 2 ? w4[i].z : w4[i].w, ws = w >> 8;
+        const uint32_t a0 = lop3_and_or(w, 0x000F000Fu, MAGIC);
+        const uint32_t a1 = lop3_and_or(w, 0x00F000F0u, MAGIC);
+        const uint32_t a2 = lop3_and_or(ws, 0x000F000Fu, MAGIC);
+        const uint32_t a3 = lop3_and_or(ws, 0x00F000F0u, MAGIC);
+        if (kk == 0 && j == 0) mma16816_z(cg[i], a0, a1, a2, a3, b0, b1);
+        else                   mma16816(cg[i], a0, a1, a2, a3, b0, b1);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < NU; ++i) {
+    const uint2 szv = *reinterpret_cast<const uint2*>(buf + i * GB + KPG * 128 + g * 8);
+    const float2 sf = __half22float2(u2h(szv.x)), zf = __half22float2(u2h(szv.y));
+    acc[i][0] = fmaf(sf.x, cg[i][0], fmaf(-sf.x * (1024.f + zf.x), xs, acc[i][0]));
+    acc[i][2] = fmaf(sf.y * 0.0625f, cg[i][2], fmaf(-sf.y * (64.f + zf.y), xs, acc[i][2]));
+  }
+}
+
 }  // namespace n730

@@ -100,6 +100,7 @@ struct Model {
   int device = 0;
   // persistent batch-1 decode (decode_persist.cu)
   bool pd_ok = false;
+  bool pd_ffn_fused = false;     // the persistent step runs each FFN as one phase
   PdPlan pd;
   // layer streaming (stream_depth > 0): per-layer weight images in pinned host
   // memory, copied into HBM slots on `cst` ahead of use
@@ -120,6 +121,7 @@ struct Model {
   float* logits_all = nullptr;   // [tp][max_batch][vocab / tp]
   int vocab_l = 0;               // lm_head rows on this rank
   float* rms_ws = nullptr;       // [max(max_batch, max_prefill)] per-token 1/rms for the tcgen05 GEMM
+  unsigned long long* ffn_acc = nullptr;  // persistent decode, fused FFN: [hidden] down_proj sums (fixed point)
 
   template <typename T>
   int alloc(T** p, size_t n) {
@@ -271,6 +273,9 @@ static int plan_persistent(Model* m) {
   for (auto& y : m->L)
     if (!tiled(y.qkv) || !tiled(y.o) || !tiled(y.gate_up) || !tiled(y.down)) return N730_OK;
   if (!tiled(m->lm_head)) return N730_OK;
+  int grid = 0;
+  if (int r = persist_grid(&grid)) return r;
+  const int g_down = m->L[0].down->n_groups;
   std::vector<PdPhase> ph;
   auto gemv_phase = [&](const QWeight* w, const float* x, const float* norm, const float* bias, float* y, int epi) {
     PdPhase p = {};
@@ -278,20 +283,53 @@ static int plan_persistent(Model* m) {
     p.x = x; p.norm_w = norm; p.bias = bias; p.y = y;
     ph.push_back(p);
   };
-  for (auto& y : m->L) {
-    gemv_phase(y.qkv, m->x, y.ln1, y.qkv_bias, m->qkv, PD_EPI_STORE);
-    PdPhase at = {};
-    at.kind = PD_ATTN; at.kv = y.kv;
-    ph.push_back(at);
-    gemv_phase(y.o, m->attn, nullptr, y.o_bias, m->x, PD_EPI_RESID);
-    gemv_phase(y.gate_up, m->x, y.ln2, y.gate_up_bias, m->mlp, PD_EPI_SWIGLU);
-    gemv_phase(y.down, m->mlp, nullptr, y.down_bias, m->x, PD_EPI_RESID);
+  // Fused FFN: the residual stream is h (m->x) + acc between a layer's FFN and
+  // the next layer's o_proj, which folds acc into h and clears it; q|k|v and
+  // the lm_head read h + acc.  Layers without a bias on down_proj only.
+  auto build = [&](bool fuse) {
+    ph.clear();
+    unsigned long long* acc = fuse ? m->ffn_acc : nullptr;
+    for (auto& y : m->L) {
+      gemv_phase(y.qkv, m->x, y.ln1, y.qkv_bias, m->qkv, PD_EPI_STORE);
+      ph.back().acc = acc;
+      PdPhase at = {};
+      at.kind = PD_ATTN; at.kv = y.kv;
+      ph.push_back(at);
+      gemv_phase(y.o, m->attn, nullptr, y.o_bias, m->x, PD_EPI_RESID);
+      ph.back().acc = acc;
+      gemv_phase(y.gate_up, m->x, y.ln2, y.gate_up_bias, m->mlp, PD_EPI_SWIGLU);
+      if (fuse) {  // gate|up + down partial sums in one phase
+        PdPhase& f = ph.back();
+        f.kind = PD_FFN;
+        f.blob2 = y.down->codes; f.rows2 = y.down->rows; f.cols2 = y.down->cols; f.G2 = y.down->n_groups;
+        f.acc = acc;
+      } else {
+        gemv_phase(y.down, m->mlp, nullptr, y.down_bias, m->x, PD_EPI_RESID);
+      }
+    }
+    gemv_phase(m->lm_head, m->x, m->final_norm, nullptr, m->logits, PD_EPI_STORE);
+    ph.back().acc = acc;
+  };
+  bool has_down_bias = false;
+  for (auto& y : m->L) has_down_bias |= y.down_bias != nullptr;
+  bool fuse = !has_down_bias && (c.ffn_fuse > 0 || (c.ffn_fuse == 0 && g_down % grid == 0));
+  if (fuse && !m->ffn_acc) {
+    if (int r = m->alloc(&m->ffn_acc, (size_t)c.hidden)) return r;
+    N730_CUDA(cudaMemsetAsync(m->ffn_acc, 0, (size_t)c.hidden * 8, m->st));
   }
-  gemv_phase(m->lm_head, m->x, m->final_norm, nullptr, m->logits, PD_EPI_STORE);
   PdPlan plan;
-  const int rc = persist_plan(ph.data(), (int)ph.size(), c.head_dim, c.heads / c.kv_heads, c.page_size, &plan);
+  build(fuse);
+  int rc = persist_plan(ph.data(), (int)ph.size(), c.head_dim, c.heads / c.kv_heads, c.page_size, &plan);
+  if (rc == N730_UNSUPPORTED && fuse) {  // shapes outside the fused phase's limits: two GEMV phases
+    fuse = false;
+    build(false);
+    rc = persist_plan(ph.data(), (int)ph.size(), c.head_dim, c.heads / c.kv_heads, c.page_size, &plan);
+  }
   if (rc == N730_UNSUPPORTED) return N730_OK;
   if (rc) return rc;
+  m->pd_ffn_fused = fuse;
+  plan.a.acc = fuse ? m->ffn_acc : nullptr;
+  plan.a.acc_n = fuse ? c.hidden : 0;
   const int GQ = c.heads / c.kv_heads;
   const int max_split = std::min(64, plan.grid / c.kv_heads);
   if (max_split < 1) return N730_OK;
@@ -910,6 +948,7 @@ N730_API int n730_model_info(void* p, int64_t* info) {
   info[7] = m->pd_ok;
   info[8] = m->lm_head != m->embed ? bytes(m->embed) : 0;  // read one row per token, not streamed
   info[9] = m->streamed_bytes;                                // host->HBM bytes per forward pass
+  info[10] = m->pd_ffn_fused;
   return N730_OK;
 }
 

@@ -32,7 +32,7 @@ class N730ModelConfig(C.Structure):
                [("rms_eps", C.c_float), ("rope_theta", C.c_float)] + \
                [(n, C.c_int32) for n in ("max_ctx", "max_batch", "page_size", "max_prefill", "tie_embeddings",
                                          "tp_rank", "tp_size", "use_graphs", "use_pdl", "exact_gemv",
-                                         "per_op_decode", "stream_depth")]
+                                         "per_op_decode", "stream_depth", "ffn_fuse")]
 
 
 def _sigs(lib):
@@ -127,13 +127,13 @@ class Engine:
     def __init__(self, shape: ModelShape, max_ctx: int = 4096, max_batch: int = 1, page_size: int = 64,
                  max_prefill: int = 512, use_graphs: bool = True, use_pdl: bool = True,
                  tp_rank: int = 0, tp_size: int = 1, exact_gemv: bool = False, per_op_decode: bool = False,
-                 stream_depth: int = 0):
+                 stream_depth: int = 0, ffn_fuse: int = 0):
         self.lib = _sigs(_lib.cuda())
         self.shape = shape
         c = N730ModelConfig(shape.hidden, shape.layers, shape.heads, shape.kv_heads, shape.head_dim, shape.ffn,
                             shape.vocab, shape.rms_eps, shape.rope_theta, max_ctx, max_batch, page_size,
                             max_prefill, int(shape.tie_embeddings), tp_rank, tp_size, int(use_graphs),
-                            int(use_pdl), int(exact_gemv), int(per_op_decode), int(stream_depth))
+                            int(use_pdl), int(exact_gemv), int(per_op_decode), int(stream_depth), int(ffn_fuse))
         self.cfg = c
         self.h = C.c_void_p()
         _lib.check(self.lib.n730_model_create(C.byref(c), C.byref(self.h)), "model_create")
@@ -185,7 +185,7 @@ class Engine:
         _lib.check(self.lib.n730_model_info(self.h, a), "model_info")
         return {"weight_bytes": a[0], "kv_bytes_per_pos": a[1], "kv_capacity_bytes": a[2], "n_split": a[3],
                 "qkv_dim": a[4], "pages_per_seq": a[5], "persistent_decode": bool(a[7]),
-                "embed_bytes": a[8], "streamed_bytes": a[9]}
+                "embed_bytes": a[8], "streamed_bytes": a[9], "ffn_fused": bool(a[10])}
 
     @staticmethod
     def tp_unique_id() -> bytes:

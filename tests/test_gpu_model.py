@@ -105,14 +105,18 @@ def test_capacity_and_reset(model):
     e.close()
 
 
-def test_persistent_decode_matches_per_op(model):
-    """Batch-1 decode through the persistent kernel (all-INT4 models) and through
-    one kernel per op: both within the bar of the oracle, and close to each other."""
+@pytest.mark.parametrize("ffn_fuse", [1, -1])
+def test_persistent_decode_matches_per_op(model, ffn_fuse):
+    """Batch-1 decode through the persistent kernel (all-INT4 models; the FFN as
+    one gate|up + down-partials phase with a fixed-order reduction, or as two
+    GEMV phases) and through one kernel per op: both within the bar of the
+    oracle, and close to each other."""
     shape, blocks, w = model
-    ep = _engine(shape, blocks, max_batch=1)
+    ep = _engine(shape, blocks, max_batch=1, ffn_fuse=ffn_fuse)
     eo = _engine(shape, blocks, max_batch=1, per_op_decode=True)
     all_int4 = all(b.prec_id == 0x44 for _, b in blocks if b.cols > 1)
     assert ep.info()["persistent_decode"] == all_int4
+    assert ep.info()["ffn_fused"] == (all_int4 and ffn_fuse == 1)
     assert not eo.info()["persistent_decode"]
     orc = OracleDecoder(shape, w, max_pos=512)
     rng = np.random.default_rng(21)
@@ -136,6 +140,7 @@ def test_decode_deterministic(model):
     shape, blocks, _ = model
     for per_op in (False, True):
         _deterministic(_engine(shape, blocks, max_batch=1, per_op_decode=per_op), shape)
+    _deterministic(_engine(shape, blocks, max_batch=1, ffn_fuse=1), shape)
 
 
 def _deterministic(e, shape):
