@@ -166,6 +166,15 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
   const int kvh = has_item ? cta / sp.ns : 0, split = has_item ? cta % sp.ns : 0;
   const int pg0 = split * sp.ppi, pg1 = min(sp.npages, pg0 + sp.ppi);
 
+  // the phase table lives in shared memory: phase transitions read it on the
+  // critical path (producer cursor and every phase's prologue)
+  PdPhase* phs = reinterpret_cast<PdPhase*>(smem + a.tab_off);
+  {
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(a.phases);
+    uint32_t* dst = reinterpret_cast<uint32_t*>(phs);
+    const int words = a.n_phases * (int)(sizeof(PdPhase) / 4);
+    for (int i = tid; i < words; i += PD_THREADS) dst[i] = __ldg(src + i);
+  }
   if (tid < 16) wcnt[tid] = 0;
   if (lane == 0) {
     for (int r = 0; r < PD_RING; ++r) mbar_init(&wb[r], 1);
@@ -178,7 +187,7 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
   int kv_uses = 0;      // copies issued (thread 0)
   int kv_waited = 0;    // copies waited for (thread 0)
   auto kv_issue = [&](int ph, int p) {
-    const PdPhase& P = a.phases[ph];
+    const PdPhase& P = phs[ph];
     const int page = a.block_table[p];
     const int64_t off = ((int64_t)page * d.n_kv + kvh) * PD_PAGE * HD;
     mbar_arrive_expect_tx(kvbar, 2 * PAGE_BYTES);
@@ -188,7 +197,7 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
   };
   auto next_attn = [&](int ph) {
     for (; ph < a.n_phases; ++ph)
-      if (a.phases[ph].kind == PD_ATTN) return ph;
+      if (phs[ph].kind == PD_ATTN) return ph;
     return a.n_phases;
   };
 
@@ -198,7 +207,7 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
   // CTA's nj groups from j0 (one bulk copy per tile).
   struct Cursor { int ph, sub, u, end, gi, G, j0, nj; const uint8_t* blob; };
   auto set_down = [&](Cursor& c, int ph) {
-    const PdPhase& P = a.phases[ph];
+    const PdPhase& P = phs[ph];
     const int j0 = pd_rng(0, P.G2, cta, NC), j1 = pd_rng(0, P.G2, cta + 1, NC);
     const int Td = (P.rows2 + 15) >> 4;
     const int w0 = pd_rng(0, Td, warp, PD_WARPS), w1 = pd_rng(0, Td, warp + 1, PD_WARPS);
@@ -208,7 +217,7 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
   };
   auto set_phase = [&](Cursor& c, int ph) {
     for (; ph < a.n_phases; ++ph) {
-      const PdPhase& P = a.phases[ph];
+      const PdPhase& P = phs[ph];
       if (P.kind != PD_GEMV && P.kind != PD_FFN) continue;
       int t0, t1;
       pd_tiles(P, cta, NC, KPG, t0, t1);
@@ -246,7 +255,7 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
     prod.gi += n;
     if (prod.gi == prod.G) prod.gi = 0;
     if (prod.u >= prod.end) {
-      if (a.phases[prod.ph].kind == PD_FFN && set_down(prod, prod.ph)) return;
+      if (phs[prod.ph].kind == PD_FFN && set_down(prod, prod.ph)) return;
       set_phase(prod, prod.ph + 1);
     }
   };
@@ -264,7 +273,7 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
   bool wfail = false;
   int bar_k = 0, attn_idx = 0;
   for (int ph = 0; ph < a.n_phases; ++ph) {
-    const PdPhase& P = a.phases[ph];
+    const PdPhase& P = phs[ph];
     if ((P.kind == PD_GEMV || P.kind == PD_FFN) && P.norm_w)  // constant: pull this thread's norm weights into L1 before the wait
       for (int i = tid; i < (P.cols >> 2); i += PD_THREADS) {
         const float* p = P.norm_w + (i >> 2) * 16 + 2 * (i & 3);
@@ -274,7 +283,6 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
     if (ph > 0 && !pd_barrier(a, ++bar_k, flag)) break;
 
     if (P.kind == PD_ATTN) {
-      // ============================ attention ============================
       if (has_item) {
         __half* q_h = reinterpret_cast<__half*>(work);                              // [PD_MAXG][HD + 8]
         float* sc = reinterpret_cast<float*>(work + (size_t)PD_MAXG * (HD + 8) * 2);  // [PD_MAXG][PD_PAGE]
@@ -292,36 +300,48 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
           }
           __syncthreads();
           const int t0 = pg * PD_PAGE, n = min(PD_PAGE, sp.L - t0);
-          // one batch of loads: the RoPE'd, pre-scaled queries (fp16, rows >= GQ zero) and,
-          // in the split holding it, the new token's k (RoPE'd) and v, to the page and the cache
-          if (pg == pg0) {
-            for (int i = tid; i < PD_MAXG * HD; i += PD_THREADS) {
-              const int j = i / HD, dd = i - j * HD;
-              float v = 0.f;
-              if (j < GQ) {
+          // one batch of loads: the queries and, in the split holding it, the new
+          // token's k and v; then RoPE (queries pre-scaled, fp16, rows >= GQ zero),
+          // k and v to the page and the cache
+          {
+            constexpr int QI = (PD_MAXG * HD + PD_THREADS - 1) / PD_THREADS;
+            const bool first = pg == pg0, kv_here = t0 <= sp.pos && sp.pos < t0 + PD_PAGE && tid < HD;
+            float qa[QI], qb[QI], qc[QI], qs[QI];
+#pragma unroll
+            for (int r = 0; r < QI; ++r) {
+              const int i = tid + r * PD_THREADS, j = i / HD, dd = i - j * HD, j0 = dd < H2 ? dd : dd - H2;
+              qa[r] = qb[r] = qc[r] = qs[r] = 0.f;
+              if (first && i < PD_MAXG * HD && j < GQ) {
                 const float* qh = a.qkv + (int64_t)(kvh * GQ + j) * HD;
-                const int j0 = dd < H2 ? dd : dd - H2;
-                const float x0 = __ldcg(qh + j0), x1 = __ldcg(qh + j0 + H2), c = cs[j0], sv = sn[j0];
-                v = (dd < H2 ? x0 * c - x1 * sv : x1 * c + x0 * sv) * d.scale;
+                qa[r] = __ldcg(qh + j0); qb[r] = __ldcg(qh + j0 + H2); qc[r] = cs[j0]; qs[r] = sn[j0];
               }
-              q_h[j * (HD + 8) + dd] = __float2half_rn(v);
             }
-            if (tid < GQ) { ml[tid * 4 + 0] = -INFINITY; ml[tid * 4 + 1] = 0.f; }
-          }
-          if (t0 <= sp.pos && sp.pos < t0 + PD_PAGE) {
-            const int r = sp.pos - t0;
-            const float* kh = a.qkv + (int64_t)(d.n_heads + kvh) * HD;
-            const float* vh = a.qkv + (int64_t)(d.n_heads + d.n_kv + kvh) * HD;
-            const int64_t off = (((int64_t)a.block_table[pg] * d.n_kv + kvh) * PD_PAGE + r) * HD;
-            for (int dd = tid; dd < HD; dd += PD_THREADS) {
-              const int j0 = dd < H2 ? dd : dd - H2;
-              const float x0 = __ldcg(kh + j0), x1 = __ldcg(kh + j0 + H2), c = cs[j0], sv = sn[j0];
-              const __half kq = __float2half_rn(dd < H2 ? x0 * c - x1 * sv : x1 * c + x0 * sv);
-              const __half vq = __float2half_rn(__ldcg(vh + dd));
-              Ks[r * HD + dd] = kq;
-              Vs[r * HD + dd] = vq;
-              P.kv.k_pages[off + dd] = kq;
-              P.kv.v_pages[off + dd] = vq;
+            const int kd = tid < HD ? tid : 0, kj0 = kd < H2 ? kd : kd - H2;
+            float ka = 0.f, kb = 0.f, kc = 0.f, ks = 0.f, vv = 0.f;
+            if (kv_here) {
+              const float* kh = a.qkv + (int64_t)(d.n_heads + kvh) * HD;
+              const float* vh = a.qkv + (int64_t)(d.n_heads + d.n_kv + kvh) * HD;
+              ka = __ldcg(kh + kj0); kb = __ldcg(kh + kj0 + H2); kc = cs[kj0]; ks = sn[kj0]; vv = __ldcg(vh + kd);
+            }
+            if (first) {
+#pragma unroll
+              for (int r = 0; r < QI; ++r) {
+                const int i = tid + r * PD_THREADS, j = i / HD, dd = i - j * HD;
+                if (i < PD_MAXG * HD)
+                  q_h[j * (HD + 8) + dd] = __float2half_rn(
+                      (dd < H2 ? qa[r] * qc[r] - qb[r] * qs[r] : qb[r] * qc[r] + qa[r] * qs[r]) * d.scale);
+              }
+              if (tid < GQ) { ml[tid * 4 + 0] = -INFINITY; ml[tid * 4 + 1] = 0.f; }
+            }
+            if (kv_here) {
+              const int r = sp.pos - t0;
+              const int64_t off = (((int64_t)a.block_table[pg] * d.n_kv + kvh) * PD_PAGE + r) * HD;
+              const __half kq = __float2half_rn(kd < H2 ? ka * kc - kb * ks : kb * kc + ka * ks);
+              const __half vq = __float2half_rn(vv);
+              Ks[r * HD + kd] = kq;
+              Vs[r * HD + kd] = vq;
+              P.kv.k_pages[off + kd] = kq;
+              P.kv.v_pages[off + kd] = vq;
             }
           }
           for (int i = tid; i < (PD_PAGE - n) * (HD / 8); i += PD_THREADS)  // V rows past the context: 0
@@ -419,24 +439,29 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
             ov[i] = __ldcg(base_o + (size_t)s2 * GQ * HD + o);
           }
           __syncthreads();
-          if (tid < nj) {
+          // warp jj < nj: split weights e^(m_s - M) of query head j_lo + jj and their
+          // denominator; lanes stride over the splits, fixed-order warp reductions
+          if (warp < nj) {
             float M = -INFINITY;
-            for (int s2 = 0; s2 < sp.ns; ++s2) M = fmaxf(M, mv[tid * sp.ns + s2]);
+            for (int s2 = lane; s2 < sp.ns; s2 += 32) M = fmaxf(M, mv[warp * sp.ns + s2]);
+            M = warp_max(M);
             float den = 0.f;
-            for (int s2 = 0; s2 < sp.ns; ++s2) {
-              const float m = mv[tid * sp.ns + s2];
+            for (int s2 = lane; s2 < sp.ns; s2 += 32) {
+              const float m = mv[warp * sp.ns + s2];
               const float w = m == -INFINITY ? 0.f : __expf(m - M);
-              mv[tid * sp.ns + s2] = w;
-              den = fmaf(w, lv[tid * sp.ns + s2], den);
+              mv[warp * sp.ns + s2] = w;
+              den = fmaf(w, lv[warp * sp.ns + s2], den);
             }
-            ml[tid * 4 + 3] = den;
+            den = warp_sum(den);
+            if (lane == 0) ml[warp * 4 + 3] = den;
           }
           __syncthreads();
-          for (int oo = tid; oo < nout; oo += PD_THREADS) {
+          for (int oo = warp; oo < nout; oo += PD_WARPS) {  // one warp per output, lanes over splits
             const int o = o_lo + oo, jj = o / HD - j_lo;
             float num = 0.f;
-            for (int s2 = 0; s2 < sp.ns; ++s2) num = fmaf(mv[jj * sp.ns + s2], ov[oo * sp.ns + s2], num);
-            a.attn_out[(int64_t)kvh * no + o] = num / (ml[jj * 4 + 3] + 1e-9f);
+            for (int s2 = lane; s2 < sp.ns; s2 += 32) num = fmaf(mv[jj * sp.ns + s2], ov[oo * sp.ns + s2], num);
+            num = warp_sum(num);
+            if (lane == 0) a.attn_out[(int64_t)kvh * no + o] = num / (ml[jj * 4 + 3] + 1e-9f);
           }
         }
       }
@@ -832,6 +857,8 @@ int persist_plan(const PdPhase* ph, int n, int head_dim, int group_q, int page_s
   off += 64 * 4;
   a.ffn_off = (int)round(off);
   off = a.ffn_off + (size_t)ffn_floats * 4;
+  a.tab_off = (int)round(off);
+  off = a.tab_off + (size_t)n * sizeof(PdPhase);
   plan->smem = round(off);
   if (plan->smem > 227 * 1024) return N730_UNSUPPORTED;
   a.d.head_dim = head_dim;

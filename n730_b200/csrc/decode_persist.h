@@ -21,7 +21,7 @@ enum : int { PD_EPI_STORE = 0, PD_EPI_RESID = 1, PD_EPI_SWIGLU = 2 };
 // the same whatever order the CTAs arrive in).  The residual stream is then
 // h + acc: a later GEMV with a non-null `acc` reads x + acc (norm phases) or,
 // with the residual epilogue, folds acc into y and clears it.
-struct PdPhase {
+struct __align__(16) PdPhase {
   int kind, epi;
   const uint8_t* blob;
   int rows, cols, G;
@@ -34,6 +34,8 @@ struct PdPhase {
   int rows2, cols2, G2;
   unsigned long long* acc;  // FFN: down_proj sums (fixed point, 2^-32); GEMV: pending residual
 };
+
+static_assert(sizeof(PdPhase) % 16 == 0, "phase table rows are copied as words");
 
 struct PdArgs {
   const PdPhase* phases;
@@ -56,7 +58,7 @@ struct PdArgs {
   unsigned long long* acc;  // FFN accumulator [acc_n], cleared by the last CTA out
   int acc_n;
   // shared-memory layout (bytes)
-  int ring_off, ring_stride, work_off, kv_off, add_off, wpart_off, misc_off, ffn_off;
+  int ring_off, ring_stride, work_off, kv_off, add_off, wpart_off, misc_off, ffn_off, tab_off;
 };
 
 struct PdPlan {
