@@ -54,17 +54,10 @@ constexpr float PD_UNFIX = 2.3283064365386963e-10f;
 // groups per chunk: ~4.2-4.6 KB per bulk copy
 __host__ __device__ constexpr int pd_gpc(int kpg) { return kpg == 4 ? 8 : kpg == 8 ? 4 : 2; }
 
-// [lo, hi) split into n near-equal parts: start of part i
+// [lo, hi) split into n near-equal parts: start of part i.  32-bit unsigned
+// arithmetic (the planner bounds (hi - lo) * n below 2^31).
 __device__ __forceinline__ int pd_rng(int lo, int hi, int i, int n) {
-  return lo + (int)((int64_t)(hi - lo) * i / n);
-}
-// the part of [lo, hi) (split into n) that holds unit u
-__device__ __forceinline__ int pd_owner(int u, int lo, int hi, int n) {
-  int i = (int)((int64_t)(u - lo) * n / (hi - lo));
-  i = min(max(i, 0), n - 1);
-  while (i > 0 && pd_rng(lo, hi, i, n) > u) --i;
-  while (i < n - 1 && pd_rng(lo, hi, i + 1, n) <= u) ++i;
-  return i;
+  return lo + (int)((unsigned)(hi - lo) * (unsigned)i / (unsigned)n);
 }
 
 __device__ __forceinline__ int ld_acquire(const int* p) {
@@ -157,6 +150,7 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
   int* wcnt = reinterpret_cast<int*>(smem + a.misc_off);         // [16]
   int* flag = wcnt + 16;                                         // [16]
   float* red = reinterpret_cast<float*>(wcnt + 32);              // [32]
+  int* wr = wcnt + 64;                                           // [PD_WARPS + 1] unit ranges of a GEMV phase
   float* mloc = reinterpret_cast<float*>(smem + a.ffn_off);      // FFN: this CTA's SwiGLU channels
 
   const PdSplits sp = pd_splits(a);
@@ -474,6 +468,7 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
     int t0, t1;
     pd_tiles(P, cta, NC, KPG, t0, t1);
     const int c0 = t0 * G, c1 = t1 * G;
+    if (tid <= PD_WARPS) wr[tid] = pd_rng(c0, c1, tid, PD_WARPS);  // read after the prologue's barrier
     const bool has_add = P.epi == PD_EPI_RESID || P.bias;
     uint4* xf = reinterpret_cast<uint4*>(work);                     // [ks_n/2][4 tq] x 2 k-steps
     float* sx = reinterpret_cast<float*>(work + (size_t)K * 2);     // [G] (+8 pad)
@@ -603,7 +598,7 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
       }
     };
 
-    const int w0 = pd_rng(c0, c1, warp, PD_WARPS), w1 = pd_rng(c0, c1, warp + 1, PD_WARPS);
+    const int w0 = wr[warp], w1 = wr[warp + 1];
     float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
     int t = w0 / G, gi = w0 - t * G;  // current row tile, group within it
     for (int u = w0; u < w1 && !wfail;) {
@@ -648,9 +643,11 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
         continue;
       }
       // shared with other warps of the CTA: the last contributor sums them in warp order
-      const int wa = pd_owner(tu0, c0, c1, PD_WARPS), wz = pd_owner(tu1 - 1, c0, c1, PD_WARPS);
+      int wa = warp, wz = warp;  // warps whose ranges meet the tile (wr[] is ascending)
+      while (wa > 0 && wr[wa] > tu0) --wa;
+      while (wz < PD_WARPS - 1 && wr[wz + 1] < tu1) ++wz;
       int contrib = 0;
-      for (int w = wa; w <= wz; ++w) contrib += pd_rng(c0, c1, w, PD_WARPS) < pd_rng(c0, c1, w + 1, PD_WARPS);
+      for (int w = wa; w <= wz; ++w) contrib += wr[w] < wr[w + 1];
       __threadfence_block();
       int last = 0;
       if (lane == 0) last = atomicAdd(&wcnt[wa], 1) == contrib - 1;
@@ -661,8 +658,8 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
       float v = 0.f;
       if (lane < 16)
         for (int w = wa; w <= wz; ++w) {
-          const int ws0 = pd_rng(c0, c1, w, PD_WARPS);
-          if (ws0 == pd_rng(c0, c1, w + 1, PD_WARPS)) continue;
+          const int ws0 = wr[w];
+          if (ws0 == wr[w + 1]) continue;
           const int sd = (tt == ws0 / G) ? 0 : 1;
           v += *reinterpret_cast<volatile float*>(wpart + (w * 2 + sd) * 16 + lane);
         }
@@ -818,6 +815,7 @@ int persist_plan(const PdPhase* ph, int n, int head_dim, int group_q, int page_s
       return N730_UNSUPPORTED;
     if (ph[i].epi == PD_EPI_SWIGLU && ph[i].rows % 2) return N730_UNSUPPORTED;
     int tiles_per_cta = ((ph[i].rows + 15) / 16 + sms - 1) / sms;
+    if ((int64_t)((ph[i].rows + 15) / 16) * ph[i].G * std::max(sms, PD_WARPS) >= (1ll << 31)) return N730_UNSUPPORTED;
     if (ph[i].kind == PD_FFN) {
       // gate|up rows interleave the down_proj input channels; whole down groups per CTA
       const int nj = (ph[i].G2 + sms - 1) / sms;
@@ -854,7 +852,7 @@ int persist_plan(const PdPhase* ph, int n, int head_dim, int group_q, int page_s
   a.wpart_off = (int)off;
   off += round((size_t)PD_WARPS * 2 * 16 * 4);
   a.misc_off = (int)off;
-  off += 64 * 4;
+  off += 96 * 4;
   a.ffn_off = (int)round(off);
   off = a.ffn_off + (size_t)ffn_floats * 4;
   a.tab_off = (int)round(off);
