@@ -48,6 +48,12 @@ constexpr int PD_MAXG = 8;         // query heads per KV head
 constexpr int PD_MAXSPLIT = 64;    // context splits per KV head
 constexpr int PD_ADDMAX = 512;     // epilogue addend rows (bias / residual) per CTA
 constexpr uint64_t PD_WAIT_NS = 200000000ull;  // grid-barrier wait limit (0.2 s)
+// Thread roles outside the weight ring (each warp's lane 0 issues that warp's
+// ring copies): the KV page copies are issued and waited for by PD_KV_T, and the
+// grid-barrier arrival, split publication and exit handshake (the release
+// fences) by PD_SYNC_T, a thread with no bulk copies of its own in flight.
+constexpr int PD_KV_T = 1;
+constexpr int PD_SYNC_T = 2;
 constexpr float PD_FIX = 4294967296.0f;          // 32.32 fixed point of the FFN accumulator
 constexpr float PD_UNFIX = 2.3283064365386963e-10f;
 
@@ -71,30 +77,36 @@ __device__ __forceinline__ int ld_relaxed(const int* p) {
   return v;
 }
 
+// Wait until *cnt >= target or the abort flag is raised: each poll issues the
+// two relaxed loads together (one L2 round trip), and one acquire fence follows
+// the wait.  Raises the abort flag and the device error word after PD_WAIT_NS.
+__device__ __forceinline__ bool pd_wait_count(const PdArgs& a, const int* cnt, int target) {
+  uint64_t t0 = 0;
+  bool ok = true;
+  for (;;) {
+    const int c = ld_relaxed(cnt), ab = ld_relaxed(&a.sync[2]);
+    if (c >= target) break;
+    if (ab) { ok = false; break; }
+    const uint64_t t = gtimer();
+    if (!t0) t0 = t;
+    else if (t - t0 > PD_WAIT_NS) {
+      atomicExch(&a.sync[2], 1);
+      atomicExch(a.err, DEV_ERR_TIMEOUT);
+      ok = false;
+      break;
+    }
+  }
+  asm volatile("fence.acq_rel.gpu;" ::: "memory");
+  return ok;
+}
+
 // Grid barrier number k (all CTAs call it in the same order).  False when the
 // launch is being aborted.
 __device__ bool pd_barrier(const PdArgs& a, int k, int* flag) {
   __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    atomicAdd(&a.sync[0], 1);
-    const int target = (int)gridDim.x * k;
-    int ok = 1;
-    if (ld_acquire(&a.sync[0]) < target) {
-      const uint64_t t0 = gtimer();
-      while (ld_acquire(&a.sync[0]) < target) {
-        if (ld_relaxed(&a.sync[2])) { ok = 0; break; }
-        if (gtimer() - t0 > PD_WAIT_NS) {
-          atomicExch(&a.sync[2], 1);
-          atomicExch(a.err, DEV_ERR_TIMEOUT);
-          ok = 0;
-          break;
-        }
-      }
-    }
-    if (ld_relaxed(&a.sync[2])) ok = 0;
-    __threadfence();
-    *flag = ok;
+  if (threadIdx.x == PD_SYNC_T) {
+    asm volatile("red.release.gpu.global.add.s32 [%0], 1;" :: "l"(&a.sync[0]) : "memory");
+    *flag = pd_wait_count(a, &a.sync[0], (int)gridDim.x * k);
   }
   __syncthreads();
   return *flag != 0;
@@ -177,9 +189,9 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
   }
   __syncthreads();
 
-  // ---- KV page copies (thread 0): page p of this CTA's KV head, layer of phase ph ----
-  int kv_uses = 0;      // copies issued (thread 0)
-  int kv_waited = 0;    // copies waited for (thread 0)
+  // ---- KV page copies (PD_KV_T): page p of this CTA's KV head, layer of phase ph ----
+  int kv_uses = 0;      // copies issued (PD_KV_T)
+  int kv_waited = 0;    // copies waited for (PD_KV_T)
   auto kv_issue = [&](int ph, int p) {
     const PdPhase& P = phs[ph];
     const int page = a.block_table[p];
@@ -257,7 +269,7 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
     set_phase(prod, 0);
     for (int r = 0; r < PD_RING; ++r) issue_next(r);
   }
-  if (tid == 0 && has_item) {
+  if (tid == PD_KV_T && has_item) {
     const int ph = next_attn(0);
     if (ph < a.n_phases) kv_issue(ph, pg0);
   }
@@ -286,7 +298,7 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
         // O accumulator fragment: warp w < HD/8 owns dims [8w, 8w+8); row g = query head g
         float oc[4] = {0.f, 0.f, 0.f, 0.f};
         for (int pg = pg0; pg < pg1; ++pg) {
-          if (tid == 0) {
+          if (tid == PD_KV_T) {
             if (pg > pg0) kv_issue(ph, pg);
             const bool okw = wait_bar(kvbar, (uint32_t)(kv_waited & 1));
             ++kv_waited;
@@ -387,11 +399,6 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
           }
           __syncthreads();
         }
-        // the page buffer is free: start copying this CTA's page of the next layer
-        if (tid == 0) {
-          const int nph = next_attn(ph + 1);
-          if (nph < a.n_phases) kv_issue(nph, pg0);
-        }
         // this split's partial: o [GQ][HD] and (m, l) per query head
         const int item = kvh * sp.ns + split;
         float* part_o = a.attn_part + (size_t)item * GQ * HD;
@@ -400,18 +407,9 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
         if (tid < GQ) *reinterpret_cast<float2*>(part_ml + tid * 2) = make_float2(ml[tid * 4 + 0], ml[tid * 4 + 1]);
         // wait for every split of this KV head (co-resident CTAs, bounded wait)
         __syncthreads();
-        if (tid == 0) {
+        if (tid == PD_SYNC_T) {
           asm volatile("red.release.gpu.global.add.s32 [%0], 1;" :: "l"(a.attn_cnt + kvh) : "memory");
-          const int target = sp.ns * (attn_idx + 1);
-          int okw = 1;
-          if (ld_acquire(a.attn_cnt + kvh) < target) {
-            const uint64_t tw = gtimer();
-            while (ld_acquire(a.attn_cnt + kvh) < target) {
-              if (ld_relaxed(&a.sync[2])) { okw = 0; break; }
-              if (gtimer() - tw > PD_WAIT_NS) { atomicExch(&a.sync[2], 1); atomicExch(a.err, DEV_ERR_TIMEOUT); okw = 0; break; }
-            }
-          }
-          flag[1] = okw;
+          flag[1] = pd_wait_count(a, a.attn_cnt + kvh, sp.ns * (attn_idx + 1));
         }
         __syncthreads();
         if (flag[1]) {
@@ -457,6 +455,11 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
             num = warp_sum(num);
             if (lane == 0) a.attn_out[(int64_t)kvh * no + o] = num / (ml[jj * 4 + 3] + 1e-9f);
           }
+        }
+        // the page buffer is free: start copying this CTA's page of the next layer
+        if (tid == PD_KV_T) {
+          const int nph = next_attn(ph + 1);
+          if (nph < a.n_phases) kv_issue(nph, pg0);
         }
       }
       ++attn_idx;
@@ -741,17 +744,17 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
   // copies still in flight (abort path) are waited for, bounded, before exit
   if (lane == 0)
     for (int q = consumed; q < issued; ++q) wait_bar(&wb[q % PD_RING], (uint32_t)((q / PD_RING) & 1));
-  if (tid == 0)
+  if (tid == PD_KV_T)
     for (; kv_waited < kv_uses; ++kv_waited) wait_bar(kvbar, (uint32_t)(kv_waited & 1));
   __syncthreads();
-  if (tid == 0) {  // the last CTA out resets the counters and the FFN accumulator for the next launch
+  if (tid == PD_SYNC_T) {  // the last CTA out resets the counters and the FFN accumulator for the next launch
     __threadfence();
     flag[2] = atomicAdd(&a.sync[1], 1) == NC - 1;
   }
   __syncthreads();
   if (flag[2]) {
     for (int i = tid; i < a.acc_n; i += PD_THREADS) a.acc[i] = 0ull;
-    if (tid == 0) {
+    if (tid == PD_SYNC_T) {
       for (int h = 0; h < d.n_kv; ++h) a.attn_cnt[h] = 0;
       a.sync[0] = 0;
       a.sync[2] = 0;
