@@ -62,9 +62,16 @@ def _args():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (small profiling cases)")
+    ap.add_argument("--tp-allreduce", type=int, default=1, choices=[0, 1],
+                    help="tp72b decode row-split sums: 0 one-shot over NVLink peer memory, 1 NCCL")
     ap.add_argument("--ffn-fuse", type=int, default=0, choices=[-1, 0, 1],
                     help="persistent decode FFN: 0 auto, 1 one fused phase, -1 two GEMV phases")
-    ap.add_argument("--workload", default="resident", choices=["resident", "streamed", "tp72b"],
+    ap.add_argument("--model", default=SHAPE_NAME, choices=["qwen2-7b", "qwen2-0.5b"],
+                    help="resident workload: model shape")
+    ap.add_argument("--pmap", default="int4_g128", choices=["int4_g128", "mixed_05b"],
+                    help="resident workload: precision map (mixed_05b: INT8 attention, INT4 g128 FFN, fp16 tied "
+                         "embedding/lm_head)")
+    ap.add_argument("--workload", default="resident", choices=["resident", "streamed", "tp72b", "linear"],
                     help="streamed: 7B aggressive mixed quant (FFN INT2 g64, attention INT4 g128, lm_head INT8 "
                          "per channel), layer weights in pinned host memory, 2-layer prefetch, 1024-token prompt; "
                          "tp72b: Qwen2-72B shape INT4 g128 split over the N ranks (tensor parallel, strong scaling)")
@@ -258,13 +265,14 @@ def run_ours(a):
         torch.cuda.set_device(0)
     from n730_b200.engine import Engine
     from n730_b200.synthetic import SHAPES, build_on_device
-    shape = SHAPES[SHAPE_NAME]
+    shape = SHAPES[a.model]
     if a.layers:
         shape = dataclasses.replace(shape, layers=a.layers)
+    headline = a.model == SHAPE_NAME and a.pmap == "int4_g128"
     B, ctx = a.batch, a.ctx
     max_ctx = ctx + 2 * (a.warmup + a.steps) + 64  # device-side steps, then the e2e steps
     eng = Engine(shape, max_ctx=max_ctx, max_batch=B, max_prefill=512, ffn_fuse=a.ffn_fuse)
-    build_on_device(shape, "int4_g128", eng, seed=rank)
+    build_on_device(shape, a.pmap, eng, seed=rank)
     eng.finalize()
     info = eng.info()
     # prefill every sequence with a 2048-token uniform-random prompt (timed separately, reported
@@ -345,8 +353,8 @@ def run_ours(a):
         torch.cuda.synchronize()
         t_kern = e4.elapsed_time(e5) / 1000.0 / (reps * shape.layers)
         kern_bytes = eng.linear_bytes(0, 2, B)
-        kern_name = "gemv_mma2_kernel on gate|up 37888x3584 INT4 g128 (+SwiGLU)"
-        traffic_file = "gemv_gateup_traffic.txt"
+        kern_name = f"gemv_mma2_kernel on gate|up {2 * shape.ffn}x{shape.hidden} INT4 g128 (+SwiGLU), batch {B}"
+        traffic_file = "gemv_gateup_traffic.txt" if headline else "none"
 
     # max over ranks
     if world > 1:
@@ -365,18 +373,25 @@ def run_ours(a):
         toks = B * a.steps * world
         kv_bytes = info["kv_bytes_per_pos"] * (ctx + a.warmup + a.steps // 2) * B
         step_bytes = info["weight_bytes"] + kv_bytes
+        params = shape.layers * (shape.hidden * (shape.heads + 2 * shape.kv_heads) * shape.head_dim
+                                 + shape.heads * shape.head_dim * shape.hidden
+                                 + 3 * shape.hidden * shape.ffn) + shape.vocab * shape.hidden
         out = {
-            "metric": METRIC, "value": round(toks / t_dev, 2), "unit": "tok/s", "n_gpus": world,
+            "metric": METRIC if headline else f"decode tok/s at {a.model}-shape ({a.pmap})",
+            "value": round(toks / t_dev, 2), "unit": "tok/s", "n_gpus": world,
             "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(t_dev / a.steps * 1000, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "int4 weights (exact dequant); fp16 x, f32 accumulate",
             "data": "synthetic (random-init N(0,0.02) weights, uniform-random token ids)",
-            "config": {"workload": f"qwen2-7b-shape decoder ({shape.layers} layers), all linears INT4 g128 "
-                                   f"(fp16 scale+zero), batch {B} decode after a {ctx}-token prefill, fp16 paged KV",
+            "config": {"workload": f"{a.model}-shape decoder ({shape.layers} layers), "
+                                   + ("all linears INT4 g128 (fp16 scale+zero)" if a.pmap == "int4_g128" else
+                                      "attention INT8 per-tensor, FFN INT4 g128, fp16 tied embedding / lm_head")
+                                   + f", batch {B} decode after a {ctx}-token prefill, fp16 paged KV",
                        "batch": B, "ctx_start": ctx, "parallelism": f"replicas x{world}" if world > 1 else "single",
                        "decode_path": ("persistent kernel" + (", FFN fused" if info["ffn_fused"] else "")
                                        if persistent else "per-op kernels (graph)"),
-                       "l2": "no flush: 3.76 GB of weights stream from HBM every step (L2 126 MB)"},
+                       "l2": f"no flush: {info['weight_bytes'] / 1e9:.2f} GB of weights stream from HBM every step "
+                             "(L2 126 MB)"},
             "e2e": {"value": round(toks / t_e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
                     "d2h_bytes_per_step": 4 * B * shape.vocab},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
@@ -389,11 +404,11 @@ def run_ours(a):
             "clocks": clk.summary(),
             "gpu_launches": a.steps * (3 if persistent else 5 * shape.layers + 3),
             "prefill": {"tokens": B * ctx, "s": round(t_prefill, 4), "tok_per_s": round(B * ctx / t_prefill, 1),
-                        "tflops": round(2 * info["weight_bytes"] / 0.53125 * B * ctx / t_prefill / 1e12, 1),
+                        "tflops": round(2 * params * B * ctx / t_prefill / 1e12, 1),
                         "path": "tcgen05 GEMM (INT4 fragment tiles dequantised to fp16 in shared memory, TMEM "
                                 "accumulators) for every linear, 512-token chunks; wall clock incl. host calls"},
         }
-        if not a.no_cpu_baseline:
+        if not a.no_cpu_baseline and headline:
             cs = CpuLayerSample(shape)
             t_token = min(cs.run() for _ in range(3))
             cs.close()
@@ -494,9 +509,9 @@ def run_tp(a):
     tp.check_shape(shape, world, 128)
     B, ctx = a.batch, a.ctx
     eng = Engine(tp.local_shape(shape, world, rank, 128), max_ctx=ctx + a.warmup + a.steps + 8, max_batch=B,
-                 max_prefill=64, tp_rank=rank, tp_size=world)
+                 max_prefill=64, tp_rank=rank, tp_size=world, tp_allreduce=a.tp_allreduce)
     if world > 1:
-        tp.init_engine_comm(eng, rank, world)
+        tp.init_engine_comm(eng, rank, world, one_shot=a.tp_allreduce == 0)
     build_on_device(shape, "int4_g128", eng, tp_rank=rank, tp_size=world)
     eng.finalize()
     info = eng.info()
@@ -535,8 +550,10 @@ def run_tp(a):
                "vs_baseline": None, "dtype": "int4 weights (exact dequant); fp16 x, f32 accumulate",
                "data": "synthetic (random-init N(0,0.02) weights)",
                "config": {"workload": f"qwen2-72b-shape ({shape.layers} layers) INT4 g128, batch {B} decode at "
-                                      f"context {ctx}, tensor parallel over {world} GPU(s) (NCCL allreduce after "
+                                      f"context {ctx}, tensor parallel over {world} GPU(s) (row-split sums after "
                                       "o_proj and down_proj, vocab-split lm_head)", "batch": B,
+                          "allreduce": ("one-shot push over NVLink peer memory, fused residual add"
+                                        if a.tp_allreduce == 0 else "NCCL") if world > 1 else None,
                           "parallelism": f"tp{world}"},
                "roofline": {"bound": "hbm", "achieved": round(step_bytes / (t / a.steps) / 1e9, 1), "peak": peak,
                             "unit": "GB/s per GPU", "frac": round(step_bytes / (t / a.steps) / 1e9 / peak, 4),
@@ -549,6 +566,81 @@ def run_tp(a):
         dist.destroy_process_group()
 
 
+def run_linear(a):
+    """Single INT4 g128 dequant-GEMV, W [4096, 4096] ~ N(0, 0.02) seed 0, batch 1 (the reference's
+    single-linear configuration): launches rotate over enough weight copies to exceed 4x L2, one CUDA
+    graph of the rotation is replayed, bytes per GEMV = codes + scale/zero + x + y."""
+    import ctypes as C
+
+    import torch
+    from n730_b200 import _lib
+    lib = _lib.cuda()
+    torch.cuda.set_device(0)
+    rows = cols = 4096
+    g = torch.Generator(device="cuda")
+    g.manual_seed(0)
+    w = torch.randn(rows, cols, generator=g, device="cuda") * 0.02
+    P = lambda t: C.c_void_p(t.data_ptr())
+    copies, qs = 64, []
+    for _ in range(copies):
+        codes = torch.empty(rows * cols // 2, dtype=torch.uint8, device="cuda")
+        s16 = torch.empty(rows, cols // 128, dtype=torch.float16, device="cuda")
+        z16 = torch.empty_like(s16)
+        _lib.check(lib.n730_quantize_grouped(P(w), rows, cols, 4, 128, P(codes), P(s16), P(z16), None), "quantize")
+        q = C.c_void_p()
+        _lib.check(lib.n730_qweight_create(0x44, rows, cols, 128, 1.0, 0.0, P(codes), P(s16), P(z16), 1, None,
+                                           C.byref(q)), "qweight_create")
+        _lib.check(lib.n730_qweight_set_layout(q, 1, None), "qweight_set_layout")
+        qs.append(q)
+    del w
+    torch.cuda.synchronize()
+    g1 = torch.Generator(device="cuda")
+    g1.manual_seed(1)
+    x = torch.randn(1, cols, generator=g1, device="cuda")
+    y = torch.empty(copies, rows, device="cuda")
+    side = torch.cuda.Stream()
+    with torch.cuda.stream(side):
+        for i in range(copies):  # warm-up outside capture
+            _lib.check(lib.n730_qlinear(qs[i], P(x), cols, 1, P(y[i]), rows, None, None, 0, None, 1e-6, 0,
+                                        C.c_void_p(side.cuda_stream)), "qlinear")
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        st = torch.cuda.current_stream().cuda_stream
+        for i in range(copies):
+            _lib.check(lib.n730_qlinear(qs[i], P(x), cols, 1, P(y[i]), rows, None, None, 0, None, 1e-6, 0,
+                                        C.c_void_p(st)), "qlinear")
+    for _ in range(a.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        e0.record()
+        for _ in range(a.steps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+    t = e0.elapsed_time(e1) / 1000.0 / (a.steps * copies)
+    bytes_per = rows * cols // 2 + rows * (cols // 128) * 4 + cols * 4 + rows * 4
+    peak, kind = _peaks()
+    out = {"metric": "single-linear INT4 g128 dequant-GEMV bandwidth (W 4096x4096, batch 1)",
+           "value": round(bytes_per / t / 1e9, 1), "unit": "GB/s", "n_gpus": 1, "steps": a.steps, "warmup": a.warmup,
+           "ms_per_step": round(t * 1e3, 5), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "dtype": "int4 weights (exact dequant); fp16 x, f32 accumulate",
+           "data": "synthetic W ~ N(0, 0.02) seed 0, x ~ N(0, 1) seed 1",
+           "config": {"workload": "one 4096x4096 INT4 g128 GEMV per step (n730_qlinear, tensor-core GEMV)",
+                      "copies": copies, "l2": f"rotation over {copies} weight copies = "
+                                              f"{copies * bytes_per / 1e6:.0f} MB (> 4x L2)", "graph": True},
+           "roofline": {"bound": "hbm", "achieved": round(bytes_per / t / 1e9, 1), "peak": peak, "unit": "GB/s",
+                        "frac": round(bytes_per / t / 1e9 / peak, 4), "traffic": None,
+                        "kernel": "gemv_mma2_kernel<8,1,16> (4096 rows, K 4096)", "bytes_per_launch": bytes_per,
+                        "ms_per_launch": round(t * 1e3, 5), "peak_source": kind},
+           "clocks": clk.summary(), "gpu_launches": a.steps * copies}
+    print(json.dumps(out), flush=True)
+    for q in qs:
+        lib.n730_qweight_destroy(q)
+
+
 def main():
     a = _args()
     if a.impl == "reference":
@@ -557,6 +649,8 @@ def main():
         run_streamed(a)
     elif a.workload == "tp72b":
         run_tp(a)
+    elif a.workload == "linear":
+        run_linear(a)
     else:
         run_ours(a)
 

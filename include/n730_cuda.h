@@ -165,6 +165,9 @@ typedef struct N730ModelConfig {
                             whole FFN quant groups, down_proj partial sums reduced in a fixed order)
                             when the down groups divide evenly over the SMs; 1 whenever the shapes
                             allow it; -1 never (two GEMV phases) */
+  int32_t tp_allreduce;  /* tensor parallel, decode-sized row-split sums: 0 one-shot over peer memory
+                            (CUDA IPC, after n730_model_tp_ipc_open), fused with the residual add;
+                            1 NCCL allreduce always */
 } N730ModelConfig;
 
 /* weight slots (n730_model_set_qweight); EMBED/LMHEAD take layer = -1 */
@@ -205,6 +208,14 @@ void* n730_model_stream(void* model);
  * id, the host shares it, every rank calls tp_init before finalize. */
 int n730_tp_unique_id(uint8_t* out_128_bytes);
 int n730_model_tp_init(void* model, const uint8_t* id_128_bytes, int rank, int size);
+/* One-shot allreduce over NVLink peer memory (config tp_allreduce 0; no counterpart in the
+ * reference, which has no multi-GPU path): after tp_init every rank exports its exchange region
+ * (N730_IPC_HANDLE_BYTES bytes), the host gathers all ranks' handles in rank order, and every
+ * rank opens them (collective; the host barriers before the first step).  Decode-sized
+ * row-split sums then bypass NCCL: push to every rank, bounded flag wait, rank-order sum. */
+#define N730_IPC_HANDLE_BYTES 64
+int n730_model_tp_ipc_handle(void* model, uint8_t* out_handle);
+int n730_model_tp_ipc_open(void* model, const uint8_t* handles, int size);
 /* Launch only the persistent kernel of a batch-1 decode step (no embedding, no
  * position update; repeated calls recompute the same position).  Timing hook;
  * N730_UNSUPPORTED (-14) when the model decodes with one kernel per op. */

@@ -90,6 +90,7 @@ struct DecSmem {
   float wo[DEC_WARPS][MAX_G][HD];     // per-warp unnormalised outputs
   float m[MAX_G], l[MAX_G];           // this CTA's split
   float o[MAX_G][HD];
+  float sw[MAX_G][16], den[MAX_G];    // cluster merge: weight e^(m_r - M) of each split, denominator
 };
 
 template <int HD>
@@ -272,24 +273,33 @@ __global__ void __launch_bounds__(DEC_THREADS) attn_decode_kernel(const DecodeAt
     if (dd == 0) { sm.m[g] = M; sm.l[g] = den; }
   }
   cluster.sync();  // every split's (m, l, o) is visible cluster-wide
-  if (split == 0) {
-    for (int i = tid; i < G * HD; i += DEC_THREADS) {
+  // every rank: split weights per head (warp g, lane r = split r, fixed-order
+  // reductions), then this rank merges its 1/S slice of the G x HD outputs
+  if (warp < G) {
+    const int g = warp;
+    const float mr = lane < S ? cluster.map_shared_rank(&sm, lane)->m[g] : -INFINITY;
+    const float lr = lane < S ? cluster.map_shared_rank(&sm, lane)->l[g] : 0.f;
+    float M = mr;
+#pragma unroll
+    for (int o2 = 16; o2 > 0; o2 >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o2));
+    const float w = mr == -INFINITY ? 0.f : __expf(mr - M);
+    float dn = w * lr;
+#pragma unroll
+    for (int o2 = 16; o2 > 0; o2 >>= 1) dn += __shfl_xor_sync(0xffffffffu, dn, o2);
+    if (lane < 16) sm.sw[g][lane] = lane < S ? w : 0.f;
+    if (lane == 0) sm.den[g] = dn;
+  }
+  __syncthreads();
+  {
+    const int n_out = G * HD, lo = split * n_out / S, hi = (split + 1) * n_out / S;
+    for (int i = lo + tid; i < hi; i += DEC_THREADS) {
       const int g = i / HD, dd = i % HD;
-      float M = -INFINITY;
-      for (int r = 0; r < S; ++r) M = fmaxf(M, cluster.map_shared_rank(&sm, r)->m[g]);
-      float num = 0.f, den = 0.f;
-      for (int r = 0; r < S; ++r) {
-        const SM* rs = cluster.map_shared_rank(&sm, r);
-        const float mr = rs->m[g];
-        if (mr == -INFINITY) continue;
-        const float w = __expf(mr - M);
-        den = fmaf(w, rs->l[g], den);
-        num = fmaf(w, rs->o[g][dd], num);
-      }
-      a.out[(int64_t)b * d.n_heads * HD + (int64_t)(kvh * G + g) * HD + dd] = num / (den + 1e-9f);
+      float num = 0.f;
+      for (int r = 0; r < S; ++r) num = fmaf(sm.sw[g][r], cluster.map_shared_rank(&sm, r)->o[g][dd], num);
+      a.out[(int64_t)b * d.n_heads * HD + (int64_t)(kvh * G + g) * HD + dd] = num / (sm.den[g] + 1e-9f);
     }
   }
-  cluster.sync();  // keep every CTA's shared memory alive until rank 0 is done
+  cluster.sync();  // keep every CTA's shared memory alive until every rank has merged
 }
 
 template <typename KernelT, typename ArgT>
@@ -339,9 +349,12 @@ int attn_decode_launch(const DecodeAttnArgs& a, cudaStream_t st) {
   N730_REQUIRE(d.head_dim == 64 || d.head_dim == 128, N730_UNSUPPORTED, "attention: head_dim %d", d.head_dim);
   N730_REQUIRE(a.batch >= 1, N730_BAD_ARG, "attention: bad batch");
   static int cl128 = 0, cl64 = 0;
-  int& cl = d.head_dim == 128 ? cl128 : cl64;
-  if (!cl) cl = d.head_dim == 128 ? decode_cluster_size<128>() : decode_cluster_size<64>();
-  if (cl < 0) return cl;
+  int& cl_max = d.head_dim == 128 ? cl128 : cl64;
+  if (!cl_max) cl_max = d.head_dim == 128 ? decode_cluster_size<128>() : decode_cluster_size<64>();
+  if (cl_max < 0) return cl_max;
+  // splits per (sequence, KV head): about two CTAs per SM in all, at least 2
+  int cl = cl_max;
+  while (cl > 2 && (int64_t)a.batch * d.n_kv * cl > 2 * (int64_t)num_sms()) cl >>= 1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(cl, d.n_kv, a.batch);
   cfg.blockDim = dim3(DEC_THREADS);

@@ -132,6 +132,12 @@ struct MmaParams {
   const float* norm_w; float eps;
   int swiglu;
   int* err;
+  // split K (blockIdx.y = K-block of kb_n, whole groups each): the CTA writes its
+  // raw partial sums to part[kb * part_stride + b * rows + row] and a fold kernel
+  // adds the K-blocks in order plus bias and residual
+  int kb_n;
+  float* part;
+  int64_t part_stride;
 };
 
 constexpr int MG2_RING = 3;   // chunks in flight per warp (fewer when shared memory is short)
@@ -159,6 +165,10 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) gemv_mma2_kernel(const
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int n_tiles = (p.rows + 15) / 16;
   const int tile0 = blockIdx.x * p.tiles_per_cta;
+  // this CTA's K-block: groups [g0, g0 + Gk), k-steps [s0, s0 + ks_loc)
+  const int kb = blockIdx.y;
+  const int g0 = (int)((int64_t)p.G * kb / p.kb_n), Gk = (int)((int64_t)p.G * (kb + 1) / p.kb_n) - g0;
+  const int s0 = g0 * KPG, ks_loc = Gk * KPG;
   if (tile0 >= n_tiles) return;
   const int ntc = min(p.tiles_per_cta, n_tiles - tile0);
   const int P = p.parts;
@@ -179,8 +189,8 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) gemv_mma2_kernel(const
     if (c.u >= n_units) return;
     c.t = tile0 + c.u / P;
     const int part = c.u % P;
-    c.ks = (part * p.G / P) * KPG;
-    c.ks_end = ((part + 1) * p.G / P) * KPG;
+    c.ks = (g0 + part * Gk / P) * KPG;
+    c.ks_end = (g0 + (part + 1) * Gk / P) * KPG;
   };
   auto issue = [&](const Cursor& c, int slot) {
     const int ng = min(MG2_CHUNK, c.ks_end - c.ks) / KPG;
@@ -232,13 +242,14 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) gemv_mma2_kernel(const
     }
     __syncthreads();
   }
-  // ---- x -> (RMS-normalised) fp16 B fragments: xf[b][s][tq] = {x[2tq], x[2tq+1], x[2tq+8], x[2tq+9]} ----
+  // ---- x -> (RMS-normalised) fp16 B fragments of the K-block:
+  //      xf[b][s - s0][tq] = {x[2tq], x[2tq+1], x[2tq+8], x[2tq+9]} of k-step s ----
   uint2* xf2 = reinterpret_cast<uint2*>(xf);
-  const int per_row = p.ks_n * 4;
+  const int per_row = ks_loc * 4;
 #pragma unroll 4
   for (int i = tid; i < nb * per_row; i += THREADS) {
     const int b = i / per_row, r = i - b * per_row;
-    const int s = r >> 2, tq = r & 3, k = s * 16 + 2 * tq;
+    const int s = r >> 2, tq = r & 3, k = (s0 + s) * 16 + 2 * tq;
     const float* xb = p.x + (int64_t)b * p.ldx;
     float2 v0 = *reinterpret_cast<const float2*>(xb + k), v1 = *reinterpret_cast<const float2*>(xb + k + 8);
     if (p.norm_w) {
@@ -248,18 +259,18 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) gemv_mma2_kernel(const
       v0.x = v0.x * iv * n0.x; v0.y = v0.y * iv * n0.y;
       v1.x = v1.x * iv * n1.x; v1.y = v1.y * iv * n1.y;
     }
-    // element (b, s, tq) at uint2 index ((b * ks_n/2 + s/2) * 4 + tq) * 2 + (s & 1)
-    xf2[(((size_t)b * (p.ks_n >> 1) + (s >> 1)) * 4 + tq) * 2 + (s & 1)] =
+    // element (b, s, tq) at uint2 index ((b * ks_loc/2 + s/2) * 4 + tq) * 2 + (s & 1)
+    xf2[(((size_t)b * (ks_loc >> 1) + (s >> 1)) * 4 + tq) * 2 + (s & 1)] =
         make_uint2(h2u(__floats2half2_rn(v0.x, v0.y)), h2u(__floats2half2_rn(v1.x, v1.y)));
   }
   __syncthreads();
   // Sx[grp][col]: sum of the fp16 x of group grp, batch row col (0 beyond the
   // batch); one thread per (group, col), sequential order
-  for (int pr = tid; pr < p.G * NT * 8; pr += THREADS) {
+  for (int pr = tid; pr < Gk * NT * 8; pr += THREADS) {
     const int grp = pr / (NT * 8), col = pr - grp * (NT * 8);
     float v = 0.f;
     if (col < nb) {
-      const uint4* src = xf + ((size_t)col * (p.ks_n >> 1) + grp * (KPG >> 1)) * 4;
+      const uint4* src = xf + ((size_t)col * (ks_loc >> 1) + grp * (KPG >> 1)) * 4;
 #pragma unroll 4
       for (int e = 0; e < KPG * 2; ++e) {  // KPG/2 k-step pairs x 4 tq
         const uint4 u = src[e];
@@ -274,7 +285,7 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) gemv_mma2_kernel(const
   pdl_launch_dependents();
 
   const int g = lane >> 2, tq = lane & 3;
-  const int ks_half = p.ks_n >> 1;
+  const int ks_half = ks_loc >> 1;
   bool aborted = false;
   Cursor cons{warp, 0, 0, 0};
   start_unit(cons);
@@ -300,8 +311,8 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) gemv_mma2_kernel(const
       const uint4* xb[NT];
 #pragma unroll
       for (int nn = 0; nn < NT; ++nn)
-        xb[nn] = xf + ((size_t)min(nn * 8 + g, nb - 1) * ks_half + ((ks0 + off) >> 1)) * 4 + tq;
-      const float* sxg = sx + grp0 * (NT * 8);
+        xb[nn] = xf + ((size_t)min(nn * 8 + g, nb - 1) * ks_half + ((ks0 + off - s0) >> 1)) * 4 + tq;
+      const float* sxg = sx + (grp0 - g0) * (NT * 8);
       if (ngr == GPC) {
         mma_chunk<KPG, NT, GPC>(buf, lane, xb, sxg, acc);
       } else {
@@ -321,7 +332,9 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) gemv_mma2_kernel(const
     // sums the slots in part order (deterministic) and writes the tile out
     const int tl = t - tile0, part = (cons.u - (cons.u / P) * P);
     constexpr int TS = 16 * NT * 8;  // floats per slot
-    float* ta = accs + ((size_t)tl * P + part) * TS;
+    // one slot per (tile, K-part); with a single part the warp's own slot serves
+    const size_t slot0 = P == 1 ? (size_t)warp : (size_t)tl * P;
+    float* ta = accs + (slot0 + part) * TS;
 #pragma unroll
     for (int nn = 0; nn < NT; ++nn) {
       const int c = nn * 8 + 2 * tq;
@@ -334,7 +347,7 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) gemv_mma2_kernel(const
     if (lane == 0) last = atomicAdd(&tile_cnt[tl], 1) == P - 1;
     if (__shfl_sync(0xffffffffu, last, 0)) {
       __threadfence_block();
-      const volatile float* tb = accs + (size_t)tl * P * TS;
+      const volatile float* tb = accs + slot0 * TS;
       auto tile_sum = [&](int i) {
         float v = 0.f;
         for (int q2 = 0; q2 < P; ++q2) v += tb[q2 * TS + i];
@@ -344,6 +357,10 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) gemv_mma2_kernel(const
         const int r = i / (NT * 8), bc = i % (NT * 8);
         const int row = t * 16 + r;
         if (bc >= nb || row >= p.rows) continue;
+        if (p.part) {  // split K: raw partial of this K-block
+          p.part[(int64_t)kb * p.part_stride + (int64_t)bc * p.rows + row] = tile_sum(i);
+          continue;
+        }
         if (p.swiglu && (r & 1)) continue;
         float v = tile_sum(i) + (p.bias ? p.bias[row] : 0.f);
         if (p.swiglu) {
@@ -367,6 +384,7 @@ int* gemv_err_word();
 
 template <int KPG, int NT, int WARPS>
 static int launch_mma2(const MmaParams& p, int grid, size_t smem, cudaStream_t st, bool pdl) {
+  const dim3 g3(grid, p.kb_n);
   static bool configured = false;
   if (!configured) {
     N730_CUDA(cudaFuncSetAttribute(gemv_mma2_kernel<KPG, NT, WARPS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -374,7 +392,7 @@ static int launch_mma2(const MmaParams& p, int grid, size_t smem, cudaStream_t s
     configured = true;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
+  cfg.gridDim = g3;
   cfg.blockDim = dim3(WARPS * 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
@@ -404,6 +422,20 @@ static int mma_warps() {
   return w;
 }
 
+// y[b][r] = residual[b][r] + bias[r] + sum over K-blocks of part[kb][b][r], in K-block order
+__global__ void split_fold_kernel(const float* part, int kb_n, int64_t stride, int nb, int rows, float* y, int ldy,
+                                  const float* residual, int ldr, const float* bias) {
+  const int64_t n = (int64_t)nb * rows;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int b = (int)(i / rows), r = (int)(i - (int64_t)b * rows);
+    float v = 0.f;
+    for (int kb = 0; kb < kb_n; ++kb) v += __ldcg(part + kb * stride + i);
+    if (bias) v += bias[r];
+    if (residual) v += residual[(int64_t)b * ldr + r];
+    y[(int64_t)b * ldy + r] = v;
+  }
+}
+
 int gemv_mma_launch(const GemvArgs& a, cudaStream_t st) {
   const QWeight& w = *a.w;
   N730_REQUIRE(w.layout == 1, N730_BAD_ARG, "gemv_mma: weight not in mma layout");
@@ -421,47 +453,74 @@ int gemv_mma_launch(const GemvArgs& a, cudaStream_t st) {
   p.ldy = a.ldy; p.bias = a.bias; p.ldr = a.ldr; p.norm_w = a.norm_w; p.eps = a.eps; p.swiglu = a.swiglu;
   p.err = err;
   const int n_tiles = (w.rows + 15) / 16;
-  // one CTA per SM: with 8 warps the other half of the SM stays free for the
-  // next kernel's CTA, which streams its weights while this one finishes
   const int ctas = num_sms();
-  p.tiles_per_cta = (n_tiles + ctas - 1) / ctas;
-  const int grid = (n_tiles + p.tiles_per_cta - 1) / p.tiles_per_cta;
-  // K-parts so every warp has a unit; each part a whole number of groups
-  p.parts = std::max(1, std::min(p.G, (WARPS + p.tiles_per_cta - 1) / p.tiles_per_cta));
   p.ring_stride = ((MG2_CHUNK / kpg) * (kpg * 128 + 64) + 127) / 128 * 128;
   const size_t cap = WARPS == 16 ? 227 * 1024 : 113 * 1024;
+  // grid for kb_n K-blocks: one CTA per SM in all, row tiles split over ceil(ctas / kb_n) CTAs
+  int grid = 0;
+  auto geometry = [&](int kb_n) {
+    p.kb_n = kb_n;
+    const int row_ctas = std::max(1, ctas / kb_n);
+    p.tiles_per_cta = (n_tiles + row_ctas - 1) / row_ctas;
+    grid = (n_tiles + p.tiles_per_cta - 1) / p.tiles_per_cta;
+    const int Gk = p.G / kb_n;  // smallest K-block
+    // K-parts so every warp has a unit; each part a whole number of groups
+    p.parts = std::max(1, std::min(Gk, (WARPS + p.tiles_per_cta - 1) / p.tiles_per_cta));
+  };
+  auto layout = [&](int nb_) {
+    const int NT = nb_ > 8 ? 2 : 1;
+    const int gk_max = (p.G + p.kb_n - 1) / p.kb_n;
+    size_t off = 128 + (size_t)WARPS * MG2_RING * 8 + (size_t)p.tiles_per_cta * 4;
+    off = (off + 127) / 128 * 128;
+    p.xf_off = (int)off;
+    off += (size_t)nb_ * gk_max * kpg * 4 * sizeof(uint2);  // k-steps of the K-block (even)
+    off = (off + 127) / 128 * 128;
+    p.sx_off = (int)off;
+    off += (size_t)gk_max * NT * 8 * 4;
+    off = (off + 127) / 128 * 128;
+    p.acc_off = (int)off;
+    const size_t slots = p.parts == 1 ? (size_t)WARPS : (size_t)p.tiles_per_cta * p.parts;
+    off += (slots * 16 * NT * 8 + (WARPS + 1) * 16) * 4;
+    off = (off + 127) / 128 * 128;
+    p.ring_off = (int)off;
+    return off + (size_t)WARPS * p.ring * p.ring_stride;
+  };
   int b0 = 0;
   while (b0 < a.batch) {
     int nb = std::min(16, a.batch - b0);
     p.ring = MG2_RING;
-    auto layout = [&](int nb_) {
-      const int NT = nb_ > 8 ? 2 : 1;
-      size_t off = 128 + (size_t)WARPS * MG2_RING * 8 + (size_t)p.tiles_per_cta * 4;
-      off = (off + 127) / 128 * 128;
-      p.xf_off = (int)off;
-      off += (size_t)nb_ * p.ks_n * 4 * sizeof(uint2);  // ks_n is even (cols % 64 == 0)
-      off = (off + 127) / 128 * 128;
-      p.sx_off = (int)off;
-      off += (size_t)p.G * NT * 8 * 4;
-      off = (off + 127) / 128 * 128;
-      p.acc_off = (int)off;
-      off += ((size_t)p.tiles_per_cta * p.parts * 16 * NT * 8 + (WARPS + 1) * 16) * 4;
-      off = (off + 127) / 128 * 128;
-      p.ring_off = (int)off;
-      return off + (size_t)WARPS * p.ring * p.ring_stride;
-    };
-    while (nb > 1 && layout(nb) > cap) --nb;
+    geometry(1);
     while (p.ring > 2 && layout(nb) > cap) --p.ring;
+    // the chunk's x fragments do not fit: split K over CTAs (partials + fold) when a workspace
+    // is given, else fewer batch columns per pass
+    if (layout(nb) > cap && a.split_ws && !a.swiglu) {
+      int kb_n = 2;
+      for (; kb_n <= std::min(p.G, 16); ++kb_n) {
+        geometry(kb_n);
+        if (layout(nb) <= cap && (int64_t)kb_n * nb * w.rows <= a.split_ws_floats) break;
+      }
+      if (kb_n > std::min(p.G, 16)) geometry(1);
+    }
+    while (nb > 1 && layout(nb) > cap) --nb;
     const size_t smem = layout(nb);
     N730_REQUIRE(smem <= cap, N730_BAD_ARG, "gemv_mma: K=%d too large for shared memory", w.cols);
     const int NT = nb > 8 ? 2 : 1;
     p.x = a.x + (int64_t)b0 * a.ldx; p.ldx = a.ldx; p.batch = nb;
     p.y = a.y + (int64_t)b0 * a.ldy;
     p.residual = a.residual ? a.residual + (int64_t)b0 * a.ldr : nullptr;
+    p.part = p.kb_n > 1 ? a.split_ws : nullptr;
+    p.part_stride = (int64_t)nb * w.rows;
     const bool pdl = a.pdl != 0;
     const int rc = WARPS == 16 ? launch_mma2_w<16>(kpg, NT, p, grid, smem, st, pdl)
                                : launch_mma2_w<8>(kpg, NT, p, grid, smem, st, pdl);
     if (rc) return rc;
+    if (p.kb_n > 1) {
+      const int64_t n = (int64_t)nb * w.rows;
+      const int fg = (int)std::min<int64_t>((n + 255) / 256, ctas * 4);
+      split_fold_kernel<<<fg, 256, 0, st>>>(a.split_ws, p.kb_n, p.part_stride, nb, w.rows, p.y, a.ldy, p.residual,
+                                            a.ldr, a.bias);
+      N730_CUDA(cudaGetLastError());
+    }
     b0 += nb;
   }
   return N730_OK;

@@ -23,6 +23,7 @@
 
 #include "attention.h"
 #include "decode_persist.h"
+#include "tp_allreduce.h"
 #include "n730_cuda.h"
 #include "qweight.h"
 
@@ -121,7 +122,15 @@ struct Model {
   float* logits_all = nullptr;   // [tp][max_batch][vocab / tp]
   int vocab_l = 0;               // lm_head rows on this rank
   float* rms_ws = nullptr;       // [max(max_batch, max_prefill)] per-token 1/rms for the tcgen05 GEMM
+  float* split_ws = nullptr;     // split-K partial sums of batched GEMVs [16][min(max_batch, 16)][hidden]
+  int64_t split_ws_floats = 0;
   unsigned long long* ffn_acc = nullptr;  // persistent decode, fused FFN: [hidden] down_proj sums (fixed point)
+  // one-shot peer-memory allreduce (tp_allreduce.cu): this rank's exchange
+  // region, the peers' regions mapped with CUDA IPC, the op counters
+  void* ar_base = nullptr;
+  std::vector<void*> ar_peer_base;
+  ArArgs ar{};
+  bool ar_ok = false;
 
   template <typename T>
   int alloc(T** p, size_t n) {
@@ -502,6 +511,10 @@ static int finalize(Model* m) {
   if (int rc = m->alloc(&m->mlp, (size_t)B * c.ffn)) return rc;
   if (int rc = m->alloc(&m->logits, (size_t)B * c.vocab)) return rc;
   if (int rc = m->alloc(&m->rms_ws, (size_t)std::max(B, c.max_prefill))) return rc;
+  if (B > 1) {  // split-K partials of batched GEMVs whose x does not fit shared memory (down_proj)
+    m->split_ws_floats = (int64_t)16 * std::min(B, 16) * c.hidden;
+    if (int rc = m->alloc(&m->split_ws, (size_t)m->split_ws_floats)) return rc;
+  }
   if (c.tp_size > 1) {
     if (int rc = m->alloc(&m->delta, (size_t)std::max(B, c.max_prefill) * c.hidden)) return rc;
     if (m->vocab_l != c.vocab)
@@ -531,6 +544,7 @@ static int gemv(Model* m, const QWeight* w, const float* x, int ldx, int batch, 
   a.w = w; a.x = x; a.ldx = ldx; a.batch = batch; a.y = y; a.ldy = ldy; a.bias = bias;
   a.residual = resid; a.ldr = ldr; a.norm_w = norm; a.eps = m->c.rms_eps; a.swiglu = swiglu;
   a.pdl = m->c.use_pdl;
+  if (w->rows <= m->c.hidden) { a.split_ws = m->split_ws; a.split_ws_floats = m->split_ws_floats; }
   if (batch >= GEMM_TC_MIN_TOKENS && gemm_tc_supported(*w, batch) && !m->c.exact_gemv)
     return gemm_tc_launch(a, m->rms_ws, m->st);
   return gemv_launch(a, m->st);
@@ -558,6 +572,13 @@ static int rowsplit_linear(Model* m, const QWeight* w, const float* a, int lda, 
   if (m->c.tp_size <= 1) return gemv(m, w, a, lda, B, x, ldx, bias, x, ldx, nullptr, 0);
   const int h = m->c.hidden;
   if (int rc = gemv(m, w, a, lda, B, m->delta, h, bias, nullptr, 0, nullptr, 0)) return rc;
+  if (m->ar_ok && (int64_t)B * h <= m->ar.cap && ldx == h) {  // decode-sized: one-shot over peer memory
+    ArArgs ar = m->ar;
+    ar.part = m->delta;
+    ar.x = x;
+    ar.n = B * h;
+    return ar_launch(ar, m->st);
+  }
   if (ncclAllReduce(m->delta, m->delta, (size_t)B * h, ncclFloat, ncclSum, m->comm, m->st) != ncclSuccess) {
     set_error("model: ncclAllReduce failed");
     return N730_COMM;
@@ -750,6 +771,54 @@ N730_API int n730_model_tp_init(void* p, const uint8_t* id_bytes, int rank, int 
     set_error("ncclCommInitRank failed (rank %d of %d)", rank, size);
     return N730_COMM;
   }
+  if (size <= AR_MAX_RANKS && m->c.tp_allreduce == 0) {  // exchange region for the one-shot allreduce
+    const int64_t cap = ((int64_t)m->c.max_batch * m->c.hidden + 3) / 4 * 4;
+    N730_CUDA(cudaMalloc(&m->ar_base, ar_region_bytes(size, cap)));
+    N730_CUDA(cudaMemset(m->ar_base, 0, ar_region_bytes(size, cap)));
+    int* ctr = nullptr;
+    if (int rc = m->alloc(&ctr, 2)) return rc;
+    N730_CUDA(cudaMemset(ctr, 0, 8));
+    N730_CUDA(cudaDeviceSynchronize());
+    m->ar.rank = rank;
+    m->ar.size = size;
+    m->ar.cap = cap;
+    m->ar.local = ar_region_at(m->ar_base, size);
+    m->ar.peer[rank] = m->ar.local;
+    m->ar.epoch = ctr;
+    m->ar.done = ctr + 1;
+    m->ar.err = gemv_err_word();
+    N730_REQUIRE(m->ar.err, N730_OOM, "tp_init: error word allocation failed");
+  }
+  return N730_OK;
+}
+
+N730_API int n730_model_tp_ipc_handle(void* p, uint8_t* out) {
+  MODEL(p);
+  N730_REQUIRE(out, N730_NULL, "tp_ipc_handle: null output");
+  N730_REQUIRE(m->ar_base, N730_STATE, "tp_ipc_handle: no exchange region (tp_init first, tp_allreduce 0)");
+  cudaIpcMemHandle_t hd;
+  N730_CUDA(cudaIpcGetMemHandle(&hd, m->ar_base));
+  static_assert(sizeof(cudaIpcMemHandle_t) == N730_IPC_HANDLE_BYTES, "IPC handle size");
+  memcpy(out, &hd, sizeof hd);
+  return N730_OK;
+}
+
+N730_API int n730_model_tp_ipc_open(void* p, const uint8_t* handles, int size) {
+  MODEL(p);
+  N730_REQUIRE(handles, N730_NULL, "tp_ipc_open: null handles");
+  N730_REQUIRE(m->ar_base && size == m->ar.size && !m->ar_ok, N730_STATE,
+               "tp_ipc_open: once, after tp_ipc_handle, with every rank's handle");
+  N730_CUDA(cudaSetDevice(m->device));
+  for (int r = 0; r < size; ++r) {
+    if (r == m->ar.rank) continue;
+    cudaIpcMemHandle_t hd;
+    memcpy(&hd, handles + (size_t)r * sizeof hd, sizeof hd);
+    void* ptr = nullptr;
+    N730_CUDA(cudaIpcOpenMemHandle(&ptr, hd, cudaIpcMemLazyEnablePeerAccess));
+    m->ar_peer_base.push_back(ptr);
+    m->ar.peer[r] = ar_region_at(ptr, size);
+  }
+  m->ar_ok = true;
   return N730_OK;
 }
 
@@ -758,6 +827,8 @@ N730_API void n730_model_destroy(void* p) {
   if (!m) return;
   cudaStreamSynchronize(m->st);
   for (auto& g : m->graphs) cudaGraphExecDestroy(g.second);  // graphs holding NCCL calls go before the comm
+  for (void* q : m->ar_peer_base) cudaIpcCloseMemHandle(q);
+  if (m->ar_base) cudaFree(m->ar_base);
   if (m->comm) ncclCommDestroy(m->comm);
   for (auto& kv : m->pend_w) qweight_destroy(kv.second);
   for (auto& y : m->L) {

@@ -45,6 +45,8 @@ struct GemvArgs {
   float eps;
   int swiglu;            // rows interleaved gate/up: y[b][r/2] = silu(g)*u
   int pdl;               // launched with programmatic dependent launch
+  float* split_ws;       // tensor-core GEMV: workspace for split-K partial sums (null: one K pass per
+  int64_t split_ws_floats;  //   batch chunk that fits shared memory)
 };
 
 int gemv_launch(const GemvArgs& a, cudaStream_t stream);
@@ -52,7 +54,7 @@ int gemv_mma_launch(const GemvArgs& a, cudaStream_t stream);
 // tcgen05 GEMM for many tokens (gemm_tc.cu); inv_ws: batch floats of workspace when norm_w is set
 bool gemm_tc_supported(const QWeight& w, int tokens);
 int gemm_tc_prepare();
-constexpr int GEMM_TC_MIN_TOKENS = 32;  // below this the GEMV streams the weights once per 16 tokens
+constexpr int GEMM_TC_MIN_TOKENS = 128;  // below this the GEMV streams the weights once per 16 tokens
 int gemm_tc_launch(const GemvArgs& a, float* inv_ws, cudaStream_t stream);
 int qweight_to_mma_layout(QWeight& w, cudaStream_t stream);
 int* gemv_err_word();

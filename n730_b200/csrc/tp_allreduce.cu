@@ -1,0 +1,117 @@
+// One-shot allreduce over NVLink peer memory for tensor-parallel decode.
+//
+// The reference sums row-split partials with NCCL (SURVEY target: one
+// exchange per row-split layer, n730's TP plan).  For decode-sized messages
+// (batch x hidden fp32, 32 KB at batch 1 for the 72B shape) an NCCL allreduce
+// is latency-bound; here one kernel does the exchange and the residual add:
+//
+//   CTA s owns slice s of the vector.  It stores its slice of this rank's
+//   partial into recv[par][rank] of EVERY rank (plain stores to peer memory
+//   mapped with CUDA IPC), fences at system scope, and raises flags[par][rank][s]
+//   = epoch on every rank.  It then waits, bounded, until flags[par][r][s] >=
+//   epoch for all r in its own region, and adds the n partials of its slice in
+//   rank order to x (deterministic, identical on every rank).
+//
+// Epochs count the ops done on this rank (device counter, updated by the op's
+// last CTA, so graph replays see fresh epochs).  Slots alternate by epoch
+// parity: a rank can be at most one op ahead of any other (it cannot finish op
+// e+1 before every rank pushed op e+1, which each does only after finishing op
+// e), so the slot a fast rank writes is never the one a slow rank still reads.
+// No TMA, no multicast: plain loads and stores.
+#include "common.cuh"
+#include "tp_allreduce.h"
+
+namespace n730 {
+
+constexpr uint64_t AR_WAIT_NS = 2000000000ull;  // a peer that never arrives: error after 2 s
+
+__device__ __forceinline__ uint64_t ar_timer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ int ar_ld_relaxed_sys(const int* p) {
+  int v;
+  asm volatile("ld.relaxed.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void ar_st_relaxed_sys(int* p, int v) {
+  asm volatile("st.relaxed.sys.global.b32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
+}
+
+__global__ void __launch_bounds__(256) ar_push_reduce_kernel(const ArArgs a) {
+  __shared__ int s_ok;
+  const int s = blockIdx.x, tid = threadIdx.x;
+  const int epoch = *reinterpret_cast<volatile int*>(a.epoch) + 1, par = epoch & 1;
+  // slice [lo, hi) in float4 units
+  const int n4 = a.n >> 2;
+  const int lo = (int)((int64_t)n4 * s / AR_SLICES), hi = (int)((int64_t)n4 * (s + 1) / AR_SLICES);
+  const float4* src = reinterpret_cast<const float4*>(a.part);
+  for (int r = 0; r < a.size; ++r) {
+    float4* dst = reinterpret_cast<float4*>(a.peer[r].recv + ((int64_t)par * a.size + a.rank) * a.cap);
+    for (int i = lo + tid; i < hi; i += blockDim.x) dst[i] = src[i];
+  }
+  __threadfence_system();  // this thread's pushes are visible to every rank before its flag
+  __syncthreads();
+  if (tid < a.size) ar_st_relaxed_sys(a.peer[tid].flags + ((int64_t)par * a.size + a.rank) * AR_SLICES + s, epoch);
+  if (tid == 0) {  // every rank's slice s has arrived here
+    bool ok = true;
+    uint64_t t0 = 0;
+    for (int r = 0; r < a.size && ok; ++r) {
+      const int* f = a.local.flags + ((int64_t)par * a.size + r) * AR_SLICES + s;
+      while (ar_ld_relaxed_sys(f) < epoch) {
+        const uint64_t t = ar_timer();
+        if (!t0) t0 = t;
+        else if (t - t0 > AR_WAIT_NS) { atomicExch(a.err, DEV_ERR_TIMEOUT); ok = false; break; }
+      }
+    }
+    __threadfence_system();
+    s_ok = ok;
+  }
+  __syncthreads();
+  if (s_ok) {
+    float4* x4 = reinterpret_cast<float4*>(a.x);
+    for (int i = lo + tid; i < hi; i += blockDim.x) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int r = 0; r < a.size; ++r) {
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(a.local.recv + ((int64_t)par * a.size + r) * a.cap) + i);
+        acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+      }
+      float4 h = x4[i];
+      h.x += acc.x; h.y += acc.y; h.z += acc.z; h.w += acc.w;
+      x4[i] = h;
+    }
+  }
+  // the op's last CTA records the epoch for the next op (every CTA read it above)
+  if (tid == 0) {
+    __threadfence();
+    if (atomicAdd(a.done, 1) == AR_SLICES - 1) {
+      *a.done = 0;
+      *a.epoch = epoch;
+      __threadfence();
+    }
+  }
+}
+
+size_t ar_region_bytes(int size, int64_t cap) {
+  const size_t fb = ((size_t)2 * size * AR_SLICES * sizeof(int) + 255) / 256 * 256;
+  return fb + (size_t)2 * size * cap * sizeof(float);
+}
+
+ArRegion ar_region_at(void* base, int size) {
+  ArRegion r;
+  r.flags = reinterpret_cast<int*>(base);
+  const size_t fb = ((size_t)2 * size * AR_SLICES * sizeof(int) + 255) / 256 * 256;
+  r.recv = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(base) + fb);
+  return r;
+}
+
+int ar_launch(const ArArgs& a, cudaStream_t st) {
+  N730_REQUIRE(a.size >= 2 && a.size <= AR_MAX_RANKS && a.n % 4 == 0 && a.n <= a.cap, N730_BAD_ARG,
+               "tp allreduce: %d elements, %d ranks, capacity %lld", a.n, a.size, (long long)a.cap);
+  ar_push_reduce_kernel<<<AR_SLICES, 256, 0, st>>>(a);
+  N730_CUDA(cudaGetLastError());
+  return N730_OK;
+}
+
+}  // namespace n730

@@ -32,7 +32,7 @@ class N730ModelConfig(C.Structure):
                [("rms_eps", C.c_float), ("rope_theta", C.c_float)] + \
                [(n, C.c_int32) for n in ("max_ctx", "max_batch", "page_size", "max_prefill", "tie_embeddings",
                                          "tp_rank", "tp_size", "use_graphs", "use_pdl", "exact_gemv",
-                                         "per_op_decode", "stream_depth", "ffn_fuse")]
+                                         "per_op_decode", "stream_depth", "ffn_fuse", "tp_allreduce")]
 
 
 def _sigs(lib):
@@ -68,6 +68,10 @@ def _sigs(lib):
     lib.n730_tp_unique_id.restype = i32
     lib.n730_model_tp_init.argtypes = [vp, vp, i32, i32]
     lib.n730_model_tp_init.restype = i32
+    lib.n730_model_tp_ipc_handle.argtypes = [vp, vp]
+    lib.n730_model_tp_ipc_handle.restype = i32
+    lib.n730_model_tp_ipc_open.argtypes = [vp, vp, i32]
+    lib.n730_model_tp_ipc_open.restype = i32
     lib.n730_model_run_step_kernel.argtypes = [vp, vp]
     lib.n730_model_run_step_kernel.restype = i32
     lib.n730_model_run_linear.argtypes = [vp, i32, i32, vp, i32, vp, vp]
@@ -127,13 +131,14 @@ class Engine:
     def __init__(self, shape: ModelShape, max_ctx: int = 4096, max_batch: int = 1, page_size: int = 64,
                  max_prefill: int = 512, use_graphs: bool = True, use_pdl: bool = True,
                  tp_rank: int = 0, tp_size: int = 1, exact_gemv: bool = False, per_op_decode: bool = False,
-                 stream_depth: int = 0, ffn_fuse: int = 0):
+                 stream_depth: int = 0, ffn_fuse: int = 0, tp_allreduce: int = 1):
         self.lib = _sigs(_lib.cuda())
         self.shape = shape
         c = N730ModelConfig(shape.hidden, shape.layers, shape.heads, shape.kv_heads, shape.head_dim, shape.ffn,
                             shape.vocab, shape.rms_eps, shape.rope_theta, max_ctx, max_batch, page_size,
                             max_prefill, int(shape.tie_embeddings), tp_rank, tp_size, int(use_graphs),
-                            int(use_pdl), int(exact_gemv), int(per_op_decode), int(stream_depth), int(ffn_fuse))
+                            int(use_pdl), int(exact_gemv), int(per_op_decode), int(stream_depth), int(ffn_fuse),
+                            int(tp_allreduce))
         self.cfg = c
         self.h = C.c_void_p()
         _lib.check(self.lib.n730_model_create(C.byref(c), C.byref(self.h)), "model_create")
@@ -197,6 +202,20 @@ class Engine:
     def tp_init(self, id_bytes: bytes, rank: int, size: int):
         buf = (C.c_uint8 * 128).from_buffer_copy(id_bytes)
         _lib.check(self.lib.n730_model_tp_init(self.h, buf, rank, size), "model_tp_init")
+
+    IPC_HANDLE_BYTES = 64
+
+    def tp_ipc_handle(self) -> bytes:
+        """This rank's exchange-region handle for the one-shot allreduce (after tp_init)."""
+        buf = (C.c_uint8 * self.IPC_HANDLE_BYTES)()
+        _lib.check(self.lib.n730_model_tp_ipc_handle(self.h, buf), "model_tp_ipc_handle")
+        return bytes(buf)
+
+    def tp_ipc_open(self, handles: bytes, size: int):
+        """Map every rank's exchange region (handles concatenated in rank order)."""
+        assert len(handles) == size * self.IPC_HANDLE_BYTES
+        buf = (C.c_uint8 * len(handles)).from_buffer_copy(handles)
+        _lib.check(self.lib.n730_model_tp_ipc_open(self.h, buf, size), "model_tp_ipc_open")
 
     def run_step_kernel(self, stream: int = 0):
         """Launch only the persistent decode kernel of a batch-1 step (timing hook)."""

@@ -118,12 +118,21 @@ def shard_block(name: str, b, shape, size: int, rank: int, ffn_group: int):
     return RawBlock(b.layer_idx, b.prec_id, r1 - r0, c1 - c0, 1.0, 0.0, payload, g)
 
 
-def init_engine_comm(engine, rank: int, size: int, group=None):
-    """Share rank 0's NCCL id over torch.distributed (any backend) and join the engine's communicator."""
+def init_engine_comm(engine, rank: int, size: int, group=None, one_shot: bool | None = None):
+    """Share rank 0's NCCL id over torch.distributed (any backend) and join the engine's
+    communicator; for the one-shot allreduce (engine built with tp_allreduce=0, the default of
+    ``one_shot``) also exchange the exchange-region handles and map every rank's region."""
+    if one_shot is None:
+        one_shot = engine.cfg.tp_allreduce == 0
     import torch.distributed as dist
     ids = [engine.tp_unique_id() if rank == 0 else None]
     dist.broadcast_object_list(ids, src=0, group=group)
     engine.tp_init(ids[0], rank, size)
+    if one_shot:
+        handles = [None] * size
+        dist.all_gather_object(handles, engine.tp_ipc_handle(), group=group)
+        engine.tp_ipc_open(b"".join(handles), size)
+        dist.barrier(group=group)  # every region is mapped and zeroed before the first push
 
 
 def ffn_group_of(pmap_fn, down_name: str, default: int = 128) -> int:

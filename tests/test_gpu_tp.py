@@ -1,5 +1,7 @@
-"""Tensor-parallel engine on 2 GPUs (NCCL allreduce after o_proj / down_proj,
-all-gathered vocab-split logits) against the oracle and the 1-GPU engine.
+"""Tensor-parallel engine on 2 GPUs (row-split sums after o_proj / down_proj by
+the one-shot peer-memory allreduce or by NCCL, all-gathered vocab-split
+logits) against the oracle and the 1-GPU engine; decode steps repeated from
+the same cached state are bit-identical.
 
 Runs as two spawned processes, one per GPU; skipped with fewer than 2 GPUs.
 """
@@ -36,7 +38,7 @@ def _run(engine, shape):
     return ys
 
 
-def _worker(rank, size, port, shape_name, path, out):
+def _worker(rank, size, port, shape_name, path, out, allreduce):
     from datetime import timedelta
 
     import torch.distributed as dist
@@ -50,8 +52,8 @@ def _worker(rank, size, port, shape_name, path, out):
         shape = synthetic.SHAPES[shape_name]
         tp.check_shape(shape, size, FFN_GROUP)
         eng = Engine(tp.local_shape(shape, size, rank, FFN_GROUP), max_ctx=256, max_batch=2, max_prefill=32,
-                     tp_rank=rank, tp_size=size)
-        tp.init_engine_comm(eng, rank, size)
+                     tp_rank=rank, tp_size=size, tp_allreduce=allreduce)
+        tp.init_engine_comm(eng, rank, size, one_shot=allreduce == 0)
         blocks = []
         for n, b in _blocks(path):
             sb = tp.shard_block(n, b, shape, size, rank, FFN_GROUP)
@@ -60,11 +62,15 @@ def _worker(rank, size, port, shape_name, path, out):
         load_tensors(eng, blocks)
         eng.finalize()
         ys = _run(eng, shape)
+        # the decode steps again from the same cached prompt: bit-identical (rank-order sums)
+        eng.set_seq_len(0, PROMPT)
+        again = [eng.forward([t]) for t in STEPS]
+        same = all(np.array_equal(a, b) for a, b in zip(ys[1:], again))
         # batched decode: both sequences step together
         eng.forward(np.arange(11) % shape.vocab, seq=1)
         yb = eng.decode(np.array([4, 6], np.int32))
         if rank == 0:
-            out.put((ys, yb.copy()))
+            out.put((ys, yb.copy(), same))
         eng.close()
     except Exception as e:  # report instead of leaving the parent waiting
         out.put(repr(e))
@@ -73,8 +79,9 @@ def _worker(rank, size, port, shape_name, path, out):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("allreduce", [0, 1], ids=["one-shot", "nccl"])
 @pytest.mark.parametrize("shape_name", ["tiny", "tiny-128"])
-def test_tp2_engine(shape_name, tmp_path):
+def test_tp2_engine(shape_name, allreduce, tmp_path):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     shape = synthetic.SHAPES[shape_name]
@@ -83,7 +90,7 @@ def test_tp2_engine(shape_name, tmp_path):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, shape_name, str(path), q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, shape_name, str(path), q, allreduce)) for r in range(2)]
     for p in procs:
         p.start()
     res = q.get(timeout=300)
@@ -91,7 +98,8 @@ def test_tp2_engine(shape_name, tmp_path):
         p.join(timeout=120)
     assert not isinstance(res, str), res
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
-    ys, yb = res
+    ys, yb, same = res
+    assert same
     w = _oracle_weights(_blocks(path))
     orc = OracleDecoder(shape, w, max_pos=256)
     rng = np.random.default_rng(17)
