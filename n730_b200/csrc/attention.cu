@@ -18,7 +18,7 @@
 // and is not reproduced.
 //
 // Prefill uses kv_write (RoPE + cache append for T tokens) and a causal
-// CUDA-core flash-attention kernel; masked keys get weight 0 (the reference
+// tensor-core flash-attention kernel; masked keys get weight 0 (the reference
 // uses -1e4 scores, weight <= e^-50).
 #include <cfloat>
 
@@ -413,91 +413,166 @@ int kv_write_launch(const KVWriteArgs& a, cudaStream_t st) {
   return launch_pdl(kv_write_kernel, dim3(a.T), dim3(256), 0, st, a.pdl, a);
 }
 
-constexpr int PF_Q = 32;     // queries per CTA
-constexpr int PF_K = 64;     // keys per tile
+// Causal prefill attention on the tensor cores (flash-attention style): one
+// CTA per (64-query block, query head), 4 warps of 16 queries.  Q is RoPE'd in
+// place by kv_write, scaled and rounded to fp16 into swizzled shared memory;
+// each warp keeps its A fragments in registers.  Key tiles of 64 positions
+// (K and V, fp16 from the paged cache) are double-buffered with cp.async; per
+// tile S = Q K^T (mma.m16n8k16, K through ldmatrix), the causal mask, an online
+// softmax per query row (quad shuffles), and O += P V with P re-packed from
+// the S fragments as the A operand and V through ldmatrix.trans.  Query blocks
+// are launched latest first (they have the most key tiles).
+constexpr int PF_Q = 64;   // queries per CTA (4 warps x 16)
+constexpr int PF_K = 64;   // keys per tile
+
+template <int HD>
+struct PfSmem {
+  __half q[PF_Q * HD];
+  __half k[2][PF_K * HD];
+  __half v[2][PF_K * HD];
+};
 
 template <int HD>
 __global__ void __launch_bounds__(128) attn_prefill_kernel(const PrefillAttnArgs a) {
-  constexpr int KS = HD + 1;                 // padded strides: conflict-free smem reads
-  constexpr int DPT = HD / 4;                // output dims per thread
-  constexpr int VS = 4 * (DPT + 1);
-  constexpr int PS = PF_K + 1;
-  extern __shared__ float pf[];
-  float* Qs = pf;                      // [PF_Q][HD+1]
-  float* Ks = Qs + PF_Q * KS;          // [PF_K][HD+1]
-  float* Vs = Ks + PF_K * KS;          // [PF_K][4][DPT+1]
-  float* Ps = Vs + PF_K * VS;          // [PF_Q][PF_K+1]
+  constexpr int KS = HD / 16, NCH = HD / 8, NTO = HD / 8;
+  extern __shared__ __align__(128) uint8_t dsm[];
+  PfSmem<HD>& sm = *reinterpret_cast<PfSmem<HD>*>(dsm);
   pdl_wait();
   const AttnDims& d = a.d;
+  const int qb = (int)gridDim.x - 1 - (int)blockIdx.x;
   const int h = blockIdx.y, kvh = h / (d.n_heads / d.n_kv);
-  const int q0 = blockIdx.x * PF_Q;
-  const int tid = threadIdx.x, qi = tid >> 2, kg = tid & 3;
-  const int nq = min(PF_Q, a.T - q0);
-  for (int i = tid; i < PF_Q * HD; i += 128) {
-    const int r = i / HD, c = i % HD;
-    Qs[r * KS + c] = r < nq ? a.qkv[(int64_t)(q0 + r) * a.ld_qkv + (int64_t)h * HD + c] * d.scale : 0.f;
+  const int q0 = qb * PF_Q, nq = min(PF_Q, a.T - q0);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, tq = lane & 3;
+  const int kend = a.pos0 + q0 + nq;  // keys [0, kend) are needed by the CTA
+  const int ntiles = (kend + PF_K - 1) / PF_K;
+  const uint32_t qs = smem_u32(sm.q);
+  const uint32_t kb[2] = {smem_u32(sm.k[0]), smem_u32(sm.k[1])};
+  const uint32_t vb[2] = {smem_u32(sm.v[0]), smem_u32(sm.v[1])};
+
+  auto stage = [&](int t, int buf) {  // K and V rows [t*PF_K, +PF_K) (zero past kend)
+    const int k0 = t * PF_K;
+    for (int i = tid; i < PF_K * NCH; i += 128) {
+      const int r = i / NCH, c = i % NCH;
+      const bool ok = k0 + r < kend;
+      const int p = ok ? k0 + r : k0;
+      cp_async16(kb[buf] + swz<HD>(r, c), page_ptr(a.kv.k_pages, a.block_table, p, d, kvh) + c * 8, ok);
+      cp_async16(vb[buf] + swz<HD>(r, c), page_ptr(a.kv.v_pages, a.block_table, p, d, kvh) + c * 8, ok);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  stage(0, 0);
+  for (int i = tid; i < PF_Q * NCH; i += 128) {  // scaled fp16 queries, rows >= nq zero
+    const int r = i / NCH, c = i % NCH;
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+    if (r < nq) {
+      const float4* src = reinterpret_cast<const float4*>(a.qkv + (int64_t)(q0 + r) * a.ld_qkv + (int64_t)h * HD + c * 8);
+      const float4 x0 = src[0], x1 = src[1];
+      w[0] = pack_half2(x0.x * d.scale, x0.y * d.scale); w[1] = pack_half2(x0.z * d.scale, x0.w * d.scale);
+      w[2] = pack_half2(x1.x * d.scale, x1.y * d.scale); w[3] = pack_half2(x1.z * d.scale, x1.w * d.scale);
+    }
+    *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(sm.q) + swz<HD>(r, c)) = make_uint4(w[0], w[1], w[2], w[3]);
   }
-  float acc[DPT];
+  __syncthreads();
+  pdl_launch_dependents();
+  uint32_t qa[KS][4];
 #pragma unroll
-  for (int j = 0; j < DPT; ++j) acc[j] = 0.f;
-  float m = -INFINITY, l = 0.f;
-  const int qpos = a.pos0 + q0 + qi;                 // this thread's query position
-  const int kend = a.pos0 + q0 + nq;                 // keys [0, kend) are needed by the CTA
-  for (int k0 = 0; k0 < kend; k0 += PF_K) {
+  for (int ks = 0; ks < KS; ++ks)
+    ldsm_x4(qs + swz<HD>(warp * 16 + (lane & 15), ks * 2 + (lane >> 4)), qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3]);
+  float o[NTO][4];
+#pragma unroll
+  for (int n = 0; n < NTO; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float mr[2] = {-INFINITY, -INFINITY}, lr[2] = {0.f, 0.f};  // rows g and g+8
+  const int qp = a.pos0 + q0 + warp * 16 + g;                 // position of row g (row g+8: qp + 8)
+  const int mi = lane >> 3, rr = lane & 7;
+
+  for (int t = 0; t < ntiles; ++t) {
+    const int buf = t & 1;
+    if (t + 1 < ntiles) {
+      stage(t + 1, buf ^ 1);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
     __syncthreads();
-    for (int i = tid; i < PF_K * HD; i += 128) {
-      const int r = i / HD, c = i % HD;
-      const int p = k0 + r;
-      float kv = 0.f, vv = 0.f;
-      if (p < kend) {
-        kv = __half2float(page_ptr(a.kv.k_pages, a.block_table, p, d, kvh)[c]);
-        vv = __half2float(page_ptr(a.kv.v_pages, a.block_table, p, d, kvh)[c]);
+    const int k0 = t * PF_K;
+    // ---- S = Q K^T, 8 n-tiles of 8 keys ----
+    float sc[8][4];
+#pragma unroll
+    for (int n = 0; n < 8; ++n) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(kb[buf] + swz<HD>(np * 16 + (mi >> 1) * 8 + rr, ks * 2 + (mi & 1)), b0, b1, b2, b3);
+        mma_16816(sc[2 * np], qa[ks], b0, b1);
+        mma_16816(sc[2 * np + 1], qa[ks], b2, b3);
       }
-      Ks[r * KS + c] = kv;
-      Vs[r * VS + (c / DPT) * (DPT + 1) + (c % DPT)] = vv;
     }
-    __syncthreads();
-    float s[PF_K / 4];
-    float mt = -INFINITY;
+    // ---- causal mask, online softmax (rows g: c0 c1, g+8: c2 c3) ----
+    float mt[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-    for (int j = 0; j < PF_K / 4; ++j) {
-      const int kk = kg + 4 * j;
-      float dot = 0.f;
-#pragma unroll 8
-      for (int c = 0; c < HD; ++c) dot = fmaf(Qs[qi * KS + c], Ks[kk * KS + c], dot);
-      const int p = k0 + kk;
-      s[j] = (qi < nq && p <= qpos) ? dot : -INFINITY;
-      mt = fmaxf(mt, s[j]);
+    for (int n = 0; n < 8; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int kp = k0 + n * 8 + 2 * tq + (e & 1);
+        const int row_p = qp + (e >> 1) * 8;
+        if (kp > row_p || kp >= kend) sc[n][e] = -INFINITY;
+        mt[e >> 1] = fmaxf(mt[e >> 1], sc[n][e]);
+      }
+    float al[2];
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      mt[hr] = fmaxf(mt[hr], __shfl_xor_sync(0xffffffffu, mt[hr], 1));
+      mt[hr] = fmaxf(mt[hr], __shfl_xor_sync(0xffffffffu, mt[hr], 2));
+      const float mn = fmaxf(mr[hr], mt[hr]);
+      al[hr] = (mr[hr] == -INFINITY || mn == -INFINITY) ? 0.f : __expf(mr[hr] - mn);
+      mr[hr] = mn;
     }
-    mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 1));
-    mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 2));
-    const float mn = fmaxf(m, mt);
-    float ts = 0.f;
+    float ts[2] = {0.f, 0.f};
 #pragma unroll
-    for (int j = 0; j < PF_K / 4; ++j) {
-      const float e = s[j] == -INFINITY ? 0.f : __expf(s[j] - mn);
-      Ps[qi * PS + kg + 4 * j] = e;
-      ts += e;
+    for (int n = 0; n < 8; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float v = sc[n][e] == -INFINITY ? 0.f : __expf(sc[n][e] - mr[e >> 1]);
+        sc[n][e] = v;
+        ts[e >> 1] += v;
+      }
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      ts[hr] += __shfl_xor_sync(0xffffffffu, ts[hr], 1);
+      ts[hr] += __shfl_xor_sync(0xffffffffu, ts[hr], 2);
+      lr[hr] = lr[hr] * al[hr] + ts[hr];
     }
-    ts += __shfl_xor_sync(0xffffffffu, ts, 1);
-    ts += __shfl_xor_sync(0xffffffffu, ts, 2);
-    const float al = m == -INFINITY ? 0.f : __expf(m - mn);
-    l = l * al + ts;
-    m = mn;
-    __syncwarp();
 #pragma unroll
-    for (int j = 0; j < DPT; ++j) acc[j] *= al;
-    for (int kk = 0; kk < PF_K; ++kk) {
-      const float pv = Ps[qi * PS + kk];
+    for (int n = 0; n < NTO; ++n) { o[n][0] *= al[0]; o[n][1] *= al[0]; o[n][2] *= al[1]; o[n][3] *= al[1]; }
+    // ---- O += P V: 4 k-steps of 16 keys, P from the S fragments ----
 #pragma unroll
-      for (int j = 0; j < DPT; ++j) acc[j] = fmaf(pv, Vs[kk * VS + kg * (DPT + 1) + j], acc[j]);
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t pa[4] = {pack_half2(sc[2 * j][0], sc[2 * j][1]), pack_half2(sc[2 * j][2], sc[2 * j][3]),
+                              pack_half2(sc[2 * j + 1][0], sc[2 * j + 1][1]),
+                              pack_half2(sc[2 * j + 1][2], sc[2 * j + 1][3])};
+#pragma unroll
+      for (int n2 = 0; n2 < HD / 16; ++n2) {
+        uint32_t v0, v1, v2, v3;
+        ldsm_x4_t(vb[buf] + swz<HD>(j * 16 + (mi & 1) * 8 + rr, n2 * 2 + (mi >> 1)), v0, v1, v2, v3);
+        mma_16816(o[2 * n2], pa, v0, v1);
+        mma_16816(o[2 * n2 + 1], pa, v2, v3);
+      }
     }
+    __syncthreads();  // buffer buf is refilled by the stage of tile t + 2
   }
-  if (qi < nq) {
-    const float inv = 1.f / (l + 1e-9f);
-    float* o = a.out + (int64_t)(q0 + qi) * d.n_heads * HD + (int64_t)h * HD + kg * DPT;
+  // ---- normalise and store rows g and g+8 of this warp ----
 #pragma unroll
-    for (int j = 0; j < DPT; ++j) o[j] = acc[j] * inv;
+  for (int hr = 0; hr < 2; ++hr) {
+    const int r = warp * 16 + g + hr * 8;
+    if (r >= nq) continue;
+    const float inv = 1.f / (lr[hr] + 1e-9f);
+    float* out = a.out + (int64_t)(q0 + r) * d.n_heads * HD + (int64_t)h * HD;
+#pragma unroll
+    for (int n = 0; n < NTO; ++n)
+      *reinterpret_cast<float2*>(out + n * 8 + 2 * tq) = make_float2(o[n][hr * 2] * inv, o[n][hr * 2 + 1] * inv);
   }
 }
 
@@ -505,24 +580,24 @@ int attn_prefill_launch(const PrefillAttnArgs& a, cudaStream_t st) {
   const AttnDims& d = a.d;
   if (a.T <= 0) return N730_OK;
   N730_REQUIRE(d.head_dim == 64 || d.head_dim == 128, N730_UNSUPPORTED, "attention: head_dim %d", d.head_dim);
+  N730_REQUIRE(a.ld_qkv % 4 == 0 && ((uintptr_t)a.qkv & 15) == 0, N730_BAD_ARG, "attention: qkv alignment");
   dim3 grid((a.T + PF_Q - 1) / PF_Q, d.n_heads);
-  const int HD = d.head_dim;
-  const size_t smem = ((size_t)PF_Q * (HD + 1) + PF_K * (HD + 1) + PF_K * 4 * (HD / 4 + 1) + PF_Q * (PF_K + 1)) *
-                      sizeof(float);
-  if (HD == 128) {
+  if (d.head_dim == 128) {
     static bool cfg = false;
     if (!cfg) {
-      N730_CUDA(cudaFuncSetAttribute(attn_prefill_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      N730_CUDA(cudaFuncSetAttribute(attn_prefill_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)sizeof(PfSmem<128>)));
       cfg = true;
     }
-    return launch_pdl(attn_prefill_kernel<128>, grid, dim3(128), smem, st, a.pdl, a);
+    return launch_pdl(attn_prefill_kernel<128>, grid, dim3(128), sizeof(PfSmem<128>), st, a.pdl, a);
   }
   static bool cfg64 = false;
   if (!cfg64) {
-    N730_CUDA(cudaFuncSetAttribute(attn_prefill_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    N730_CUDA(cudaFuncSetAttribute(attn_prefill_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)sizeof(PfSmem<64>)));
     cfg64 = true;
   }
-  return launch_pdl(attn_prefill_kernel<64>, grid, dim3(128), smem, st, a.pdl, a);
+  return launch_pdl(attn_prefill_kernel<64>, grid, dim3(128), sizeof(PfSmem<64>), st, a.pdl, a);
 }
 
 }  // namespace n730
