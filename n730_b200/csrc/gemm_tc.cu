@@ -5,15 +5,19 @@
 // with the decoder's epilogues: bias, residual add (in place), SwiGLU of
 // interleaved gate/up rows, and RMSNorm folded into the A operand.
 //
-// One CTA computes a 128-token x 128-row output tile over K in steps of 64:
-//  * all 8 warps stage the step's A tile (x, normalised, rounded to fp16) and
-//    B tile (codes -> (q - z) * s in fp32 -> fp16) into shared memory in the
-//    K-major, 128-byte-swizzled layout the UMMA shared-memory descriptors
-//    read (8-row x 128-byte atoms, 16-byte chunk c of row r at c ^ (r % 8));
-//  * one thread issues four tcgen05.mma.kind::f16 (M 128, N 128, K 16, fp32
-//    accumulate in tensor memory) and a tcgen05.commit that frees the stage
-//    when those MMAs have read it; the next step's staging overlaps them
-//    (2 stages);
+// A pre-pass packs x once per call (RMS-normalised, rounded to fp16) into
+// 128-token x 64-column blocks already in the K-major, 128-byte-swizzled
+// layout the UMMA shared-memory descriptors read (8-row x 128-byte atoms,
+// 16-byte chunk c of row r at c ^ (r % 8)).  One CTA computes a 128-token x
+// 128-row output tile over K in steps of 64 through a 4-stage pipeline:
+//  * one thread keeps three steps of bulk copies in flight: the packed A tile
+//    and, per 16-row tile of W, the step's 512-byte code quad and the group's
+//    scale/zero block;
+//  * all 8 warps dequantise a landed step's codes ((q - z) * s in fp32 -> fp16)
+//    into the swizzled B tile;
+//  * the same thread issues four tcgen05.mma.kind::f16 (M 128, N 128, K 16,
+//    fp32 accumulate in tensor memory) and a tcgen05.commit to the stage's
+//    empty barrier, which gates that stage's next copies;
 //  * after the last step the accumulator is read back with tcgen05.ld
 //    (32 lanes x 32 columns per warp and instruction) and written with the
 //    epilogue.
@@ -29,16 +33,17 @@
 
 namespace n730 {
 
-constexpr int TC_BM = 128, TC_BN = 128, TC_BK = 64, TC_STAGES = 2, TC_THREADS = 256;
+constexpr int TC_BM = 128, TC_BN = 128, TC_BK = 64, TC_STAGES = 4, TC_THREADS = 256;
 constexpr int TC_TILE = TC_BM * TC_BK * 2;  // bytes of one fp16 operand tile (A or B)
+constexpr int TC_RAW = 8 * 576;             // one k-step quad (512 B) + scale/zero block (64 B) per 16-row tile
+constexpr int TC_STAGE = 2 * TC_TILE + 5120;  // A | B | raw B, a multiple of 1024
 constexpr uint32_t TC_TMEM_COLS = 128;      // fp32 accumulator columns (N)
 
 struct TcArgs {
   const uint8_t* blob;  // fragment tiles: group u = tile*G + g at u * (kpg*128 + 64)
   int rows, cols, G, kpg;
-  const float* x; int ldx; int T;
-  const float* inv_rms;  // [T] per-token 1/rms, or null (no norm)
-  const float* norm_w;   // [cols]
+  const uint8_t* x16;   // packed A: [token tile][k-step] blocks of 128 x 64 fp16, 128B-swizzled
+  int T;
   float* y; int ldy;
   const float* bias;
   const float* residual; int ldr;
@@ -94,21 +99,59 @@ __device__ __forceinline__ uint32_t sw128(int r, int k) {
   return (uint32_t)(r * 128 + ((((k >> 3) ^ (r & 7)) & 7) << 4) + ((k & 7) << 1));
 }
 
+// A operand packing: x [T][ldx] (RMS-normalised with inv_rms and norm_w when
+// given) -> fp16 blocks of 128 tokens x 64 columns, each laid out exactly as
+// the GEMM's shared-memory A tile (row r: 128 bytes, 16-byte chunk c at
+// c ^ (r % 8)); tokens >= T are zero.  Grid (K / 64, token tiles).
+__global__ void x16_pack_kernel(const float* x, int ldx, int T, const float* inv_rms, const float* norm_w,
+                                uint8_t* out) {
+  const int kb = blockIdx.x, tt = blockIdx.y;
+  uint8_t* blk = out + ((size_t)tt * gridDim.x + kb) * TC_TILE;
+  for (int i = threadIdx.x; i < TC_BM * 8; i += blockDim.x) {
+    const int r = i >> 3, c8 = i & 7, tok = tt * TC_BM + r, k = kb * TC_BK + c8 * 8;
+    uint4 pk = make_uint4(0u, 0u, 0u, 0u);
+    if (tok < T) {
+      const float4* src = reinterpret_cast<const float4*>(x + (int64_t)tok * ldx + k);
+      float4 a = src[0], b = src[1];
+      if (inv_rms) {
+        const float iv = inv_rms[tok];
+        const float4* nw = reinterpret_cast<const float4*>(norm_w + k);
+        const float4 na = nw[0], nb = nw[1];
+        a.x *= iv * na.x; a.y *= iv * na.y; a.z *= iv * na.z; a.w *= iv * na.w;
+        b.x *= iv * nb.x; b.y *= iv * nb.y; b.z *= iv * nb.z; b.w *= iv * nb.w;
+      }
+      pk = make_uint4(h2u(__floats2half2_rn(a.x, a.y)), h2u(__floats2half2_rn(a.z, a.w)),
+                      h2u(__floats2half2_rn(b.x, b.y)), h2u(__floats2half2_rn(b.z, b.w)));
+    }
+    *reinterpret_cast<uint4*>(blk + r * 128 + ((c8 ^ (r & 7)) << 4)) = pk;
+  }
+}
+
+// One CTA per 128-token x 128-row output tile; K in steps of 64 through a
+// 4-stage pipeline.  Thread 0 is the producer and the MMA issuer: it keeps the
+// bulk copies of the next 3 steps in flight (the packed A tile, and per 16-row
+// tile the step's 512-byte code quad plus the group's scale/zero block); all
+// 8 warps dequantise a landed step's codes (warp w: row tile w) into the
+// swizzled fp16 B tile; thread 0 then issues the step's four MMAs and commits
+// them to the stage's empty barrier, which gates the stage's next copies.
 __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_kernel(const TcArgs p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* As = smem;                                 // [STAGES][TC_TILE]
-  uint8_t* Bs = smem + TC_STAGES * TC_TILE;           // [STAGES][TC_TILE]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(Bs + TC_STAGES * TC_TILE);  // empty[STAGES], done
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + TC_STAGES + 1);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + TC_STAGES * TC_STAGE);  // [STAGES]
+  uint64_t* empty = full + TC_STAGES;                                          // [STAGES]
+  uint64_t* done = empty + TC_STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   int* flag = reinterpret_cast<int*>(tmem_slot + 1);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int n0 = blockIdx.x * TC_BN, m0 = blockIdx.y * TC_BM;
+  const int n0 = blockIdx.x * TC_BN, tt = blockIdx.y, m0 = tt * TC_BM;
   const int GB = p.kpg * 128 + 64;
-  const int n_tiles = (p.rows + 15) >> 4;
+  const int n_tiles = (p.rows + 15) >> 4, tile0 = n0 >> 4;
+  const int nt_here = min(8, n_tiles - tile0);  // 16-row tiles of W in this CTA's B (>= 1)
+  const uint32_t stage_tx = (uint32_t)(TC_TILE + nt_here * 576);
+  const int KT = p.cols / TC_BK;
 
   if (tid == 0) {
-    for (int s = 0; s <= TC_STAGES; ++s) mbar_init(&bars[s], 1);
+    for (int s = 0; s < 2 * TC_STAGES + 1; ++s) mbar_init(&full[s], 1);
     fence_mbar_init();
     *flag = 0;
   }
@@ -122,49 +165,40 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_kernel(const TcArgs p) 
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  const int KT = p.cols / TC_BK;
-  int issued = 0;  // k-steps whose MMAs were issued (thread 0)
+  auto produce = [&](int kt) {  // thread 0
+    const int s = kt % TC_STAGES;
+    uint8_t* st = smem + s * TC_STAGE;
+    mbar_arrive_expect_tx(&full[s], stage_tx);
+    bulk_g2s(st, p.x16 + ((size_t)tt * KT + kt) * TC_TILE, TC_TILE, &full[s]);
+    const int s0 = kt * 4, gi = s0 / p.kpg, s4 = (s0 % p.kpg) >> 2;
+    for (int w = 0; w < nt_here; ++w) {
+      const uint8_t* grp = p.blob + ((int64_t)(tile0 + w) * p.G + gi) * GB;
+      bulk_g2s(st + 2 * TC_TILE + w * 576, grp + s4 * 512, 512, &full[s]);
+      bulk_g2s(st + 2 * TC_TILE + w * 576 + 512, grp + p.kpg * 128, 64, &full[s]);
+    }
+  };
+  int produced = 0, issued = 0;
+  if (tid == 0)
+    for (; produced < min(TC_STAGES, KT); ++produced) produce(produced);
+
   for (int kt = 0; kt < KT; ++kt) {
     const int s = kt % TC_STAGES;
-    if (kt >= TC_STAGES) {  // the MMAs that read this stage last must be done
-      if (tid == 0 && !wait_bar(&bars[s], (uint32_t)(((kt / TC_STAGES) - 1) & 1))) {
-        atomicExch(p.err, DEV_ERR_TIMEOUT);
-        *flag = 1;
-      }
-      __syncthreads();
-      if (*flag) break;
+    uint8_t* st = smem + s * TC_STAGE;
+    if (tid == 0 && !wait_bar(&full[s], (uint32_t)((kt / TC_STAGES) & 1))) {
+      atomicExch(p.err, DEV_ERR_TIMEOUT);
+      *flag = 1;
     }
-    uint8_t* as = As + s * TC_TILE;
-    uint8_t* bs = Bs + s * TC_TILE;
-    // ---- A: x rows m0.., columns kt*64.., (RMS-normalised) to fp16 ----
-    for (int i = tid; i < TC_BM * 8; i += TC_THREADS) {
-      const int r = i >> 3, c8 = i & 7, tok = m0 + r, k = kt * TC_BK + c8 * 8;
-      uint4 pk = make_uint4(0u, 0u, 0u, 0u);
-      if (tok < p.T) {
-        const float4* src = reinterpret_cast<const float4*>(p.x + (int64_t)tok * p.ldx + k);
-        float4 a = src[0], b = src[1];
-        if (p.inv_rms) {
-          const float iv = p.inv_rms[tok];
-          const float4* nw = reinterpret_cast<const float4*>(p.norm_w + k);
-          const float4 na = nw[0], nb = nw[1];
-          a.x *= iv * na.x; a.y *= iv * na.y; a.z *= iv * na.z; a.w *= iv * na.w;
-          b.x *= iv * nb.x; b.y *= iv * nb.y; b.z *= iv * nb.z; b.w *= iv * nb.w;
-        }
-        pk = make_uint4(h2u(__floats2half2_rn(a.x, a.y)), h2u(__floats2half2_rn(a.z, a.w)),
-                        h2u(__floats2half2_rn(b.x, b.y)), h2u(__floats2half2_rn(b.z, b.w)));
-      }
-      *reinterpret_cast<uint4*>(as + r * 128 + ((c8 ^ (r & 7)) << 4)) = pk;
-    }
-    // ---- B: rows n0.. from the fragment tiles: warp w = row tile, lane = fragment lane ----
+    __syncthreads();
+    if (*flag) break;
+    // ---- B: warp w dequantises row tile w's quad: lane's word j holds k-step j of its fragment ----
     {
-      const int tile = (n0 >> 4) + warp;
-      const int s0 = kt * 4, gi = s0 / p.kpg, s4 = (s0 % p.kpg) >> 2;
+      uint8_t* bs = st + TC_TILE;
       const int r0 = warp * 16 + (lane >> 2), r1 = r0 + 8;  // rows within the B tile
       const int kb = 2 * (lane & 3);
-      if (tile < n_tiles) {
-        const uint8_t* grp = p.blob + ((int64_t)tile * p.G + gi) * GB;
-        const uint4 w4 = __ldg(reinterpret_cast<const uint4*>(grp + s4 * 512 + lane * 16));
-        const uint2 szv = __ldg(reinterpret_cast<const uint2*>(grp + p.kpg * 128 + (lane >> 2) * 8));
+      if (warp < nt_here) {
+        const uint8_t* raw = st + 2 * TC_TILE + warp * 576;
+        const uint4 w4 = *reinterpret_cast<const uint4*>(raw + lane * 16);
+        const uint2 szv = *reinterpret_cast<const uint2*>(raw + 512 + (lane >> 2) * 8);
         const float2 sc = __half22float2(u2h(szv.x)), zp = __half22float2(u2h(szv.y));
         const uint32_t wv[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
@@ -198,19 +232,31 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_kernel(const TcArgs p) 
     __syncthreads();
     if (tid == 0) {
       tc_fence_after();
-      const uint32_t a0 = smem_u32(as), b0 = smem_u32(bs);
+      const uint32_t a0 = smem_u32(st), b0 = smem_u32(st + TC_TILE);
 #pragma unroll
       for (int j = 0; j < TC_BK / 16; ++j)  // K = 16 per MMA: 32 bytes along the swizzled row
         tc_mma(tmem, umma_desc_sw128(a0 + j * 32), umma_desc_sw128(b0 + j * 32), (kt > 0 || j > 0) ? 1u : 0u);
-      tc_commit(&bars[s]);
+      tc_commit(&empty[s]);
       ++issued;
+      // refill the slot of step kt - 1 (its MMAs were issued a step ago) with step kt - 1 + STAGES
+      if (kt >= 1 && produced < KT) {
+        const int ps = (kt - 1) % TC_STAGES;
+        if (wait_bar(&empty[ps], (uint32_t)(((kt - 1) / TC_STAGES) & 1))) {
+          produce(produced);
+          ++produced;
+        } else {
+          atomicExch(p.err, DEV_ERR_TIMEOUT);
+          *flag = 1;
+        }
+      }
     }
   }
-  // all MMAs issued so far complete -> done barrier
+  // all MMAs issued so far complete -> done barrier; copies still in flight (abort) are waited for
   if (tid == 0) {
+    for (int q = issued; q < produced; ++q) wait_bar(&full[q % TC_STAGES], (uint32_t)((q / TC_STAGES) & 1));
     if (issued > 0) {
-      tc_commit(&bars[TC_STAGES]);
-      if (!wait_bar(&bars[TC_STAGES], 0)) {
+      tc_commit(done);
+      if (!wait_bar(done, 0)) {
         atomicExch(p.err, DEV_ERR_TIMEOUT);
         *flag = 1;
       }
@@ -278,7 +324,7 @@ __global__ void inv_rms_kernel(const float* x, int ldx, int T, int K, float eps,
 
 int* gemv_err_word();
 
-constexpr size_t TC_SMEM = 1024 + 2 * TC_STAGES * TC_TILE + 64;
+constexpr size_t TC_SMEM = 1024 + (size_t)TC_STAGES * TC_STAGE + (2 * TC_STAGES + 1) * 8 + 16;
 
 // One-time kernel attribute set-up (call before any stream capture).
 int gemm_tc_prepare() {
@@ -294,6 +340,29 @@ bool gemm_tc_supported(const QWeight& w, int T) {
   return w.layout == 1 && w.bits == 4 && w.cols % TC_BK == 0 && (w.group / 16) % 4 == 0 && T >= 1;
 }
 
+// Packed-A workspace of the current device, grown on demand (never inside a stream capture).
+static int x16_workspace(size_t bytes, cudaStream_t st, uint8_t** out) {
+  static uint8_t* buf[64] = {};
+  static size_t cap[64] = {};
+  int dev = 0;
+  N730_CUDA(cudaGetDevice(&dev));
+  N730_REQUIRE(dev >= 0 && dev < 64, N730_BAD_ARG, "gemm_tc: device %d", dev);
+  if (cap[dev] < bytes) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    N730_CUDA(cudaStreamIsCapturing(st, &cs));
+    N730_REQUIRE(cs == cudaStreamCaptureStatusNone, N730_STATE,
+                 "gemm_tc: packed-A workspace must grow outside stream capture (%zu bytes)", bytes);
+    N730_CUDA(cudaStreamSynchronize(st));  // a kernel in flight may still read the old buffer
+    if (buf[dev]) N730_CUDA(cudaFree(buf[dev]));
+    buf[dev] = nullptr;
+    cap[dev] = 0;
+    N730_CUDA(cudaMalloc(&buf[dev], bytes));
+    cap[dev] = bytes;
+  }
+  *out = buf[dev];
+  return N730_OK;
+}
+
 int gemm_tc_launch(const GemvArgs& a, float* inv_ws, cudaStream_t st) {
   const QWeight& w = *a.w;
   N730_REQUIRE(gemm_tc_supported(w, a.batch), N730_UNSUPPORTED, "gemm_tc: needs INT4 fragment tiles, K %% 64 == 0");
@@ -303,18 +372,22 @@ int gemm_tc_launch(const GemvArgs& a, float* inv_ws, cudaStream_t st) {
                "gemm_tc: RMSNorm needs a workspace of batch floats and 16-byte aligned weights");
   int* err = gemv_err_word();
   N730_REQUIRE(err, N730_OOM, "gemm_tc: error word allocation failed");
+  if (int rc = gemm_tc_prepare()) return rc;
+  const int TT = (a.batch + TC_BM - 1) / TC_BM, KT = w.cols / TC_BK;
+  uint8_t* x16 = nullptr;
+  if (int rc = x16_workspace((size_t)TT * KT * TC_TILE, st, &x16)) return rc;
   if (a.norm_w) {
     inv_rms_kernel<<<(a.batch + 7) / 8, 256, 0, st>>>(a.x, a.ldx, a.batch, w.cols, a.eps, inv_ws);
     N730_CHECK_LAUNCH();
   }
+  x16_pack_kernel<<<dim3(KT, TT), 256, 0, st>>>(a.x, a.ldx, a.batch, a.norm_w ? inv_ws : nullptr, a.norm_w, x16);
+  N730_CHECK_LAUNCH();
   TcArgs p = {};
   p.blob = w.codes; p.rows = w.rows; p.cols = w.cols; p.G = w.n_groups; p.kpg = w.group / 16;
-  p.x = a.x; p.ldx = a.ldx; p.T = a.batch;
-  p.inv_rms = a.norm_w ? inv_ws : nullptr; p.norm_w = a.norm_w;
+  p.x16 = x16; p.T = a.batch;
   p.y = a.y; p.ldy = a.ldy; p.bias = a.bias; p.residual = a.residual; p.ldr = a.ldr; p.swiglu = a.swiglu;
   p.err = err;
-  if (int rc = gemm_tc_prepare()) return rc;
-  const dim3 grid((w.rows + TC_BN - 1) / TC_BN, (a.batch + TC_BM - 1) / TC_BM);
+  const dim3 grid((w.rows + TC_BN - 1) / TC_BN, TT);
   gemm_tc_kernel<<<grid, TC_THREADS, TC_SMEM, st>>>(p);
   N730_CHECK_LAUNCH();
   return N730_OK;
