@@ -33,7 +33,7 @@
 
 namespace n730 {
 
-constexpr int TC_BM = 128, TC_BN = 128, TC_BK = 64, TC_STAGES = 4, TC_THREADS = 256;
+constexpr int TC_BM = 128, TC_BN = 128, TC_BK = 64, TC_STAGES = 4;
 constexpr int TC_TILE = TC_BM * TC_BK * 2;  // bytes of one fp16 operand tile (A or B)
 constexpr int TC_RAW = 8 * 576;             // one k-step quad (512 B) + scale/zero block (64 B) per 16-row tile
 constexpr int TC_STAGE = 2 * TC_TILE + 5120;  // A | B | raw B, a multiple of 1024
@@ -127,21 +127,43 @@ __global__ void x16_pack_kernel(const float* x, int ldx, int T, const float* inv
   }
 }
 
+// Bounded mbarrier wait that also gives up when another role raised the
+// CTA's abort flag; raises it itself after 2 s.
+__device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile int* abortf) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = gtimer();
+  while (!mbar_try_wait(bar, parity)) {
+    if (*abortf) return false;
+    if (gtimer() - t0 > 2000000000ull) { *abortf = 1; return false; }
+  }
+  return true;
+}
+__device__ __forceinline__ void mbar_arrive1(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" :: "r"(smem_u32(bar)) : "memory");
+}
+
 // One CTA per 128-token x 128-row output tile; K in steps of 64 through a
-// 4-stage pipeline.  Thread 0 is the producer and the MMA issuer: it keeps the
-// bulk copies of the next 3 steps in flight (the packed A tile, and per 16-row
-// tile the step's 512-byte code quad plus the group's scale/zero block); all
-// 8 warps dequantise a landed step's codes (warp w: row tile w) into the
-// swizzled fp16 B tile; thread 0 then issues the step's four MMAs and commits
-// them to the stage's empty barrier, which gates the stage's next copies.
-__global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_kernel(const TcArgs p) {
+// 4-stage pipeline with specialised warps and no CTA-wide barrier in the loop:
+//  * warp 8 (producer): once a stage's MMAs are done (empty[s]) it issues the
+//    next step's bulk copies into it (the packed A tile; per 16-row tile of W
+//    the step's 512-byte code quad and the group's scale/zero block) -> full[s];
+//  * warps 0-7 (dequant, then epilogue): warp w waits for full[s], turns row
+//    tile w's codes into (q - z) * s fp16 in the swizzled B tile and arrives on
+//    conv[s];
+//  * warp 9 (MMA): waits for conv[s], issues four tcgen05.mma.kind::f16 and
+//    commits them to empty[s]; after the last step, to `done`.
+constexpr int TC_WARPS = 10;
+
+__global__ void __launch_bounds__(TC_WARPS * 32, 1) gemm_tc_kernel(const TcArgs p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + TC_STAGES * TC_STAGE);  // [STAGES]
-  uint64_t* empty = full + TC_STAGES;                                          // [STAGES]
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + TC_STAGES * TC_STAGE);  // [STAGES] copies landed
+  uint64_t* conv = full + TC_STAGES;                                           // [STAGES] B tile converted
+  uint64_t* empty = conv + TC_STAGES;                                          // [STAGES] MMAs done
   uint64_t* done = empty + TC_STAGES;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
-  int* flag = reinterpret_cast<int*>(tmem_slot + 1);
+  volatile int* abortf = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* counts = const_cast<int*>(abortf) + 1;  // [0] steps produced, [1] steps issued, [2] result ok
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int n0 = blockIdx.x * TC_BN, tt = blockIdx.y, m0 = tt * TC_BM;
   const int GB = p.kpg * 128 + 64;
@@ -151,9 +173,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_kernel(const TcArgs p) 
   const int KT = p.cols / TC_BK;
 
   if (tid == 0) {
-    for (int s = 0; s < 2 * TC_STAGES + 1; ++s) mbar_init(&full[s], 1);
+    for (int s = 0; s < TC_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&conv[s], 8);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
     fence_mbar_init();
-    *flag = 0;
+    *abortf = 0;
+    counts[0] = counts[1] = counts[2] = 0;
   }
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
@@ -165,36 +193,59 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_kernel(const TcArgs p) 
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  auto produce = [&](int kt) {  // thread 0
-    const int s = kt % TC_STAGES;
-    uint8_t* st = smem + s * TC_STAGE;
-    mbar_arrive_expect_tx(&full[s], stage_tx);
-    bulk_g2s(st, p.x16 + ((size_t)tt * KT + kt) * TC_TILE, TC_TILE, &full[s]);
-    const int s0 = kt * 4, gi = s0 / p.kpg, s4 = (s0 % p.kpg) >> 2;
-    for (int w = 0; w < nt_here; ++w) {
-      const uint8_t* grp = p.blob + ((int64_t)(tile0 + w) * p.G + gi) * GB;
-      bulk_g2s(st + 2 * TC_TILE + w * 576, grp + s4 * 512, 512, &full[s]);
-      bulk_g2s(st + 2 * TC_TILE + w * 576 + 512, grp + p.kpg * 128, 64, &full[s]);
+  if (warp == 8) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      int kt = 0;
+      for (; kt < KT; ++kt) {
+        const int s = kt % TC_STAGES;
+        if (kt >= TC_STAGES && !tc_wait(&empty[s], (uint32_t)(((kt / TC_STAGES) - 1) & 1), abortf)) break;
+        uint8_t* st = smem + s * TC_STAGE;
+        mbar_arrive_expect_tx(&full[s], stage_tx);
+        bulk_g2s(st, p.x16 + ((size_t)tt * KT + kt) * TC_TILE, TC_TILE, &full[s]);
+        const int s0 = kt * 4, gi = s0 / p.kpg, s4 = (s0 % p.kpg) >> 2;
+        for (int w = 0; w < nt_here; ++w) {
+          const uint8_t* grp = p.blob + ((int64_t)(tile0 + w) * p.G + gi) * GB;
+          bulk_g2s(st + 2 * TC_TILE + w * 576, grp + s4 * 512, 512, &full[s]);
+          bulk_g2s(st + 2 * TC_TILE + w * 576 + 512, grp + p.kpg * 128, 64, &full[s]);
+        }
+      }
+      counts[0] = kt;
     }
-  };
-  int produced = 0, issued = 0;
-  if (tid == 0)
-    for (; produced < min(TC_STAGES, KT); ++produced) produce(produced);
-
-  for (int kt = 0; kt < KT; ++kt) {
-    const int s = kt % TC_STAGES;
-    uint8_t* st = smem + s * TC_STAGE;
-    if (tid == 0 && !wait_bar(&full[s], (uint32_t)((kt / TC_STAGES) & 1))) {
-      atomicExch(p.err, DEV_ERR_TIMEOUT);
-      *flag = 1;
+  } else if (warp == 9) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      int kt = 0;
+      for (; kt < KT; ++kt) {
+        const int s = kt % TC_STAGES;
+        if (!tc_wait(&conv[s], (uint32_t)((kt / TC_STAGES) & 1), abortf)) break;
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(smem + s * TC_STAGE), b0 = a0 + TC_TILE;
+#pragma unroll
+        for (int j = 0; j < TC_BK / 16; ++j)  // K = 16 per MMA: 32 bytes along the swizzled row
+          tc_mma(tmem, umma_desc_sw128(a0 + j * 32), umma_desc_sw128(b0 + j * 32), (kt > 0 || j > 0) ? 1u : 0u);
+        tc_commit(&empty[s]);
+      }
+      counts[1] = kt;
+      if (kt > 0) {
+        tc_commit(done);
+        // every MMA must be complete before the accumulator is read or freed (bounded, even on abort)
+        const bool ok = wait_bar(done, 0);
+        counts[2] = ok && kt == KT && !*abortf;
+        if (!ok) *abortf = 1;
+      }
     }
-    __syncthreads();
-    if (*flag) break;
-    // ---- B: warp w dequantises row tile w's quad: lane's word j holds k-step j of its fragment ----
-    {
+  } else {
+    // ---------------- dequant warps 0-7: row tile `warp` of the B tile ----------------
+    const int r0 = warp * 16 + (lane >> 2), r1 = r0 + 8;
+    const int kb = 2 * (lane & 3);
+    for (int kt = 0; kt < KT; ++kt) {
+      const int s = kt % TC_STAGES;
+      int ok = 1;
+      if (lane == 0) ok = tc_wait(&full[s], (uint32_t)((kt / TC_STAGES) & 1), abortf);
+      if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      uint8_t* st = smem + s * TC_STAGE;
       uint8_t* bs = st + TC_TILE;
-      const int r0 = warp * 16 + (lane >> 2), r1 = r0 + 8;  // rows within the B tile
-      const int kb = 2 * (lane & 3);
       if (warp < nt_here) {
         const uint8_t* raw = st + 2 * TC_TILE + warp * 576;
         const uint4 w4 = *reinterpret_cast<const uint4*>(raw + lane * 16);
@@ -225,49 +276,22 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_kernel(const TcArgs p) 
           *reinterpret_cast<uint32_t*>(bs + sw128(r1, k0 + 8)) = 0u;
         }
       }
-    }
-    // generic-proxy shared-memory writes -> visible to the tensor core's (async proxy) reads
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {
-      tc_fence_after();
-      const uint32_t a0 = smem_u32(st), b0 = smem_u32(st + TC_TILE);
-#pragma unroll
-      for (int j = 0; j < TC_BK / 16; ++j)  // K = 16 per MMA: 32 bytes along the swizzled row
-        tc_mma(tmem, umma_desc_sw128(a0 + j * 32), umma_desc_sw128(b0 + j * 32), (kt > 0 || j > 0) ? 1u : 0u);
-      tc_commit(&empty[s]);
-      ++issued;
-      // refill the slot of step kt - 1 (its MMAs were issued a step ago) with step kt - 1 + STAGES
-      if (kt >= 1 && produced < KT) {
-        const int ps = (kt - 1) % TC_STAGES;
-        if (wait_bar(&empty[ps], (uint32_t)(((kt - 1) / TC_STAGES) & 1))) {
-          produce(produced);
-          ++produced;
-        } else {
-          atomicExch(p.err, DEV_ERR_TIMEOUT);
-          *flag = 1;
-        }
-      }
+      // generic-proxy shared-memory writes -> visible to the tensor core's (async proxy) reads
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive1(&conv[s]);
     }
   }
-  // all MMAs issued so far complete -> done barrier; copies still in flight (abort) are waited for
-  if (tid == 0) {
-    for (int q = issued; q < produced; ++q) wait_bar(&full[q % TC_STAGES], (uint32_t)((q / TC_STAGES) & 1));
-    if (issued > 0) {
-      tc_commit(done);
-      if (!wait_bar(done, 0)) {
-        atomicExch(p.err, DEV_ERR_TIMEOUT);
-        *flag = 1;
-      }
-    } else {
-      *flag = 1;
-    }
-  }
+  __syncthreads();
+  // copies still in flight (abort path) land before the CTA exits
+  if (tid == 8 * 32)
+    for (int q = counts[1]; q < counts[0]; ++q)
+      wait_bar(&full[q % TC_STAGES], (uint32_t)((q / TC_STAGES) & 1));
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (!*flag) {
+  if (*abortf && tid == 0) atomicExch(p.err, DEV_ERR_TIMEOUT);
+  if (counts[2] && warp < 8) {
     // ---- epilogue: warp w reads TMEM lanes 32*(w%4).. (tokens), columns 64*(w/4).. (rows) ----
     const int qd = warp & 3, half = warp >> 2;
     const int m = qd * 32 + lane, tok = m0 + m;
@@ -324,7 +348,7 @@ __global__ void inv_rms_kernel(const float* x, int ldx, int T, int K, float eps,
 
 int* gemv_err_word();
 
-constexpr size_t TC_SMEM = 1024 + (size_t)TC_STAGES * TC_STAGE + (2 * TC_STAGES + 1) * 8 + 16;
+constexpr size_t TC_SMEM = 1024 + (size_t)TC_STAGES * TC_STAGE + (3 * TC_STAGES + 1) * 8 + 32;
 
 // One-time kernel attribute set-up (call before any stream capture).
 int gemm_tc_prepare() {
@@ -388,7 +412,7 @@ int gemm_tc_launch(const GemvArgs& a, float* inv_ws, cudaStream_t st) {
   p.y = a.y; p.ldy = a.ldy; p.bias = a.bias; p.residual = a.residual; p.ldr = a.ldr; p.swiglu = a.swiglu;
   p.err = err;
   const dim3 grid((w.rows + TC_BN - 1) / TC_BN, TT);
-  gemm_tc_kernel<<<grid, TC_THREADS, TC_SMEM, st>>>(p);
+  gemm_tc_kernel<<<grid, TC_WARPS * 32, TC_SMEM, st>>>(p);
   N730_CHECK_LAUNCH();
   return N730_OK;
 }
