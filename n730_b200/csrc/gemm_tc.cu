@@ -33,16 +33,17 @@
 
 namespace n730 {
 
-constexpr int TC_BM = 128, TC_BN = 128, TC_BK = 64, TC_STAGES = 4;
-constexpr int TC_TILE = TC_BM * TC_BK * 2;  // bytes of one fp16 operand tile (A or B)
-constexpr int TC_RAW = 8 * 576;             // one k-step quad (512 B) + scale/zero block (64 B) per 16-row tile
-constexpr int TC_STAGE = 2 * TC_TILE + 5120;  // A | B | raw B, a multiple of 1024
+constexpr int TC_BM = 128, TC_BN = 128, TC_BK = 128, TC_STAGES = 3;
+constexpr int TC_SUB = 128 * 64 * 2;        // one 128-row x 64-column fp16 sub-tile (one 128-byte swizzle atom wide)
+constexpr int TC_TILE = 2 * TC_SUB;         // A or B operand of one K-step (two sub-tiles)
+constexpr int TC_RAWT = 1152;               // raw codes + scale/zero blocks of one 16-row tile per K-step
+constexpr int TC_STAGE = 2 * TC_TILE + 9216;  // A | B | raw B (8 x TC_RAWT), a multiple of 1024
 constexpr uint32_t TC_TMEM_COLS = 128;      // fp32 accumulator columns (N)
 
 struct TcArgs {
   const uint8_t* blob;  // fragment tiles: group u = tile*G + g at u * (kpg*128 + 64)
   int rows, cols, G, kpg;
-  const uint8_t* x16;   // packed A: [token tile][k-step] blocks of 128 x 64 fp16, 128B-swizzled
+  const uint8_t* x16;   // packed A: [token tile][64-column block] sub-tiles of 128 x 64 fp16, 128B-swizzled
   int T;
   float* y; int ldy;
   const float* bias;
@@ -106,9 +107,9 @@ __device__ __forceinline__ uint32_t sw128(int r, int k) {
 __global__ void x16_pack_kernel(const float* x, int ldx, int T, const float* inv_rms, const float* norm_w,
                                 uint8_t* out) {
   const int kb = blockIdx.x, tt = blockIdx.y;
-  uint8_t* blk = out + ((size_t)tt * gridDim.x + kb) * TC_TILE;
+  uint8_t* blk = out + ((size_t)tt * gridDim.x + kb) * TC_SUB;
   for (int i = threadIdx.x; i < TC_BM * 8; i += blockDim.x) {
-    const int r = i >> 3, c8 = i & 7, tok = tt * TC_BM + r, k = kb * TC_BK + c8 * 8;
+    const int r = i >> 3, c8 = i & 7, tok = tt * TC_BM + r, k = kb * 64 + c8 * 8;
     uint4 pk = make_uint4(0u, 0u, 0u, 0u);
     if (tok < T) {
       const float4* src = reinterpret_cast<const float4*>(x + (int64_t)tok * ldx + k);
@@ -142,11 +143,12 @@ __device__ __forceinline__ void mbar_arrive1(uint64_t* bar) {
   asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" :: "r"(smem_u32(bar)) : "memory");
 }
 
-// One CTA per 128-token x 128-row output tile; K in steps of 64 through a
-// 4-stage pipeline with specialised warps and no CTA-wide barrier in the loop:
+// One CTA per 128-token x 128-row output tile; K in steps of 128 through a
+// 3-stage pipeline with specialised warps and no CTA-wide barrier in the loop:
 //  * warp 8 (producer): once a stage's MMAs are done (empty[s]) it issues the
-//    next step's bulk copies into it (the packed A tile; per 16-row tile of W
-//    the step's 512-byte code quad and the group's scale/zero block) -> full[s];
+//    next step's bulk copies into it (the packed A tile, 32 KB; per 16-row tile
+//    of W the step's codes with their scale/zero blocks, one copy when the
+//    step covers whole groups) -> full[s];
 //  * warps 0-7 (dequant, then epilogue): warp w waits for full[s], turns row
 //    tile w's codes into (q - z) * s fp16 in the swizzled B tile and arrives on
 //    conv[s];
@@ -169,7 +171,11 @@ __global__ void __launch_bounds__(TC_WARPS * 32, 1) gemm_tc_kernel(const TcArgs 
   const int GB = p.kpg * 128 + 64;
   const int n_tiles = (p.rows + 15) >> 4, tile0 = n0 >> 4;
   const int nt_here = min(8, n_tiles - tile0);  // 16-row tiles of W in this CTA's B (>= 1)
-  const uint32_t stage_tx = (uint32_t)(TC_TILE + nt_here * 576);
+  // per 16-row tile and K-step: whole groups (kpg <= 8: 8/kpg contiguous group
+  // blocks) or, for kpg 16, half a group's codes plus its scale/zero block
+  const int gps = p.kpg <= 8 ? 8 / p.kpg : 1;                  // groups touched per step
+  const uint32_t raw_b = p.kpg <= 8 ? (uint32_t)(gps * GB) : 1088u;
+  const uint32_t stage_tx = (uint32_t)TC_TILE + (uint32_t)nt_here * raw_b;
   const int KT = p.cols / TC_BK;
 
   if (tid == 0) {
@@ -203,11 +209,16 @@ __global__ void __launch_bounds__(TC_WARPS * 32, 1) gemm_tc_kernel(const TcArgs 
         uint8_t* st = smem + s * TC_STAGE;
         mbar_arrive_expect_tx(&full[s], stage_tx);
         bulk_g2s(st, p.x16 + ((size_t)tt * KT + kt) * TC_TILE, TC_TILE, &full[s]);
-        const int s0 = kt * 4, gi = s0 / p.kpg, s4 = (s0 % p.kpg) >> 2;
+        const int s0 = kt * 8, gi = s0 / p.kpg;  // first k-step and group of this step
         for (int w = 0; w < nt_here; ++w) {
           const uint8_t* grp = p.blob + ((int64_t)(tile0 + w) * p.G + gi) * GB;
-          bulk_g2s(st + 2 * TC_TILE + w * 576, grp + s4 * 512, 512, &full[s]);
-          bulk_g2s(st + 2 * TC_TILE + w * 576 + 512, grp + p.kpg * 128, 64, &full[s]);
+          uint8_t* dst = st + 2 * TC_TILE + w * TC_RAWT;
+          if (p.kpg <= 8) {
+            bulk_g2s(dst, grp, raw_b, &full[s]);
+          } else {  // half of a 16-k-step group: quads 2h, 2h+1, then the group's scale/zero block
+            bulk_g2s(dst, grp + ((s0 % 16) >> 3) * 1024, 1024, &full[s]);
+            bulk_g2s(dst + 1024, grp + 16 * 128, 64, &full[s]);
+          }
         }
       }
       counts[0] = kt;
@@ -222,8 +233,10 @@ __global__ void __launch_bounds__(TC_WARPS * 32, 1) gemm_tc_kernel(const TcArgs 
         tc_fence_after();
         const uint32_t a0 = smem_u32(smem + s * TC_STAGE), b0 = a0 + TC_TILE;
 #pragma unroll
-        for (int j = 0; j < TC_BK / 16; ++j)  // K = 16 per MMA: 32 bytes along the swizzled row
-          tc_mma(tmem, umma_desc_sw128(a0 + j * 32), umma_desc_sw128(b0 + j * 32), (kt > 0 || j > 0) ? 1u : 0u);
+        for (int j = 0; j < TC_BK / 16; ++j) {  // K = 16 per MMA: 32 bytes along the swizzled row of a sub-tile
+          const uint32_t off = (uint32_t)((j >> 2) * TC_SUB + (j & 3) * 32);
+          tc_mma(tmem, umma_desc_sw128(a0 + off), umma_desc_sw128(b0 + off), (kt > 0 || j > 0) ? 1u : 0u);
+        }
         tc_commit(&empty[s]);
       }
       counts[1] = kt;
@@ -246,34 +259,40 @@ __global__ void __launch_bounds__(TC_WARPS * 32, 1) gemm_tc_kernel(const TcArgs 
       if (!__shfl_sync(0xffffffffu, ok, 0)) break;
       uint8_t* st = smem + s * TC_STAGE;
       uint8_t* bs = st + TC_TILE;
-      if (warp < nt_here) {
-        const uint8_t* raw = st + 2 * TC_TILE + warp * 576;
-        const uint4 w4 = *reinterpret_cast<const uint4*>(raw + lane * 16);
-        const uint2 szv = *reinterpret_cast<const uint2*>(raw + 512 + (lane >> 2) * 8);
-        const float2 sc = __half22float2(u2h(szv.x)), zp = __half22float2(u2h(szv.y));
-        const uint32_t wv[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint32_t w = wv[j];
-          const int k0 = j * 16 + kb;
-          auto q = [&](int sh) { return (float)((w >> sh) & 15u); };
-          *reinterpret_cast<uint32_t*>(bs + sw128(r0, k0)) =
-              h2u(__floats2half2_rn((q(0) - zp.x) * sc.x, (q(16) - zp.x) * sc.x));
-          *reinterpret_cast<uint32_t*>(bs + sw128(r1, k0)) =
-              h2u(__floats2half2_rn((q(4) - zp.y) * sc.y, (q(20) - zp.y) * sc.y));
-          *reinterpret_cast<uint32_t*>(bs + sw128(r0, k0 + 8)) =
-              h2u(__floats2half2_rn((q(8) - zp.x) * sc.x, (q(24) - zp.x) * sc.x));
-          *reinterpret_cast<uint32_t*>(bs + sw128(r1, k0 + 8)) =
-              h2u(__floats2half2_rn((q(12) - zp.y) * sc.y, (q(28) - zp.y) * sc.y));
-        }
-      } else {
+      for (int h = 0; h < 2; ++h) {  // quad h: k-steps 4h..4h+3 of the step -> sub-tile h of B
+        uint8_t* sb = bs + h * TC_SUB;
+        if (warp < nt_here) {
+          const uint8_t* raw = st + 2 * TC_TILE + warp * TC_RAWT;
+          // kpg 4: [quad | sz] per group; kpg 8 and 16: [quad 0 | quad 1 | sz]
+          const int qoff = p.kpg == 4 ? h * 576 : h * 512, zoff = p.kpg == 4 ? h * 576 + 512 : 1024;
+          const uint4 w4 = *reinterpret_cast<const uint4*>(raw + qoff + lane * 16);
+          const uint2 szv = *reinterpret_cast<const uint2*>(raw + zoff + (lane >> 2) * 8);
+          const float2 sc = __half22float2(u2h(szv.x)), zp = __half22float2(u2h(szv.y));
+          const uint32_t wv[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int k0 = j * 16 + kb;
-          *reinterpret_cast<uint32_t*>(bs + sw128(r0, k0)) = 0u;
-          *reinterpret_cast<uint32_t*>(bs + sw128(r1, k0)) = 0u;
-          *reinterpret_cast<uint32_t*>(bs + sw128(r0, k0 + 8)) = 0u;
-          *reinterpret_cast<uint32_t*>(bs + sw128(r1, k0 + 8)) = 0u;
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t w = wv[j];
+            const int k0 = j * 16 + kb;
+            auto q = [&](int sh) { return (float)((w >> sh) & 15u); };
+            *reinterpret_cast<uint32_t*>(sb + sw128(r0, k0)) =
+                h2u(__floats2half2_rn((q(0) - zp.x) * sc.x, (q(16) - zp.x) * sc.x));
+            *reinterpret_cast<uint32_t*>(sb + sw128(r1, k0)) =
+                h2u(__floats2half2_rn((q(4) - zp.y) * sc.y, (q(20) - zp.y) * sc.y));
+            *reinterpret_cast<uint32_t*>(sb + sw128(r0, k0 + 8)) =
+                h2u(__floats2half2_rn((q(8) - zp.x) * sc.x, (q(24) - zp.x) * sc.x));
+            *reinterpret_cast<uint32_t*>(sb + sw128(r1, k0 + 8)) =
+                h2u(__floats2half2_rn((q(12) - zp.y) * sc.y, (q(28) - zp.y) * sc.y));
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int k0 = j * 16 + kb;
+            *reinterpret_cast<uint32_t*>(sb + sw128(r0, k0)) = 0u;
+            *reinterpret_cast<uint32_t*>(sb + sw128(r1, k0)) = 0u;
+            *reinterpret_cast<uint32_t*>(sb + sw128(r0, k0 + 8)) = 0u;
+            *reinterpret_cast<uint32_t*>(sb + sw128(r1, k0 + 8)) = 0u;
+          }
         }
       }
       // generic-proxy shared-memory writes -> visible to the tensor core's (async proxy) reads
@@ -361,7 +380,8 @@ int gemm_tc_prepare() {
 }
 
 bool gemm_tc_supported(const QWeight& w, int T) {
-  return w.layout == 1 && w.bits == 4 && w.cols % TC_BK == 0 && (w.group / 16) % 4 == 0 && T >= 1;
+  const int kpg = w.group / 16;
+  return w.layout == 1 && w.bits == 4 && w.cols % TC_BK == 0 && (kpg == 4 || kpg == 8 || kpg == 16) && T >= 1;
 }
 
 // Packed-A workspace of the current device, grown on demand (never inside a stream capture).
@@ -397,14 +417,14 @@ int gemm_tc_launch(const GemvArgs& a, float* inv_ws, cudaStream_t st) {
   int* err = gemv_err_word();
   N730_REQUIRE(err, N730_OOM, "gemm_tc: error word allocation failed");
   if (int rc = gemm_tc_prepare()) return rc;
-  const int TT = (a.batch + TC_BM - 1) / TC_BM, KT = w.cols / TC_BK;
+  const int TT = (a.batch + TC_BM - 1) / TC_BM, KB = w.cols / 64;
   uint8_t* x16 = nullptr;
-  if (int rc = x16_workspace((size_t)TT * KT * TC_TILE, st, &x16)) return rc;
+  if (int rc = x16_workspace((size_t)TT * KB * TC_SUB, st, &x16)) return rc;
   if (a.norm_w) {
     inv_rms_kernel<<<(a.batch + 7) / 8, 256, 0, st>>>(a.x, a.ldx, a.batch, w.cols, a.eps, inv_ws);
     N730_CHECK_LAUNCH();
   }
-  x16_pack_kernel<<<dim3(KT, TT), 256, 0, st>>>(a.x, a.ldx, a.batch, a.norm_w ? inv_ws : nullptr, a.norm_w, x16);
+  x16_pack_kernel<<<dim3(KB, TT), 256, 0, st>>>(a.x, a.ldx, a.batch, a.norm_w ? inv_ws : nullptr, a.norm_w, x16);
   N730_CHECK_LAUNCH();
   TcArgs p = {};
   p.blob = w.codes; p.rows = w.rows; p.cols = w.cols; p.G = w.n_groups; p.kpg = w.group / 16;
