@@ -24,8 +24,8 @@
 // Every mbarrier wait is bounded (%globaltimer, 2 s); a wait that runs out sets
 // the device error word, stops issuing, waits (bounded) for the MMAs in
 // flight, and still frees the tensor memory.
-// Numerics: dequantised weights and x rounded to fp16 (relative 2^-11 each),
-// fp32 accumulation.
+// Numerics: dequantised weights in fp16 ((q - z) s from an fp16 FMA with the
+// zero-point term z s rounded to fp16), x rounded to fp16, fp32 accumulation.
 #include <algorithm>
 
 #include "mma_gemv.cuh"
@@ -269,20 +269,25 @@ __global__ void __launch_bounds__(TC_WARPS * 32, 1) gemm_tc_kernel(const TcArgs 
           const uint4 w4 = *reinterpret_cast<const uint4*>(raw + qoff + lane * 16);
           const uint2 szv = *reinterpret_cast<const uint2*>(raw + zoff + (lane >> 2) * 8);
           const float2 sc = __half22float2(u2h(szv.x)), zp = __half22float2(u2h(szv.y));
+          // (q - z) s in fp16: the code nibble ORed into fp16 1024 (low nibbles) or 64 (bits 4-7)
+          // gives 1024 + q / 64 + q exactly, one subtraction gives q, one FMA q s - z s (z s
+          // rounded to fp16 once: <= 2^-12 relative of z s per weight)
+          const __half2 s0 = __float2half2_rn(sc.x), s1 = __float2half2_rn(sc.y);
+          const __half2 c0 = __float2half2_rn(-zp.x * sc.x), c1 = __float2half2_rn(-zp.y * sc.y);
+          const __half2 k1024 = u2h(0x64006400u), k64 = u2h(0x54005400u);
           const uint32_t wv[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const uint32_t w = wv[j];
+            const uint32_t w = wv[j], ws = w >> 8;
             const int k0 = j * 16 + kb;
-            auto q = [&](int sh) { return (float)((w >> sh) & 15u); };
-            *reinterpret_cast<uint32_t*>(sb + sw128(r0, k0)) =
-                h2u(__floats2half2_rn((q(0) - zp.x) * sc.x, (q(16) - zp.x) * sc.x));
-            *reinterpret_cast<uint32_t*>(sb + sw128(r1, k0)) =
-                h2u(__floats2half2_rn((q(4) - zp.y) * sc.y, (q(20) - zp.y) * sc.y));
-            *reinterpret_cast<uint32_t*>(sb + sw128(r0, k0 + 8)) =
-                h2u(__floats2half2_rn((q(8) - zp.x) * sc.x, (q(24) - zp.x) * sc.x));
-            *reinterpret_cast<uint32_t*>(sb + sw128(r1, k0 + 8)) =
-                h2u(__floats2half2_rn((q(12) - zp.y) * sc.y, (q(28) - zp.y) * sc.y));
+            const __half2 q0 = __hsub2(u2h(lop3_and_or(w, 0x000F000Fu, 0x64006400u)), k1024);   // r0, k0 / k0+1
+            const __half2 q1 = __hsub2(u2h(lop3_and_or(w, 0x00F000F0u, 0x54005400u)), k64);     // r1, k0 / k0+1
+            const __half2 q2 = __hsub2(u2h(lop3_and_or(ws, 0x000F000Fu, 0x64006400u)), k1024);  // r0, k0+8 / +9
+            const __half2 q3 = __hsub2(u2h(lop3_and_or(ws, 0x00F000F0u, 0x54005400u)), k64);    // r1, k0+8 / +9
+            *reinterpret_cast<uint32_t*>(sb + sw128(r0, k0)) = h2u(__hfma2(q0, s0, c0));
+            *reinterpret_cast<uint32_t*>(sb + sw128(r1, k0)) = h2u(__hfma2(q1, s1, c1));
+            *reinterpret_cast<uint32_t*>(sb + sw128(r0, k0 + 8)) = h2u(__hfma2(q2, s0, c0));
+            *reinterpret_cast<uint32_t*>(sb + sw128(r1, k0 + 8)) = h2u(__hfma2(q3, s1, c1));
           }
         } else {
 #pragma unroll
