@@ -56,3 +56,19 @@ def test_ctypes_load_without_gpu():
     lib = _lib.cuda()
     assert b"sm_100a" in lib.n730_cuda_version()
     assert _lib.core().n730_version()
+
+
+def test_model_config_layout_matches_header():
+    """The ctypes N730ModelConfig (n730_b200.engine) lists the header's fields in the same order
+    and types: the struct crosses the C ABI by value layout."""
+    import re
+
+    from n730_b200.engine import N730ModelConfig
+    hdr = (REPO / "include" / "n730_cuda.h").read_text()
+    body = hdr[hdr.index("typedef struct N730ModelConfig {"):hdr.index("} N730ModelConfig;")]
+    body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
+    fields = []
+    for ctype, names in re.findall(r"\b(int32_t|float)\s+([^;]+);", body):
+        fields += [(n.strip(), ctype) for n in names.split(",")]
+    py = [(n, "float" if t.__name__ == "c_float" else "int32_t") for n, t in N730ModelConfig._fields_]
+    assert py == fields
