@@ -421,14 +421,28 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
           float* ov = lv + 4 * PD_MAXSPLIT;             // [nout][ns] (<= GQ*HD + ns)
           const float* base_o = a.attn_part + (size_t)kvh * sp.ns * GQ * HD;
           const float* base_ml = a.attn_part + (size_t)d.n_kv * a.max_split * GQ * HD + (size_t)kvh * sp.ns * GQ * 2;
-          for (int i = tid; i < nj * sp.ns; i += PD_THREADS) {
-            const int jj = i / sp.ns, s2 = i - jj * sp.ns;
-            const float2 v = __ldcg(reinterpret_cast<const float2*>(base_ml + ((size_t)s2 * GQ + j_lo + jj) * 2));
-            mv[i] = v.x; lv[i] = v.y;
-          }
-          for (int i = tid; i < nout * sp.ns; i += PD_THREADS) {
-            const int oo = i / sp.ns, s2 = i - oo * sp.ns, o = o_lo + oo;
-            ov[i] = __ldcg(base_o + (size_t)s2 * GQ * HD + o);
+          {  // one batch of loads (nj * ns <= PD_MAXG * PD_MAXSPLIT = PD_THREADS; nout * ns bounded below)
+            constexpr int MAXI = (PD_MAXG * HD + PD_MAXSPLIT + PD_THREADS - 1) / PD_THREADS;
+            float2 mlv = make_float2(0.f, 0.f);
+            const bool has_ml = tid < nj * sp.ns;
+            if (has_ml) {
+              const int jj = tid / sp.ns, s2 = tid - jj * sp.ns;
+              mlv = __ldcg(reinterpret_cast<const float2*>(base_ml + ((size_t)s2 * GQ + j_lo + jj) * 2));
+            }
+            float ovr[MAXI];
+#pragma unroll
+            for (int r = 0; r < MAXI; ++r) {
+              const int i = tid + r * PD_THREADS;
+              ovr[r] = 0.f;
+              if (i < nout * sp.ns) {
+                const int oo = i / sp.ns, s2 = i - oo * sp.ns;
+                ovr[r] = __ldcg(base_o + (size_t)s2 * GQ * HD + o_lo + oo);
+              }
+            }
+            if (has_ml) { mv[tid] = mlv.x; lv[tid] = mlv.y; }
+#pragma unroll
+            for (int r = 0; r < MAXI; ++r)
+              if (tid + r * PD_THREADS < nout * sp.ns) ov[tid + r * PD_THREADS] = ovr[r];
           }
           __syncthreads();
           // warp jj < nj: split weights e^(m_s - M) of query head j_lo + jj and their
