@@ -66,6 +66,8 @@ def _args():
                     help="tp72b decode row-split sums: 0 one-shot over NVLink peer memory, 1 NCCL")
     ap.add_argument("--ffn-fuse", type=int, default=0, choices=[-1, 0, 1],
                     help="persistent decode FFN: 0 auto, 1 one fused phase, -1 two GEMV phases")
+    ap.add_argument("--per-op", action="store_true",
+                    help="tp72b: batch-1 decode through the per-op kernels instead of the persistent kernel")
     ap.add_argument("--model", default=SHAPE_NAME, choices=["qwen2-7b", "qwen2-0.5b"],
                     help="resident workload: model shape")
     ap.add_argument("--pmap", default="int4_g128", choices=["int4_g128", "mixed_05b"],
@@ -509,9 +511,10 @@ def run_tp(a):
     tp.check_shape(shape, world, 128)
     B, ctx = a.batch, a.ctx
     eng = Engine(tp.local_shape(shape, world, rank, 128), max_ctx=ctx + a.warmup + a.steps + 8, max_batch=B,
-                 max_prefill=64, tp_rank=rank, tp_size=world, tp_allreduce=a.tp_allreduce)
+                 max_prefill=64, tp_rank=rank, tp_size=world, tp_allreduce=a.tp_allreduce,
+                 per_op_decode=a.per_op, ffn_fuse=a.ffn_fuse)
     if world > 1:
-        tp.init_engine_comm(eng, rank, world, one_shot=a.tp_allreduce == 0)
+        tp.init_engine_comm(eng, rank, world)
     build_on_device(shape, "int4_g128", eng, tp_rank=rank, tp_size=world)
     eng.finalize()
     info = eng.info()
@@ -552,13 +555,19 @@ def run_tp(a):
                "config": {"workload": f"qwen2-72b-shape ({shape.layers} layers) INT4 g128, batch {B} decode at "
                                       f"context {ctx}, tensor parallel over {world} GPU(s) (row-split sums after "
                                       "o_proj and down_proj, vocab-split lm_head)", "batch": B,
-                          "allreduce": ("one-shot push over NVLink peer memory, fused residual add"
+                          "allreduce": ("in-kernel: partial sums pushed to every rank over NVLink peer memory, "
+                                        "cross-GPU barrier, rank-order sums" if info["persistent_decode"] else
+                                        "one-shot push over NVLink peer memory, fused residual add"
                                         if a.tp_allreduce == 0 else "NCCL") if world > 1 else None,
+                          "decode_path": ("persistent kernel" + (", phase table in global memory"
+                                                                 if info["phase_table_global"] else "")
+                                          if info["persistent_decode"] else "per-op kernels (graph)"),
                           "parallelism": f"tp{world}"},
                "roofline": {"bound": "hbm", "achieved": round(step_bytes / (t / a.steps) / 1e9, 1), "peak": peak,
                             "unit": "GB/s per GPU", "frac": round(step_bytes / (t / a.steps) / 1e9 / peak, 4),
                             "traffic": None, "kernel": "whole decode step, per-rank bytes", "peak_source": kind},
-               "clocks": clk.summary(), "gpu_launches": a.steps * (7 * shape.layers + 6)}
+               "clocks": clk.summary(),
+               "gpu_launches": a.steps * (4 if info["persistent_decode"] else 7 * shape.layers + 6)}
         print(json.dumps(out), flush=True)
     eng.close()
     if world > 1:

@@ -112,6 +112,51 @@ __device__ bool pd_barrier(const PdArgs& a, int k, int* flag) {
   return *flag != 0;
 }
 
+// Cross-GPU barrier number k of this launch (tensor parallel): every CTA of
+// every rank arrives on every rank's counter (system-scope release after the
+// CTA's peer stores), then waits until its own rank's counter shows all
+// tp_size x grid arrivals.  The counters are never reset: launch e's barrier k
+// completes at tp_size * grid * (e * n_xbar + k) (32-bit wrapping compare), so
+// a rank that starts the next launch early cannot disturb a slow one.  Waits
+// end after PD_XWAIT_NS (a peer whose launch never comes) with the abort flag
+// and the device error word raised.
+constexpr uint64_t PD_XWAIT_NS = 20000000000ull;
+__device__ __forceinline__ int ld_relaxed_sys(const int* p) {
+  int v;
+  asm volatile("ld.relaxed.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ bool pd_xbarrier(const PdArgs& a, int xep, int k, int* flag) {
+  __syncthreads();
+  if (threadIdx.x == PD_SYNC_T) {
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+#pragma unroll
+    for (int r = 0; r < PD_MAX_RANKS; ++r)
+      if (r < a.tp_size) asm volatile("red.release.sys.global.add.s32 [%0], 1;" :: "l"(a.xcnt[r]) : "memory");
+    const unsigned target = (unsigned)a.tp_size * gridDim.x * ((unsigned)xep * (unsigned)a.n_xbar + (unsigned)k);
+    const int* cnt = a.xcnt_local;
+    uint64_t t0 = 0;
+    bool ok = true;
+    for (;;) {
+      const int c = ld_relaxed_sys(cnt), ab = ld_relaxed(&a.sync[2]);
+      if ((int)((unsigned)c - target) >= 0) break;
+      if (ab) { ok = false; break; }
+      const uint64_t t = gtimer();
+      if (!t0) t0 = t;
+      else if (t - t0 > PD_XWAIT_NS) {
+        atomicExch(&a.sync[2], 1);
+        atomicExch(a.err, DEV_ERR_TIMEOUT);
+        ok = false;
+        break;
+      }
+    }
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    *flag = ok;
+  }
+  __syncthreads();
+  return *flag != 0;
+}
+
 // This CTA's row tiles [t0, t1) of weight-streaming phase P: an even share of
 // a GEMV's tiles, or for an FFN phase the gate|up tiles of the CTA's FFN
 // groups (2 kpg tiles of 8 interleaved gate/up channel pairs per group).
@@ -140,7 +185,9 @@ __device__ __forceinline__ PdSplits pd_splits(const PdArgs& a) {
   return s;
 }
 
-template <int KPG, int HD>
+// EXT: the tensor-parallel exchange (push epilogue, cross-GPU barriers, rank
+// sums) and phase tables in global memory; without it that code is compiled out.
+template <int KPG, int HD, bool EXT>
 __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdArgs a) {
   constexpr int GPC = pd_gpc(KPG);
   constexpr int GB = KPG * 128 + 64;  // bytes per group
@@ -174,8 +221,10 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
 
   // the phase table lives in shared memory: phase transitions read it on the
   // critical path (producer cursor and every phase's prologue)
-  PdPhase* phs = reinterpret_cast<PdPhase*>(smem + a.tab_off);
-  {
+  // (tables too large for shared memory are read from global memory)
+  PdPhase* phs = !EXT || a.tab_off >= 0 ? reinterpret_cast<PdPhase*>(smem + a.tab_off)
+                                        : const_cast<PdPhase*>(a.phases);
+  if (!EXT || a.tab_off >= 0) {
     const uint32_t* src = reinterpret_cast<const uint32_t*>(a.phases);
     uint32_t* dst = reinterpret_cast<uint32_t*>(phs);
     const int words = a.n_phases * (int)(sizeof(PdPhase) / 4);
@@ -278,6 +327,7 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
   // every CTA then leaves at its next grid barrier (a CTA-uniform decision).
   bool wfail = false;
   int bar_k = 0, attn_idx = 0;
+  const int xep = EXT && a.tp_size > 1 ? *reinterpret_cast<volatile int*>(a.xepoch) : 0;  // this launch's number
   for (int ph = 0; ph < a.n_phases; ++ph) {
     const PdPhase& P = phs[ph];
     if ((P.kind == PD_GEMV || P.kind == PD_FFN) && P.norm_w)  // constant: pull this thread's norm weights into L1 before the wait
@@ -286,7 +336,7 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
         asm volatile("prefetch.global.L1 [%0];" :: "l"(p));
         asm volatile("prefetch.global.L1 [%0];" :: "l"(p + 8));
       }
-    if (ph > 0 && !pd_barrier(a, ++bar_k, flag)) break;
+    if (ph > 0 && !(EXT && P.xbar ? pd_xbarrier(a, xep, P.xbar, flag) : pd_barrier(a, ++bar_k, flag))) break;
 
     if (P.kind == PD_ATTN) {
       if (has_item) {
@@ -526,6 +576,61 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
       if (P.norm_w) {  // K <= PD_KNORM: the row stays in registers across the reduction
         float xv[PD_NREG][4];
         float ss = 0.f;
+        if (EXT && P.xsum) {  // tensor parallel: x = h + every rank's partial sums, added in rank order
+          const float* rb = a.xrecv_local + (int64_t)P.xpar * a.tp_size * a.xcap;
+#pragma unroll
+          for (int j = 0; j < PD_NREG; ++j) {
+            const int i = tid + j * PD_THREADS;
+            xv[j][0] = xv[j][1] = xv[j][2] = xv[j][3] = 0.f;
+            if (i < items) {
+              const int k = (i >> 2) * 16 + 2 * (i & 3);
+              const float2 v0 = __ldcg(reinterpret_cast<const float2*>(P.x + k));
+              const float2 v1 = __ldcg(reinterpret_cast<const float2*>(P.x + k + 8));
+              xv[j][0] = v0.x; xv[j][1] = v0.y; xv[j][2] = v1.x; xv[j][3] = v1.y;
+            }
+          }
+          for (int r = 0; r < a.tp_size; r += 2) {  // two ranks' loads in one batch
+            const bool two = r + 1 < a.tp_size;
+            const float* r0p = rb + (int64_t)r * a.xcap;
+            const float* r1p = r0p + a.xcap;
+            float2 u[PD_NREG][4];
+#pragma unroll
+            for (int j = 0; j < PD_NREG; ++j) {
+              const int i = tid + j * PD_THREADS;
+              const int k = (i >> 2) * 16 + 2 * (i & 3);
+              u[j][0] = u[j][1] = u[j][2] = u[j][3] = make_float2(0.f, 0.f);
+              if (i < items) {
+                u[j][0] = __ldcg(reinterpret_cast<const float2*>(r0p + k));
+                u[j][1] = __ldcg(reinterpret_cast<const float2*>(r0p + k + 8));
+                if (two) {
+                  u[j][2] = __ldcg(reinterpret_cast<const float2*>(r1p + k));
+                  u[j][3] = __ldcg(reinterpret_cast<const float2*>(r1p + k + 8));
+                }
+              }
+            }
+#pragma unroll
+            for (int j = 0; j < PD_NREG; ++j) {
+              xv[j][0] += u[j][0].x; xv[j][1] += u[j][0].y; xv[j][2] += u[j][1].x; xv[j][3] += u[j][1].y;
+              if (two) { xv[j][0] += u[j][2].x; xv[j][1] += u[j][2].y; xv[j][2] += u[j][3].x; xv[j][3] += u[j][3].y; }
+            }
+          }
+          // the new residual: this CTA's share of the rows goes to the other buffer
+          const int o0 = pd_rng(0, K, cta, NC), o1 = pd_rng(0, K, cta + 1, NC);
+#pragma unroll
+          for (int j = 0; j < PD_NREG; ++j) {
+            const int i = tid + j * PD_THREADS;
+            if (i < items) {
+              const int k = (i >> 2) * 16 + 2 * (i & 3);
+              if (P.h_out) {
+                if (k >= o0 && k < o1) P.h_out[k] = xv[j][0];
+                if (k + 1 >= o0 && k + 1 < o1) P.h_out[k + 1] = xv[j][1];
+                if (k + 8 >= o0 && k + 8 < o1) P.h_out[k + 8] = xv[j][2];
+                if (k + 9 >= o0 && k + 9 < o1) P.h_out[k + 9] = xv[j][3];
+              }
+              ss += xv[j][0] * xv[j][0] + xv[j][1] * xv[j][1] + xv[j][2] * xv[j][2] + xv[j][3] * xv[j][3];
+            }
+          }
+        } else {
 #pragma unroll
         for (int j = 0; j < PD_NREG; ++j) {
           const int i = tid + j * PD_THREADS;
@@ -544,6 +649,7 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
             }
             ss += xv[j][0] * xv[j][0] + xv[j][1] * xv[j][1] + xv[j][2] * xv[j][2] + xv[j][3] * xv[j][3];
           }
+        }
         }
         const float inv = rsqrtf(block_sum(ss, red) / K + a.eps);
 #pragma unroll
@@ -609,6 +715,13 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
           const float m = (v / (1.0f + expf(-v))) * up;
           if (P.kind == PD_FFN) mloc[(row >> 1) - t0 * 8] = m;
           else P.y[row >> 1] = m;
+        }
+      } else if (EXT && P.epi == PD_EPI_XPUSH) {  // this rank's partial sum of the row into every rank's slot
+        if (in) {
+          const int64_t off = ((int64_t)P.xpar * a.tp_size + a.tp_rank) * a.xcap + row;
+#pragma unroll
+          for (int r = 0; r < PD_MAX_RANKS; ++r)
+            if (r < a.tp_size) a.xrecv[r][off] = v;
         }
       } else if (in) {
         P.y[row] = v;
@@ -769,6 +882,7 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
   if (flag[2]) {
     for (int i = tid; i < a.acc_n; i += PD_THREADS) a.acc[i] = 0ull;
     if (tid == PD_SYNC_T) {
+      if (EXT && a.tp_size > 1) *a.xepoch = xep + 1;
       for (int h = 0; h < d.n_kv; ++h) a.attn_cnt[h] = 0;
       a.sync[0] = 0;
       a.sync[2] = 0;
@@ -778,9 +892,9 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
   }
 }
 
-template <int KPG, int HD>
+template <int KPG, int HD, bool EXT>
 static int persist_setup(const PdPlan& plan, bool launch, cudaStream_t st, int* max_blocks) {
-  auto kern = persist_decode_kernel<KPG, HD>;
+  auto kern = persist_decode_kernel<KPG, HD, EXT>;
   static bool configured = false;
   if (!configured) {
     N730_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
@@ -804,17 +918,22 @@ static int persist_setup(const PdPlan& plan, bool launch, cudaStream_t st, int* 
 
 static int persist_dispatch(const PdPlan& plan, int head_dim, bool launch, cudaStream_t st, int* max_blocks) {
   const int kpg = plan.a.kpg;
-  if (head_dim == 128) {
-    if (kpg == 8) return persist_setup<8, 128>(plan, launch, st, max_blocks);
-    if (kpg == 4) return persist_setup<4, 128>(plan, launch, st, max_blocks);
-    return persist_setup<16, 128>(plan, launch, st, max_blocks);
+  if (plan.a.tp_size > 1 || plan.a.tab_off < 0) {  // exchange / global phase table: group 128 only
+    if (kpg != 8) return N730_UNSUPPORTED;
+    if (head_dim == 128) return persist_setup<8, 128, true>(plan, launch, st, max_blocks);
+    return persist_setup<8, 64, true>(plan, launch, st, max_blocks);
   }
-  if (kpg == 8) return persist_setup<8, 64>(plan, launch, st, max_blocks);
-  if (kpg == 4) return persist_setup<4, 64>(plan, launch, st, max_blocks);
-  return persist_setup<16, 64>(plan, launch, st, max_blocks);
+  if (head_dim == 128) {
+    if (kpg == 8) return persist_setup<8, 128, false>(plan, launch, st, max_blocks);
+    if (kpg == 4) return persist_setup<4, 128, false>(plan, launch, st, max_blocks);
+    return persist_setup<16, 128, false>(plan, launch, st, max_blocks);
+  }
+  if (kpg == 8) return persist_setup<8, 64, false>(plan, launch, st, max_blocks);
+  if (kpg == 4) return persist_setup<4, 64, false>(plan, launch, st, max_blocks);
+  return persist_setup<16, 64, false>(plan, launch, st, max_blocks);
 }
 
-int persist_plan(const PdPhase* ph, int n, int head_dim, int group_q, int page_size, PdPlan* plan) {
+int persist_plan(const PdPhase* ph, int n, int head_dim, int group_q, int page_size, int tp_size, PdPlan* plan) {
   auto round = [](size_t v) { return (v + 127) / 128 * 128; };
   if (!(head_dim == 64 || head_dim == 128) || group_q < 1 || group_q > PD_MAXG || page_size != PD_PAGE)
     return N730_UNSUPPORTED;
@@ -831,6 +950,7 @@ int persist_plan(const PdPhase* ph, int n, int head_dim, int group_q, int page_s
         !(k == 4 || k == 8 || k == 16))
       return N730_UNSUPPORTED;
     if (ph[i].epi == PD_EPI_SWIGLU && ph[i].rows % 2) return N730_UNSUPPORTED;
+    if (ph[i].xsum && (!ph[i].norm_w || ph[i].kind != PD_GEMV)) return N730_UNSUPPORTED;
     int tiles_per_cta = ((ph[i].rows + 15) / 16 + sms - 1) / sms;
     if ((int64_t)((ph[i].rows + 15) / 16) * ph[i].G * std::max(sms, PD_WARPS) >= (1ll << 31)) return N730_UNSUPPORTED;
     if (ph[i].kind == PD_FFN) {
@@ -852,6 +972,7 @@ int persist_plan(const PdPhase* ph, int n, int head_dim, int group_q, int page_s
   if (!kpg) return N730_UNSUPPORTED;
   PdArgs& a = plan->a;
   a.kpg = kpg;
+  a.tp_size = tp_size;
   const int gb = kpg * 128 + 64;
   a.ring_stride = (int)round((size_t)pd_gpc(kpg) * gb);
   size_t off = round((size_t)(PD_WARPS * PD_RING + 1) * 8);
@@ -873,7 +994,12 @@ int persist_plan(const PdPhase* ph, int n, int head_dim, int group_q, int page_s
   a.ffn_off = (int)round(off);
   off = a.ffn_off + (size_t)ffn_floats * 4;
   a.tab_off = (int)round(off);
-  off = a.tab_off + (size_t)n * sizeof(PdPhase);
+  if (round(a.tab_off + (size_t)n * sizeof(PdPhase)) <= 227 * 1024) {
+    off = a.tab_off + (size_t)n * sizeof(PdPhase);
+  } else {  // the phase table stays in global memory
+    off = a.tab_off;
+    a.tab_off = -1;
+  }
   plan->smem = round(off);
   if (plan->smem > 227 * 1024) return N730_UNSUPPORTED;
   a.d.head_dim = head_dim;

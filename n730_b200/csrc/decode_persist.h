@@ -1,11 +1,14 @@
 // Persistent single-launch decode step (batch 1, INT4 fragment-tiled weights).
 #pragma once
+#include <cstdint>
+
 #include "attention.h"
 
 namespace n730 {
 
 enum : int { PD_GEMV = 0, PD_ATTN = 1, PD_FFN = 2 };
-enum : int { PD_EPI_STORE = 0, PD_EPI_RESID = 1, PD_EPI_SWIGLU = 2 };
+enum : int { PD_EPI_STORE = 0, PD_EPI_RESID = 1, PD_EPI_SWIGLU = 2, PD_EPI_XPUSH = 3 };
+constexpr int PD_MAX_RANKS = 8;
 
 // One op of the step.  GEMV: y (+)= W x with W in fragment tiles (`blob`,
 // rows x cols, G groups per row), optional RMSNorm of x (`norm_w`) and bias;
@@ -21,21 +24,33 @@ enum : int { PD_EPI_STORE = 0, PD_EPI_RESID = 1, PD_EPI_SWIGLU = 2 };
 // the same whatever order the CTAs arrive in).  The residual stream is then
 // h + acc: a later GEMV with a non-null `acc` reads x + acc (norm phases) or,
 // with the residual epilogue, folds acc into y and clears it.
+// Tensor parallel (several ranks, one launch per rank): a row-split GEMV
+// (o_proj / down_proj over this rank's K columns) ends with PD_EPI_XPUSH: each
+// row's partial sum is stored into slot [xpar][rank] of EVERY rank's exchange
+// area (peer memory).  The barrier before the next GEMV is then cross-GPU
+// (`xbar`), and its prologue (`xsum`) reads x = h + sum over ranks of slot
+// [xpar][r] in rank order (identical on every rank), the CTA owning a row
+// range also writing the new residual to `h_out` (the other residual buffer).
 struct __align__(16) PdPhase {
-  int kind, epi;
+  int8_t kind, epi;
+  int8_t xpar, xsum;        // tensor parallel: exchange slot parity; x = h + sum of the ranks' slots
+  int xbar;                 // tensor parallel: the barrier before this phase is cross-GPU barrier xbar (0: local)
   const uint8_t* blob;
   int rows, cols, G;
+  int rows2;                // FFN: down_proj rows
   const float* x;
   const float* norm_w;
   const float* bias;
   float* y;
   KVLayer kv;
   const uint8_t* blob2;     // FFN: down_proj
-  int rows2, cols2, G2;
+  int cols2, G2;
   unsigned long long* acc;  // FFN: down_proj sums (fixed point, 2^-32); GEMV: pending residual
+  float* h_out;             // tensor parallel: residual stream after this exchange
 };
 
 static_assert(sizeof(PdPhase) % 16 == 0, "phase table rows are copied as words");
+static_assert(sizeof(PdPhase) == 112, "an 80-layer phase table (fused FFN) must fit in shared memory");
 
 struct PdArgs {
   const PdPhase* phases;
@@ -57,8 +72,18 @@ struct PdArgs {
   int* err;                 // device error word (DEV_ERR_TIMEOUT on a wait that ran out)
   unsigned long long* acc;  // FFN accumulator [acc_n], cleared by the last CTA out
   int acc_n;
-  // shared-memory layout (bytes)
+  // shared-memory layout (bytes); tab_off < 0: the phase table is read from global memory
   int ring_off, ring_stride, work_off, kv_off, add_off, wpart_off, misc_off, ffn_off, tab_off;
+  // tensor parallel (tp_size > 1): exchange areas [2 parity][tp_size][xcap] floats and
+  // cross-barrier counters of every rank (own at tp_rank), mapped into this process
+  int tp_rank, tp_size;
+  int64_t xcap;
+  float* xrecv[PD_MAX_RANKS];
+  int* xcnt[PD_MAX_RANKS];
+  float* xrecv_local;       // xrecv[tp_rank]
+  int* xcnt_local;          // xcnt[tp_rank]
+  int* xepoch;              // launches completed on this rank (the same count on every rank)
+  int n_xbar;               // cross barriers per launch
 };
 
 struct PdPlan {
@@ -75,7 +100,8 @@ constexpr int PD_PAGE = 64;
 constexpr int PD_FFN_MAXG = 4;
 // CTAs of the persistent launch on the current device (one per SM)
 int persist_grid(int* grid);
-int persist_plan(const PdPhase* host_phases, int n_phases, int head_dim, int group_q, int page_size, PdPlan* plan);
+int persist_plan(const PdPhase* host_phases, int n_phases, int head_dim, int group_q, int page_size, int tp_size,
+                 PdPlan* plan);
 int persist_launch(const PdPlan& plan, cudaStream_t st);
 
 }  // namespace n730

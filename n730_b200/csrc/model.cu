@@ -90,7 +90,7 @@ struct Model {
   int max_pages = 0, n_split = 1;
   // decode workspace
   int* d_tokens = nullptr;
-  float *x = nullptr, *qkv = nullptr, *attn = nullptr, *mlp = nullptr, *logits = nullptr;
+  float *x = nullptr, *x2 = nullptr, *qkv = nullptr, *attn = nullptr, *mlp = nullptr, *logits = nullptr;
   // prefill workspace
   int* p_tokens = nullptr;
   float *px = nullptr, *pqkv = nullptr, *pattn = nullptr, *pmlp = nullptr;
@@ -277,7 +277,10 @@ static int stream_release(Model* m, int l) {
 // differ, or the shapes exceed the kernel's limits.
 static int plan_persistent(Model* m) {
   const N730ModelConfig& c = m->c;
-  if (c.stream_depth > 0 || c.tp_size > 1) return N730_OK;  // weights not resident / collectives between ops
+  if (c.stream_depth > 0) return N730_OK;  // weights not resident
+  // tensor parallel: the row-split sums cross over the mapped peer exchange regions
+  const bool tp = c.tp_size > 1;
+  if (tp && !(m->ar_ok && c.tp_size <= PD_MAX_RANKS && m->ar.cap >= c.hidden)) return N730_OK;
   auto tiled = [](const QWeight* w) { return w && w->layout == 1; };
   for (auto& y : m->L)
     if (!tiled(y.qkv) || !tiled(y.o) || !tiled(y.gate_up) || !tiled(y.down)) return N730_OK;
@@ -295,6 +298,41 @@ static int plan_persistent(Model* m) {
   // Fused FFN: the residual stream is h (m->x) + acc between a layer's FFN and
   // the next layer's o_proj, which folds acc into h and clears it; q|k|v and
   // the lm_head read h + acc.  Layers without a bias on down_proj only.
+  // Tensor parallel (tp): q|k|v and gate|up are this rank's columns, o_proj and
+  // down_proj its K columns.  Each of those row-split GEMVs pushes its partial
+  // sums into every rank's exchange slot (parity e & 1 for exchange e); after
+  // the cross-GPU barrier the next norm GEMV reads x = h + the ranks' sums in
+  // rank order and writes the new residual to the other h buffer.  The bias of
+  // a row-split projection is added on rank 0 only.
+  auto build_tp = [&]() {
+    ph.clear();
+    float* hb[2] = {m->x, m->x2};
+    int cur = 0, e = 0, xb = 0;
+    auto xsum = [&](PdPhase& p, bool write_h) {
+      p.x = hb[cur]; p.xsum = 1; p.xpar = (e - 1) & 1; p.xbar = ++xb;
+      p.h_out = write_h ? hb[cur ^ 1] : nullptr;
+      cur ^= 1;
+    };
+    const bool r0 = c.tp_rank == 0;
+    for (int l = 0; l < c.layers; ++l) {
+      const Layer& y = m->L[l];
+      gemv_phase(y.qkv, hb[cur], y.ln1, y.qkv_bias, m->qkv, PD_EPI_STORE);
+      if (l > 0) xsum(ph.back(), true);
+      PdPhase at = {};
+      at.kind = PD_ATTN; at.kv = y.kv;
+      ph.push_back(at);
+      gemv_phase(y.o, m->attn, nullptr, r0 ? y.o_bias : nullptr, nullptr, PD_EPI_XPUSH);
+      ph.back().xpar = e++ & 1;
+      gemv_phase(y.gate_up, hb[cur], y.ln2, y.gate_up_bias, m->mlp, PD_EPI_SWIGLU);
+      xsum(ph.back(), true);
+      gemv_phase(y.down, m->mlp, nullptr, r0 ? y.down_bias : nullptr, nullptr, PD_EPI_XPUSH);
+      ph.back().xpar = e++ & 1;
+    }
+    float* lg = m->vocab_l == c.vocab ? m->logits : m->logits_all + (size_t)c.tp_rank * m->vocab_l;
+    gemv_phase(m->lm_head, hb[cur], m->final_norm, nullptr, lg, PD_EPI_STORE);
+    xsum(ph.back(), false);
+    return xb;
+  };
   auto build = [&](bool fuse) {
     ph.clear();
     unsigned long long* acc = fuse ? m->ffn_acc : nullptr;
@@ -321,18 +359,22 @@ static int plan_persistent(Model* m) {
   };
   bool has_down_bias = false;
   for (auto& y : m->L) has_down_bias |= y.down_bias != nullptr;
-  bool fuse = !has_down_bias && (c.ffn_fuse > 0 || (c.ffn_fuse == 0 && g_down % grid == 0));
+  bool fuse = !tp && !has_down_bias && (c.ffn_fuse > 0 || (c.ffn_fuse == 0 && g_down % grid == 0));
+  if (tp && !m->x2)
+    if (int r = m->alloc(&m->x2, (size_t)c.hidden)) return r;
   if (fuse && !m->ffn_acc) {
     if (int r = m->alloc(&m->ffn_acc, (size_t)c.hidden)) return r;
     N730_CUDA(cudaMemsetAsync(m->ffn_acc, 0, (size_t)c.hidden * 8, m->st));
   }
   PdPlan plan;
-  build(fuse);
-  int rc = persist_plan(ph.data(), (int)ph.size(), c.head_dim, c.heads / c.kv_heads, c.page_size, &plan);
+  int n_xbar = 0;
+  if (tp) n_xbar = build_tp();
+  else build(fuse);
+  int rc = persist_plan(ph.data(), (int)ph.size(), c.head_dim, c.heads / c.kv_heads, c.page_size, c.tp_size, &plan);
   if (rc == N730_UNSUPPORTED && fuse) {  // shapes outside the fused phase's limits: two GEMV phases
     fuse = false;
     build(false);
-    rc = persist_plan(ph.data(), (int)ph.size(), c.head_dim, c.heads / c.kv_heads, c.page_size, &plan);
+    rc = persist_plan(ph.data(), (int)ph.size(), c.head_dim, c.heads / c.kv_heads, c.page_size, c.tp_size, &plan);
   }
   if (rc == N730_UNSUPPORTED) return N730_OK;
   if (rc) return rc;
@@ -358,6 +400,20 @@ static int plan_persistent(Model* m) {
   N730_CUDA(cudaMemsetAsync(a.attn_cnt, 0, c.kv_heads * 4, m->st));
   N730_CUDA(cudaMemsetAsync(a.sync, 0, 16, m->st));
   a.err = gemv_err_word();
+  if (tp) {
+    a.tp_rank = c.tp_rank;
+    a.tp_size = c.tp_size;
+    a.xcap = m->ar.cap;
+    for (int r = 0; r < c.tp_size; ++r) {
+      a.xrecv[r] = m->ar.peer[r].recv;
+      a.xcnt[r] = m->ar.peer[r].xcnt;
+    }
+    a.xrecv_local = a.xrecv[c.tp_rank];
+    a.xcnt_local = a.xcnt[c.tp_rank];
+    a.n_xbar = n_xbar;
+    if (int r = m->alloc(&a.xepoch, 1)) return r;
+    N730_CUDA(cudaMemsetAsync(a.xepoch, 0, 4, m->st));
+  }
   N730_REQUIRE(a.err, N730_OOM, "model: error word allocation failed");
   m->pd = plan;
   m->pd_ok = true;
@@ -572,7 +628,7 @@ static int rowsplit_linear(Model* m, const QWeight* w, const float* a, int lda, 
   if (m->c.tp_size <= 1) return gemv(m, w, a, lda, B, x, ldx, bias, x, ldx, nullptr, 0);
   const int h = m->c.hidden;
   if (int rc = gemv(m, w, a, lda, B, m->delta, h, bias, nullptr, 0, nullptr, 0)) return rc;
-  if (m->ar_ok && (int64_t)B * h <= m->ar.cap && ldx == h) {  // decode-sized: one-shot over peer memory
+  if (m->ar_ok && m->c.tp_allreduce == 0 && (int64_t)B * h <= m->ar.cap && ldx == h) {  // one-shot, peer memory
     ArArgs ar = m->ar;
     ar.part = m->delta;
     ar.x = x;
@@ -587,6 +643,8 @@ static int rowsplit_linear(Model* m, const QWeight* w, const float* a, int lda, 
   return launch_add(m, x, m->delta, (int64_t)B * h);
 }
 
+static int gather_logits(Model* m, int B, float* logits);
+
 // logits [B][vocab] = lm_head(final_norm(x)); vocab-split lm_head: gather the shards
 static int lm_head_logits(Model* m, const float* x, int B, float* logits) {
   const N730ModelConfig& c = m->c;
@@ -595,6 +653,13 @@ static int lm_head_logits(Model* m, const float* x, int B, float* logits) {
   float* part = m->logits_all + (size_t)c.tp_rank * B * m->vocab_l;
   if (int rc = gemv(m, m->lm_head, x, c.hidden, B, part, m->vocab_l, nullptr, nullptr, 0, m->final_norm, 0))
     return rc;
+  return gather_logits(m, B, logits);
+}
+
+// vocab-split lm_head: every rank's shard (logits_all[rank]) -> logits [B][vocab]
+static int gather_logits(Model* m, int B, float* logits) {
+  const N730ModelConfig& c = m->c;
+  float* part = m->logits_all + (size_t)c.tp_rank * B * m->vocab_l;
   if (ncclAllGather(part, m->logits_all, (size_t)B * m->vocab_l, ncclFloat, m->comm, m->st) != ncclSuccess) {
     set_error("model: ncclAllGather failed");
     return N730_COMM;
@@ -620,8 +685,11 @@ static int enqueue_decode(Model* m, int B) {
   const int h = c.hidden, ad = c.heads * c.head_dim;
   if (int rc = embed_launch(*m->embed, m->d_tokens, B, m->x, m->st)) return rc;
   const bool persistent = B == 1 && m->pd_ok;
-  if (persistent)
+  if (persistent) {
     if (int rc = persist_launch(m->pd, m->st)) return rc;
+    if (c.tp_size > 1 && m->vocab_l != c.vocab)  // the kernel wrote this rank's vocab shard
+      if (int rc = gather_logits(m, 1, m->logits)) return rc;
+  }
   if (!persistent)
     if (int rc = stream_begin(m)) return rc;
   for (int l = 0; l < c.layers && !persistent; ++l) {
@@ -771,7 +839,7 @@ N730_API int n730_model_tp_init(void* p, const uint8_t* id_bytes, int rank, int 
     set_error("ncclCommInitRank failed (rank %d of %d)", rank, size);
     return N730_COMM;
   }
-  if (size <= AR_MAX_RANKS && m->c.tp_allreduce == 0) {  // exchange region for the one-shot allreduce
+  if (size <= AR_MAX_RANKS) {  // exchange region: one-shot allreduce, persistent decode's exchanges
     const int64_t cap = ((int64_t)m->c.max_batch * m->c.hidden + 3) / 4 * 4;
     N730_CUDA(cudaMalloc(&m->ar_base, ar_region_bytes(size, cap)));
     N730_CUDA(cudaMemset(m->ar_base, 0, ar_region_bytes(size, cap)));
@@ -795,7 +863,8 @@ N730_API int n730_model_tp_init(void* p, const uint8_t* id_bytes, int rank, int 
 N730_API int n730_model_tp_ipc_handle(void* p, uint8_t* out) {
   MODEL(p);
   N730_REQUIRE(out, N730_NULL, "tp_ipc_handle: null output");
-  N730_REQUIRE(m->ar_base, N730_STATE, "tp_ipc_handle: no exchange region (tp_init first, tp_allreduce 0)");
+  N730_REQUIRE(m->ar_base, N730_STATE, "tp_ipc_handle: no exchange region (tp_init first, at most %d ranks)",
+               AR_MAX_RANKS);
   cudaIpcMemHandle_t hd;
   N730_CUDA(cudaIpcGetMemHandle(&hd, m->ar_base));
   static_assert(sizeof(cudaIpcMemHandle_t) == N730_IPC_HANDLE_BYTES, "IPC handle size");
@@ -996,7 +1065,7 @@ N730_API int n730_model_forward(void* p, int seq, const int32_t* host_tokens, in
 
 // info[16]: weight bytes, kv bytes per position, kv capacity bytes, n_split,
 // qkv_dim, max_pages, finalized, persistent batch-1 decode, untied embedding bytes,
-// streamed layer bytes per pass
+// streamed layer bytes per pass, FFN fused, phase table in global memory
 N730_API int n730_model_info(void* p, int64_t* info) {
   MODEL(p);
   if (!info) return N730_NULL;
@@ -1020,6 +1089,7 @@ N730_API int n730_model_info(void* p, int64_t* info) {
   info[8] = m->lm_head != m->embed ? bytes(m->embed) : 0;  // read one row per token, not streamed
   info[9] = m->streamed_bytes;                                // host->HBM bytes per forward pass
   info[10] = m->pd_ffn_fused;
+  info[11] = m->pd_ok && m->pd.a.tab_off < 0;  // persistent kernel reads its phase table from global memory
   return N730_OK;
 }
 

@@ -93,16 +93,18 @@ __global__ void __launch_bounds__(256) ar_push_reduce_kernel(const ArArgs a) {
   }
 }
 
+static size_t ar_flag_words(int size) { return (size_t)2 * size * AR_SLICES; }
+static size_t ar_head_bytes(int size) { return ((ar_flag_words(size) + 1) * sizeof(int) + 255) / 256 * 256; }
+
 size_t ar_region_bytes(int size, int64_t cap) {
-  const size_t fb = ((size_t)2 * size * AR_SLICES * sizeof(int) + 255) / 256 * 256;
-  return fb + (size_t)2 * size * cap * sizeof(float);
+  return ar_head_bytes(size) + (size_t)2 * size * cap * sizeof(float);
 }
 
 ArRegion ar_region_at(void* base, int size) {
   ArRegion r;
   r.flags = reinterpret_cast<int*>(base);
-  const size_t fb = ((size_t)2 * size * AR_SLICES * sizeof(int) + 255) / 256 * 256;
-  r.recv = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(base) + fb);
+  r.xcnt = r.flags + ar_flag_words(size);
+  r.recv = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(base) + ar_head_bytes(size));
   return r;
 }
 

@@ -12,10 +12,13 @@ constexpr int AR_SLICES = 32;  // CTAs of one allreduce; slice s of the vector i
 // The exchange region of one rank (one cudaMalloc, exported with cudaIpcGetMemHandle):
 //   flags [2 parity][ranks][AR_SLICES] int    - epoch of the last slice each rank pushed here
 //   recv  [2 parity][ranks][cap] float        - the partial sums each rank pushed here
+//   xcnt  int                                 - cross-GPU barrier counter of the persistent
+//                                               tensor-parallel decode kernel (which reuses recv)
 // plus, not shared: epoch (int, ops done) and done (int, CTAs finished in the current op).
 struct ArRegion {
   int* flags = nullptr;
   float* recv = nullptr;
+  int* xcnt = nullptr;
 };
 
 struct ArArgs {

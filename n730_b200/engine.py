@@ -190,7 +190,8 @@ class Engine:
         _lib.check(self.lib.n730_model_info(self.h, a), "model_info")
         return {"weight_bytes": a[0], "kv_bytes_per_pos": a[1], "kv_capacity_bytes": a[2], "n_split": a[3],
                 "qkv_dim": a[4], "pages_per_seq": a[5], "persistent_decode": bool(a[7]),
-                "embed_bytes": a[8], "streamed_bytes": a[9], "ffn_fused": bool(a[10])}
+                "embed_bytes": a[8], "streamed_bytes": a[9], "ffn_fused": bool(a[10]),
+                "phase_table_global": bool(a[11])}
 
     @staticmethod
     def tp_unique_id() -> bytes:

@@ -118,17 +118,17 @@ def shard_block(name: str, b, shape, size: int, rank: int, ffn_group: int):
     return RawBlock(b.layer_idx, b.prec_id, r1 - r0, c1 - c0, 1.0, 0.0, payload, g)
 
 
-def init_engine_comm(engine, rank: int, size: int, group=None, one_shot: bool | None = None):
+def init_engine_comm(engine, rank: int, size: int, group=None, map_peers: bool = True):
     """Share rank 0's NCCL id over torch.distributed (any backend) and join the engine's
-    communicator; for the one-shot allreduce (engine built with tp_allreduce=0, the default of
-    ``one_shot``) also exchange the exchange-region handles and map every rank's region."""
-    if one_shot is None:
-        one_shot = engine.cfg.tp_allreduce == 0
+    communicator; with ``map_peers`` (ranks on one node) also exchange the exchange-region
+    handles and map every rank's region: the persistent batch-1 decode kernel pushes its
+    row-split sums there, and with tp_allreduce=0 so does the one-shot allreduce.  Without it
+    every step uses the per-op kernels and NCCL."""
     import torch.distributed as dist
     ids = [engine.tp_unique_id() if rank == 0 else None]
     dist.broadcast_object_list(ids, src=0, group=group)
     engine.tp_init(ids[0], rank, size)
-    if one_shot:
+    if map_peers:
         handles = [None] * size
         dist.all_gather_object(handles, engine.tp_ipc_handle(), group=group)
         engine.tp_ipc_open(b"".join(handles), size)

@@ -1,7 +1,9 @@
-"""Tensor-parallel engine on 2 GPUs (row-split sums after o_proj / down_proj by
-the one-shot peer-memory allreduce or by NCCL, all-gathered vocab-split
-logits) against the oracle and the 1-GPU engine; decode steps repeated from
-the same cached state are bit-identical.
+"""Tensor-parallel engine on 2 GPUs against the oracle and the 1-GPU engine:
+batch-1 decode through the persistent kernel (row-split sums pushed into every
+rank's exchange slot over peer memory, cross-GPU barrier, rank-order sums) or
+through the per-op kernels (one-shot peer-memory allreduce or NCCL); batch-2
+decode through the per-op kernels; all-gathered vocab-split logits.  Decode
+steps repeated from the same cached state are bit-identical.
 
 Runs as two spawned processes, one per GPU; skipped with fewer than 2 GPUs.
 """
@@ -38,7 +40,7 @@ def _run(engine, shape):
     return ys
 
 
-def _worker(rank, size, port, shape_name, path, out, allreduce):
+def _worker(rank, size, port, shape_name, path, out, allreduce, per_op):
     from datetime import timedelta
 
     import torch.distributed as dist
@@ -52,8 +54,8 @@ def _worker(rank, size, port, shape_name, path, out, allreduce):
         shape = synthetic.SHAPES[shape_name]
         tp.check_shape(shape, size, FFN_GROUP)
         eng = Engine(tp.local_shape(shape, size, rank, FFN_GROUP), max_ctx=256, max_batch=2, max_prefill=32,
-                     tp_rank=rank, tp_size=size, tp_allreduce=allreduce)
-        tp.init_engine_comm(eng, rank, size, one_shot=allreduce == 0)
+                     tp_rank=rank, tp_size=size, tp_allreduce=allreduce, per_op_decode=per_op)
+        tp.init_engine_comm(eng, rank, size)
         blocks = []
         for n, b in _blocks(path):
             sb = tp.shard_block(n, b, shape, size, rank, FFN_GROUP)
@@ -61,6 +63,7 @@ def _worker(rank, size, port, shape_name, path, out, allreduce):
                 blocks.append((n, sb))
         load_tensors(eng, blocks)
         eng.finalize()
+        persistent = eng.info()["persistent_decode"]
         ys = _run(eng, shape)
         # the decode steps again from the same cached prompt: bit-identical (rank-order sums)
         eng.set_seq_len(0, PROMPT)
@@ -70,7 +73,7 @@ def _worker(rank, size, port, shape_name, path, out, allreduce):
         eng.forward(np.arange(11) % shape.vocab, seq=1)
         yb = eng.decode(np.array([4, 6], np.int32))
         if rank == 0:
-            out.put((ys, yb.copy(), same))
+            out.put((ys, yb.copy(), same, persistent))
         eng.close()
     except Exception as e:  # report instead of leaving the parent waiting
         out.put(repr(e))
@@ -79,9 +82,10 @@ def _worker(rank, size, port, shape_name, path, out, allreduce):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("allreduce", [0, 1], ids=["one-shot", "nccl"])
+@pytest.mark.parametrize("allreduce,per_op", [(1, False), (0, True), (1, True)],
+                         ids=["persistent", "one-shot", "nccl"])
 @pytest.mark.parametrize("shape_name", ["tiny", "tiny-128"])
-def test_tp2_engine(shape_name, allreduce, tmp_path):
+def test_tp2_engine(shape_name, allreduce, per_op, tmp_path):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     shape = synthetic.SHAPES[shape_name]
@@ -90,7 +94,7 @@ def test_tp2_engine(shape_name, allreduce, tmp_path):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, shape_name, str(path), q, allreduce)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, shape_name, str(path), q, allreduce, per_op)) for r in range(2)]
     for p in procs:
         p.start()
     res = q.get(timeout=300)
@@ -98,7 +102,8 @@ def test_tp2_engine(shape_name, allreduce, tmp_path):
         p.join(timeout=120)
     assert not isinstance(res, str), res
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
-    ys, yb, same = res
+    ys, yb, same, persistent = res
+    assert persistent == (not per_op)
     assert same
     w = _oracle_weights(_blocks(path))
     orc = OracleDecoder(shape, w, max_pos=256)

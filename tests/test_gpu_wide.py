@@ -2,10 +2,14 @@
 
 * split-K batched GEMV: a one-layer decoder with a 7B-wide FFN (down_proj K = 18944, whose x
   fragments for 8 batch columns exceed shared memory), decoded at batch 8;
-* the tcgen05 GEMM inside the model: prefill chunks of >= 128 tokens (max_prefill 256).
+* the tcgen05 GEMM inside the model: prefill chunks of >= 128 tokens (max_prefill 256);
+* the persistent decode kernel with a phase table too large for shared memory (200 layers,
+  1001 phases): read from global memory.
 
 Both against the oracle decoder within the 1e-2 logit bar.
 """
+import dataclasses
+
 import numpy as np
 import pytest
 
@@ -60,4 +64,23 @@ def test_long_prefill_uses_gemm(tmp_path, shape_name):
     assert rel_err(e.forward(prompt), orc.forward(prompt)) <= TOL
     for t in (3, 17):
         assert rel_err(e.forward([t]), orc.forward([t])) <= TOL
+    e.close()
+
+
+def test_persistent_phase_table_in_global_memory(tmp_path):
+    shape = dataclasses.replace(synthetic.SHAPES["tiny"], layers=200)
+    blocks, w = _model(tmp_path, shape, seed=45)
+    e = Engine(shape, max_ctx=256, max_batch=1, max_prefill=64)
+    load_tensors(e, blocks)
+    e.finalize()
+    assert e.info()["persistent_decode"] and e.info()["phase_table_global"]
+    orc = OracleDecoder(shape, w, max_pos=256)
+    rng = np.random.default_rng(12)
+    prompt = rng.integers(0, shape.vocab, 80)
+    assert rel_err(e.forward(prompt), orc.forward(prompt)) <= TOL
+    tok = 7
+    for step in range(5):
+        y, yr = e.forward([tok]), orc.forward([tok])
+        assert rel_err(y, yr) <= TOL, step
+        tok = int(np.argmax(yr))
     e.close()
