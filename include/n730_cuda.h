@@ -163,8 +163,9 @@ typedef struct N730ModelConfig {
                             N730Scheduler prefetch, scheduler.py:236-287, as host->HBM copies) */
   int32_t ffn_fuse;      /* persistent decode: 0 runs gate|up and down_proj as ONE phase (each CTA owns
                             whole FFN quant groups, down_proj partial sums reduced in a fixed order)
-                            when the down groups divide evenly over the SMs; 1 whenever the shapes
-                            allow it; -1 never (two GEMV phases) */
+                            when the down groups divide evenly over the SMs, or when the two-phase
+                            FFN does not fit the kernel (72B); 1 whenever the shapes allow it;
+                            -1 never (two GEMV phases) */
   int32_t tp_allreduce;  /* tensor parallel, decode-sized row-split sums: 0 one-shot over peer memory
                             (CUDA IPC, after n730_model_tp_ipc_open), fused with the residual add;
                             1 NCCL allreduce always */

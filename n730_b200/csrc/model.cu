@@ -375,6 +375,16 @@ static int plan_persistent(Model* m) {
     fuse = false;
     build(false);
     rc = persist_plan(ph.data(), (int)ph.size(), c.head_dim, c.heads / c.kv_heads, c.page_size, c.tp_size, &plan);
+  } else if (rc == N730_UNSUPPORTED && !tp && !has_down_bias && c.ffn_fuse == 0) {
+    // auto mode, uneven down groups per SM: the two-phase FFN did not fit (down_proj's x in shared
+    // memory, 72B: 29568 fp16), the fused one still runs persistently (faster than per-op kernels)
+    fuse = true;
+    if (!m->ffn_acc) {
+      if (int r = m->alloc(&m->ffn_acc, (size_t)c.hidden)) return r;
+      N730_CUDA(cudaMemsetAsync(m->ffn_acc, 0, (size_t)c.hidden * 8, m->st));
+    }
+    build(true);
+    rc = persist_plan(ph.data(), (int)ph.size(), c.head_dim, c.heads / c.kv_heads, c.page_size, c.tp_size, &plan);
   }
   if (rc == N730_UNSUPPORTED) return N730_OK;
   if (rc) return rc;
