@@ -67,7 +67,7 @@ def _args():
     ap.add_argument("--ffn-fuse", type=int, default=0, choices=[-1, 0, 1],
                     help="persistent decode FFN: 0 auto, 1 one fused phase, -1 two GEMV phases")
     ap.add_argument("--per-op", action="store_true",
-                    help="tp72b: batch-1 decode through the per-op kernels instead of the persistent kernel")
+                    help="batch-1 decode through the per-op kernels instead of the persistent kernel")
     ap.add_argument("--model", default=SHAPE_NAME, choices=["qwen2-7b", "qwen2-0.5b"],
                     help="resident workload: model shape")
     ap.add_argument("--pmap", default="int4_g128", choices=["int4_g128", "mixed_05b"],
@@ -273,7 +273,8 @@ def run_ours(a):
     headline = a.model == SHAPE_NAME and a.pmap == "int4_g128"
     B, ctx = a.batch, a.ctx
     max_ctx = ctx + 2 * (a.warmup + a.steps) + 64  # device-side steps, then the e2e steps
-    eng = Engine(shape, max_ctx=max_ctx, max_batch=B, max_prefill=512, ffn_fuse=a.ffn_fuse)
+    eng = Engine(shape, max_ctx=max_ctx, max_batch=B, max_prefill=512, ffn_fuse=a.ffn_fuse,
+                 per_op_decode=a.per_op)
     build_on_device(shape, a.pmap, eng, seed=rank)
     eng.finalize()
     info = eng.info()

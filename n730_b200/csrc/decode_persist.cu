@@ -185,8 +185,46 @@ __device__ __forceinline__ PdSplits pd_splits(const PdArgs& a) {
   return s;
 }
 
+// One INT8 unit (16 rows x KPG k-steps, PdTile layout) against x fragments xb
+// (k-step pairs as in mma_chunk) and the x sum xs of its 128 columns:
+// codes become fp16 1024 + q by a byte permute, so with C = sum (1024 + q) x,
+// row r gets scale_r * (C - (1024 + zero_r) * xs).
+template <int KPG>
+__device__ __forceinline__ void pd_unit_i8(const uint8_t* u, int lane, const uint4* xb, float xs, float& y_g,
+                                           float& y_g8) {
+  constexpr uint32_t M = 0x64646464u;
+  float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int s2 = 0; s2 < KPG / 2; ++s2) {
+    const uint4 w = *reinterpret_cast<const uint4*>(u + (s2 * 32 + lane) * 16);
+    const uint4 v = xb[s2 * 4];
+    mma16816(c, __byte_perm(w.x, M, 0x5140), __byte_perm(w.x, M, 0x5342), __byte_perm(w.y, M, 0x5140),
+             __byte_perm(w.y, M, 0x5342), v.x, v.y);
+    mma16816(c, __byte_perm(w.z, M, 0x5140), __byte_perm(w.z, M, 0x5342), __byte_perm(w.w, M, 0x5140),
+             __byte_perm(w.w, M, 0x5342), v.z, v.w);
+  }
+  const float4 sz = reinterpret_cast<const float4*>(u + 16 * PD_TILE_K)[lane >> 2];
+  y_g = fmaf(sz.x, c[0] - (1024.f + sz.y) * xs, y_g);
+  y_g8 = fmaf(sz.z, c[2] - (1024.f + sz.w) * xs, y_g8);
+}
+
+// One FP16 unit: the tiles are the A fragments themselves.
+template <int KPG>
+__device__ __forceinline__ void pd_unit_f16(const uint8_t* u, int lane, const uint4* xb, float& y_g, float& y_g8) {
+  float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int s = 0; s < KPG; ++s) {
+    const uint4 w = *reinterpret_cast<const uint4*>(u + (s * 32 + lane) * 16);
+    const uint4 v = xb[(s >> 1) * 4];
+    mma16816(c, w.x, w.y, w.z, w.w, (s & 1) ? v.z : v.x, (s & 1) ? v.w : v.y);
+  }
+  y_g += c[0];
+  y_g8 += c[2];
+}
+
 // EXT: the tensor-parallel exchange (push epilogue, cross-GPU barriers, rank
-// sums) and phase tables in global memory; without it that code is compiled out.
+// sums), phase tables in global memory and INT8 / FP16 weight tiles; without
+// it that code is compiled out.
 template <int KPG, int HD, bool EXT>
 __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdArgs a) {
   constexpr int GPC = pd_gpc(KPG);
@@ -260,7 +298,11 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
   // sub 0: [tile][group] units of the phase's (gate|up) GEMV; sub 1: an FFN
   // phase's down_proj units, whole row tiles [u, end) of the warp, each the
   // CTA's nj groups from j0 (one bulk copy per tile).
-  struct Cursor { int ph, sub, u, end, gi, G, j0, nj; const uint8_t* blob; };
+  struct Cursor { int ph, sub, u, end, gi, G, j0, nj, gb, gpc; const uint8_t* blob; };
+  // bytes and units per ring chunk of a phase's tiles (INT8 / FP16 tiles: EXT only)
+  auto unit_bytes = [&](const PdPhase& P) {
+    return !EXT || P.prec == 4 || P.prec == 0 ? GB : P.prec == 8 ? PD_UNIT8 : PD_UNIT16;
+  };
   auto set_down = [&](Cursor& c, int ph) {
     const PdPhase& P = phs[ph];
     const int j0 = pd_rng(0, P.G2, cta, NC), j1 = pd_rng(0, P.G2, cta + 1, NC);
@@ -280,6 +322,8 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
       const int w0 = pd_rng(c0, c1, warp, PD_WARPS), w1 = pd_rng(c0, c1, warp + 1, PD_WARPS);
       if (w0 < w1) {
         c.ph = ph; c.sub = 0; c.u = w0; c.end = w1; c.gi = w0 % P.G; c.G = P.G; c.j0 = 0; c.nj = 0; c.blob = P.blob;
+        c.gb = unit_bytes(P);
+        c.gpc = EXT ? a.ring_stride / c.gb : GPC;
         return;
       }
       if (P.kind == PD_FFN && set_down(c, ph)) return;
@@ -287,7 +331,7 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
     c.ph = a.n_phases;
   };
   int issued = 0, consumed = 0;
-  Cursor prod{0, 0, 0, 0, 0, 1, 0, 0, nullptr};
+  Cursor prod{0, 0, 0, 0, 0, 1, 0, 0, GB, GPC, nullptr};
   auto issue_next = [&](int slot) {  // lane 0
     if (prod.ph >= a.n_phases) return;
     uint8_t* dst = ring + (size_t)slot * a.ring_stride;
@@ -302,9 +346,10 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
       if (prod.u >= prod.end) set_phase(prod, prod.ph + 1);
       return;
     }
-    const int n = min(min(GPC, prod.end - prod.u), prod.G - prod.gi);  // never crosses a row tile
-    mbar_arrive_expect_tx(&wb[slot], (uint32_t)(n * GB));
-    bulk_g2s(dst, prod.blob + (int64_t)prod.u * GB, (uint32_t)(n * GB), &wb[slot]);
+    const int gb = EXT ? prod.gb : GB;
+    const int n = min(min(EXT ? prod.gpc : GPC, prod.end - prod.u), prod.G - prod.gi);  // never crosses a row tile
+    mbar_arrive_expect_tx(&wb[slot], (uint32_t)(n * gb));
+    bulk_g2s(dst, prod.blob + (int64_t)prod.u * gb, (uint32_t)(n * gb), &wb[slot]);
     ++issued;
     prod.u += n;
     prod.gi += n;
@@ -731,8 +776,10 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
     const int w0 = wr[warp], w1 = wr[warp + 1];
     float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
     int t = w0 / G, gi = w0 - t * G;  // current row tile, group within it
+    const int uprec = EXT ? (P.prec == 0 ? 4 : P.prec) : 4;
+    const int ugpc = uprec == 4 ? GPC : uprec == 8 ? a.ring_stride / PD_UNIT8 : a.ring_stride / PD_UNIT16;
     for (int u = w0; u < w1 && !wfail;) {
-      const int n = min(min(GPC, w1 - u), G - gi);
+      const int n = min(min(ugpc, w1 - u), G - gi);
       const int slot = consumed % PD_RING;
       int okl = 0;
       if (lane == 0) okl = wait_bar(&wb[slot], (uint32_t)((consumed / PD_RING) & 1));
@@ -744,7 +791,12 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
       const uint8_t* buf = ring + (size_t)slot * a.ring_stride;
       const uint4* xb[1] = {xf + gi * KPG * 2 + tq};
       const float* sxg = sx + gi;
-      if (n == GPC) {
+      if (EXT && uprec != 4) {
+        for (int gr = 0; gr < n; ++gr) {
+          if (uprec == 8) pd_unit_i8<KPG>(buf + gr * PD_UNIT8, lane, xb[0] + gr * KPG * 2, sxg[gr], acc[0][0], acc[0][2]);
+          else pd_unit_f16<KPG>(buf + gr * PD_UNIT16, lane, xb[0] + gr * KPG * 2, acc[0][0], acc[0][2]);
+        }
+      } else if (n == GPC) {
         mma_chunk<KPG, 1, GPC, true, 1>(buf, lane, xb, sxg, acc);
       } else {
         for (int gr = 0; gr < n; ++gr) {
@@ -918,7 +970,7 @@ static int persist_setup(const PdPlan& plan, bool launch, cudaStream_t st, int* 
 
 static int persist_dispatch(const PdPlan& plan, int head_dim, bool launch, cudaStream_t st, int* max_blocks) {
   const int kpg = plan.a.kpg;
-  if (plan.a.tp_size > 1 || plan.a.tab_off < 0) {  // exchange / global phase table: group 128 only
+  if (plan.a.tp_size > 1 || plan.a.tab_off < 0 || plan.a.mixed) {  // EXT features: group 128 only
     if (kpg != 8) return N730_UNSUPPORTED;
     if (head_dim == 128) return persist_setup<8, 128, true>(plan, launch, st, max_blocks);
     return persist_setup<8, 64, true>(plan, launch, st, max_blocks);
@@ -943,8 +995,15 @@ int persist_plan(const PdPhase* ph, int n, int head_dim, int group_q, int page_s
   N730_CUDA(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev));
   if (!coop) return N730_UNSUPPORTED;
   int kpg = 0, kmax = 0, gmax = 0, ffn_floats = 0;
+  bool mixed = false;
   for (int i = 0; i < n; ++i) {
     if (ph[i].kind != PD_GEMV && ph[i].kind != PD_FFN) continue;
+    if (ph[i].prec == 8 || ph[i].prec == 16) {  // INT8 / FP16 tiles: GEMV phases, 128-column units
+      if (ph[i].kind != PD_GEMV || ph[i].cols % PD_TILE_K || ph[i].G != ph[i].cols / PD_TILE_K) return N730_UNSUPPORTED;
+      mixed = true;
+    } else if (ph[i].prec != 0 && ph[i].prec != 4) {
+      return N730_UNSUPPORTED;
+    }
     const int k = ph[i].cols / ph[i].G / 16;
     if (ph[i].cols % 64 || (ph[i].norm_w && ph[i].cols > PD_KNORM) || (kpg && k != kpg) ||
         !(k == 4 || k == 8 || k == 16))
@@ -973,8 +1032,10 @@ int persist_plan(const PdPhase* ph, int n, int head_dim, int group_q, int page_s
   PdArgs& a = plan->a;
   a.kpg = kpg;
   a.tp_size = tp_size;
+  a.mixed = mixed;
   const int gb = kpg * 128 + 64;
   a.ring_stride = (int)round((size_t)pd_gpc(kpg) * gb);
+  if (mixed && a.ring_stride < PD_UNIT16) return N730_UNSUPPORTED;
   size_t off = round((size_t)(PD_WARPS * PD_RING + 1) * 8);
   a.ring_off = (int)off;
   off += (size_t)PD_WARPS * PD_RING * a.ring_stride;
@@ -1006,6 +1067,68 @@ int persist_plan(const PdPhase* ph, int n, int head_dim, int group_q, int page_s
   if (int rc = persist_dispatch(*plan, head_dim, false, nullptr, &maxb)) return rc;
   if (maxb < 1) return N730_UNSUPPORTED;
   plan->grid = sms;
+  return N730_OK;
+}
+
+// ---- INT8 / FP16 weights as persistent tiles (layout in decode_persist.h) ----
+__device__ __forceinline__ float2 pd_sz_rowmajor(const QWeight& w, int r, int c) {
+  const uint8_t* row = reinterpret_cast<const uint8_t*>(w.sz) + (int64_t)r * w.sz_pitch;
+  if (w.sz_mode == 0) return __half22float2(reinterpret_cast<const __half2*>(row)[c / w.group]);
+  return *reinterpret_cast<const float2*>(row);
+}
+
+// one thread per output element of a unit (codes; then the 32 scale/zero floats for INT8)
+__global__ void pd_tile_kernel(const QWeight w, uint8_t* out, int G) {
+  const int per = w.bits == 8 ? 16 * PD_TILE_K + 32 : 16 * PD_TILE_K;
+  const int64_t n = (int64_t)((w.rows + 15) / 16) * G * per;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t unit = i / per;
+    const int e = (int)(i - unit * per);
+    const int t = (int)(unit / G), j = (int)(unit - (int64_t)t * G);
+    if (w.bits == 8) {
+      uint8_t* ub = out + unit * PD_UNIT8;
+      if (e >= 16 * PD_TILE_K) {  // {scale_g, zero_g, scale_g+8, zero_g+8}, g = 0..7
+        const int f = e - 16 * PD_TILE_K, g = f >> 2, k = f & 3;
+        const int r = t * 16 + g + 8 * (k >> 1);
+        float v = 0.f;
+        if (r < w.rows) {
+          const float2 sz = pd_sz_rowmajor(w, r, j * PD_TILE_K);
+          v = (k & 1) ? sz.y : sz.x;
+        }
+        reinterpret_cast<float*>(ub + 16 * PD_TILE_K)[f] = v;
+        continue;
+      }
+      const int s2 = e >> 9, rem = e & 511, lane = rem >> 4, b = rem & 15;
+      const int s = s2 * 2 + (b >> 3), kh = (b >> 2) & 1, h = (b >> 1) & 1, el = b & 1;
+      const int r = t * 16 + (lane >> 2) + 8 * h;
+      const int c = j * PD_TILE_K + s * 16 + 2 * (lane & 3) + el + 8 * kh;
+      ub[e] = r < w.rows ? w.codes[(int64_t)r * w.row_bytes + c] : (uint8_t)0;
+    } else {
+      __half* ub = reinterpret_cast<__half*>(out + unit * PD_UNIT16);
+      const int s = e >> 8, rem = e & 255, lane = rem >> 3, q = rem & 7;
+      const int reg = q >> 1, el = q & 1, h = reg & 1, kh = reg >> 1;
+      const int r = t * 16 + (lane >> 2) + 8 * h;
+      const int c = j * PD_TILE_K + s * 16 + 2 * (lane & 3) + el + 8 * kh;
+      ub[e] = r < w.rows ? reinterpret_cast<const __half*>(w.codes + (int64_t)r * w.row_bytes)[c] : __float2half(0.f);
+    }
+  }
+}
+
+int64_t pd_tile_bytes(int bits, int rows, int cols) {
+  const int64_t units = (int64_t)((rows + 15) / 16) * (cols / PD_TILE_K);
+  return units * (bits == 8 ? PD_UNIT8 : PD_UNIT16);
+}
+
+int pd_tile_launch(const QWeight& w, uint8_t* out, cudaStream_t st) {
+  N730_REQUIRE((w.bits == 8 || w.bits == 16) && w.layout == 0 && w.cols % PD_TILE_K == 0, N730_UNSUPPORTED,
+               "persistent tiles: %d-bit weight, layout %d, %d columns", w.bits, w.layout, w.cols);
+  N730_REQUIRE(w.bits == 16 || w.sz_mode == 1 || w.group % PD_TILE_K == 0, N730_UNSUPPORTED,
+               "persistent tiles: INT8 group %d", w.group);
+  const int G = w.cols / PD_TILE_K;
+  const int64_t n = (int64_t)((w.rows + 15) / 16) * G * (w.bits == 8 ? 16 * PD_TILE_K + 32 : 16 * PD_TILE_K);
+  const unsigned blocks = (unsigned)std::min<int64_t>((n + 255) / 256, 65536);
+  pd_tile_kernel<<<blocks, 256, 0, st>>>(w, out, G);
+  N730_CUDA(cudaGetLastError());
   return N730_OK;
 }
 

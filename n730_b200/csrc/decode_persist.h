@@ -34,7 +34,9 @@ constexpr int PD_MAX_RANKS = 8;
 struct __align__(16) PdPhase {
   int8_t kind, epi;
   int8_t xpar, xsum;        // tensor parallel: exchange slot parity; x = h + sum of the ranks' slots
-  int xbar;                 // tensor parallel: the barrier before this phase is cross-GPU barrier xbar (0: local)
+  int16_t xbar;             // tensor parallel: the barrier before this phase is cross-GPU barrier xbar (0: local)
+  int8_t prec;              // weight tiles: 4 INT4 fragment tiles (0 reads as 4), 8 INT8, 16 FP16 (PdTile*)
+  int8_t pad_;
   const uint8_t* blob;
   int rows, cols, G;
   int rows2;                // FFN: down_proj rows
@@ -51,6 +53,23 @@ struct __align__(16) PdPhase {
 
 static_assert(sizeof(PdPhase) % 16 == 0, "phase table rows are copied as words");
 static_assert(sizeof(PdPhase) == 112, "an 80-layer phase table (fused FFN) must fit in shared memory");
+
+// Weight tiles of the persistent kernel for INT8 (per-tensor, per-channel or
+// grouped scale/zero) and FP16 weights, one unit per 16 rows x 128 columns,
+// units [row tile][column block] like the INT4 fragment tiles:
+//   INT8: 2048 B codes, [k-step pair][lane][16 B]: per k-step 8 B = the A
+//         fragment of mma.m16n8k16 (rows g / g+8, columns 2tq.. / 2tq+8..) as
+//         bytes {a0.0, a0.1, a1.0, a1.1, a2.0, a2.1, a3.0, a3.1}; then 128 B
+//         {scale_g, zero_g, scale_g+8, zero_g+8} fp32 per g = 0..7.
+//   FP16: 4096 B, [k-step][lane][16 B]: the four A fragment registers.
+constexpr int PD_TILE_K = 128;
+constexpr int PD_UNIT8 = 16 * PD_TILE_K + 128;
+constexpr int PD_UNIT16 = 16 * PD_TILE_K * 2;
+// Bytes of the tiles of an INT8 / FP16 weight (rows x cols, cols % 128 == 0).
+int64_t pd_tile_bytes(int bits, int rows, int cols);
+// Write weight `w` (INT8 row-major with scale/zero, or FP16) as persistent tiles into `out`.
+struct QWeight;
+int pd_tile_launch(const QWeight& w, uint8_t* out, cudaStream_t st);
 
 struct PdArgs {
   const PdPhase* phases;
@@ -84,6 +103,7 @@ struct PdArgs {
   int* xcnt_local;          // xcnt[tp_rank]
   int* xepoch;              // launches completed on this rank (the same count on every rank)
   int n_xbar;               // cross barriers per launch
+  int mixed;                // some phases stream INT8 / FP16 tiles (set by persist_plan)
 };
 
 struct PdPlan {

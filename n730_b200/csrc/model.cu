@@ -102,6 +102,7 @@ struct Model {
   // persistent batch-1 decode (decode_persist.cu)
   bool pd_ok = false;
   bool pd_ffn_fused = false;     // the persistent step runs each FFN as one phase
+  std::map<const QWeight*, uint8_t*> pd_tiles;  // INT8 / FP16 weights as persistent-kernel tiles
   PdPlan pd;
   // layer streaming (stream_depth > 0): per-layer weight images in pinned host
   // memory, copied into HBM slots on `cst` ahead of use
@@ -275,16 +276,44 @@ static int stream_release(Model* m, int l) {
 // Phase table + scratch for the persistent batch-1 decode kernel.  Leaves
 // pd_ok false (per-op kernels) when a weight is not in fragment tiles, groups
 // differ, or the shapes exceed the kernel's limits.
+constexpr int64_t PD_AUTO_MIN_LAYER_BYTES = 32ll << 20;
+
 static int plan_persistent(Model* m) {
   const N730ModelConfig& c = m->c;
   if (c.stream_depth > 0) return N730_OK;  // weights not resident
+  if (c.per_op_decode == 0) {  // auto: small layers decode faster through the per-op kernels
+    int64_t b = 0;
+    for (auto& y : m->L)
+      for (const QWeight* w : {y.qkv, y.o, y.gate_up, y.down}) b += dev_code_bytes(w) + dev_sz_bytes(w);
+    if (b < (int64_t)c.layers * PD_AUTO_MIN_LAYER_BYTES) return N730_OK;
+  }
   // tensor parallel: the row-split sums cross over the mapped peer exchange regions
   const bool tp = c.tp_size > 1;
   if (tp && !(m->ar_ok && c.tp_size <= PD_MAX_RANKS && m->ar.cap >= c.hidden)) return N730_OK;
+  // INT4 in fragment tiles stream as they are; INT8 (any scale/zero layout) and
+  // FP16 weights get a tiled copy for the persistent kernel (decode_persist.h)
   auto tiled = [](const QWeight* w) { return w && w->layout == 1; };
+  auto tileable = [&](const QWeight* w) {
+    return w && (tiled(w) || ((w->bits == 8 || w->bits == 16) && w->layout == 0 && w->cols % PD_TILE_K == 0 &&
+                              (w->bits == 16 || w->sz_mode == 1 || w->group % PD_TILE_K == 0)));
+  };
   for (auto& y : m->L)
-    if (!tiled(y.qkv) || !tiled(y.o) || !tiled(y.gate_up) || !tiled(y.down)) return N730_OK;
-  if (!tiled(m->lm_head)) return N730_OK;
+    if (!tileable(y.qkv) || !tileable(y.o) || !tiled(y.gate_up) || !tiled(y.down)) return N730_OK;
+  if (!tileable(m->lm_head)) return N730_OK;
+  for (auto& y : m->L)
+    for (const QWeight* w : {y.qkv, y.o})
+      if (!tiled(w) && !m->pd_tiles.count(w)) {
+        uint8_t* t = nullptr;
+        if (int r = m->alloc(&t, (size_t)pd_tile_bytes(w->bits, w->rows, w->cols))) return r;
+        if (int r = pd_tile_launch(*w, t, m->st)) return r;
+        m->pd_tiles[w] = t;
+      }
+  if (!tiled(m->lm_head) && !m->pd_tiles.count(m->lm_head)) {
+    uint8_t* t = nullptr;
+    if (int r = m->alloc(&t, (size_t)pd_tile_bytes(m->lm_head->bits, m->lm_head->rows, m->lm_head->cols))) return r;
+    if (int r = pd_tile_launch(*m->lm_head, t, m->st)) return r;
+    m->pd_tiles[m->lm_head] = t;
+  }
   int grid = 0;
   if (int r = persist_grid(&grid)) return r;
   const int g_down = m->L[0].down->n_groups;
@@ -292,6 +321,8 @@ static int plan_persistent(Model* m) {
   auto gemv_phase = [&](const QWeight* w, const float* x, const float* norm, const float* bias, float* y, int epi) {
     PdPhase p = {};
     p.kind = PD_GEMV; p.epi = epi; p.blob = w->codes; p.rows = w->rows; p.cols = w->cols; p.G = w->n_groups;
+    p.prec = 4;
+    if (!tiled(w)) { p.blob = m->pd_tiles.at(w); p.G = w->cols / PD_TILE_K; p.prec = (int8_t)w->bits; }
     p.x = x; p.norm_w = norm; p.bias = bias; p.y = y;
     ph.push_back(p);
   };
@@ -595,7 +626,7 @@ static int finalize(Model* m) {
   if (int rc = m->alloc(&m->pmlp, (size_t)P * c.ffn)) return rc;
   N730_CUDA(cudaMallocHost(&m->h_tok, (size_t)std::max(B, P) * 4));
   N730_CUDA(cudaMallocHost(&m->h_logits, (size_t)B * c.vocab * 4));
-  if (!c.per_op_decode)
+  if (c.per_op_decode <= 0)
     if (int rc = plan_persistent(m)) return rc;
   N730_CUDA(cudaStreamSynchronize(m->st));
   m->finalized = true;

@@ -130,7 +130,7 @@ class Engine:
 
     def __init__(self, shape: ModelShape, max_ctx: int = 4096, max_batch: int = 1, page_size: int = 64,
                  max_prefill: int = 512, use_graphs: bool = True, use_pdl: bool = True,
-                 tp_rank: int = 0, tp_size: int = 1, exact_gemv: bool = False, per_op_decode: bool = False,
+                 tp_rank: int = 0, tp_size: int = 1, exact_gemv: bool = False, per_op_decode: int = 0,
                  stream_depth: int = 0, ffn_fuse: int = 0, tp_allreduce: int = 1):
         self.lib = _sigs(_lib.cuda())
         self.shape = shape

@@ -105,18 +105,33 @@ def test_capacity_and_reset(model):
     e.close()
 
 
+def _persistent_ok(blocks):
+    """The persistent kernel streams INT4 g128 fragment tiles, and INT8 (per-tensor,
+    per-channel or g128) / FP16 tiles for q|k|v, o_proj and the lm_head; the FFN must be INT4."""
+    for name, b in blocks:
+        if b.cols <= 1:
+            continue
+        if name.split(".")[-2] in ("gate_proj", "up_proj", "down_proj"):
+            if b.prec_id != 0x44:
+                return False
+        elif b.prec_id not in (0x44, 0x48, 8, 16):
+            return False
+    return True
+
+
 @pytest.mark.parametrize("ffn_fuse", [1, -1])
 def test_persistent_decode_matches_per_op(model, ffn_fuse):
-    """Batch-1 decode through the persistent kernel (all-INT4 models; the FFN as
+    """Batch-1 decode through the persistent kernel (INT4 g128 models, and the mixed
+    INT8-attention / FP16-lm_head model through INT8 and FP16 tiles; the FFN as
     one gate|up + down-partials phase with a fixed-order reduction, or as two
     GEMV phases) and through one kernel per op: both within the bar of the
     oracle, and close to each other."""
     shape, blocks, w = model
-    ep = _engine(shape, blocks, max_batch=1, ffn_fuse=ffn_fuse)
+    ep = _engine(shape, blocks, max_batch=1, ffn_fuse=ffn_fuse, per_op_decode=-1)
     eo = _engine(shape, blocks, max_batch=1, per_op_decode=True)
-    all_int4 = all(b.prec_id == 0x44 for _, b in blocks if b.cols > 1)
-    assert ep.info()["persistent_decode"] == all_int4
-    assert ep.info()["ffn_fused"] == (all_int4 and ffn_fuse == 1)
+    ok = _persistent_ok(blocks)
+    assert ep.info()["persistent_decode"] == ok
+    assert ep.info()["ffn_fused"] == (ok and ffn_fuse == 1)
     assert not eo.info()["persistent_decode"]
     orc = OracleDecoder(shape, w, max_pos=512)
     rng = np.random.default_rng(21)
@@ -138,9 +153,9 @@ def test_decode_deterministic(model):
     logits on both decode paths: split tiles, K-parts and attention splits are
     merged in a fixed order."""
     shape, blocks, _ = model
-    for per_op in (False, True):
+    for per_op in (-1, 1):
         _deterministic(_engine(shape, blocks, max_batch=1, per_op_decode=per_op), shape)
-    _deterministic(_engine(shape, blocks, max_batch=1, ffn_fuse=1), shape)
+    _deterministic(_engine(shape, blocks, max_batch=1, ffn_fuse=1, per_op_decode=-1), shape)
 
 
 def _deterministic(e, shape):

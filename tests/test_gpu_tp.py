@@ -54,7 +54,7 @@ def _worker(rank, size, port, shape_name, path, out, allreduce, per_op):
         shape = synthetic.SHAPES[shape_name]
         tp.check_shape(shape, size, FFN_GROUP)
         eng = Engine(tp.local_shape(shape, size, rank, FFN_GROUP), max_ctx=256, max_batch=2, max_prefill=32,
-                     tp_rank=rank, tp_size=size, tp_allreduce=allreduce, per_op_decode=per_op)
+                     tp_rank=rank, tp_size=size, tp_allreduce=allreduce, per_op_decode=1 if per_op else -1)
         tp.init_engine_comm(eng, rank, size)
         blocks = []
         for n, b in _blocks(path):

@@ -70,7 +70,7 @@ def test_long_prefill_uses_gemm(tmp_path, shape_name):
 def test_persistent_phase_table_in_global_memory(tmp_path):
     shape = dataclasses.replace(synthetic.SHAPES["tiny"], layers=200)
     blocks, w = _model(tmp_path, shape, seed=45)
-    e = Engine(shape, max_ctx=256, max_batch=1, max_prefill=64)
+    e = Engine(shape, max_ctx=256, max_batch=1, max_prefill=64, per_op_decode=-1)
     load_tensors(e, blocks)
     e.finalize()
     assert e.info()["persistent_decode"] and e.info()["phase_table_global"]
