@@ -129,10 +129,12 @@ __device__ __forceinline__ int ld_relaxed_sys(const int* p) {
 __device__ bool pd_xbarrier(const PdArgs& a, int xep, int k, int* flag) {
   __syncthreads();
   if (threadIdx.x == PD_SYNC_T) {
+    // one system-scope fence orders this CTA's pushes (ordered before it by the CTA barrier)
+    // before all of its arrivals, which are then relaxed
     asm volatile("fence.acq_rel.sys;" ::: "memory");
 #pragma unroll
     for (int r = 0; r < PD_MAX_RANKS; ++r)
-      if (r < a.tp_size) asm volatile("red.release.sys.global.add.s32 [%0], 1;" :: "l"(a.xcnt[r]) : "memory");
+      if (r < a.tp_size) asm volatile("red.relaxed.sys.global.add.s32 [%0], 1;" :: "l"(a.xcnt[r]) : "memory");
     const unsigned target = (unsigned)a.tp_size * gridDim.x * ((unsigned)xep * (unsigned)a.n_xbar + (unsigned)k);
     const int* cnt = a.xcnt_local;
     uint64_t t0 = 0;
