@@ -300,20 +300,18 @@ static int plan_persistent(Model* m) {
   for (auto& y : m->L)
     if (!tileable(y.qkv) || !tileable(y.o) || !tiled(y.gate_up) || !tiled(y.down)) return N730_OK;
   if (!tileable(m->lm_head)) return N730_OK;
+  auto make_tiles = [&](const QWeight* w) -> int {
+    if (tiled(w) || m->pd_tiles.count(w)) return N730_OK;
+    uint8_t* t = nullptr;
+    if (int r = m->alloc(&t, (size_t)pd_tile_bytes(w->bits, w->rows, w->cols))) return r;
+    if (int r = pd_tile_launch(*w, t, m->st)) return r;
+    m->pd_tiles[w] = t;
+    return N730_OK;
+  };
   for (auto& y : m->L)
     for (const QWeight* w : {y.qkv, y.o})
-      if (!tiled(w) && !m->pd_tiles.count(w)) {
-        uint8_t* t = nullptr;
-        if (int r = m->alloc(&t, (size_t)pd_tile_bytes(w->bits, w->rows, w->cols))) return r;
-        if (int r = pd_tile_launch(*w, t, m->st)) return r;
-        m->pd_tiles[w] = t;
-      }
-  if (!tiled(m->lm_head) && !m->pd_tiles.count(m->lm_head)) {
-    uint8_t* t = nullptr;
-    if (int r = m->alloc(&t, (size_t)pd_tile_bytes(m->lm_head->bits, m->lm_head->rows, m->lm_head->cols))) return r;
-    if (int r = pd_tile_launch(*m->lm_head, t, m->st)) return r;
-    m->pd_tiles[m->lm_head] = t;
-  }
+      if (int r = make_tiles(w)) return r;
+  if (int r = make_tiles(m->lm_head)) return r;
   int grid = 0;
   if (int r = persist_grid(&grid)) return r;
   const int g_down = m->L[0].down->n_groups;
