@@ -78,8 +78,10 @@ __device__ __forceinline__ int ld_relaxed(const int* p) {
 }
 
 // Wait until *cnt >= target or the abort flag is raised: each poll issues the
-// two relaxed loads together (one L2 round trip), and one acquire fence follows
-// the wait.  Raises the abort flag and the device error word after PD_WAIT_NS.
+// two relaxed loads together (one L2 round trip); once the count is reached one
+// acquire load of it synchronises with the arrivals' release operations (an
+// acq_rel fence would also wait for this thread's own arrival to complete).
+// Raises the abort flag and the device error word after PD_WAIT_NS.
 __device__ __forceinline__ bool pd_wait_count(const PdArgs& a, const int* cnt, int target) {
   uint64_t t0 = 0;
   bool ok = true;
@@ -96,7 +98,8 @@ __device__ __forceinline__ bool pd_wait_count(const PdArgs& a, const int* cnt, i
       break;
     }
   }
-  asm volatile("fence.acq_rel.gpu;" ::: "memory");
+  if (ok) (void)ld_acquire(cnt);
+  else asm volatile("fence.acq_rel.gpu;" ::: "memory");
   return ok;
 }
 
