@@ -338,7 +338,7 @@ def run_ours(a):
         torch.cuda.synchronize()
         t_kern = e4.elapsed_time(e5) / 1000.0 / reps
         kern_bytes = info["weight_bytes"] - info["embed_bytes"] + kv_read
-        kern_name = "persist_decode_kernel<8,128> (whole batch-1 step, 148 CTAs x 512 threads)"
+        kern_name = "persist_decode_kernel<8,128,0> (whole batch-1 step, 148 CTAs x 512 threads)"
         traffic_file = "decode_persist_7b_traffic.txt"
     else:
         x = torch.randn(B, shape.hidden, device="cuda")
