@@ -63,6 +63,127 @@ class TPOracle(OracleDecoder):
         return torch.cat(parts).numpy()
 
 
+class TPPushOracle(TPOracle):
+    """The persistent kernel's exchange: every rank's partial sums land in one slot per rank
+    (here an all-gather) and each rank adds them to its residual in rank order,
+    ((x + p_0) + p_1) + ..., so the new residual is bit-identical on every rank."""
+
+    def _resid(self, x, y):
+        t = torch.from_numpy(np.ascontiguousarray(y, np.float32))
+        parts = [torch.empty_like(t) for _ in range(dist.get_world_size())]
+        dist.all_gather(parts, t)
+        acc = x.astype(np.float32)
+        for part in parts:
+            acc = (acc + part.numpy()).astype(np.float32)
+        return acc
+
+    def layer(self, i, x, offset):
+        c = self.cfg
+        p = f"model.layers.{i}"
+        h = rms_norm(x, self._norm(f"{p}.input_layernorm.weight"), c.rms_norm_eps)
+        q = apply_rope(self._lin(h, f"{p}.self_attn.q_proj"), c.num_attention_heads, c.head_dim, offset, self.cos, self.sin)
+        k = apply_rope(self._lin(h, f"{p}.self_attn.k_proj"), c.num_kv_heads, c.head_dim, offset, self.cos, self.sin)
+        v = self._lin(h, f"{p}.self_attn.v_proj")
+        self.k[i] = np.concatenate([self.k[i], k])
+        self.v[i] = np.concatenate([self.v[i], v])
+        a = attention(q, self.k[i], self.v[i], c.num_attention_heads, c.num_kv_heads, c.head_dim, offset)
+        x = self._resid(x, self._lin(a, f"{p}.self_attn.o_proj"))
+        h2 = rms_norm(x, self._norm(f"{p}.post_attention_layernorm.weight"), c.rms_norm_eps)
+        m = swiglu(self._lin(h2, f"{p}.mlp.gate_proj"), self._lin(h2, f"{p}.mlp.up_proj"))
+        return self._resid(x, self._lin(m, f"{p}.mlp.down_proj"))
+
+
+def _push_worker(rank, size, port, out):
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=size)
+    try:
+        shape = synthetic.SHAPES["tiny"]
+        full = dict(synthetic.host_tensors(shape, seed=6))
+        local = {n: np.ascontiguousarray(s) for n, w in full.items()
+                 if (s := tp.shard(n, w, shape, size, rank, FFN_GROUP)) is not None}
+        o = TPPushOracle(shape, local, rank, size)
+        rng = np.random.default_rng(4)
+        ys = [o.forward(rng.integers(0, shape.vocab, 7))] + [o.forward([t]) for t in (2, 9)]
+        # every rank must hold the same logits, bit for bit
+        t = torch.from_numpy(np.concatenate(ys))
+        gathered = [torch.empty_like(t) for _ in range(size)]
+        dist.all_gather(gathered, t)
+        same = all(torch.equal(gathered[0], g) for g in gathered)
+        if rank == 0:
+            ref = OracleDecoder(shape, full, max_pos=256)
+            rng = np.random.default_rng(4)
+            refs = [ref.forward(rng.integers(0, shape.vocab, 7))] + [ref.forward([t]) for t in (2, 9)]
+            out.put((same, max(float(np.max(np.abs(a - b)) / np.max(np.abs(b))) for a, b in zip(ys, refs))))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp2_rank_order_push_sums():
+    """The persistent decode kernel's exchange (partials pushed to per-rank slots, summed into
+    the residual in rank order on every rank): identical on both ranks, = unsharded <= 1e-5."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_push_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    same, err = q.get(timeout=5)
+    assert same and err <= 1e-5
+
+
+class _FakeEngine:
+    """Stands in for Engine in the communicator handshake (no GPU): records the calls."""
+
+    def __init__(self, rank):
+        self.rank, self.calls = rank, []
+
+    def tp_unique_id(self):
+        return b"id-of-rank-0".ljust(128, b"\0")
+
+    def tp_init(self, uid, rank, size):
+        self.calls.append(("init", uid[:12], rank, size))
+
+    def tp_ipc_handle(self):
+        return bytes([self.rank]) * 64
+
+    def tp_ipc_open(self, handles, size):
+        self.calls.append(("open", handles, size))
+
+
+def _handshake_worker(rank, size, port, map_peers, out):
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=size)
+    try:
+        e = _FakeEngine(rank)
+        tp.init_engine_comm(e, rank, size, map_peers=map_peers)
+        out.put((rank, e.calls))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("map_peers", [True, False])
+def test_engine_comm_handshake(map_peers):
+    """Rank 0's NCCL id reaches every rank; with map_peers every rank opens all ranks'
+    exchange-region handles in rank order (the persistent kernel's peer pointers)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_handshake_worker, args=(r, 2, port, map_peers, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    got = dict(q.get(timeout=5) for _ in range(2))
+    for rank, calls in got.items():
+        assert calls[0] == ("init", b"id-of-rank-0", rank, 2)
+        if map_peers:
+            assert calls[1] == ("open", bytes([0]) * 64 + bytes([1]) * 64, 2) and len(calls) == 2
+        else:
+            assert len(calls) == 1
+
+
 def _worker(rank, size, port, shape_name, out):
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=size)
     try:
