@@ -24,10 +24,17 @@
 //  * Attention: each split is one KV page (64 positions) of one KV head.  The
 //    page's K and V are bulk-copied into shared memory a whole layer ahead (the
 //    cached positions do not depend on this step); the split holding the new
-//    position RoPEs and appends k/v; scores and P V on CUDA cores with an
-//    online softmax; the last split of a head merges all splits with one batch
-//    of loads:  out = sum_s e^(m_s-M) o_s / (sum_s e^(m_s-M) l_s + 1e-9)
+//    position RoPEs and appends k/v; scores and P V on the tensor cores with an
+//    online softmax; once every split of a head has published, each split
+//    merges a slice of the head's outputs with one batch of loads:
+//    out = sum_s e^(m_s-M) o_s / (sum_s e^(m_s-M) l_s + 1e-9)
 //    (the reference normalisation, n730_cuda.cu:236-257).
+//  * Template variant EXT = true adds what only some models need, so that the
+//    INT4 single-GPU kernel carries none of it: phase tables read from global
+//    memory (too large for shared memory), INT8 / FP16 weight tiles
+//    (decode_persist.h), and the tensor-parallel exchange (a push epilogue into
+//    every rank's exchange slot over peer memory, cross-GPU barriers on
+//    counters in every rank's region, rank-order sums in the next prologue).
 // Data written by other CTAs during the launch is read with ld.global.cg (L2),
 // never through a possibly stale L1 line.
 #include <algorithm>
