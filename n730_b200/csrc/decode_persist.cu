@@ -242,7 +242,6 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
   constexpr int GPC = pd_gpc(KPG);
   constexpr int GB = KPG * 128 + 64;  // bytes per group
   constexpr int H2 = HD / 2;
-  constexpr int CH = HD / 8;          // 16-byte chunks per K/V row
   constexpr uint32_t PAGE_BYTES = PD_PAGE * HD * 2;
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -625,10 +624,11 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
         return (f01.x + f01.y) + (f23.x + f23.y);
       };
       auto group_sum = [&](int i, float v) {  // all 32 lanes; lane 0 of the group writes
-        if (KPG > 8) return;
+        if constexpr (KPG <= 8) {
 #pragma unroll
-        for (int o = KPG * 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        if ((lane & (KPG * 4 - 1)) == 0 && i < items) sx[i / (KPG * 4)] = v;
+          for (int o = KPG * 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+          if ((lane & (KPG * 4 - 1)) == 0 && i < items) sx[i / (KPG * 4)] = v;
+        }
       };
       if (P.norm_w) {  // K <= PD_KNORM: the row stays in registers across the reduction
         float xv[PD_NREG][4];
