@@ -23,13 +23,19 @@ decode steps run at context 2048.. with the fp16 paged KV cache.
   (28 layers x 4 KV heads x 128 x 2 x 2 B per cached position), against the
   measured HBM peak in MEASURED_PEAKS.json.  For batch > 1 (per-op kernels)
   the gate|up dequant-GEMV is timed alone instead.
-* ``cpu_baseline``: the reference's CPU path for one decoder layer of this
-  shape (its own n730core read+dequant, built from its source, plus numpy
-  fp32 GEMV), extrapolated to a token; per-tensor INT4 stands in for g128
-  (the reference has no group-wise format).
+* ``cpu_baseline``: the reference's CPU path for whole decode tokens of this
+  shape (its own n730core read+dequant, built from its source, on a reader
+  thread pool, plus numpy fp32 GEMVs and the attention over an fp32 KV
+  cache); per-tensor INT4 stands in for g128 (the reference has no
+  group-wise format).
 
-N > 1 (torchrun, one rank per GPU): every rank decodes its own batch
-(independent replicas, weak scaling); time is the max over ranks.
+Launched by torchrun (any N, including 1): the Qwen2-72B-shape INT4 g128
+model decodes at batch 1 tensor parallel over the N ranks (q/k/v, gate/up
+column-split, o_proj/down_proj row-split with one exchange each, vocab-split
+lm_head): one model, strong scaling, time the max over ranks.  So the
+multi-GPU scaling points measure tensor-parallel decode of one 72B model, and
+their N = 1 point is that model on one GPU.  ``--workload resident`` under
+torchrun runs independent 7B replicas instead.
 """
 from __future__ import annotations
 
@@ -50,6 +56,17 @@ sys.path.insert(0, str(REPO))
 
 SHAPE_NAME = "qwen2-7b"
 METRIC = "decode tok/s at Qwen2-7B-shape INT4; dequant-GEMV HBM GB/s vs ~8 TB/s peak"
+TP_METRIC = "decode tok/s, Qwen2-72B-shape INT4 g128, tensor parallel"
+
+
+def _under_torchrun() -> bool:
+    return "TORCHELASTIC_RUN_ID" in os.environ or "LOCAL_WORLD_SIZE" in os.environ
+
+
+def _tp_workload(a) -> bool:
+    """The 72B tensor-parallel workload: asked for, or (by default) whenever torchrun launched us,
+    at any N: the multi-GPU scaling points measure tensor-parallel decode of one 72B model."""
+    return a.workload == "tp72b" or (a.workload == "auto" and _under_torchrun())
 
 
 def _args():
@@ -73,8 +90,10 @@ def _args():
     ap.add_argument("--pmap", default="int4_g128", choices=["int4_g128", "mixed_05b"],
                     help="resident workload: precision map (mixed_05b: INT8 attention, INT4 g128 FFN, fp16 tied "
                          "embedding/lm_head)")
-    ap.add_argument("--workload", default="resident", choices=["resident", "streamed", "tp72b", "linear"],
-                    help="streamed: 7B aggressive mixed quant (FFN INT2 g64, attention INT4 g128, lm_head INT8 "
+    ap.add_argument("--workload", default="auto", choices=["auto", "resident", "streamed", "tp72b", "linear"],
+                    help="auto: tp72b when launched by torchrun (any N), else resident (the 7B headline); "
+                         "resident: the model resident in HBM (N ranks: independent replicas); "
+                         "streamed: 7B aggressive mixed quant (FFN INT2 g64, attention INT4 g128, lm_head INT8 "
                          "per channel), layer weights in pinned host memory, 2-layer prefetch, 1024-token prompt; "
                          "tp72b: Qwen2-72B shape INT4 g128 split over the N ranks (tensor parallel, strong scaling)")
     return ap.parse_args()
@@ -152,24 +171,40 @@ def _dist():
 
 
 # ---------------------------------------------------------------------------
-# CPU baseline: the reference's own CPU path on one decoder layer
+# CPU baseline: the reference's own CPU path for a whole decode token
 # ---------------------------------------------------------------------------
-class CpuLayerSample:
-    """The reference's CPU path on one decoder layer of `shape`.
+def _host_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
 
-    Per tensor: the reference core's n730_read_layer (file read + per-tensor
-    INT4 dequant to fp32; the library is built from the reference source by
-    oracle/Makefile) then numpy fp32 ``W @ x`` (inference.py:668,
-    scheduler.py:324).  ``run()`` returns seconds per token: the layer time
-    x layers + lm_head at the same per-parameter rate.
+
+class CpuReferenceDecoder:
+    """The reference's CPU decode path for one token of a Qwen2-shape decoder.
+
+    Per layer, the seven projection weights are read and dequantised from a
+    ``.n730`` file by the reference core's ``n730_read_layer`` (built from its
+    own source by oracle/Makefile; per-tensor INT4, the reference has no
+    group-wise format), as its layer scheduler does (``scheduler.py:198-230``),
+    then applied as numpy fp32 ``W @ x`` (``inference.py:668``, ``scheduler.py:324``)
+    around the oracle's RMSNorm, RoPE, GQA attention over an fp32 KV cache of
+    ``ctx`` positions and SwiGLU; then the final norm and the lm_head (read,
+    dequantised, GEMV).  Reads run on a pool of ``threads`` workers, each with its
+    own file handle (a handle is not thread-safe, ``scheduler.py:242-244``),
+    up to ``ahead`` tensors ahead of the layer being computed; the GEMVs use
+    OpenBLAS's threads.  The file holds one layer's seven tensors and the
+    lm_head; every layer reads the same seven blocks (same sizes, same work;
+    the codes are uniform random bytes: dequant and GEMV cost do not depend on
+    the values).
     """
 
-    def __init__(self, shape, seed=0):
+    def __init__(self, shape, ctx, threads=None, ahead=16, seed=0):
         import ctypes as C
         import struct
         import tempfile
+        from concurrent.futures import ThreadPoolExecutor
 
-        from oracle import quant as oq
         core_so = REPO / "oracle" / "_ref" / "n730core.so"
         if not core_so.exists():
             raise FileNotFoundError("oracle/_ref/n730core.so missing (built by __graft_entry__.build)")
@@ -181,47 +216,105 @@ class CpuLayerSample:
         core.n730_read_layer.restype = C.c_int32
         core.n730_close.argtypes = [C.c_int64]
         self.core = core
-        self.shape = shape
-        h, q, kv, f = shape.hidden, shape.heads * shape.head_dim, shape.kv_heads * shape.head_dim, shape.ffn
-        self.tensors = [(q, h), (kv, h), (kv, h), (h, q), (f, h), (f, h), (h, f)]
-        tmp = tempfile.NamedTemporaryFile(suffix=".n730", delete=False)
+        self.shape = s = shape
+        self.ctx = ctx
+        h, q, kv, f = s.hidden, s.heads * s.head_dim, s.kv_heads * s.head_dim, s.ffn
+        self.tensors = [(q, h), (kv, h), (kv, h), (h, q), (f, h), (f, h), (h, f), (s.vocab, h)]
+        rng = np.random.default_rng(seed)
+        tmp = tempfile.NamedTemporaryFile(suffix=".n730", delete=False, dir=os.environ.get("TMPDIR"))
         self.path = tmp.name
         self.offs = []
         with open(self.path, "wb") as fo:
             fo.write(b"N730\x00\x01\x00\x00" + struct.pack(">II", 1, 2) + b"{}")
             fo.write(bytes(4096 - 18))
-            for i, shp in enumerate(self.tensors):
-                w = np.random.default_rng(seed + i).normal(0, 0.02, shp).astype(np.float32)
-                codes, scale, zp = oq.quantize_int4(w)
+            for i, (r, c) in enumerate(self.tensors):
+                codes = rng.integers(0, 256, (r * c + 1) // 2, dtype=np.uint8)
                 self.offs.append(fo.tell())
-                blk = struct.pack(">4sIBIIffi", b"LYR\x00", i, 4, shp[0], shp[1], scale, zp, len(codes)) + codes
-                fo.write(blk + bytes((-len(blk)) % 4096))
-        self.h = core.n730_open(self.path.encode())
-        self.x = np.random.default_rng(1).normal(0, 1, h).astype(np.float32)
-        self.xf = np.random.default_rng(2).normal(0, 1, f).astype(np.float32)
+                fo.write(struct.pack(">4sIBIIffi", b"LYR\x00", i, 4, r, c, 0.0025, 8.0, codes.size))
+                codes.tofile(fo)
+                fo.write(bytes((-(29 + codes.size)) % 4096))
+        self.threads = threads or _host_cores()
+        self.ahead = ahead
+        self.handles = [core.n730_open(self.path.encode()) for _ in range(self.threads)]
+        assert all(hd >= 0 for hd in self.handles), self.handles
+        import threading
+        self._tls = threading.local()
+        self._hid = iter(range(self.threads))
+        self._hlock = threading.Lock()
+        self.pool = ThreadPoolExecutor(self.threads)
+        from oracle.model import rope_table
+        self.cos, self.sin = rope_table(ctx + 64, s.head_dim, s.rope_theta)
+        self.kc = [rng.normal(0, 1, (ctx, kv)).astype(np.float32) for _ in range(s.layers)]
+        self.vc = [rng.normal(0, 1, (ctx, kv)).astype(np.float32) for _ in range(s.layers)]
+        self.bias = [rng.normal(0, 0.02, q + 2 * kv).astype(np.float32) for _ in range(s.layers)]
+        self.ones = np.ones(h, np.float32)
+        self.x0 = rng.normal(0, 1, h).astype(np.float32)
         try:
             import threadpoolctl
             self.blas = max(i.get("num_threads", 1) for i in threadpoolctl.threadpool_info())
         except Exception:
             self.blas = os.cpu_count() or 1
 
-    def run(self):
+    def _handle(self):
+        hd = getattr(self._tls, "h", None)
+        if hd is None:
+            with self._hlock:
+                hd = self._tls.h = self.handles[next(self._hid)]
+        return hd
+
+    def _read(self, k):
         C = self.C
-        t0 = time.perf_counter()
-        for off, shp in zip(self.offs, self.tensors):
-            buf = np.empty(shp[0] * shp[1], np.float32)
-            r, c, p = C.c_int32(), C.c_int32(), C.c_int32()
-            rc = self.core.n730_read_layer(self.h, off, buf.ctypes.data, C.byref(r), C.byref(c), C.byref(p))
-            assert rc == 0, rc
-            W = buf.reshape(shp)
-            _ = W @ (self.xf if shp[1] == self.shape.ffn else self.x)
-        self.t_layer = time.perf_counter() - t0
-        layer_params = sum(a * b for a, b in self.tensors)
-        lm_params = self.shape.vocab * self.shape.hidden
-        return self.t_layer * self.shape.layers + self.t_layer / layer_params * lm_params
+        r, c = self.tensors[k]
+        buf = np.empty(r * c, np.float32)
+        ro, co, po = C.c_int32(), C.c_int32(), C.c_int32()
+        rc = self.core.n730_read_layer(self._handle(), self.offs[k], buf.ctypes.data, C.byref(ro), C.byref(co),
+                                       C.byref(po))
+        if rc != 0:
+            raise RuntimeError(f"n730_read_layer failed: {rc}")
+        return buf.reshape(r, c)
+
+    def step(self):
+        """One decode token at position ``ctx`` (the cache is not extended: every step is the same work)."""
+        from collections import deque
+        from oracle.model import apply_rope, attention, rms_norm, swiglu
+        s = self.shape
+        q_dim, kv_dim = s.heads * s.head_dim, s.kv_heads * s.head_dim
+        order = [(l, k) for l in range(s.layers) for k in range(7)] + [(s.layers, 7)]
+        pend = deque()
+        nxt = 0
+
+        def fill():
+            nonlocal nxt
+            while nxt < len(order) and len(pend) < self.ahead:
+                pend.append(self.pool.submit(self._read, order[nxt][1]))
+                nxt += 1
+
+        def take():
+            fill()
+            w = pend.popleft().result()
+            fill()
+            return w
+
+        x = self.x0.copy()
+        for l in range(s.layers):
+            hn = rms_norm(x[None], self.ones, s.rms_eps)[0]
+            qkv = np.concatenate([take() @ hn, take() @ hn, take() @ hn]) + self.bias[l]
+            qv = apply_rope(qkv[None, :q_dim], s.heads, s.head_dim, self.ctx, self.cos, self.sin)
+            kv = apply_rope(qkv[None, q_dim:q_dim + kv_dim], s.kv_heads, s.head_dim, self.ctx, self.cos, self.sin)
+            ks = np.concatenate([self.kc[l], kv])
+            vs = np.concatenate([self.vc[l], qkv[None, q_dim + kv_dim:]])
+            a = attention(qv, ks, vs, s.heads, s.kv_heads, s.head_dim, self.ctx)[0]
+            x = x + take() @ a
+            h2 = rms_norm(x[None], self.ones, s.rms_eps)[0]
+            g, u = take() @ h2, take() @ h2
+            x = x + take() @ swiglu(g, u)
+        last = rms_norm(x[None], self.ones, s.rms_eps)[0]
+        return take() @ last
 
     def close(self):
-        self.core.n730_close(self.h)
+        self.pool.shutdown()
+        for hd in self.handles:
+            self.core.n730_close(hd)
         os.unlink(self.path)
 
 
@@ -230,24 +323,36 @@ def run_reference(a):
     if rank != 0:
         return
     from n730_b200.synthetic import SHAPES
-    shape = SHAPES[SHAPE_NAME]
-    cs = CpuLayerSample(shape)
-    for _ in range(a.warmup):
-        cs.run()
-    times = [cs.run() for _ in range(a.steps)]
+    tp72 = _tp_workload(a)
+    shape = SHAPES["qwen2-72b" if tp72 else SHAPE_NAME]
+    if a.layers:
+        shape = dataclasses.replace(shape, layers=a.layers)
+    cs = CpuReferenceDecoder(shape, a.ctx)
+    t0 = time.perf_counter()
+    cs.step()
+    t_first = time.perf_counter() - t0
+    # every step is one whole token; the step count is capped so the arm ends within ~2 minutes
+    steps = max(1, min(a.steps, int(120.0 / max(t_first, 1e-3))))
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        cs.step()
+    t = (time.perf_counter() - t0) / steps
     cs.close()
-    kind, blas = "reference", cs.blas
-    t = statistics.median(times)
     v = a.batch / t
-    out = {"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tok/s", "n_gpus": a.gpus,
-           "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(t * 1000 * a.batch, 1),
-           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-           "config": {"workload": "qwen2-7b-shape decoder, INT4 (per-tensor: the reference has no group-wise "
-                                  "format), batch 1 decode step on the host CPU",
-                      "batch": a.batch, "ctx": a.ctx},
-           "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": blas + 1, "kind": kind,
-                            "sample": "one decoder layer per step (n730_read_layer + numpy fp32 GEMV for 7 "
-                                      "tensors), scaled by 28 layers + lm_head params"},
+    name = "qwen2-72b" if tp72 else "qwen2-7b"
+    sample = (f"whole {name}-shape decode tokens at context {a.ctx} ({steps} timed, 1 warm-up): {shape.layers} "
+              f"layers x 7 reference n730_read_layer reads (per-tensor INT4) on {cs.threads} reader threads + numpy "
+              f"fp32 GEMVs on {cs.blas} OpenBLAS threads, attention over an fp32 KV cache, final norm + lm_head")
+    out = {"impl": "reference", "metric": TP_METRIC if tp72 else METRIC, "value": round(v, 4), "unit": "tok/s",
+           "n_gpus": a.gpus, "steps": steps, "warmup": 1, "ms_per_step": round(t * 1000, 1),
+           "higher_is_better": True, "scaling": "strong" if tp72 else "weak", "vs_baseline": None, "dtype": "f32",
+           "data": "synthetic",
+           "config": {"workload": f"{name}-shape decoder ({shape.layers} layers), INT4 (per-tensor: the reference "
+                                  "has no group-wise format), batch 1 decode step on the host CPU (the reference "
+                                  "has no tensor parallelism: one host at every N)",
+                      "batch": a.batch, "ctx": a.ctx, "steps_requested": a.steps, "warmup_requested": a.warmup},
+           "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": _host_cores(), "kind": "reference",
+                            "blas_threads": cs.blas, "reader_threads": cs.threads, "sample": sample},
            "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(out), flush=True)
 
@@ -412,14 +517,19 @@ def run_ours(a):
                                 "accumulators) for every linear, 512-token chunks; wall clock incl. host calls"},
         }
         if not a.no_cpu_baseline and headline:
-            cs = CpuLayerSample(shape)
-            t_token = min(cs.run() for _ in range(3))
+            cs = CpuReferenceDecoder(shape, ctx)
+            cs.step()
+            t0 = time.perf_counter()
+            for _ in range(2):
+                cs.step()
+            t_token = (time.perf_counter() - t0) / 2
             cs.close()
-            out["cpu_baseline"] = {"value": round(1.0 / t_token, 4), "unit": "tok/s", "cores": cs.blas + 1,
-                                   "kind": "reference",
-                                   "sample": f"one qwen2-7b-shape decoder layer (best of 3, {cs.t_layer:.2f} s: "
-                                             "reference n730_read_layer per-tensor INT4, 1 thread, + numpy fp32 "
-                                             "GEMV on OpenBLAS threads), scaled to 28 layers + lm_head"}
+            out["cpu_baseline"] = {"value": round(1.0 / t_token, 4), "unit": "tok/s", "cores": _host_cores(),
+                                   "kind": "reference", "blas_threads": cs.blas, "reader_threads": cs.threads,
+                                   "sample": f"2 whole qwen2-7b-shape decode tokens at context {ctx} after 1 "
+                                             f"warm-up ({t_token:.2f} s each): 28 layers x 7 reference "
+                                             "n730_read_layer reads (per-tensor INT4) on a reader pool + numpy "
+                                             "fp32 GEMVs, attention over an fp32 KV cache, final norm + lm_head"}
         print(json.dumps(out), flush=True)
     eng.close()
     if world > 1:
@@ -505,13 +615,13 @@ def run_tp(a):
     world, rank, local = _dist()
     torch.cuda.set_device(local)
     if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device(f"cuda:{local}"))
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=torch.device(f"cuda:{local}"))
     shape = SHAPES["qwen2-72b"]
     if a.layers:
         shape = dataclasses.replace(shape, layers=a.layers)
     tp.check_shape(shape, world, 128)
     B, ctx = a.batch, a.ctx
-    eng = Engine(tp.local_shape(shape, world, rank, 128), max_ctx=ctx + a.warmup + a.steps + 8, max_batch=B,
+    eng = Engine(tp.local_shape(shape, world, rank, 128), max_ctx=ctx + a.warmup + 2 * a.steps + 16, max_batch=B,
                  max_prefill=64, tp_rank=rank, tp_size=world, tp_allreduce=a.tp_allreduce,
                  per_op_decode=a.per_op, ffn_fuse=a.ffn_fuse)
     if world > 1:
@@ -540,15 +650,26 @@ def run_tp(a):
         e1.record(st)
         barrier()
     t = e0.elapsed_time(e1) / 1000.0
+    # e2e: host token ids in, host logits (all-gathered over the ranks) out, through the C ABI
+    host_tok = np.random.default_rng(3).integers(0, shape.vocab, B).astype(np.int32)
+    eng.decode(host_tok)
+    barrier()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record(st)
+    for _ in range(a.steps):
+        eng.decode(host_tok)
+    e3.record(st)
+    barrier()
+    t_e2e = e2.elapsed_time(e3) / 1000.0
     if world > 1:
-        tt = torch.tensor([t], device="cuda", dtype=torch.float64)
+        tt = torch.tensor([t, t_e2e], device="cuda", dtype=torch.float64)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        t = float(tt.item())
+        t, t_e2e = tt.tolist()
     if rank == 0:
         peak, kind = _peaks()
         kv = info["kv_bytes_per_pos"] * (ctx + a.warmup + a.steps // 2) * B
         step_bytes = info["weight_bytes"] - info["embed_bytes"] + kv  # per rank
-        out = {"metric": "decode tok/s, Qwen2-72B-shape INT4 g128, tensor parallel", "value": round(B * a.steps / t, 3),
+        out = {"metric": TP_METRIC, "value": round(B * a.steps / t, 3),
                "unit": "tok/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
                "ms_per_step": round(t / a.steps * 1e3, 4), "higher_is_better": True, "scaling": "strong",
                "vs_baseline": None, "dtype": "int4 weights (exact dequant); fp16 x, f32 accumulate",
@@ -563,7 +684,13 @@ def run_tp(a):
                           "decode_path": ("persistent kernel" + (", phase table in global memory"
                                                                  if info["phase_table_global"] else "")
                                           if info["persistent_decode"] else "per-op kernels (graph)"),
-                          "parallelism": f"tp{world}"},
+                          "parallelism": f"tp{world}",
+                          "scale_point": f"one qwen2-72b-shape model over {world} GPU(s); the N = 1 point is the "
+                                         "same model on one GPU (strong scaling)",
+                          "plan_mismatch": info["tp_plan_mismatch"],
+                          "l2": f"no flush: {step_bytes / 1e9:.2f} GB per rank stream from HBM every step (L2 126 MB)"},
+               "e2e": {"value": round(B * a.steps / t_e2e, 3), "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
+                       "d2h_bytes_per_step": 4 * B * shape.vocab},
                "roofline": {"bound": "hbm", "achieved": round(step_bytes / (t / a.steps) / 1e9, 1), "peak": peak,
                             "unit": "GB/s per GPU", "frac": round(step_bytes / (t / a.steps) / 1e9 / peak, 4),
                             "traffic": None, "kernel": "whole decode step, per-rank bytes", "peak_source": kind},
@@ -657,7 +784,7 @@ def main():
         run_reference(a)
     elif a.workload == "streamed":
         run_streamed(a)
-    elif a.workload == "tp72b":
+    elif _tp_workload(a):
         run_tp(a)
     elif a.workload == "linear":
         run_linear(a)

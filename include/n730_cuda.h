@@ -70,8 +70,8 @@ int n730_attention_forward(void* ctx, const float* d_q, const float* d_k_cache, 
                            int head_dim, int cache_offset);
 /* No counterpart in the reference: n730_attention_forward without a context
  * and without allocating.  The [n_heads, seq_q, seq_total] scores live in a
- * fixed 4 MiB device array (heads * seq_q * seq_total <= 1 Mi floats, else
- * N730_BAD_ARG); first call per device resolves it (make it outside stream
+ * fixed 4 MiB device array (heads * seq_q * seq_total <= 1 Mi floats and
+ * seq_q, heads <= 65535, else N730_BAD_ARG); first call per device resolves it (make it outside stream
  * capture); calls that overlap in time race on it.  Runs on `stream`. */
 int n730_attention_forward_noalloc(const float* d_q, const float* d_k_cache, const float* d_v_cache,
                                    float* d_out, int seq_q, int seq_total, int n_heads, int n_kv_heads,
@@ -200,7 +200,9 @@ int n730_model_forward(void* model, int seq, const int32_t* host_tokens, int n, 
 int n730_model_decode(void* model, const int32_t* host_tokens, int batch, float* host_logits);
 /* Same step with device-resident ids/logits, asynchronous on `stream`. */
 int n730_model_decode_device(void* model, const int32_t* d_tokens, int batch, float* d_logits, void* stream);
-/* info[16]: weight bytes, KV bytes per position, KV capacity bytes, splits, qkv dim, pages/seq, finalized. */
+/* info[16]: weight bytes, KV bytes per position, KV capacity bytes, splits, qkv dim, pages/seq, finalized,
+ * persistent batch-1 decode, untied embedding bytes, streamed bytes per pass, FFN fused, phase table in
+ * global memory, tensor-parallel plan mismatch (every rank fell back to per-op), persistent grid. */
 int n730_model_info(void* model, int64_t* info);
 void* n730_model_stream(void* model);
 /* One resident linear alone (which: 0 q|k|v, 1 o, 2 gate|up + SwiGLU, 3 down, 4 lm_head),

@@ -348,9 +348,20 @@ int attn_decode_launch(const DecodeAttnArgs& a, cudaStream_t st) {
                "attention: n_heads/n_kv must be an integer <= %d", MAX_G);
   N730_REQUIRE(d.head_dim == 64 || d.head_dim == 128, N730_UNSUPPORTED, "attention: head_dim %d", d.head_dim);
   N730_REQUIRE(a.batch >= 1, N730_BAD_ARG, "attention: bad batch");
-  static int cl128 = 0, cl64 = 0;
-  int& cl_max = d.head_dim == 128 ? cl128 : cl64;
-  if (!cl_max) cl_max = d.head_dim == 128 ? decode_cluster_size<128>() : decode_cluster_size<64>();
+  // the kernel attributes and the cluster size are set up once per device
+  static std::mutex mu;
+  static int cl128[N730_MAX_DEVICES] = {}, cl64[N730_MAX_DEVICES] = {};
+  int dev = 0;
+  N730_CUDA(cudaGetDevice(&dev));
+  N730_REQUIRE(dev >= 0 && dev < N730_MAX_DEVICES, N730_BAD_ARG, "attention: device ordinal %d", dev);
+  int cl_max = 0;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    int& slot = d.head_dim == 128 ? cl128[dev] : cl64[dev];
+    if (!slot) slot = d.head_dim == 128 ? decode_cluster_size<128>() : decode_cluster_size<64>();
+    cl_max = slot;
+    if (cl_max < 0) slot = 0;  // set-up failed: try again on the next call
+  }
   if (cl_max < 0) return cl_max;
   // splits per (sequence, KV head): about two CTAs per SM in all, at least 2
   int cl = cl_max;
@@ -583,20 +594,10 @@ int attn_prefill_launch(const PrefillAttnArgs& a, cudaStream_t st) {
   N730_REQUIRE(a.ld_qkv % 4 == 0 && ((uintptr_t)a.qkv & 15) == 0, N730_BAD_ARG, "attention: qkv alignment");
   dim3 grid((a.T + PF_Q - 1) / PF_Q, d.n_heads);
   if (d.head_dim == 128) {
-    static bool cfg = false;
-    if (!cfg) {
-      N730_CUDA(cudaFuncSetAttribute(attn_prefill_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)sizeof(PfSmem<128>)));
-      cfg = true;
-    }
+    if (int rc = smem_attr_once<attn_prefill_kernel<128>>((int)sizeof(PfSmem<128>))) return rc;
     return launch_pdl(attn_prefill_kernel<128>, grid, dim3(128), sizeof(PfSmem<128>), st, a.pdl, a);
   }
-  static bool cfg64 = false;
-  if (!cfg64) {
-    N730_CUDA(cudaFuncSetAttribute(attn_prefill_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)sizeof(PfSmem<64>)));
-    cfg64 = true;
-  }
+  if (int rc = smem_attr_once<attn_prefill_kernel<64>>((int)sizeof(PfSmem<64>))) return rc;
   return launch_pdl(attn_prefill_kernel<64>, grid, dim3(128), sizeof(PfSmem<64>), st, a.pdl, a);
 }
 

@@ -4,6 +4,7 @@
 #include <cuda_fp16.h>
 #include <cstdint>
 #include <cstdio>
+#include <mutex>
 
 #define N730_API extern "C" __attribute__((visibility("default")))
 
@@ -73,6 +74,26 @@ static inline int num_sms() {
     if (n <= 0) n = 148;
   }
   return n;
+}
+
+// Set kernel Kern's dynamic shared-memory limit to `bytes` once per device.
+// The attribute belongs to the device that is current when it is set, so a
+// process driving several GPUs sets it on each of them before its first launch
+// there.  Thread-safe.
+constexpr int N730_MAX_DEVICES = 128;
+template <auto Kern>
+int smem_attr_once(int bytes) {
+  static std::mutex mu;
+  static bool done[N730_MAX_DEVICES] = {};
+  int dev = 0;
+  N730_CUDA(cudaGetDevice(&dev));
+  N730_REQUIRE(dev >= 0 && dev < N730_MAX_DEVICES, N730_BAD_ARG, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lk(mu);
+  if (!done[dev]) {
+    N730_CUDA(cudaFuncSetAttribute(Kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    done[dev] = true;
+  }
+  return N730_OK;
 }
 
 // ---------------------------------------------------------------------------

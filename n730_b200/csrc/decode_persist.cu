@@ -129,8 +129,10 @@ __device__ bool pd_barrier(const PdArgs& a, int k, int* flag) {
 // completes at tp_size * grid * (e * n_xbar + k) (32-bit wrapping compare), so
 // a rank that starts the next launch early cannot disturb a slow one.  Waits
 // end after PD_XWAIT_NS (a peer whose launch never comes) with the abort flag
-// and the device error word raised.
-constexpr uint64_t PD_XWAIT_NS = 20000000000ull;
+// and the device error word raised.  The limit covers the skew between the
+// ranks' launches (host work between steps, graph instantiation: milliseconds)
+// plus a whole step (72B at one rank: ~11 ms), with a wide margin.
+constexpr uint64_t PD_XWAIT_NS = 2000000000ull;
 __device__ __forceinline__ int ld_relaxed_sys(const int* p) {
   int v;
   asm volatile("ld.relaxed.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -959,11 +961,7 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
 template <int KPG, int HD, bool EXT>
 static int persist_setup(const PdPlan& plan, bool launch, cudaStream_t st, int* max_blocks) {
   auto kern = persist_decode_kernel<KPG, HD, EXT>;
-  static bool configured = false;
-  if (!configured) {
-    N730_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
-    configured = true;
-  }
+  if (int rc = smem_attr_once<persist_decode_kernel<KPG, HD, EXT>>(227 * 1024)) return rc;
   if (max_blocks) N730_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(max_blocks, kern, PD_THREADS, plan.smem));
   if (!launch) return N730_OK;
   cudaLaunchConfig_t cfg = {};

@@ -9,13 +9,14 @@
 // 128-token x 64-column blocks already in the K-major, 128-byte-swizzled
 // layout the UMMA shared-memory descriptors read (8-row x 128-byte atoms,
 // 16-byte chunk c of row r at c ^ (r % 8)).  One CTA computes a 128-token x
-// 128-row output tile over K in steps of 64 through a 4-stage pipeline:
-//  * one thread keeps three steps of bulk copies in flight: the packed A tile
-//    and, per 16-row tile of W, the step's 512-byte code quad and the group's
-//    scale/zero block;
-//  * all 8 warps dequantise a landed step's codes ((q - z) * s in fp32 -> fp16)
-//    into the swizzled B tile;
-//  * the same thread issues four tcgen05.mma.kind::f16 (M 128, N 128, K 16,
+// 128-row output tile over K in steps of 128 (one group) through a 3-stage
+// pipeline of specialised warps, with no CTA-wide barrier inside the K loop:
+//  * a producer warp issues, once a stage's previous MMAs have completed, one
+//    bulk copy of the packed A tile and one bulk copy per 16-row tile of W
+//    (the step's whole group blocks: codes and fp16 scale/zero);
+//  * 8 dequant warps turn their row tile's codes into (q - z) * s fp16 values
+//    in the swizzled B tile and arrive on the stage's conversion barrier;
+//  * an MMA warp issues eight tcgen05.mma.kind::f16 (M 128, N 128, K 16,
 //    fp32 accumulate in tensor memory) and a tcgen05.commit to the stage's
 //    empty barrier, which gates that stage's next copies;
 //  * after the last step the accumulator is read back with tcgen05.ld
@@ -376,12 +377,7 @@ constexpr size_t TC_SMEM = 1024 + (size_t)TC_STAGES * TC_STAGE + (3 * TC_STAGES 
 
 // One-time kernel attribute set-up (call before any stream capture).
 int gemm_tc_prepare() {
-  static bool configured = false;
-  if (!configured) {
-    N730_CUDA(cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM));
-    configured = true;
-  }
-  return N730_OK;
+  return smem_attr_once<gemm_tc_kernel>((int)TC_SMEM);
 }
 
 bool gemm_tc_supported(const QWeight& w, int T) {

@@ -420,11 +420,7 @@ static int* device_err_word() {
 template <int BITS, int SZM, int NB, int R>
 static int launch_t(const GemvParams& p, int grid, size_t smem, cudaStream_t st, bool pdl) {
   auto fn = gemv_kernel<BITS, SZM, NB, R>;
-  static bool configured = false;
-  if (!configured) {
-    N730_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
-    configured = true;
-  }
+  if (int rc = smem_attr_once<gemv_kernel<BITS, SZM, NB, R>>(227 * 1024)) return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(GEMV_THREADS);

@@ -385,12 +385,7 @@ int* gemv_err_word();
 template <int KPG, int NT, int WARPS>
 static int launch_mma2(const MmaParams& p, int grid, size_t smem, cudaStream_t st, bool pdl) {
   const dim3 g3(grid, p.kb_n);
-  static bool configured = false;
-  if (!configured) {
-    N730_CUDA(cudaFuncSetAttribute(gemv_mma2_kernel<KPG, NT, WARPS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   227 * 1024));
-    configured = true;
-  }
+  if (int rc = smem_attr_once<gemv_mma2_kernel<KPG, NT, WARPS>>(227 * 1024)) return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = g3;
   cfg.blockDim = dim3(WARPS * 32);

@@ -395,8 +395,8 @@ N730_API int n730_attention_forward(void* ctx, const float* d_q, const float* d_
 // not fit (64 heads x 8192^2 positions is 17 GB of scores), and cudaMalloc /
 // cudaFree per call would synchronise the device under work on other streams.
 //  * Limit: heads * seq_q * seq_total <= N730_ATTN_SCRATCH_FLOATS (1 Mi floats,
-//    4 MiB; e.g. decode of 64 heads over 16384 positions); larger requests
-//    return N730_BAD_ARG before any GPU work.
+//    4 MiB; e.g. decode of 64 heads over 16384 positions), and seq_q, heads
+//    <= 65535; larger requests return N730_BAD_ARG before any GPU work.
 //  * The scratch address is resolved with cudaGetSymbolAddress once per device,
 //    on that device's first call; make that first call outside stream capture.
 //  * Nothing in the scratch must start at zero: scores_kernel writes every
@@ -432,6 +432,9 @@ N730_API int n730_attention_forward_noalloc(const float* d_q, const float* d_k_c
   N730_REQUIRE((int64_t)n_heads * seq_q * seq_total <= N730_ATTN_SCRATCH_FLOATS, N730_BAD_ARG,
                "attention_noalloc: %d heads x %d x %d scores exceed the %lld-float scratch", n_heads, seq_q,
                seq_total, (long long)N730_ATTN_SCRATCH_FLOATS);
+  // seq_q and n_heads index grid.y / grid.z of the score and P V launches (at most 65535 each)
+  N730_REQUIRE(seq_q <= 65535 && n_heads <= 65535, N730_BAD_ARG,
+               "attention_noalloc: seq_q %d / heads %d exceed the 65535 launch-grid limit", seq_q, n_heads);
   int dev = 0;
   N730_CUDA(cudaGetDevice(&dev));
   N730_REQUIRE(dev >= 0 && dev < 128, N730_BAD_ARG, "attention_noalloc: device %d", dev);

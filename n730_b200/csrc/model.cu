@@ -101,6 +101,7 @@ struct Model {
   int device = 0;
   // persistent batch-1 decode (decode_persist.cu)
   bool pd_ok = false;
+  bool plan_mismatch = false;    // tensor parallel: the ranks' persistent plans differed (per-op path)
   bool pd_ffn_fused = false;     // the persistent step runs each FFN as one phase
   std::map<const QWeight*, uint8_t*> pd_tiles;  // INT8 / FP16 weights as persistent-kernel tiles
   PdPlan pd;
@@ -132,6 +133,7 @@ struct Model {
   std::vector<void*> ar_peer_base;
   ArArgs ar{};
   bool ar_ok = false;
+  bool ar_off = false;           // a peer-memory exchange timed out: NCCL for the rest of the model's life
 
   template <typename T>
   int alloc(T** p, size_t n) {
@@ -459,6 +461,38 @@ static int plan_persistent(Model* m) {
   return N730_OK;
 }
 
+// Tensor parallel: every rank must take the same batch-1 decode path.  The
+// persistent kernel's cross-GPU barriers count tp_size x grid arrivals per
+// barrier and its exchanges follow the phase table, so ranks that planned
+// differently (another SM count, a persistent plan on one rank only, another
+// number of phases) would pass barriers early or wait on a peer that runs the
+// per-op kernels.  The ranks all-gather (persistent, grid, cross barriers,
+// phases); unless all agree, every rank drops to the per-op path (NCCL), the
+// same decision on every rank.
+static int agree_decode_path(Model* m) {
+  const N730ModelConfig& c = m->c;
+  N730_REQUIRE(m->comm, N730_STATE, "model: tensor parallel finalize before tp_init");
+  const int sig[4] = {m->pd_ok ? 1 : 0, m->pd_ok ? m->pd.grid : 0, m->pd_ok ? m->pd.a.n_xbar : 0,
+                      m->pd_ok ? m->pd.a.n_phases : 0};
+  int* d = nullptr;
+  if (int rc = m->alloc(&d, (size_t)4 * (c.tp_size + 1))) return rc;
+  N730_CUDA(cudaMemcpyAsync(d, sig, sizeof sig, cudaMemcpyHostToDevice, m->st));
+  if (ncclAllGather(d, d + 4, 4, ncclInt32, m->comm, m->st) != ncclSuccess) {
+    set_error("model: ncclAllGather of the decode plans failed");
+    return N730_COMM;
+  }
+  std::vector<int> all((size_t)4 * c.tp_size);
+  N730_CUDA(cudaMemcpyAsync(all.data(), d + 4, all.size() * 4, cudaMemcpyDeviceToHost, m->st));
+  N730_CUDA(cudaStreamSynchronize(m->st));
+  for (int r = 1; r < c.tp_size; ++r)
+    if (memcmp(&all[4 * r], &all[0], 16) != 0) {
+      m->pd_ok = false;
+      m->plan_mismatch = true;
+      break;
+    }
+  return N730_OK;
+}
+
 static int finalize(Model* m) {
   const N730ModelConfig& c = m->c;
   if (int rc = gemv_prepare()) return rc;
@@ -626,6 +660,8 @@ static int finalize(Model* m) {
   N730_CUDA(cudaMallocHost(&m->h_logits, (size_t)B * c.vocab * 4));
   if (c.per_op_decode <= 0)
     if (int rc = plan_persistent(m)) return rc;
+  if (c.tp_size > 1)
+    if (int rc = agree_decode_path(m)) return rc;
   N730_CUDA(cudaStreamSynchronize(m->st));
   m->finalized = true;
   return N730_OK;
@@ -667,7 +703,7 @@ static int rowsplit_linear(Model* m, const QWeight* w, const float* a, int lda, 
   if (m->c.tp_size <= 1) return gemv(m, w, a, lda, B, x, ldx, bias, x, ldx, nullptr, 0);
   const int h = m->c.hidden;
   if (int rc = gemv(m, w, a, lda, B, m->delta, h, bias, nullptr, 0, nullptr, 0)) return rc;
-  if (m->ar_ok && m->c.tp_allreduce == 0 && (int64_t)B * h <= m->ar.cap && ldx == h) {  // one-shot, peer memory
+  if (m->ar_ok && !m->ar_off && m->c.tp_allreduce == 0 && (int64_t)B * h <= m->ar.cap && ldx == h) {  // one-shot
     ArArgs ar = m->ar;
     ar.part = m->delta;
     ar.x = x;
@@ -1014,6 +1050,25 @@ N730_API int n730_model_seq_len(void* p, int seq) {
   return m->h_seq[seq];
 }
 
+// Status of the work enqueued so far (call after a synchronisation).  A
+// bounded device wait that ran out during a tensor-parallel step leaves the
+// ranks' exchange counters (persistent kernel) or epochs (one-shot allreduce)
+// out of step, so every later exchange over peer memory would wait for
+// arrivals that never match.  After such a timeout the model stops using
+// both for good: the persistent kernel and the one-shot allreduce are switched
+// off and the captured step graphs dropped; later steps run the per-op kernels
+// with NCCL.  The caller still gets N730_TIMEOUT for the failed step.
+static int step_status(Model* m) {
+  const int rc = gemv_check_error(true);
+  if (rc == N730_TIMEOUT && m->c.tp_size > 1 && (m->pd_ok || (m->ar_ok && !m->ar_off))) {
+    m->pd_ok = false;
+    m->ar_off = true;
+    for (auto& g : m->graphs) cudaGraphExecDestroy(g.second);
+    m->graphs.clear();
+  }
+  return rc;
+}
+
 // Decode one token for each of sequences [0, batch): host token ids in,
 // host logits [batch][vocab] out (pinned staging, copies inside the call).
 N730_API int n730_model_decode(void* p, const int32_t* host_tokens, int batch, float* host_logits) {
@@ -1034,7 +1089,7 @@ N730_API int n730_model_decode(void* p, const int32_t* host_tokens, int batch, f
   N730_CUDA(cudaStreamSynchronize(m->st));
   if (host_logits) memcpy(host_logits, m->h_logits, (size_t)batch * m->c.vocab * 4);
   for (int b = 0; b < batch; ++b) m->h_seq[b] += 1;
-  return gemv_check_error(true);
+  return step_status(m);
 }
 
 // Device-resident decode step (no host copies, no synchronisation): d_tokens
@@ -1099,12 +1154,13 @@ N730_API int n730_model_forward(void* p, int seq, const int32_t* host_tokens, in
   if (host_logits) N730_CUDA(cudaMemcpyAsync(m->h_logits, m->logits, (size_t)m->c.vocab * 4, cudaMemcpyDeviceToHost, m->st));
   N730_CUDA(cudaStreamSynchronize(m->st));
   if (host_logits) memcpy(host_logits, m->h_logits, (size_t)m->c.vocab * 4);
-  return gemv_check_error(true);
+  return step_status(m);
 }
 
 // info[16]: weight bytes, kv bytes per position, kv capacity bytes, n_split,
 // qkv_dim, max_pages, finalized, persistent batch-1 decode, untied embedding bytes,
-// streamed layer bytes per pass, FFN fused, phase table in global memory
+// streamed layer bytes per pass, FFN fused, phase table in global memory,
+// tensor-parallel plan mismatch, persistent grid
 N730_API int n730_model_info(void* p, int64_t* info) {
   MODEL(p);
   if (!info) return N730_NULL;
@@ -1129,6 +1185,8 @@ N730_API int n730_model_info(void* p, int64_t* info) {
   info[9] = m->streamed_bytes;                                // host->HBM bytes per forward pass
   info[10] = m->pd_ffn_fused;
   info[11] = m->pd_ok && m->pd.a.tab_off < 0;  // persistent kernel reads its phase table from global memory
+  info[12] = m->plan_mismatch;                 // tensor parallel: plans differed, every rank runs per-op
+  info[13] = m->pd_ok ? m->pd.grid : 0;        // CTAs of the persistent launch
   return N730_OK;
 }
 

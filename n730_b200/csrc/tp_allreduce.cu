@@ -1,7 +1,8 @@
 // One-shot allreduce over NVLink peer memory for tensor-parallel decode.
 //
-// The reference sums row-split partials with NCCL (SURVEY target: one
-// exchange per row-split layer, n730's TP plan).  For decode-sized messages
+// The reference runs on one GPU and has no tensor parallelism.  Here the
+// row-split projections (o_proj, down_proj) of a tensor-parallel decoder end
+// with one sum of every rank's partial output.  For decode-sized messages
 // (batch x hidden fp32, 32 KB at batch 1 for the 72B shape) an NCCL allreduce
 // is latency-bound; here one kernel does the exchange and the residual add:
 //

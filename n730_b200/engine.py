@@ -191,7 +191,17 @@ class Engine:
         return {"weight_bytes": a[0], "kv_bytes_per_pos": a[1], "kv_capacity_bytes": a[2], "n_split": a[3],
                 "qkv_dim": a[4], "pages_per_seq": a[5], "persistent_decode": bool(a[7]),
                 "embed_bytes": a[8], "streamed_bytes": a[9], "ffn_fused": bool(a[10]),
-                "phase_table_global": bool(a[11])}
+                "phase_table_global": bool(a[11]), "tp_plan_mismatch": bool(a[12]), "persistent_grid": a[13]}
+
+    def tp_signature(self) -> tuple:
+        """Configuration fields every tensor-parallel rank must share (its FFN share may differ:
+        whole quantisation groups split unevenly, and tp_rank differs by definition)."""
+        c = self.cfg
+        return tuple(getattr(c, f) for f in ("hidden", "layers", "heads", "kv_heads", "head_dim", "vocab",
+                                              "max_ctx", "max_batch", "page_size", "max_prefill",
+                                              "tie_embeddings", "tp_size", "use_graphs", "use_pdl",
+                                              "exact_gemv", "per_op_decode", "ffn_fuse", "tp_allreduce")) + \
+            (round(float(c.rms_eps), 12), float(c.rope_theta))
 
     @staticmethod
     def tp_unique_id() -> bytes:

@@ -8,9 +8,10 @@ reads + dequantises layers (per-tensor and group-wise blocks) into a bounded
 queue while the caller consumes them.
 
 The GPU side of layer streaming - weights held in pinned host memory and
-copied into HBM slots ahead of the layer that needs them - is
-``DeviceLayerStreamer`` below, driving the C++ streamer of the whole-model
-engine (``n730_model_*``; see ``n730_b200.engine.Engine(streamed=...)``).
+copied into HBM slots ahead of the layer that needs them - lives in the C++
+whole-model engine: ``n730_b200.engine.Engine(stream_depth=d)`` keeps every
+layer's device image in pinned host memory and copies layer ``l + d`` into a
+free HBM slot on a copy stream while layer ``l`` computes.
 """
 from __future__ import annotations
 

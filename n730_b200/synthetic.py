@@ -96,13 +96,19 @@ def write_n730(path, shape: ModelShape, pmap: str, seed: int = 0, biases: bool =
 
 
 def build_on_device(shape: ModelShape, pmap: str, engine: Engine, seed: int = 0, std: float = 0.02,
-                    biases: bool = True, tp_rank: int = 0, tp_size: int = 1):
+                    biases: bool = True, tp_rank: int = 0, tp_size: int = 1, export=None):
     """Draw every tensor on the GPU and quantise it there; hand the packed weights
     to ``engine``.  Group-wise precisions use the library's GPU quantiser;
     per-tensor INT8 and FP16 (small tensors in the mixed map) are packed on
     the host by the converter's quantisers.  With ``tp_size > 1`` every rank
     draws the same full tensors and keeps its tensor-parallel shard
-    (``n730_b200.tp.shard``); ``shape`` is the global shape."""
+    (``n730_b200.tp.shard``); ``shape`` is the global shape.
+
+    ``export(name, item)``, when given, receives a host copy of what the engine
+    was handed for each tensor: ``{"kind": "grouped", "bits", "group", "rows",
+    "cols", "codes", "s16", "z16"}`` (numpy), ``{"kind": "block", "block":
+    RawBlock}`` for per-tensor formats, or ``{"kind": "vector", "v": fp32}`` for
+    biases - so a checker can dequantise exactly the codes the engine runs."""
     from . import tp as tpmod
     import ctypes as C
 
@@ -128,7 +134,10 @@ def build_on_device(shape: ModelShape, pmap: str, engine: Engine, seed: int = 0,
         if len(shp) == 1:
             layer = int(name.split(".")[2])
             base = name.split(".", 3)[3].rsplit(".", 1)[0]
-            engine.set_vector(layer, BIAS_SLOTS[base], w.cpu().numpy())
+            v = w.cpu().numpy()
+            engine.set_vector(layer, BIAS_SLOTS[base], v)
+            if export:
+                export(name, {"kind": "vector", "v": v})
             continue
         prec, group = parse_precision(f(name), {}, shp[1])
         if prec in ("INT2G", "INT4G", "INT8G"):
@@ -143,13 +152,20 @@ def build_on_device(shape: ModelShape, pmap: str, engine: Engine, seed: int = 0,
             qw = qweight_from_device(0x40 | bits, rows, cols, group, codes.data_ptr(), s16.data_ptr(),
                                      z16.data_ptr(), stream=stream)
             torch.cuda.current_stream().synchronize()
+            if export:
+                export(name, {"kind": "grouped", "bits": bits, "group": group, "rows": rows, "cols": cols,
+                              "codes": codes.cpu().numpy().reshape(rows, -1), "s16": s16.cpu().numpy(),
+                              "z16": z16.cpu().numpy()})
             del codes, s16, z16
         else:
             block, _ = serialize_layer(0, prec, w.cpu().numpy(), name)
             import io
             import struct
             _, _, pid, r, c, sc, zp, dsz = struct.unpack(">4sIBIIffi", block[:29])
-            qw = qweight_from_block(RawBlock(0, pid, r, c, sc, zp, block[29:29 + dsz], 0))
+            rb = RawBlock(0, pid, r, c, sc, zp, block[29:29 + dsz], 0)
+            qw = qweight_from_block(rb)
+            if export:
+                export(name, {"kind": "block", "block": rb})
         del w
         if name == "model.embed_tokens.weight":
             engine.set_qweight(-1, W_EMBED, qw)

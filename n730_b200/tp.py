@@ -123,8 +123,23 @@ def init_engine_comm(engine, rank: int, size: int, group=None, map_peers: bool =
     communicator; with ``map_peers`` (ranks on one node) also exchange the exchange-region
     handles and map every rank's region: the persistent batch-1 decode kernel pushes its
     row-split sums there, and with tp_allreduce=0 so does the one-shot allreduce.  Without it
-    every step uses the per-op kernels and NCCL."""
+    every step uses the per-op kernels and NCCL.
+
+    First every rank's (rank, size, engine configuration) is all-gathered over the process
+    group: NCCL's communicator set-up has no timeout, so a rank that never arrives (or joins
+    with another tensor-parallel configuration) is caught here, where the process group's
+    timeout ends the wait with an error (RuntimeError), before any rank enters NCCL.
+    Configurations that differ raise ValueError on every rank."""
     import torch.distributed as dist
+    sig = (rank, size, engine.tp_signature())
+    sigs = [None] * size
+    dist.all_gather_object(sigs, sig, group=group)
+    if [s[0] for s in sigs] != list(range(size)) or any(s[1] != size for s in sigs):
+        raise ValueError(f"tensor-parallel ranks disagree on rank numbering / size: {[s[:2] for s in sigs]}")
+    bad = [s[0] for s in sigs if s[2] != sigs[0][2]]
+    if bad:
+        raise ValueError(f"tensor-parallel ranks {bad} were configured differently from rank 0: "
+                         f"{sigs[bad[0]][2]} vs {sigs[0][2]}")
     ids = [engine.tp_unique_id() if rank == 0 else None]
     dist.broadcast_object_list(ids, src=0, group=group)
     engine.tp_init(ids[0], rank, size)

@@ -2,7 +2,8 @@
 
 Run in a container that has the reference tree (read-only) at REF_ROOT:
 
-    python tests/golden/make_golden.py [--ref-root /root/reference]
+    make -C oracle REF_ROOT=<reference root>
+    python tests/golden/make_golden.py --ref-root <reference root>
 
 It imports the reference ``src-code/converter.py`` and calls its own
 ``convert()``/``read_layer()`` and quantisers, and loads the reference C core
@@ -57,7 +58,7 @@ def _small_tensors():
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref-root", default="/root/reference")
+    ap.add_argument("--ref-root", required=True, help="root of the reference checkout (holds src-code/)")
     args = ap.parse_args()
     ref = Path(args.ref_root)
     sys.path.insert(0, str(ref / "src-code"))

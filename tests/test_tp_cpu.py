@@ -136,8 +136,11 @@ def test_tp2_rank_order_push_sums():
 class _FakeEngine:
     """Stands in for Engine in the communicator handshake (no GPU): records the calls."""
 
-    def __init__(self, rank):
-        self.rank, self.calls = rank, []
+    def __init__(self, rank, sig=(896, 2, 7, 1, 64, 1000)):
+        self.rank, self.calls, self.sig = rank, [], sig
+
+    def tp_signature(self):
+        return self.sig
 
     def tp_unique_id(self):
         return b"id-of-rank-0".ljust(128, b"\0")
@@ -262,3 +265,71 @@ def test_shard_block_matches_sliced_dequant(name, rows, cols):
         r0, r1, c0, c1 = tp.shard_ranges(name, r, c, shape, 2, rank, FFN_GROUP)
         part = oq.dequant_grouped(sb.codes, sb.scales16, sb.zeros16, 4, sb.rows, sb.cols)
         assert np.array_equal(part, full[r0:r1, c0:c1])
+
+
+def _missing_rank_worker(rank, size, port, out):
+    from datetime import timedelta
+    import time
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=size,
+                            timeout=timedelta(seconds=3))
+    if rank == 1:  # joins the process group but never the engine communicator
+        time.sleep(12)
+        out.put((1, None, 0.0))
+        return
+    t0 = time.monotonic()
+    e = _FakeEngine(rank)
+    try:
+        tp.init_engine_comm(e, rank, size)
+        out.put((0, "returned", time.monotonic() - t0))
+    except Exception as ex:  # the process group's timeout ends the handshake
+        out.put((0, type(ex).__name__, time.monotonic() - t0, e.calls))
+
+
+def test_engine_comm_rank_never_joins():
+    """A rank that never calls init_engine_comm: the other rank's handshake ends with an error
+    at the process group's timeout (3 s here), before it enters NCCL's set-up (which has no
+    timeout of its own): no tp_init call was made."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_missing_rank_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(2):
+        r = q.get(timeout=60)
+        res[r[0]] = r
+    for p in procs:
+        p.join(timeout=60)
+    kind, elapsed, calls = res[0][1], res[0][2], res[0][3]
+    assert kind != "returned" and elapsed < 11.0, res[0]
+    assert calls == []
+
+
+def _mismatch_worker(rank, size, port, out):
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=size)
+    try:
+        e = _FakeEngine(rank, sig=(896, 2, 7, 1, 64, 1000 + rank))  # rank 1 built another vocabulary
+        try:
+            tp.init_engine_comm(e, rank, size)
+            out.put((rank, "returned", e.calls))
+        except ValueError as ex:
+            out.put((rank, str(ex), e.calls))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_engine_comm_config_mismatch():
+    """Ranks configured differently: every rank raises ValueError before any NCCL set-up."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_mismatch_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    got = dict((r, (msg, calls)) for r, msg, calls in (q.get(timeout=5) for _ in range(2)))
+    for rank in range(2):
+        msg, calls = got[rank]
+        assert "configured differently" in msg and calls == []

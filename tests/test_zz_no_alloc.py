@@ -84,3 +84,6 @@ def test_noalloc_rejects_oversize_and_null():
     assert lib.n730_attention_forward_noalloc(one, one, one, one, 1, total, heads, 8, 128, total - 1, None) == -13
     assert lib.n730_attention_forward_noalloc(None, one, one, one, 1, 10, 8, 2, 64, 9, None) == -12
     assert lib.n730_attention_forward_noalloc(one, one, one, one, 1, 10, 8, 3, 64, 9, None) == -13
+    # within the scratch but beyond the launch-grid limit of 65535 queries / heads
+    assert lib.n730_attention_forward_noalloc(one, one, one, one, 65536, 1, 1, 1, 64, 0, None) == -13
+    assert lib.n730_attention_forward_noalloc(one, one, one, one, 1, 1, 65536, 1, 64, 0, None) == -13
