@@ -90,12 +90,16 @@ def _args():
     ap.add_argument("--pmap", default="int4_g128", choices=["int4_g128", "mixed_05b"],
                     help="resident workload: precision map (mixed_05b: INT8 attention, INT4 g128 FFN, fp16 tied "
                          "embedding/lm_head)")
-    ap.add_argument("--workload", default="auto", choices=["auto", "resident", "streamed", "tp72b", "linear"],
+    ap.add_argument("--pf-sweep", default="0,2,4,6,8",
+                    help="phases workload: L2 prefetch distances (chunks per warp) to time the kernel at")
+    ap.add_argument("--workload", default="auto",
+                    choices=["auto", "resident", "streamed", "tp72b", "linear", "phases"],
                     help="auto: tp72b when launched by torchrun (any N), else resident (the 7B headline); "
                          "resident: the model resident in HBM (N ranks: independent replicas); "
                          "streamed: 7B aggressive mixed quant (FFN INT2 g64, attention INT4 g128, lm_head INT8 "
                          "per channel), layer weights in pinned host memory, 2-layer prefetch, 1024-token prompt; "
-                         "tp72b: Qwen2-72B shape INT4 g128 split over the N ranks (tensor parallel, strong scaling)")
+                         "tp72b: Qwen2-72B shape INT4 g128 split over the N ranks (tensor parallel, strong scaling); "
+                         "phases: per-phase timing of the persistent decode kernel and an L2 prefetch sweep")
     return ap.parse_args()
 
 
@@ -778,12 +782,94 @@ def run_linear(a):
         lib.n730_qweight_destroy(q)
 
 
+def run_phases(a):
+    """Per-phase timing of the persistent decode kernel (7B headline model, batch 1, context
+    --ctx): --steps traced launches (n730_model_trace_step), each phase's wall time (from the last
+    CTA leaving the barrier that starts it to the last CTA leaving the next one), the barrier's
+    arrival spread (slowest minus fastest CTA) and release latency (last arrival to first
+    departure), and the phase's algorithmic bytes per wall time; then the same kernel timed with
+    CUDA events at each L2 prefetch distance of --pf-sweep.  Prints one JSON line."""
+    import torch
+    torch.cuda.set_device(0)
+    from n730_b200.engine import Engine
+    from n730_b200.synthetic import SHAPES, build_on_device
+    shape = SHAPES[a.model]
+    if a.layers:
+        shape = dataclasses.replace(shape, layers=a.layers)
+    eng = Engine(shape, max_ctx=a.ctx + 64, max_batch=1, max_prefill=512, ffn_fuse=a.ffn_fuse)
+    build_on_device(shape, a.pmap, eng)
+    eng.finalize()
+    info = eng.info()
+    assert info["persistent_decode"], "the model does not decode through the persistent kernel"
+    eng.set_seq_len(0, a.ctx)
+    st = torch.cuda.ExternalStream(eng.stream)
+    h, qd, kvd, f = shape.hidden, shape.heads * shape.head_dim, shape.kv_heads * shape.head_dim, shape.ffn
+    wb = lambda rows, cols: rows * cols // 2 + rows * (cols // 128) * 4  # INT4 g128 codes + fp16 scale/zero
+    kv_layer = info["kv_bytes_per_pos"] // shape.layers * (a.ctx + 1)
+    runs = []
+    for _ in range(max(1, a.steps)):
+        times, kinds = eng.trace_step(eng.stream)
+        runs.append(times.astype(np.int64))
+    T = np.median(np.stack(runs), axis=0)  # [2 n + 1][grid]
+    n = len(kinds)
+    dep = T[1::2][:n].max(axis=1)          # last CTA out of the barrier starting phase p
+    end = np.append(dep[1:], T[2 * n].max())
+    rows = []
+    gemv_i = 0
+    for p in range(n):
+        arr = T[2 * p]
+        k = int(kinds[p])
+        if k == 1:
+            name, nbytes = "attention", kv_layer
+        elif k == 2:
+            name, nbytes = "ffn (gate|up + down)", wb(2 * f, h) + wb(h, f)
+        else:
+            if p == n - 1:
+                name, nbytes = "lm_head", wb(shape.vocab, h)
+            else:
+                name, nbytes = ("qkv", wb(qd + 2 * kvd, h)) if gemv_i % 2 == 0 else ("o_proj", wb(h, qd))
+                gemv_i += 1
+        wall = (end[p] - dep[p]) / 1e3
+        rows.append({"phase": name, "wall_us": wall, "gbs": nbytes / max(wall, 1e-9) / 1e3,
+                     "spread_us": (arr.max() - arr.min()) / 1e3 if p else 0.0,
+                     "release_us": (T[2 * p + 1].min() - arr.max()) / 1e3 if p else 0.0})
+    summary = {}
+    for r in rows:
+        d = summary.setdefault(r["phase"], {"n": 0, "wall_us": 0.0, "gbs": 0.0, "spread_us": 0.0, "release_us": 0.0})
+        d["n"] += 1
+        for key in ("wall_us", "gbs", "spread_us", "release_us"):
+            d[key] += r[key]
+    for d in summary.values():
+        for key in ("wall_us", "gbs", "spread_us", "release_us"):
+            d[key] = round(d[key] / d["n"], 3)
+    total_us = (T[2 * n].max() - T[0].min()) / 1e3
+    sweep = {}
+    for pf in [int(x) for x in a.pf_sweep.split(",") if x != ""]:
+        eng.set_prefetch(pf)
+        for _ in range(3):
+            eng.run_step_kernel(eng.stream)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(20):
+            eng.run_step_kernel(eng.stream)
+        e1.record(st)
+        torch.cuda.synchronize()
+        sweep[pf] = round(e0.elapsed_time(e1) / 20, 4)
+    out = {"workload": f"{a.model}-shape ({shape.layers} layers, {a.pmap}) persistent decode at context {a.ctx}",
+           "traced_launches": len(runs), "launch_us": round(total_us, 1), "phases_per_layer": summary,
+           "prefetch_sweep_ms_per_launch": sweep, "ffn_fused": info["ffn_fused"], "grid": info["persistent_grid"]}
+    print(json.dumps(out), flush=True)
+    eng.close()
+
+
 def main():
     a = _args()
     if a.impl == "reference":
         run_reference(a)
     elif a.workload == "streamed":
         run_streamed(a)
+    elif a.workload == "phases":
+        run_phases(a)
     elif _tp_workload(a):
         run_tp(a)
     elif a.workload == "linear":

@@ -112,9 +112,10 @@ __device__ __forceinline__ bool pd_wait_count(const PdArgs& a, const int* cnt, i
 
 // Grid barrier number k (all CTAs call it in the same order).  False when the
 // launch is being aborted.
-__device__ bool pd_barrier(const PdArgs& a, int k, int* flag) {
+__device__ bool pd_barrier(const PdArgs& a, int k, int* flag, unsigned long long* t_arrive) {
   __syncthreads();
   if (threadIdx.x == PD_SYNC_T) {
+    if (t_arrive) *t_arrive = gtimer();
     asm volatile("red.release.gpu.global.add.s32 [%0], 1;" :: "l"(&a.sync[0]) : "memory");
     *flag = pd_wait_count(a, &a.sync[0], (int)gridDim.x * k);
   }
@@ -138,9 +139,10 @@ __device__ __forceinline__ int ld_relaxed_sys(const int* p) {
   asm volatile("ld.relaxed.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ bool pd_xbarrier(const PdArgs& a, int xep, int k, int* flag) {
+__device__ bool pd_xbarrier(const PdArgs& a, int xep, int k, int* flag, unsigned long long* t_arrive) {
   __syncthreads();
   if (threadIdx.x == PD_SYNC_T) {
+    if (t_arrive) *t_arrive = gtimer();
     // one system-scope fence orders this CTA's pushes (ordered before it by the CTA barrier)
     // before all of its arrivals, which are then relaxed
     asm volatile("fence.acq_rel.sys;" ::: "memory");
@@ -287,6 +289,7 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
     if (warp == 0) mbar_init(kvbar, 1);
     fence_mbar_init();
   }
+  if (a.trace && tid == PD_SYNC_T) a.trace[cta] = gtimer();  // launch start (phase 0 has no barrier)
   __syncthreads();
 
   // ---- KV page copies (PD_KV_T): page p of this CTA's KV head, layer of phase ph ----
@@ -312,6 +315,7 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
   // phase's down_proj units, whole row tiles [u, end) of the warp, each the
   // CTA's nj groups from j0 (one bulk copy per tile).
   struct Cursor { int ph, sub, u, end, gi, G, j0, nj, gb, gpc; const uint8_t* blob; };
+  static_assert(sizeof(Cursor) <= PD_CURSOR_BYTES, "prefetch cursors are stored in PD_CURSOR_BYTES slots");
   // bytes and units per ring chunk of a phase's tiles (INT8 / FP16 tiles: EXT only)
   auto unit_bytes = [&](const PdPhase& P) {
     return !EXT || P.prec == 4 || P.prec == 0 ? GB : P.prec == 8 ? PD_UNIT8 : PD_UNIT16;
@@ -345,35 +349,60 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
   };
   int issued = 0, consumed = 0;
   Cursor prod{0, 0, 0, 0, 0, 1, 0, 0, GB, GPC, nullptr};
+  // The next chunk of cursor c: r_n copies of r_bytes at r_base + i * r_stride; advances c.
+  struct ChunkRef { const uint8_t* base; int64_t stride; int n; uint32_t bytes; };
+  auto next_chunk = [&](Cursor& c, ChunkRef& r) -> bool {
+    if (c.ph >= a.n_phases) return false;
+    if (c.sub == 1) {  // whole down tiles, nj groups each
+      const int n = min(max(1, GPC / c.nj), c.end - c.u);
+      r.base = c.blob + ((int64_t)c.u * c.G + c.j0) * GB;
+      r.stride = (int64_t)c.G * GB;
+      r.n = n;
+      r.bytes = (uint32_t)(c.nj * GB);
+      c.u += n;
+      if (c.u >= c.end) set_phase(c, c.ph + 1);
+      return true;
+    }
+    const int gb = EXT ? c.gb : GB;
+    const int n = min(min(EXT ? c.gpc : GPC, c.end - c.u), c.G - c.gi);  // never crosses a row tile
+    r.base = c.blob + (int64_t)c.u * gb;
+    r.stride = 0;
+    r.n = 1;
+    r.bytes = (uint32_t)(n * gb);
+    c.u += n;
+    c.gi += n;
+    if (c.gi == c.G) c.gi = 0;
+    if (c.u >= c.end) {
+      if (phs[c.ph].kind == PD_FFN && set_down(c, c.ph)) return true;
+      set_phase(c, c.ph + 1);
+    }
+    return true;
+  };
+  // L2 prefetch cursor of this warp (lane 0), a.pf_dist chunks ahead of the copy cursor:
+  // more weight bytes in flight than the shared-memory ring holds
+  Cursor* pfc = reinterpret_cast<Cursor*>(smem + a.pf_off) + warp;
+  auto prefetch_next = [&]() {  // lane 0
+    ChunkRef q;
+    if (!next_chunk(*pfc, q)) return;
+    for (int i = 0; i < q.n; ++i)
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" :: "l"(q.base + i * q.stride), "r"(q.bytes)
+                   : "memory");
+  };
   auto issue_next = [&](int slot) {  // lane 0
-    if (prod.ph >= a.n_phases) return;
+    ChunkRef r;
+    if (!next_chunk(prod, r)) return;
     uint8_t* dst = ring + (size_t)slot * a.ring_stride;
-    if (prod.sub == 1) {  // whole down tiles, nj groups each
-      const int n = min(max(1, GPC / prod.nj), prod.end - prod.u);
-      const uint32_t tb = (uint32_t)(prod.nj * GB);
-      mbar_arrive_expect_tx(&wb[slot], (uint32_t)n * tb);
-      for (int i = 0; i < n; ++i)
-        bulk_g2s(dst + (size_t)i * tb, prod.blob + ((int64_t)(prod.u + i) * prod.G + prod.j0) * GB, tb, &wb[slot]);
-      ++issued;
-      prod.u += n;
-      if (prod.u >= prod.end) set_phase(prod, prod.ph + 1);
-      return;
-    }
-    const int gb = EXT ? prod.gb : GB;
-    const int n = min(min(EXT ? prod.gpc : GPC, prod.end - prod.u), prod.G - prod.gi);  // never crosses a row tile
-    mbar_arrive_expect_tx(&wb[slot], (uint32_t)(n * gb));
-    bulk_g2s(dst, prod.blob + (int64_t)prod.u * gb, (uint32_t)(n * gb), &wb[slot]);
+    mbar_arrive_expect_tx(&wb[slot], (uint32_t)r.n * r.bytes);
+    for (int i = 0; i < r.n; ++i) bulk_g2s(dst + (size_t)i * r.bytes, r.base + i * r.stride, r.bytes, &wb[slot]);
     ++issued;
-    prod.u += n;
-    prod.gi += n;
-    if (prod.gi == prod.G) prod.gi = 0;
-    if (prod.u >= prod.end) {
-      if (phs[prod.ph].kind == PD_FFN && set_down(prod, prod.ph)) return;
-      set_phase(prod, prod.ph + 1);
-    }
+    if (a.pf_dist) prefetch_next();
   };
   if (lane == 0) {
     set_phase(prod, 0);
+    if (a.pf_dist) {
+      *pfc = prod;
+      for (int i = 0; i < a.pf_dist; ++i) prefetch_next();
+    }
     for (int r = 0; r < PD_RING; ++r) issue_next(r);
   }
   if (tid == PD_KV_T && has_item) {
@@ -394,7 +423,10 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
         asm volatile("prefetch.global.L1 [%0];" :: "l"(p));
         asm volatile("prefetch.global.L1 [%0];" :: "l"(p + 8));
       }
-    if (ph > 0 && !(EXT && P.xbar ? pd_xbarrier(a, xep, P.xbar, flag) : pd_barrier(a, ++bar_k, flag))) break;
+    unsigned long long* t_arr = a.trace ? a.trace + ((size_t)2 * ph) * NC + cta : nullptr;
+    if (ph > 0 && !(EXT && P.xbar ? pd_xbarrier(a, xep, P.xbar, flag, t_arr) : pd_barrier(a, ++bar_k, flag, t_arr)))
+      break;
+    if (a.trace && tid == PD_SYNC_T) a.trace[((size_t)2 * ph + 1) * NC + cta] = gtimer();
 
     if (P.kind == PD_ATTN) {
       if (has_item) {
@@ -934,6 +966,10 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
     }
   }
 
+  if (a.trace) {  // end of this CTA's last phase
+    __syncthreads();
+    if (tid == PD_SYNC_T) a.trace[((size_t)2 * a.n_phases) * NC + cta] = gtimer();
+  }
   // copies still in flight (abort path) are waited for, bounded, before exit
   if (lane == 0)
     for (int q = consumed; q < issued; ++q) wait_bar(&wb[q % PD_RING], (uint32_t)((q / PD_RING) & 1));
@@ -1062,6 +1098,8 @@ int persist_plan(const PdPhase* ph, int n, int head_dim, int group_q, int page_s
   off += round((size_t)PD_WARPS * 2 * 16 * 4);
   a.misc_off = (int)off;
   off += 96 * 4;
+  a.pf_off = (int)off;
+  off += (size_t)PD_WARPS * PD_CURSOR_BYTES;
   a.ffn_off = (int)round(off);
   off = a.ffn_off + (size_t)ffn_floats * 4;
   a.tab_off = (int)round(off);

@@ -104,7 +104,17 @@ struct PdArgs {
   int* xepoch;              // launches completed on this rank (the same count on every rank)
   int n_xbar;               // cross barriers per launch
   int mixed;                // some phases stream INT8 / FP16 tiles (set by persist_plan)
+  // L2 prefetch: each warp keeps its weight stream pf_dist chunks ahead of its copy ring in
+  // flight as cp.async.bulk.prefetch.L2 (0: off); the cursors live in shared memory at pf_off
+  int pf_dist, pf_off;
+  // per-phase timing (null: off): [2 * n_phases + 1][grid] %globaltimer ns; row 2p: the CTA's
+  // arrival at the barrier before phase p (p = 0: launch start), row 2p+1: its departure from
+  // it (the start of phase p), row 2 n_phases: the end of its last phase
+  unsigned long long* trace;
 };
+constexpr int PD_CURSOR_BYTES = 64;
+// default prefetch distance, chunks per warp (about 4.4 KB each)
+constexpr int PD_PF_DIST = 4;
 
 struct PdPlan {
   PdArgs a{};

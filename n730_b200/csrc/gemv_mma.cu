@@ -159,8 +159,10 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) gemv_mma2_kernel(const
   int* tile_cnt = reinterpret_cast<int*>(smem + WARPS * MG2_RING * 8);  // [tiles_per_cta]
   uint4* xf = reinterpret_cast<uint4*>(smem + p.xf_off);                // [batch][ks_n/2][4 tq] x 2 k-steps
   float* sx = reinterpret_cast<float*>(smem + p.sx_off);                // [G][NT*8]
-  float* accs = reinterpret_cast<float*>(smem + p.acc_off);             // [tiles_per_cta][parts][16][NT*8]
-  float* red = accs + p.tiles_per_cta * p.parts * 16 * NT * 8;          // [WARPS][16] + [16]
+  // [slots][16][NT*8]: one slot per (tile, K-part), or per warp when there is one part
+  float* accs = reinterpret_cast<float*>(smem + p.acc_off);
+  const int acc_slots = p.parts == 1 ? WARPS : p.tiles_per_cta * p.parts;  // as laid out by the host
+  float* red = accs + acc_slots * 16 * NT * 8;                          // [WARPS][16] + [16]
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int n_tiles = (p.rows + 15) / 16;

@@ -101,7 +101,9 @@ struct Model {
   int device = 0;
   // persistent batch-1 decode (decode_persist.cu)
   bool pd_ok = false;
-  bool plan_mismatch = false;    // tensor parallel: the ranks' persistent plans differed (per-op path)
+  bool plan_mismatch = false;
+  std::vector<int8_t> pd_kinds;   // the persistent plan's phase kinds (PD_GEMV / PD_ATTN / PD_FFN), host copy
+  unsigned long long* pd_trace = nullptr;  // per-phase timing buffer (n730_model_trace_step)    // tensor parallel: the ranks' persistent plans differed (per-op path)
   bool pd_ffn_fused = false;     // the persistent step runs each FFN as one phase
   std::map<const QWeight*, uint8_t*> pd_tiles;  // INT8 / FP16 weights as persistent-kernel tiles
   PdPlan pd;
@@ -435,6 +437,10 @@ static int plan_persistent(Model* m) {
   a.qkv = m->qkv; a.attn_out = m->attn; a.cos_t = m->cos_t; a.sin_t = m->sin_t;
   a.seq_lens = m->seq_lens; a.block_table = m->block_table; a.d = dims(m);
   a.max_split = max_split;
+  a.pf_dist = PD_PF_DIST;
+  a.trace = nullptr;
+  m->pd_kinds.clear();
+  for (const PdPhase& q : ph) m->pd_kinds.push_back(q.kind);
   if (int r = m->alloc(&a.attn_part, (size_t)c.kv_heads * max_split * GQ * (c.head_dim + 2))) return r;
   if (int r = m->alloc(&a.attn_cnt, (size_t)c.kv_heads)) return r;
   if (int r = m->alloc(&a.sync, 4)) return r;
@@ -1125,6 +1131,52 @@ N730_API int n730_model_run_step_kernel(void* p, void* stream) {
   N730_REQUIRE(m->pd_ok, N730_UNSUPPORTED, "model: batch-1 decode does not use the persistent kernel");
   N730_REQUIRE(m->h_seq[0] < m->c.max_ctx, N730_STATE, "KV cache capacity exceeded");
   return persist_launch(m->pd, stream ? (cudaStream_t)stream : m->st);
+}
+
+// Run the persistent decode kernel of a batch-1 step once with per-phase
+// timing (like n730_model_run_step_kernel: the position does not advance).
+// host_times [2 n_phases + 1][grid] receives %globaltimer ns per CTA: row 2p
+// its arrival at the barrier before phase p (p = 0: the launch start), row
+// 2p+1 its departure from that barrier, the last row the end of its last
+// phase; host_kinds [n_phases] the phase kinds (0 GEMV, 1 attention, 2 FFN).
+// With host_times null only *n_phases and *grid are written (a size query).
+N730_API int n730_model_trace_step(void* p, void* stream, uint64_t* host_times, int64_t cap, int8_t* host_kinds,
+                                   int* n_phases, int* grid) {
+  MODEL(p);
+  N730_REQUIRE(m->finalized, N730_STATE, "model: not finalized");
+  N730_REQUIRE(m->pd_ok, N730_UNSUPPORTED, "model: batch-1 decode does not use the persistent kernel");
+  N730_REQUIRE(m->h_seq[0] < m->c.max_ctx, N730_STATE, "KV cache capacity exceeded");
+  const int np = m->pd.a.n_phases, g = m->pd.grid;
+  if (n_phases) *n_phases = np;
+  if (grid) *grid = g;
+  if (!host_times) return N730_OK;
+  const int64_t need = (int64_t)(2 * np + 1) * g;
+  N730_REQUIRE(cap >= need, N730_BAD_ARG, "trace_step: %lld entries needed", (long long)need);
+  if (!m->pd_trace)
+    if (int rc = m->alloc(&m->pd_trace, (size_t)need)) return rc;
+  cudaStream_t st = stream ? (cudaStream_t)stream : m->st;
+  N730_CUDA(cudaMemsetAsync(m->pd_trace, 0, (size_t)need * 8, st));
+  PdPlan plan = m->pd;
+  plan.a.trace = m->pd_trace;
+  if (int rc = persist_launch(plan, st)) return rc;
+  N730_CUDA(cudaMemcpyAsync(host_times, m->pd_trace, (size_t)need * 8, cudaMemcpyDeviceToHost, st));
+  N730_CUDA(cudaStreamSynchronize(st));
+  if (host_kinds) memcpy(host_kinds, m->pd_kinds.data(), (size_t)np);
+  return gemv_check_error(true);
+}
+
+// L2 prefetch distance of the persistent decode kernel: every warp keeps
+// `chunks` chunks (about 4.4 KB each) of its weight stream in flight beyond its
+// shared-memory ring (0 turns it off).  Drops the captured decode graphs.
+N730_API int n730_model_set_prefetch(void* p, int chunks) {
+  MODEL(p);
+  N730_REQUIRE(m->finalized, N730_STATE, "model: not finalized");
+  N730_REQUIRE(chunks >= 0 && chunks <= 64, N730_BAD_ARG, "set_prefetch: %d chunks", chunks);
+  N730_CUDA(cudaStreamSynchronize(m->st));
+  m->pd.a.pf_dist = chunks;
+  for (auto& g : m->graphs) cudaGraphExecDestroy(g.second);
+  m->graphs.clear();
+  return N730_OK;
 }
 
 // Append `n` tokens to sequence `seq` (prefill when n > 1, the decode graph

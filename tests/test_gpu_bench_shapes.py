@@ -204,3 +204,27 @@ def test_qgemm_matches_oracle(rows, cols, tokens, epi):
     got = y.cpu().numpy()
     assert np.isfinite(got).all()
     assert rel_err(got, ref) <= 5e-3
+
+
+@pytest.mark.parametrize("batch", [1, 8])
+def test_lm_head_gemv_matches_oracle(batch):
+    """The tensor-core GEMV at lm_head size (152064 x 3584 INT4 g128, 65 row tiles per CTA) with
+    the final RMSNorm folded in: the per-op decode and prefill logits path, against the oracle."""
+    import torch
+    lib = _lib.cuda()
+    P = lambda t: C.c_void_p(t.data_ptr()) if t is not None else None
+    rows, cols = 152064, 3584
+    q, W = _gpu_weight(rows, cols, seed=11)
+    rng = np.random.default_rng(batch)
+    x = rng.normal(0, 1, (batch, cols)).astype(np.float32)
+    nw = (1 + 0.1 * rng.normal(0, 1, cols)).astype(np.float32)
+    dx, dn = torch.from_numpy(x).cuda(), torch.from_numpy(nw).cuda()
+    y = torch.full((batch, rows), float("nan"), device="cuda")
+    _lib.check(lib.n730_qlinear(q, P(dx), cols, batch, P(y), rows, None, None, 0, P(dn), 1e-6, 0, None), "qlinear")
+    torch.cuda.synchronize()
+    lib.n730_qweight_destroy(q)
+    ref = oq.gemv(W, rms_norm(x, nw, 1e-6))
+    got = y.cpu().numpy()
+    assert np.isfinite(got).all()
+    for b in range(batch):
+        assert rel_err(got[b], ref[b]) <= 2e-3, b
