@@ -90,8 +90,6 @@ def _args():
     ap.add_argument("--pmap", default="int4_g128", choices=["int4_g128", "mixed_05b"],
                     help="resident workload: precision map (mixed_05b: INT8 attention, INT4 g128 FFN, fp16 tied "
                          "embedding/lm_head)")
-    ap.add_argument("--pf-sweep", default="0,2,4,6,8",
-                    help="phases workload: L2 prefetch distances (chunks per warp) to time the kernel at")
     ap.add_argument("--workload", default="auto",
                     choices=["auto", "resident", "streamed", "tp72b", "linear", "phases"],
                     help="auto: tp72b when launched by torchrun (any N), else resident (the 7B headline); "
@@ -99,7 +97,7 @@ def _args():
                          "streamed: 7B aggressive mixed quant (FFN INT2 g64, attention INT4 g128, lm_head INT8 "
                          "per channel), layer weights in pinned host memory, 2-layer prefetch, 1024-token prompt; "
                          "tp72b: Qwen2-72B shape INT4 g128 split over the N ranks (tensor parallel, strong scaling); "
-                         "phases: per-phase timing of the persistent decode kernel and an L2 prefetch sweep")
+                         "phases: per-phase timing of the persistent decode kernel")
     return ap.parse_args()
 
 
@@ -783,12 +781,14 @@ def run_linear(a):
 
 
 def run_phases(a):
-    """Per-phase timing of the persistent decode kernel (7B headline model, batch 1, context
-    --ctx): --steps traced launches (n730_model_trace_step), each phase's wall time (from the last
-    CTA leaving the barrier that starts it to the last CTA leaving the next one), the barrier's
-    arrival spread (slowest minus fastest CTA) and release latency (last arrival to first
-    departure), and the phase's algorithmic bytes per wall time; then the same kernel timed with
-    CUDA events at each L2 prefetch distance of --pf-sweep.  Prints one JSON line."""
+    """Per-phase timing of the persistent decode kernel (--model, batch 1, context --ctx): --steps
+    traced launches (n730_model_trace_step, medians over them).  Per phase kind, averaged over the
+    layers: the wall time (last CTA leaving the barrier that starts the phase to the last CTA
+    leaving the next one), the algorithmic bytes per wall time, the arrival spread at the barrier
+    that starts it (slowest minus fastest CTA) and its release latency (last arrival to first
+    departure), and the median CTA's time to the marks inside the phase (prologue done; FFN:
+    gate|up done; attention: split written, all splits of the head published).  Then the
+    untraced kernel timed with CUDA events.  Prints one JSON line."""
     import torch
     torch.cuda.set_device(0)
     from n730_b200.engine import Engine
@@ -809,55 +809,69 @@ def run_phases(a):
     runs = []
     for _ in range(max(1, a.steps)):
         times, kinds = eng.trace_step(eng.stream)
-        runs.append(times.astype(np.int64))
-    T = np.median(np.stack(runs), axis=0)  # [2 n + 1][grid]
+        runs.append(times.astype(np.float64))
+    T = np.median(np.stack(runs), axis=0)  # [4 n + 1][grid] ns
     n = len(kinds)
-    dep = T[1::2][:n].max(axis=1)          # last CTA out of the barrier starting phase p
-    end = np.append(dep[1:], T[2 * n].max())
+    arr = lambda p: T[4 * p] if p < n else T[4 * n]
+    dep = np.array([T[4 * p + 1].max() for p in range(n)] + [T[4 * n].max()])
+
+    def med(x):
+        x = x[np.isfinite(x)]
+        return float(np.median(x)) / 1e3 if x.size else None
+
+    def since(row, start):  # per-CTA interval, CTAs without the mark left out
+        d = np.where((row > 0) & (start > 0), row - start, np.nan)
+        return med(d)
+
     rows = []
     gemv_i = 0
     for p in range(n):
-        arr = T[2 * p]
         k = int(kinds[p])
+        st0, m1, m2, nxt = T[4 * p + 1], T[4 * p + 2], T[4 * p + 3], arr(p + 1)
+        r = {}
         if k == 1:
             name, nbytes = "attention", kv_layer
+            r = {"split_us": since(m1, st0), "publish_wait_us": since(m2, m1), "merge_us": since(nxt, m2)}
         elif k == 2:
             name, nbytes = "ffn (gate|up + down)", wb(2 * f, h) + wb(h, f)
+            r = {"prologue_us": since(m1, st0), "gate_up_us": since(m2, m1), "down_us": since(nxt, m2)}
         else:
             if p == n - 1:
                 name, nbytes = "lm_head", wb(shape.vocab, h)
             else:
                 name, nbytes = ("qkv", wb(qd + 2 * kvd, h)) if gemv_i % 2 == 0 else ("o_proj", wb(h, qd))
                 gemv_i += 1
-        wall = (end[p] - dep[p]) / 1e3
-        rows.append({"phase": name, "wall_us": wall, "gbs": nbytes / max(wall, 1e-9) / 1e3,
-                     "spread_us": (arr.max() - arr.min()) / 1e3 if p else 0.0,
-                     "release_us": (T[2 * p + 1].min() - arr.max()) / 1e3 if p else 0.0})
+            r = {"prologue_us": since(m1, st0), "stream_us": since(nxt, m1)}
+        wall = (dep[p + 1] - dep[p]) / 1e3
+        a_p = arr(p)
+        r.update({"phase": name, "wall_us": wall, "gbs": nbytes / max(wall, 1e-9) / 1e3,
+                  "spread_us": (a_p.max() - a_p.min()) / 1e3 if p else 0.0,
+                  "release_us": (T[4 * p + 1].min() - a_p.max()) / 1e3 if p else 0.0})
+        rows.append(r)
     summary = {}
     for r in rows:
-        d = summary.setdefault(r["phase"], {"n": 0, "wall_us": 0.0, "gbs": 0.0, "spread_us": 0.0, "release_us": 0.0})
+        d = summary.setdefault(r["phase"], {"n": 0})
         d["n"] += 1
-        for key in ("wall_us", "gbs", "spread_us", "release_us"):
-            d[key] += r[key]
+        for key, v in r.items():
+            if key != "phase" and v is not None:
+                d[key] = d.get(key, 0.0) + v
     for d in summary.values():
-        for key in ("wall_us", "gbs", "spread_us", "release_us"):
-            d[key] = round(d[key] / d["n"], 3)
-    total_us = (T[2 * n].max() - T[0].min()) / 1e3
-    sweep = {}
-    for pf in [int(x) for x in a.pf_sweep.split(",") if x != ""]:
-        eng.set_prefetch(pf)
-        for _ in range(3):
-            eng.run_step_kernel(eng.stream)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(st)
-        for _ in range(20):
-            eng.run_step_kernel(eng.stream)
-        e1.record(st)
-        torch.cuda.synchronize()
-        sweep[pf] = round(e0.elapsed_time(e1) / 20, 4)
+        for key in list(d):
+            if key != "n":
+                d[key] = round(d[key] / d["n"], 3)
+    total_us = (T[4 * n].max() - T[0].min()) / 1e3
+    for _ in range(3):
+        eng.run_step_kernel(eng.stream)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(20):
+        eng.run_step_kernel(eng.stream)
+    e1.record(st)
+    torch.cuda.synchronize()
     out = {"workload": f"{a.model}-shape ({shape.layers} layers, {a.pmap}) persistent decode at context {a.ctx}",
-           "traced_launches": len(runs), "launch_us": round(total_us, 1), "phases_per_layer": summary,
-           "prefetch_sweep_ms_per_launch": sweep, "ffn_fused": info["ffn_fused"], "grid": info["persistent_grid"]}
+           "traced_launches": len(runs), "traced_launch_us": round(total_us, 1),
+           "untraced_ms_per_launch": round(e0.elapsed_time(e1) / 20, 4), "phases_per_layer": summary,
+           "ffn_fused": info["ffn_fused"], "grid": info["persistent_grid"]}
     print(json.dumps(out), flush=True)
     eng.close()
 

@@ -227,14 +227,12 @@ int n730_model_tp_ipc_open(void* model, const uint8_t* handles, int size);
  * N730_UNSUPPORTED (-14) when the model decodes with one kernel per op. */
 int n730_model_run_step_kernel(void* model, void* stream);
 /* The same launch with per-phase timing (profiling hook, no counterpart in the reference):
- * host_times [2 n_phases + 1][grid] %globaltimer ns per CTA (row 2p: arrival at the barrier
- * before phase p, row 2p+1: departure from it, last row: end of the last phase), host_kinds
+ * host_times [4 n_phases + 1][grid] %globaltimer ns per CTA (row 4p: arrival at the barrier
+ * before phase p, row 4p+1: departure from it, rows 4p+2/4p+3: marks inside the phase, last
+ * row: end of the last phase), host_kinds
  * [n_phases] (0 GEMV, 1 attention, 2 FFN).  host_times null: only *n_phases and *grid. */
 int n730_model_trace_step(void* model, void* stream, uint64_t* host_times, int64_t cap, int8_t* host_kinds,
                           int* n_phases, int* grid);
-/* L2 prefetch distance of the persistent kernel, in chunks of about 4.4 KB per warp
- * (default 4, 0 off); drops the captured decode graphs. */
-int n730_model_set_prefetch(void* model, int chunks);
 int n730_model_run_linear(void* model, int layer, int which, const float* d_x, int batch, float* d_y,
                           void* stream);
 /* Algorithmic bytes of that linear for `batch` rows: codes + fp16 scale/zero + x + y. */

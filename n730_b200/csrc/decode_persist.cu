@@ -315,7 +315,6 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
   // phase's down_proj units, whole row tiles [u, end) of the warp, each the
   // CTA's nj groups from j0 (one bulk copy per tile).
   struct Cursor { int ph, sub, u, end, gi, G, j0, nj, gb, gpc; const uint8_t* blob; };
-  static_assert(sizeof(Cursor) <= PD_CURSOR_BYTES, "prefetch cursors are stored in PD_CURSOR_BYTES slots");
   // bytes and units per ring chunk of a phase's tiles (INT8 / FP16 tiles: EXT only)
   auto unit_bytes = [&](const PdPhase& P) {
     return !EXT || P.prec == 4 || P.prec == 0 ? GB : P.prec == 8 ? PD_UNIT8 : PD_UNIT16;
@@ -326,7 +325,8 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
     const int Td = (P.rows2 + 15) >> 4;
     const int w0 = pd_rng(0, Td, warp, PD_WARPS), w1 = pd_rng(0, Td, warp + 1, PD_WARPS);
     if (j0 == j1 || w0 == w1) return false;
-    c.ph = ph; c.sub = 1; c.u = w0; c.end = w1; c.gi = 0; c.G = P.G2; c.j0 = j0; c.nj = j1 - j0; c.blob = P.blob2;
+    // c.G: row tiles of down_proj, the stride of its group-major units
+    c.ph = ph; c.sub = 1; c.u = w0; c.end = w1; c.gi = 0; c.G = Td; c.j0 = j0; c.nj = j1 - j0; c.blob = P.blob2;
     return true;
   };
   auto set_phase = [&](Cursor& c, int ph) {
@@ -349,60 +349,36 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
   };
   int issued = 0, consumed = 0;
   Cursor prod{0, 0, 0, 0, 0, 1, 0, 0, GB, GPC, nullptr};
-  // The next chunk of cursor c: r_n copies of r_bytes at r_base + i * r_stride; advances c.
-  struct ChunkRef { const uint8_t* base; int64_t stride; int n; uint32_t bytes; };
-  auto next_chunk = [&](Cursor& c, ChunkRef& r) -> bool {
-    if (c.ph >= a.n_phases) return false;
-    if (c.sub == 1) {  // whole down tiles, nj groups each
-      const int n = min(max(1, GPC / c.nj), c.end - c.u);
-      r.base = c.blob + ((int64_t)c.u * c.G + c.j0) * GB;
-      r.stride = (int64_t)c.G * GB;
-      r.n = n;
-      r.bytes = (uint32_t)(c.nj * GB);
-      c.u += n;
-      if (c.u >= c.end) set_phase(c, c.ph + 1);
-      return true;
-    }
-    const int gb = EXT ? c.gb : GB;
-    const int n = min(min(EXT ? c.gpc : GPC, c.end - c.u), c.G - c.gi);  // never crosses a row tile
-    r.base = c.blob + (int64_t)c.u * gb;
-    r.stride = 0;
-    r.n = 1;
-    r.bytes = (uint32_t)(n * gb);
-    c.u += n;
-    c.gi += n;
-    if (c.gi == c.G) c.gi = 0;
-    if (c.u >= c.end) {
-      if (phs[c.ph].kind == PD_FFN && set_down(c, c.ph)) return true;
-      set_phase(c, c.ph + 1);
-    }
-    return true;
-  };
-  // L2 prefetch cursor of this warp (lane 0), a.pf_dist chunks ahead of the copy cursor:
-  // more weight bytes in flight than the shared-memory ring holds
-  Cursor* pfc = reinterpret_cast<Cursor*>(smem + a.pf_off) + warp;
-  auto prefetch_next = [&]() {  // lane 0
-    ChunkRef q;
-    if (!next_chunk(*pfc, q)) return;
-    for (int i = 0; i < q.n; ++i)
-      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" :: "l"(q.base + i * q.stride), "r"(q.bytes)
-                   : "memory");
-  };
   auto issue_next = [&](int slot) {  // lane 0
-    ChunkRef r;
-    if (!next_chunk(prod, r)) return;
+    if (prod.ph >= a.n_phases) return;
     uint8_t* dst = ring + (size_t)slot * a.ring_stride;
-    mbar_arrive_expect_tx(&wb[slot], (uint32_t)r.n * r.bytes);
-    for (int i = 0; i < r.n; ++i) bulk_g2s(dst + (size_t)i * r.bytes, r.base + i * r.stride, r.bytes, &wb[slot]);
+    if (prod.sub == 1) {  // n whole down tiles of the CTA's nj groups: one copy per group (group-major units)
+      const int n = min(max(1, GPC / prod.nj), prod.end - prod.u);
+      const uint32_t gbytes = (uint32_t)(n * GB);
+      mbar_arrive_expect_tx(&wb[slot], (uint32_t)prod.nj * gbytes);
+      for (int jj = 0; jj < prod.nj; ++jj)
+        bulk_g2s(dst + (size_t)jj * gbytes, prod.blob + ((int64_t)(prod.j0 + jj) * prod.G + prod.u) * GB, gbytes,
+                 &wb[slot]);
+      ++issued;
+      prod.u += n;
+      if (prod.u >= prod.end) set_phase(prod, prod.ph + 1);
+      return;
+    }
+    const int gb = EXT ? prod.gb : GB;
+    const int n = min(min(EXT ? prod.gpc : GPC, prod.end - prod.u), prod.G - prod.gi);  // never crosses a row tile
+    mbar_arrive_expect_tx(&wb[slot], (uint32_t)(n * gb));
+    bulk_g2s(dst, prod.blob + (int64_t)prod.u * gb, (uint32_t)(n * gb), &wb[slot]);
     ++issued;
-    if (a.pf_dist) prefetch_next();
+    prod.u += n;
+    prod.gi += n;
+    if (prod.gi == prod.G) prod.gi = 0;
+    if (prod.u >= prod.end) {
+      if (phs[prod.ph].kind == PD_FFN && set_down(prod, prod.ph)) return;
+      set_phase(prod, prod.ph + 1);
+    }
   };
   if (lane == 0) {
     set_phase(prod, 0);
-    if (a.pf_dist) {
-      *pfc = prod;
-      for (int i = 0; i < a.pf_dist; ++i) prefetch_next();
-    }
     for (int r = 0; r < PD_RING; ++r) issue_next(r);
   }
   if (tid == PD_KV_T && has_item) {
@@ -423,10 +399,12 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
         asm volatile("prefetch.global.L1 [%0];" :: "l"(p));
         asm volatile("prefetch.global.L1 [%0];" :: "l"(p + 8));
       }
-    unsigned long long* t_arr = a.trace ? a.trace + ((size_t)2 * ph) * NC + cta : nullptr;
+    unsigned long long* t_arr = a.trace ? a.trace + ((size_t)4 * ph) * NC + cta : nullptr;
     if (ph > 0 && !(EXT && P.xbar ? pd_xbarrier(a, xep, P.xbar, flag, t_arr) : pd_barrier(a, ++bar_k, flag, t_arr)))
       break;
-    if (a.trace && tid == PD_SYNC_T) a.trace[((size_t)2 * ph + 1) * NC + cta] = gtimer();
+    // trace marks of this phase: row 4 ph + 1 departure, + 2 and + 3 the marks below
+    unsigned long long* t_mark = a.trace && tid == PD_SYNC_T ? a.trace + ((size_t)4 * ph + 1) * NC + cta : nullptr;
+    if (t_mark) *t_mark = gtimer();
 
     if (P.kind == PD_ATTN) {
       if (has_item) {
@@ -547,11 +525,13 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
         if (tid < GQ) *reinterpret_cast<float2*>(part_ml + tid * 2) = make_float2(ml[tid * 4 + 0], ml[tid * 4 + 1]);
         // wait for every split of this KV head (co-resident CTAs, bounded wait)
         __syncthreads();
+        if (t_mark) t_mark[NC] = gtimer();  // this split's partial is written
         if (tid == PD_SYNC_T) {
           asm volatile("red.release.gpu.global.add.s32 [%0], 1;" :: "l"(a.attn_cnt + kvh) : "memory");
           flag[1] = pd_wait_count(a, a.attn_cnt + kvh, sp.ns * (attn_idx + 1));
         }
         __syncthreads();
+        if (t_mark) t_mark[2 * NC] = gtimer();  // every split of the head has published
         if (flag[1]) {
           // this split merges outputs [o_lo, o_hi) of its head group (GQ*HD values): one batch of loads
           const int no = GQ * HD, o_lo = split * no / sp.ns, o_hi = (split + 1) * no / sp.ns;
@@ -795,6 +775,8 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
       }
     }
 
+    if (t_mark) t_mark[NC] = gtimer();  // prologue done: x fragments and group sums in shared memory
+
     // epilogue of the 16 rows of tile t (all 32 lanes; lane r < 16 holds row t*16 + r)
     auto tile_out = [&](int t, float v) {
       const int row = t * 16 + lane;
@@ -897,6 +879,7 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
 
     // ============ FFN: down_proj partial sums over this CTA's channels ============
     __syncthreads();  // every SwiGLU channel of the CTA is in mloc
+    if (t_mark) t_mark[2 * NC] = gtimer();  // gate|up done
     const int j0 = pd_rng(0, P.G2, cta, NC), nj = pd_rng(0, P.G2, cta + 1, NC) - j0;
     if (nj == 0) continue;
     {
@@ -954,7 +937,7 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
           float acc1[1][4] = {{0.f, 0.f, 0.f, 0.f}};
           for (int jj = 0; jj < nj; ++jj) {
             const uint4* xg[1] = {xf + jj * KPG * 2 + tq};
-            mma_chunk<KPG, 1, 1, true, 1>(buf + (size_t)(i * nj + jj) * GB, lane, xg, sx + jj, acc1);
+            mma_chunk<KPG, 1, 1, true, 1>(buf + (size_t)(jj * n + i) * GB, lane, xg, sx + jj, acc1);
           }
           put_rows(u + i, acc1[0][0], acc1[0][2]);
         }
@@ -968,7 +951,7 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
 
   if (a.trace) {  // end of this CTA's last phase
     __syncthreads();
-    if (tid == PD_SYNC_T) a.trace[((size_t)2 * a.n_phases) * NC + cta] = gtimer();
+    if (tid == PD_SYNC_T) a.trace[((size_t)4 * a.n_phases) * NC + cta] = gtimer();
   }
   // copies still in flight (abort path) are waited for, bounded, before exit
   if (lane == 0)
@@ -1098,8 +1081,6 @@ int persist_plan(const PdPhase* ph, int n, int head_dim, int group_q, int page_s
   off += round((size_t)PD_WARPS * 2 * 16 * 4);
   a.misc_off = (int)off;
   off += 96 * 4;
-  a.pf_off = (int)off;
-  off += (size_t)PD_WARPS * PD_CURSOR_BYTES;
   a.ffn_off = (int)round(off);
   off = a.ffn_off + (size_t)ffn_floats * 4;
   a.tab_off = (int)round(off);
@@ -1176,6 +1157,33 @@ int pd_tile_launch(const QWeight& w, uint8_t* out, cudaStream_t st) {
   const int64_t n = (int64_t)((w.rows + 15) / 16) * G * (w.bits == 8 ? 16 * PD_TILE_K + 32 : 16 * PD_TILE_K);
   const unsigned blocks = (unsigned)std::min<int64_t>((n + 255) / 256, 65536);
   pd_tile_kernel<<<blocks, 256, 0, st>>>(w, out, G);
+  N730_CUDA(cudaGetLastError());
+  return N730_OK;
+}
+
+// down_proj units in group-major order for the fused FFN: unit (t, g) of the
+// fragment tiles (byte (t * G + g) * gb) moves to byte (g * T + t) * gb, so the
+// row tiles of one group (one CTA's slice) are contiguous and a chunk of them
+// is one bulk copy.
+__global__ void pd_group_major_kernel(const uint4* src, uint4* dst, int T, int G, int words) {
+  const int64_t n = (int64_t)T * G * words;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t unit = i / words;
+    const int w = (int)(i - unit * words);
+    const int t = (int)(unit / G), g = (int)(unit - (int64_t)t * G);
+    dst[((int64_t)g * T + t) * words + w] = src[i];
+  }
+}
+
+int pd_group_major_launch(const uint8_t* tiles, int rows, int n_groups, int group, uint8_t* out, cudaStream_t st) {
+  const int gb = (group / 16) * 128 + 64;
+  N730_REQUIRE(gb % 16 == 0 && ((uintptr_t)tiles & 15) == 0 && ((uintptr_t)out & 15) == 0, N730_BAD_ARG,
+               "group-major copy: alignment");
+  const int T = (rows + 15) / 16;
+  const int64_t n = (int64_t)T * n_groups * (gb / 16);
+  const unsigned blocks = (unsigned)std::min<int64_t>((n + 255) / 256, 65536);
+  pd_group_major_kernel<<<blocks, 256, 0, st>>>(reinterpret_cast<const uint4*>(tiles), reinterpret_cast<uint4*>(out),
+                                                T, n_groups, gb / 16);
   N730_CUDA(cudaGetLastError());
   return N730_OK;
 }

@@ -19,7 +19,8 @@ constexpr int PD_MAX_RANKS = 8;
 // quantisation groups [j0, j1) of down_proj's input (the FFN channels); it
 // computes the gate|up rows of exactly those channels (`blob`, interleaved,
 // SwiGLU into shared memory) and then down_proj's partial sums over them for
-// every output row (`blob2`: rows2 x cols2, G2 groups), added into `acc` as
+// every output row (`blob2`: rows2 x cols2, G2 groups, units in group-major
+// order so a CTA's groups are contiguous: pd_group_major_launch), added into `acc` as
 // 32.32 fixed-point integers (integer addition is associative, so the sum is
 // the same whatever order the CTAs arrive in).  The residual stream is then
 // h + acc: a later GEMV with a non-null `acc` reads x + acc (norm phases) or,
@@ -45,7 +46,7 @@ struct __align__(16) PdPhase {
   const float* bias;
   float* y;
   KVLayer kv;
-  const uint8_t* blob2;     // FFN: down_proj
+  const uint8_t* blob2;     // FFN: down_proj, group-major fragment tiles
   int cols2, G2;
   unsigned long long* acc;  // FFN: down_proj sums (fixed point, 2^-32); GEMV: pending residual
   float* h_out;             // tensor parallel: residual stream after this exchange
@@ -70,6 +71,9 @@ int64_t pd_tile_bytes(int bits, int rows, int cols);
 // Write weight `w` (INT8 row-major with scale/zero, or FP16) as persistent tiles into `out`.
 struct QWeight;
 int pd_tile_launch(const QWeight& w, uint8_t* out, cudaStream_t st);
+// Copy of INT4 fragment tiles (rows x n_groups groups of `group`) with units in
+// group-major order [group][row tile]: the fused FFN's down_proj (`blob2`).
+int pd_group_major_launch(const uint8_t* tiles, int rows, int n_groups, int group, uint8_t* out, cudaStream_t st);
 
 struct PdArgs {
   const PdPhase* phases;
@@ -104,17 +108,13 @@ struct PdArgs {
   int* xepoch;              // launches completed on this rank (the same count on every rank)
   int n_xbar;               // cross barriers per launch
   int mixed;                // some phases stream INT8 / FP16 tiles (set by persist_plan)
-  // L2 prefetch: each warp keeps its weight stream pf_dist chunks ahead of its copy ring in
-  // flight as cp.async.bulk.prefetch.L2 (0: off); the cursors live in shared memory at pf_off
-  int pf_dist, pf_off;
-  // per-phase timing (null: off): [2 * n_phases + 1][grid] %globaltimer ns; row 2p: the CTA's
-  // arrival at the barrier before phase p (p = 0: launch start), row 2p+1: its departure from
-  // it (the start of phase p), row 2 n_phases: the end of its last phase
+  // per-phase timing (null: off): [4 * n_phases + 1][grid] %globaltimer ns; row 4p: the CTA's
+  // arrival at the barrier before phase p (p = 0: launch start), row 4p+1: its departure from
+  // it (the start of phase p), rows 4p+2 and 4p+3: marks inside the phase (GEMV: prologue done;
+  // FFN: prologue done, gate|up done; attention: split partial written, head's splits all
+  // published), row 4 n_phases: the end of its last phase; 0 where a CTA has no mark
   unsigned long long* trace;
 };
-constexpr int PD_CURSOR_BYTES = 64;
-// default prefetch distance, chunks per warp (about 4.4 KB each)
-constexpr int PD_PF_DIST = 4;
 
 struct PdPlan {
   PdArgs a{};

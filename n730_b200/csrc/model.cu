@@ -106,6 +106,7 @@ struct Model {
   unsigned long long* pd_trace = nullptr;  // per-phase timing buffer (n730_model_trace_step)    // tensor parallel: the ranks' persistent plans differed (per-op path)
   bool pd_ffn_fused = false;     // the persistent step runs each FFN as one phase
   std::map<const QWeight*, uint8_t*> pd_tiles;  // INT8 / FP16 weights as persistent-kernel tiles
+  std::map<const QWeight*, uint8_t*> pd_down_gm;  // fused FFN: down_proj tiles in group-major order
   PdPlan pd;
   // layer streaming (stream_depth > 0): per-layer weight images in pinned host
   // memory, copied into HBM slots on `cst` ahead of use
@@ -381,7 +382,7 @@ static int plan_persistent(Model* m) {
       if (fuse) {  // gate|up + down partial sums in one phase
         PdPhase& f = ph.back();
         f.kind = PD_FFN;
-        f.blob2 = y.down->codes; f.rows2 = y.down->rows; f.cols2 = y.down->cols; f.G2 = y.down->n_groups;
+        f.blob2 = m->pd_down_gm.count(y.down) ? m->pd_down_gm.at(y.down) : nullptr; f.rows2 = y.down->rows; f.cols2 = y.down->cols; f.G2 = y.down->n_groups;
         f.acc = acc;
       } else {
         gemv_phase(y.down, m->mlp, nullptr, y.down_bias, m->x, PD_EPI_RESID);
@@ -389,6 +390,19 @@ static int plan_persistent(Model* m) {
     }
     gemv_phase(m->lm_head, m->x, m->final_norm, nullptr, m->logits, PD_EPI_STORE);
     ph.back().acc = acc;
+  };
+  // the fused FFN streams down_proj from a group-major copy of its tiles (made once, kept)
+  auto prep_down_gm = [&]() -> int {
+    for (auto& y : m->L) {
+      if (m->pd_down_gm.count(y.down)) continue;
+      uint8_t* t = nullptr;
+      const QWeight* w = y.down;
+      const size_t bytes = (size_t)((w->rows + 15) / 16) * w->n_groups * ((size_t)(w->group / 16) * 128 + 64);
+      if (int r = m->alloc(&t, bytes)) return r;
+      if (int r = pd_group_major_launch(w->codes, w->rows, w->n_groups, w->group, t, m->st)) return r;
+      m->pd_down_gm[w] = t;
+    }
+    return N730_OK;
   };
   bool has_down_bias = false;
   for (auto& y : m->L) has_down_bias |= y.down_bias != nullptr;
@@ -401,6 +415,8 @@ static int plan_persistent(Model* m) {
   }
   PdPlan plan;
   int n_xbar = 0;
+  if (fuse)
+    if (int r = prep_down_gm()) return r;
   if (tp) n_xbar = build_tp();
   else build(fuse);
   int rc = persist_plan(ph.data(), (int)ph.size(), c.head_dim, c.heads / c.kv_heads, c.page_size, c.tp_size, &plan);
@@ -416,6 +432,7 @@ static int plan_persistent(Model* m) {
       if (int r = m->alloc(&m->ffn_acc, (size_t)c.hidden)) return r;
       N730_CUDA(cudaMemsetAsync(m->ffn_acc, 0, (size_t)c.hidden * 8, m->st));
     }
+    if (int r = prep_down_gm()) return r;
     build(true);
     rc = persist_plan(ph.data(), (int)ph.size(), c.head_dim, c.heads / c.kv_heads, c.page_size, c.tp_size, &plan);
   }
@@ -437,7 +454,6 @@ static int plan_persistent(Model* m) {
   a.qkv = m->qkv; a.attn_out = m->attn; a.cos_t = m->cos_t; a.sin_t = m->sin_t;
   a.seq_lens = m->seq_lens; a.block_table = m->block_table; a.d = dims(m);
   a.max_split = max_split;
-  a.pf_dist = PD_PF_DIST;
   a.trace = nullptr;
   m->pd_kinds.clear();
   for (const PdPhase& q : ph) m->pd_kinds.push_back(q.kind);
@@ -1135,10 +1151,13 @@ N730_API int n730_model_run_step_kernel(void* p, void* stream) {
 
 // Run the persistent decode kernel of a batch-1 step once with per-phase
 // timing (like n730_model_run_step_kernel: the position does not advance).
-// host_times [2 n_phases + 1][grid] receives %globaltimer ns per CTA: row 2p
+// host_times [4 n_phases + 1][grid] receives %globaltimer ns per CTA: row 4p
 // its arrival at the barrier before phase p (p = 0: the launch start), row
-// 2p+1 its departure from that barrier, the last row the end of its last
-// phase; host_kinds [n_phases] the phase kinds (0 GEMV, 1 attention, 2 FFN).
+// 4p+1 its departure from that barrier, rows 4p+2 / 4p+3 marks inside the
+// phase (GEMV: prologue done; FFN: prologue done, gate|up done; attention:
+// split partial written, all splits of the head published; 0 where absent),
+// the last row the end of its last phase; host_kinds [n_phases] the phase
+// kinds (0 GEMV, 1 attention, 2 FFN).
 // With host_times null only *n_phases and *grid are written (a size query).
 N730_API int n730_model_trace_step(void* p, void* stream, uint64_t* host_times, int64_t cap, int8_t* host_kinds,
                                    int* n_phases, int* grid) {
@@ -1150,7 +1169,7 @@ N730_API int n730_model_trace_step(void* p, void* stream, uint64_t* host_times, 
   if (n_phases) *n_phases = np;
   if (grid) *grid = g;
   if (!host_times) return N730_OK;
-  const int64_t need = (int64_t)(2 * np + 1) * g;
+  const int64_t need = (int64_t)(4 * np + 1) * g;
   N730_REQUIRE(cap >= need, N730_BAD_ARG, "trace_step: %lld entries needed", (long long)need);
   if (!m->pd_trace)
     if (int rc = m->alloc(&m->pd_trace, (size_t)need)) return rc;
@@ -1163,20 +1182,6 @@ N730_API int n730_model_trace_step(void* p, void* stream, uint64_t* host_times, 
   N730_CUDA(cudaStreamSynchronize(st));
   if (host_kinds) memcpy(host_kinds, m->pd_kinds.data(), (size_t)np);
   return gemv_check_error(true);
-}
-
-// L2 prefetch distance of the persistent decode kernel: every warp keeps
-// `chunks` chunks (about 4.4 KB each) of its weight stream in flight beyond its
-// shared-memory ring (0 turns it off).  Drops the captured decode graphs.
-N730_API int n730_model_set_prefetch(void* p, int chunks) {
-  MODEL(p);
-  N730_REQUIRE(m->finalized, N730_STATE, "model: not finalized");
-  N730_REQUIRE(chunks >= 0 && chunks <= 64, N730_BAD_ARG, "set_prefetch: %d chunks", chunks);
-  N730_CUDA(cudaStreamSynchronize(m->st));
-  m->pd.a.pf_dist = chunks;
-  for (auto& g : m->graphs) cudaGraphExecDestroy(g.second);
-  m->graphs.clear();
-  return N730_OK;
 }
 
 // Append `n` tokens to sequence `seq` (prefill when n > 1, the decode graph

@@ -80,8 +80,6 @@ def _sigs(lib):
     lib.n730_model_linear_bytes.restype = C.c_int64
     lib.n730_model_trace_step.argtypes = [vp, vp, vp, C.c_int64, vp, C.POINTER(i32), C.POINTER(i32)]
     lib.n730_model_trace_step.restype = i32
-    lib.n730_model_set_prefetch.argtypes = [vp, i32]
-    lib.n730_model_set_prefetch.restype = i32
     lib._model_sigs = True
     return lib
 
@@ -238,21 +236,18 @@ class Engine:
                    "model_run_step_kernel")
 
     def trace_step(self, stream: int = 0):
-        """One persistent-kernel launch with per-phase timing: (times [2 n_phases + 1, grid] ns,
+        """One persistent-kernel launch with per-phase timing: (times [4 n_phases + 1, grid] ns,
         kinds [n_phases]); see include/n730_cuda.h."""
         st = C.c_void_p(stream) if stream else None
         npz, grid = C.c_int32(), C.c_int32()
         _lib.check(self.lib.n730_model_trace_step(self.h, st, None, 0, None, C.byref(npz), C.byref(grid)),
                    "model_trace_step")
-        times = np.zeros((2 * npz.value + 1, grid.value), np.uint64)
+        times = np.zeros((4 * npz.value + 1, grid.value), np.uint64)
         kinds = np.zeros(npz.value, np.int8)
         _lib.check(self.lib.n730_model_trace_step(self.h, st, times.ctypes.data_as(C.c_void_p), times.size,
                                                   kinds.ctypes.data_as(C.c_void_p), C.byref(npz), C.byref(grid)),
                    "model_trace_step")
         return times, kinds
-
-    def set_prefetch(self, chunks: int):
-        _lib.check(self.lib.n730_model_set_prefetch(self.h, chunks), "model_set_prefetch")
 
     def run_linear(self, layer: int, which: int, d_x: int, batch: int, d_y: int, stream: int = 0):
         _lib.check(self.lib.n730_model_run_linear(self.h, layer, which, C.c_void_p(d_x), batch, C.c_void_p(d_y),
