@@ -79,6 +79,10 @@ def _args():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (small profiling cases)")
+    ap.add_argument("--vocab", type=int, default=0, help="phases workload: override the vocabulary (profiling cases)")
+    ap.add_argument("--linear-shape", default="4096x4096", help="linear workload: rows x cols of W")
+    ap.add_argument("--copies", type=int, default=0,
+                    help="linear workload: weight copies rotated through (default: > 4x L2 of bytes)")
     ap.add_argument("--tp-allreduce", type=int, default=1, choices=[0, 1],
                     help="tp72b decode row-split sums: 0 one-shot over NVLink peer memory, 1 NCCL")
     ap.add_argument("--ffn-fuse", type=int, default=0, choices=[-1, 0, 1],
@@ -715,12 +719,14 @@ def run_linear(a):
     from n730_b200 import _lib
     lib = _lib.cuda()
     torch.cuda.set_device(0)
-    rows = cols = 4096
+    rows, cols = (int(v) for v in a.linear_shape.lower().split("x"))
     g = torch.Generator(device="cuda")
     g.manual_seed(0)
     w = torch.randn(rows, cols, generator=g, device="cuda") * 0.02
     P = lambda t: C.c_void_p(t.data_ptr())
-    copies, qs = 64, []
+    per = rows * cols // 2 + rows * (cols // 128) * 4
+    copies = a.copies or max(4, -(-4 * 126 * 2**20 // per))
+    qs = []
     for _ in range(copies):
         codes = torch.empty(rows * cols // 2, dtype=torch.uint8, device="cuda")
         s16 = torch.empty(rows, cols // 128, dtype=torch.float16, device="cuda")
@@ -762,17 +768,17 @@ def run_linear(a):
     t = e0.elapsed_time(e1) / 1000.0 / (a.steps * copies)
     bytes_per = rows * cols // 2 + rows * (cols // 128) * 4 + cols * 4 + rows * 4
     peak, kind = _peaks()
-    out = {"metric": "single-linear INT4 g128 dequant-GEMV bandwidth (W 4096x4096, batch 1)",
+    out = {"metric": f"single-linear INT4 g128 dequant-GEMV bandwidth (W {rows}x{cols}, batch 1)",
            "value": round(bytes_per / t / 1e9, 1), "unit": "GB/s", "n_gpus": 1, "steps": a.steps, "warmup": a.warmup,
            "ms_per_step": round(t * 1e3, 5), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
            "dtype": "int4 weights (exact dequant); fp16 x, f32 accumulate",
            "data": "synthetic W ~ N(0, 0.02) seed 0, x ~ N(0, 1) seed 1",
-           "config": {"workload": "one 4096x4096 INT4 g128 GEMV per step (n730_qlinear, tensor-core GEMV)",
+           "config": {"workload": f"one {rows}x{cols} INT4 g128 GEMV per step (n730_qlinear, tensor-core GEMV)",
                       "copies": copies, "l2": f"rotation over {copies} weight copies = "
                                               f"{copies * bytes_per / 1e6:.0f} MB (> 4x L2)", "graph": True},
            "roofline": {"bound": "hbm", "achieved": round(bytes_per / t / 1e9, 1), "peak": peak, "unit": "GB/s",
                         "frac": round(bytes_per / t / 1e9 / peak, 4), "traffic": None,
-                        "kernel": "gemv_mma2_kernel<8,1,16> (4096 rows, K 4096)", "bytes_per_launch": bytes_per,
+                        "kernel": f"gemv_mma2_kernel<8,1,16> ({rows} rows, K {cols})", "bytes_per_launch": bytes_per,
                         "ms_per_launch": round(t * 1e3, 5), "peak_source": kind},
            "clocks": clk.summary(), "gpu_launches": a.steps * copies}
     print(json.dumps(out), flush=True)
@@ -786,8 +792,9 @@ def run_phases(a):
     layers: the wall time (last CTA leaving the barrier that starts the phase to the last CTA
     leaving the next one), the algorithmic bytes per wall time, the arrival spread at the barrier
     that starts it (slowest minus fastest CTA) and its release latency (last arrival to first
-    departure), and the median CTA's time to the marks inside the phase (prologue done; FFN:
-    gate|up done; attention: split written, all splits of the head published).  Then the
+    departure), the median CTA's time to the marks inside the phase (prologue done; FFN:
+    gate|up done; attention: split written, all splits of the head published), and the mean
+    time a warp spent waiting for its weight chunks.  Then the
     untraced kernel timed with CUDA events.  Prints one JSON line."""
     import torch
     torch.cuda.set_device(0)
@@ -796,6 +803,8 @@ def run_phases(a):
     shape = SHAPES[a.model]
     if a.layers:
         shape = dataclasses.replace(shape, layers=a.layers)
+    if a.vocab:
+        shape = dataclasses.replace(shape, vocab=a.vocab)
     eng = Engine(shape, max_ctx=a.ctx + 64, max_batch=1, max_prefill=512, ffn_fuse=a.ffn_fuse)
     build_on_device(shape, a.pmap, eng)
     eng.finalize()
@@ -810,10 +819,11 @@ def run_phases(a):
     for _ in range(max(1, a.steps)):
         times, kinds = eng.trace_step(eng.stream)
         runs.append(times.astype(np.float64))
-    T = np.median(np.stack(runs), axis=0)  # [4 n + 1][grid] ns
+    R = 6  # trace rows per phase
+    T = np.median(np.stack(runs), axis=0)  # [R n + 1][grid] ns
     n = len(kinds)
-    arr = lambda p: T[4 * p] if p < n else T[4 * n]
-    dep = np.array([T[4 * p + 1].max() for p in range(n)] + [T[4 * n].max()])
+    arr = lambda p: T[R * p] if p < n else T[R * n]
+    dep = np.array([T[R * p + 1].max() for p in range(n)] + [T[R * n].max()])
 
     def med(x):
         x = x[np.isfinite(x)]
@@ -827,26 +837,28 @@ def run_phases(a):
     gemv_i = 0
     for p in range(n):
         k = int(kinds[p])
-        st0, m1, m2, nxt = T[4 * p + 1], T[4 * p + 2], T[4 * p + 3], arr(p + 1)
+        st0, m1, m2, nxt = T[R * p + 1], T[R * p + 2], T[R * p + 3], arr(p + 1)
+        w1, w2 = float(np.mean(T[R * p + 4])) / 16e3, float(np.mean(T[R * p + 5])) / 16e3  # per warp, us
         r = {}
         if k == 1:
             name, nbytes = "attention", kv_layer
             r = {"split_us": since(m1, st0), "publish_wait_us": since(m2, m1), "merge_us": since(nxt, m2)}
         elif k == 2:
             name, nbytes = "ffn (gate|up + down)", wb(2 * f, h) + wb(h, f)
-            r = {"prologue_us": since(m1, st0), "gate_up_us": since(m2, m1), "down_us": since(nxt, m2)}
+            r = {"prologue_us": since(m1, st0), "gate_up_us": since(m2, m1), "down_us": since(nxt, m2),
+                 "gate_up_wait_us": w1, "down_wait_us": w2}
         else:
             if p == n - 1:
                 name, nbytes = "lm_head", wb(shape.vocab, h)
             else:
                 name, nbytes = ("qkv", wb(qd + 2 * kvd, h)) if gemv_i % 2 == 0 else ("o_proj", wb(h, qd))
                 gemv_i += 1
-            r = {"prologue_us": since(m1, st0), "stream_us": since(nxt, m1)}
+            r = {"prologue_us": since(m1, st0), "stream_us": since(nxt, m1), "chunk_wait_us": w1}
         wall = (dep[p + 1] - dep[p]) / 1e3
         a_p = arr(p)
         r.update({"phase": name, "wall_us": wall, "gbs": nbytes / max(wall, 1e-9) / 1e3,
                   "spread_us": (a_p.max() - a_p.min()) / 1e3 if p else 0.0,
-                  "release_us": (T[4 * p + 1].min() - a_p.max()) / 1e3 if p else 0.0})
+                  "release_us": (T[R * p + 1].min() - a_p.max()) / 1e3 if p else 0.0})
         rows.append(r)
     summary = {}
     for r in rows:
@@ -859,7 +871,7 @@ def run_phases(a):
         for key in list(d):
             if key != "n":
                 d[key] = round(d[key] / d["n"], 3)
-    total_us = (T[4 * n].max() - T[0].min()) / 1e3
+    total_us = (T[R * n].max() - T[0].min()) / 1e3
     for _ in range(3):
         eng.run_step_kernel(eng.stream)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

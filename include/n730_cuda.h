@@ -227,9 +227,9 @@ int n730_model_tp_ipc_open(void* model, const uint8_t* handles, int size);
  * N730_UNSUPPORTED (-14) when the model decodes with one kernel per op. */
 int n730_model_run_step_kernel(void* model, void* stream);
 /* The same launch with per-phase timing (profiling hook, no counterpart in the reference):
- * host_times [4 n_phases + 1][grid] %globaltimer ns per CTA (row 4p: arrival at the barrier
- * before phase p, row 4p+1: departure from it, rows 4p+2/4p+3: marks inside the phase, last
- * row: end of the last phase), host_kinds
+ * host_times [6 n_phases + 1][grid] per CTA (row 6p: arrival at the barrier before phase p,
+ * 6p+1: departure from it, 6p+2/6p+3: marks inside the phase, 6p+4/6p+5: ns its warps waited
+ * for weight chunks, last row: end of the last phase; %globaltimer ns), host_kinds
  * [n_phases] (0 GEMV, 1 attention, 2 FFN).  host_times null: only *n_phases and *grid. */
 int n730_model_trace_step(void* model, void* stream, uint64_t* host_times, int64_t cap, int8_t* host_kinds,
                           int* n_phases, int* grid);

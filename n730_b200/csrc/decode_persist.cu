@@ -263,6 +263,8 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
   int* flag = wcnt + 16;                                         // [16]
   float* red = reinterpret_cast<float*>(wcnt + 32);              // [32]
   int* wr = wcnt + 64;                                           // [PD_WARPS + 1] unit ranges of a GEMV phase
+  // tracing: ns the warps spent waiting for weight chunks in this phase ([0] GEMV / gate|up, [1] down)
+  unsigned long long* wacc = reinterpret_cast<unsigned long long*>(wcnt + 82);
   float* mloc = reinterpret_cast<float*>(smem + a.ffn_off);      // FFN: this CTA's SwiGLU channels
 
   const PdSplits sp = pd_splits(a);
@@ -399,12 +401,22 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
         asm volatile("prefetch.global.L1 [%0];" :: "l"(p));
         asm volatile("prefetch.global.L1 [%0];" :: "l"(p + 8));
       }
-    unsigned long long* t_arr = a.trace ? a.trace + ((size_t)4 * ph) * NC + cta : nullptr;
+    unsigned long long* t_arr = a.trace ? a.trace + ((size_t)PD_TRACE_ROWS * ph) * NC + cta : nullptr;
     if (ph > 0 && !(EXT && P.xbar ? pd_xbarrier(a, xep, P.xbar, flag, t_arr) : pd_barrier(a, ++bar_k, flag, t_arr)))
       break;
-    // trace marks of this phase: row 4 ph + 1 departure, + 2 and + 3 the marks below
-    unsigned long long* t_mark = a.trace && tid == PD_SYNC_T ? a.trace + ((size_t)4 * ph + 1) * NC + cta : nullptr;
-    if (t_mark) *t_mark = gtimer();
+    // trace marks of this phase: row PD_TRACE_ROWS ph + 1 departure, + 2 and + 3 the marks below; the
+    // previous phase's chunk-wait sums (complete: every warp has passed the barrier) go to its rows + 4, + 5
+    unsigned long long* t_mark =
+        a.trace && tid == PD_SYNC_T ? a.trace + ((size_t)PD_TRACE_ROWS * ph + 1) * NC + cta : nullptr;
+    if (t_mark) {
+      *t_mark = gtimer();
+      if (ph > 0) {
+        unsigned long long* prev = a.trace + ((size_t)PD_TRACE_ROWS * (ph - 1)) * NC + cta;
+        prev[4 * NC] = wacc[0];
+        prev[5 * NC] = wacc[1];
+      }
+      wacc[0] = wacc[1] = 0ull;
+    }
 
     if (P.kind == PD_ATTN) {
       if (has_item) {
@@ -810,7 +822,11 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
       const int n = min(min(ugpc, w1 - u), G - gi);
       const int slot = consumed % PD_RING;
       int okl = 0;
-      if (lane == 0) okl = wait_bar(&wb[slot], (uint32_t)((consumed / PD_RING) & 1));
+      if (lane == 0) {
+        const uint64_t tw = a.trace ? gtimer() : 0;
+        okl = wait_bar(&wb[slot], (uint32_t)((consumed / PD_RING) & 1));
+        if (a.trace) atomicAdd(&wacc[0], (unsigned long long)(gtimer() - tw));
+      }
       if (!__shfl_sync(0xffffffffu, okl, 0)) {
         if (lane == 0) { atomicExch(&a.sync[2], 1); atomicExch(a.err, DEV_ERR_TIMEOUT); }
         wfail = true;
@@ -918,7 +934,11 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
       const int n = min(per, d1 - u);
       const int slot = consumed % PD_RING;
       int okl = 0;
-      if (lane == 0) okl = wait_bar(&wb[slot], (uint32_t)((consumed / PD_RING) & 1));
+      if (lane == 0) {
+        const uint64_t tw = a.trace ? gtimer() : 0;
+        okl = wait_bar(&wb[slot], (uint32_t)((consumed / PD_RING) & 1));
+        if (a.trace) atomicAdd(&wacc[1], (unsigned long long)(gtimer() - tw));
+      }
       if (!__shfl_sync(0xffffffffu, okl, 0)) {
         if (lane == 0) { atomicExch(&a.sync[2], 1); atomicExch(a.err, DEV_ERR_TIMEOUT); }
         wfail = true;
@@ -951,7 +971,12 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
 
   if (a.trace) {  // end of this CTA's last phase
     __syncthreads();
-    if (tid == PD_SYNC_T) a.trace[((size_t)4 * a.n_phases) * NC + cta] = gtimer();
+    if (tid == PD_SYNC_T) {
+      unsigned long long* last = a.trace + ((size_t)PD_TRACE_ROWS * (a.n_phases - 1)) * NC + cta;
+      last[4 * NC] = wacc[0];
+      last[5 * NC] = wacc[1];
+      a.trace[((size_t)PD_TRACE_ROWS * a.n_phases) * NC + cta] = gtimer();
+    }
   }
   // copies still in flight (abort path) are waited for, bounded, before exit
   if (lane == 0)

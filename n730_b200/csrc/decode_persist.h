@@ -108,13 +108,16 @@ struct PdArgs {
   int* xepoch;              // launches completed on this rank (the same count on every rank)
   int n_xbar;               // cross barriers per launch
   int mixed;                // some phases stream INT8 / FP16 tiles (set by persist_plan)
-  // per-phase timing (null: off): [4 * n_phases + 1][grid] %globaltimer ns; row 4p: the CTA's
-  // arrival at the barrier before phase p (p = 0: launch start), row 4p+1: its departure from
-  // it (the start of phase p), rows 4p+2 and 4p+3: marks inside the phase (GEMV: prologue done;
-  // FFN: prologue done, gate|up done; attention: split partial written, head's splits all
-  // published), row 4 n_phases: the end of its last phase; 0 where a CTA has no mark
+  // per-phase timing (null: off): [PD_TRACE_ROWS * n_phases + 1][grid] %globaltimer ns; for
+  // phase p, row 6p: the CTA's arrival at the barrier before it (p = 0: launch start), 6p+1: its
+  // departure from it (the start of phase p), 6p+2 and 6p+3: marks inside the phase (GEMV:
+  // prologue done; FFN: prologue done, gate|up done; attention: split partial written, head's
+  // splits all published; 0 where a CTA has none), 6p+4 and 6p+5: ns its warps spent waiting
+  // for weight chunks, summed over the warps (GEMV or gate|up; down_proj); the last row: the
+  // end of its last phase
   unsigned long long* trace;
 };
+constexpr int PD_TRACE_ROWS = 6;
 
 struct PdPlan {
   PdArgs a{};

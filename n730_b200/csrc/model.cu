@@ -1151,13 +1151,14 @@ N730_API int n730_model_run_step_kernel(void* p, void* stream) {
 
 // Run the persistent decode kernel of a batch-1 step once with per-phase
 // timing (like n730_model_run_step_kernel: the position does not advance).
-// host_times [4 n_phases + 1][grid] receives %globaltimer ns per CTA: row 4p
+// host_times [6 n_phases + 1][grid] receives per CTA (%globaltimer ns): row 6p
 // its arrival at the barrier before phase p (p = 0: the launch start), row
-// 4p+1 its departure from that barrier, rows 4p+2 / 4p+3 marks inside the
+// 6p+1 its departure from that barrier, rows 6p+2 / 6p+3 marks inside the
 // phase (GEMV: prologue done; FFN: prologue done, gate|up done; attention:
 // split partial written, all splits of the head published; 0 where absent),
-// the last row the end of its last phase; host_kinds [n_phases] the phase
-// kinds (0 GEMV, 1 attention, 2 FFN).
+// rows 6p+4 / 6p+5 the time its warps spent waiting for weight chunks, summed
+// over the warps (GEMV or gate|up; down_proj), the last row the end of its
+// last phase; host_kinds [n_phases] the phase kinds (0 GEMV, 1 attention, 2 FFN).
 // With host_times null only *n_phases and *grid are written (a size query).
 N730_API int n730_model_trace_step(void* p, void* stream, uint64_t* host_times, int64_t cap, int8_t* host_kinds,
                                    int* n_phases, int* grid) {
@@ -1169,7 +1170,7 @@ N730_API int n730_model_trace_step(void* p, void* stream, uint64_t* host_times, 
   if (n_phases) *n_phases = np;
   if (grid) *grid = g;
   if (!host_times) return N730_OK;
-  const int64_t need = (int64_t)(4 * np + 1) * g;
+  const int64_t need = (int64_t)(PD_TRACE_ROWS * np + 1) * g;
   N730_REQUIRE(cap >= need, N730_BAD_ARG, "trace_step: %lld entries needed", (long long)need);
   if (!m->pd_trace)
     if (int rc = m->alloc(&m->pd_trace, (size_t)need)) return rc;

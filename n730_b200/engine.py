@@ -236,13 +236,13 @@ class Engine:
                    "model_run_step_kernel")
 
     def trace_step(self, stream: int = 0):
-        """One persistent-kernel launch with per-phase timing: (times [4 n_phases + 1, grid] ns,
+        """One persistent-kernel launch with per-phase timing: (times [6 n_phases + 1, grid] ns,
         kinds [n_phases]); see include/n730_cuda.h."""
         st = C.c_void_p(stream) if stream else None
         npz, grid = C.c_int32(), C.c_int32()
         _lib.check(self.lib.n730_model_trace_step(self.h, st, None, 0, None, C.byref(npz), C.byref(grid)),
                    "model_trace_step")
-        times = np.zeros((4 * npz.value + 1, grid.value), np.uint64)
+        times = np.zeros((6 * npz.value + 1, grid.value), np.uint64)
         kinds = np.zeros(npz.value, np.int8)
         _lib.check(self.lib.n730_model_trace_step(self.h, st, times.ctypes.data_as(C.c_void_p), times.size,
                                                   kinds.ctypes.data_as(C.c_void_p), C.byref(npz), C.byref(grid)),
