@@ -409,14 +409,18 @@ static int launch_mma2_w(int kpg, int NT, const MmaParams& p, int grid, size_t s
   return NT == 1 ? launch_mma2<16, 1, WARPS>(p, grid, smem, st, pdl) : launch_mma2<16, 2, WARPS>(p, grid, smem, st, pdl);
 }
 
-// Warps per CTA: 16 (one CTA per SM, the most bytes in flight) unless
-// N730_GEMV_WARPS=8 asks for two 8-warp CTAs per SM.
-static int mma_warps() {
-  static int w = [] {
+// Warps per CTA: 16 (one CTA per SM, the most bytes in flight), except for a
+// single-row GEMV too small to give every warp two chunks: 8, so that two CTAs
+// fit on an SM and the next kernel of a PDL chain streams its weights while this
+// one finishes (measured: batched decode is faster with 16 warps throughout).
+// N730_GEMV_WARPS=8 or 16 forces one of them.
+static int mma_warps(int64_t chunks, int batch) {
+  static int forced = [] {
     const char* e = getenv("N730_GEMV_WARPS");
-    return (e && atoi(e) == 8) ? 8 : 16;
+    return e ? atoi(e) : 0;
   }();
-  return w;
+  if (forced == 8 || forced == 16) return forced;
+  return batch > 1 || chunks >= (int64_t)num_sms() * 16 * 2 ? 16 : 8;
 }
 
 // y[b][r] = residual[b][r] + bias[r] + sum over K-blocks of part[kb][b][r], in K-block order
@@ -443,7 +447,8 @@ int gemv_mma_launch(const GemvArgs& a, cudaStream_t st) {
   N730_REQUIRE(kpg == 4 || kpg == 8 || kpg == 16, N730_UNSUPPORTED, "gemv_mma: group %d", w.group);
   N730_REQUIRE(((uintptr_t)a.x & 15) == 0 && a.ldx % 4 == 0 && (!a.norm_w || ((uintptr_t)a.norm_w & 7) == 0),
                N730_BAD_ARG, "gemv_mma: x must be 16-byte aligned with ldx %% 4 == 0");
-  const int WARPS = mma_warps();
+  const int n_tiles0 = (w.rows + 15) / 16;
+  const int WARPS = mma_warps((int64_t)n_tiles0 * ((w.n_groups * kpg + MG2_CHUNK - 1) / MG2_CHUNK), a.batch);
   MmaParams p = {};
   p.blob = w.codes;
   p.rows = w.rows; p.cols = w.cols; p.ks_n = w.cols / 16; p.G = w.n_groups;
@@ -487,6 +492,13 @@ int gemv_mma_launch(const GemvArgs& a, cudaStream_t st) {
     int nb = std::min(16, a.batch - b0);
     p.ring = MG2_RING;
     geometry(1);
+    // no more ring slots than the warp has chunks (a small GEMV then fits two CTAs per SM)
+    auto fit_ring = [&]() {
+      const int chunks_per_unit = ((p.G / p.kb_n + p.parts - 1) / p.parts * kpg + MG2_CHUNK - 1) / MG2_CHUNK;
+      const int per_warp = (p.tiles_per_cta * p.parts + WARPS - 1) / WARPS * chunks_per_unit;
+      p.ring = std::max(1, std::min(MG2_RING, per_warp));
+    };
+    fit_ring();
     while (p.ring > 2 && layout(nb) > cap) --p.ring;
     // the chunk's x fragments do not fit: split K over CTAs (partials + fold) when a workspace
     // is given, else fewer batch columns per pass
@@ -494,9 +506,13 @@ int gemv_mma_launch(const GemvArgs& a, cudaStream_t st) {
       int kb_n = 2;
       for (; kb_n <= std::min(p.G, 16); ++kb_n) {
         geometry(kb_n);
+        fit_ring();
+        while (p.ring > 2 && layout(nb) > cap) --p.ring;
         if (layout(nb) <= cap && (int64_t)kb_n * nb * w.rows <= a.split_ws_floats) break;
       }
       if (kb_n > std::min(p.G, 16)) geometry(1);
+      fit_ring();
+      while (p.ring > 2 && layout(nb) > cap) --p.ring;
     }
     while (nb > 1 && layout(nb) > cap) --nb;
     const size_t smem = layout(nb);

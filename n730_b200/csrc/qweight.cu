@@ -425,7 +425,10 @@ N730_API int n730_qlinear(void* qw, const float* d_x, int ldx, int batch, float*
   GemvArgs a = {};
   a.w = (const QWeight*)qw; a.x = d_x; a.ldx = ldx; a.batch = batch; a.y = d_y; a.ldy = ldy;
   a.bias = d_bias; a.residual = d_residual; a.ldr = ldr; a.norm_w = d_norm_w; a.eps = eps;
-  a.swiglu = swiglu; a.pdl = 0;
+  // programmatic dependent launch: the GEMV may start while the previous kernel on the stream
+  // finishes; it streams only its weights (complete when n730_qweight_create / _set_layout
+  // returned) before the dependency wait, and reads x, bias, residual and norm weights after it
+  a.swiglu = swiglu; a.pdl = 1;
   return gemv_launch(a, (cudaStream_t)stream);
 }
 
