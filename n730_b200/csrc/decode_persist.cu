@@ -139,6 +139,11 @@ __device__ __forceinline__ int ld_relaxed_sys(const int* p) {
   asm volatile("ld.relaxed.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 __device__ bool pd_xbarrier(const PdArgs& a, int xep, int k, int* flag, unsigned long long* t_arrive) {
   __syncthreads();
   if (threadIdx.x == PD_SYNC_T) {
@@ -166,7 +171,10 @@ __device__ bool pd_xbarrier(const PdArgs& a, int xep, int k, int* flag, unsigned
         break;
       }
     }
-    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    // a completed wait ends with one acquire load of the counter, which synchronises with every
+    // rank's release pattern (system fence, then relaxed arrivals); an aborted one with a fence
+    if (ok) (void)ld_acquire_sys(cnt);
+    else asm volatile("fence.acq_rel.sys;" ::: "memory");
     *flag = ok;
   }
   __syncthreads();
