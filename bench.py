@@ -13,8 +13,11 @@ decode steps run at context 2048.. with the fp16 paged KV cache.
 * ``value``: tok/s with token ids and logits resident in HBM (device-side
   decode graph), CUDA events on the model's stream.  Weights (3.76 GB) exceed
   L2 (126 MB), so every step streams them from HBM; no L2 flush is needed.
-* ``e2e``: the same through the host C-ABI call ``n730_model_decode`` with host
-  token ids in and host fp32 logits out (copies inside the timed region).
+* ``e2e``: the same through the host C-ABI call ``n730_model_decode_sample``:
+  host token ids in, the next ids sampled on the GPU (temperature 0.7, top-p
+  0.9, the reference's defaults) out, copies inside the timed region;
+  ``e2e.logits_out`` times ``n730_model_decode`` (host fp32 logits out, the
+  reference's forward() contract) beside it.
 * ``roofline``: the dominant kernel, the persistent decode kernel (one
   cooperative launch runs all 28 layers and the lm_head of a batch-1 step),
   timed alone with CUDA events on the model's stream; algorithmic bytes per
@@ -383,7 +386,7 @@ def run_ours(a):
         shape = dataclasses.replace(shape, layers=a.layers)
     headline = a.model == SHAPE_NAME and a.pmap == "int4_g128"
     B, ctx = a.batch, a.ctx
-    max_ctx = ctx + 2 * (a.warmup + a.steps) + 64  # device-side steps, then the e2e steps
+    max_ctx = ctx + 3 * (a.warmup + a.steps) + 64  # device-side steps, then the two e2e passes
     eng = Engine(shape, max_ctx=max_ctx, max_batch=B, max_prefill=512, ffn_fuse=a.ffn_fuse,
                  per_op_decode=a.per_op)
     build_on_device(shape, a.pmap, eng, seed=rank)
@@ -421,18 +424,28 @@ def run_ours(a):
         e1.record(st)
         barrier()
     t_dev = e0.elapsed_time(e1) / 1000.0
-    # ---- e2e: host ids in, host logits out, through the C ABI ----
+    # ---- e2e: host ids in, sampled next ids out (GPU temperature 0.7 / top-p 0.9 sampling), C ABI ----
     host_tok = rng.integers(0, shape.vocab, B).astype(np.int32)
+    for _ in range(2):
+        host_tok = eng.decode_sample(host_tok, 0.7, 0.9, 1234)
+    barrier()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record(st)
+    for _ in range(a.steps):
+        host_tok = eng.decode_sample(host_tok, 0.7, 0.9, 1234)
+    e3.record(st)
+    barrier()
+    t_e2e = e2.elapsed_time(e3) / 1000.0
+    # the same with host fp32 logits out (the reference's forward() contract), for comparison
     for _ in range(2):
         eng.decode(host_tok)
     barrier()
-    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2.record(st)
     for _ in range(a.steps):
         eng.decode(host_tok)
     e3.record(st)
     barrier()
-    t_e2e = e2.elapsed_time(e3) / 1000.0
+    t_e2e_logits = e2.elapsed_time(e3) / 1000.0
     # ---- roofline: the dominant kernel alone ----
     persistent = B == 1 and info["persistent_decode"]
     kv_read = info["kv_bytes_per_pos"] * (eng.seq_len(0) + 1)  # K and V of every layer, cached + new position
@@ -472,9 +485,9 @@ def run_ours(a):
 
     # max over ranks
     if world > 1:
-        tt = torch.tensor([t_dev, t_e2e, t_kern], device="cuda", dtype=torch.float64)
+        tt = torch.tensor([t_dev, t_e2e, t_kern, t_e2e_logits], device="cuda", dtype=torch.float64)
         torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
-        t_dev, t_e2e, t_kern = tt.tolist()
+        t_dev, t_e2e, t_kern, t_e2e_logits = tt.tolist()
     if rank == 0:
         peak, peak_kind = _peaks()
         achieved = kern_bytes / t_kern / 1e9
@@ -507,7 +520,9 @@ def run_ours(a):
                        "l2": f"no flush: {info['weight_bytes'] / 1e9:.2f} GB of weights stream from HBM every step "
                              "(L2 126 MB)"},
             "e2e": {"value": round(toks / t_e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
-                    "d2h_bytes_per_step": 4 * B * shape.vocab},
+                    "d2h_bytes_per_step": 8 * B, "call": "n730_model_decode_sample (next ids + draws back)",
+                    "logits_out": {"value": round(toks / t_e2e_logits, 2), "call": "n730_model_decode",
+                                   "d2h_bytes_per_step": 4 * B * shape.vocab}},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic, "kernel": kern_name,
                          "bytes_per_launch": kern_bytes, "ms_per_launch": round(t_kern * 1000, 4),
@@ -517,6 +532,7 @@ def run_ours(a):
                               "frac": round(step_bytes / (t_dev / a.steps) / 1e9 / peak, 4)},
             "clocks": clk.summary(),
             "gpu_launches": a.steps * (3 if persistent else 5 * shape.layers + 3),
+            "gpu_launches_e2e_per_step": (3 if persistent else 5 * shape.layers + 3) + 1,
             "prefill": {"tokens": B * ctx, "s": round(t_prefill, 4), "tok_per_s": round(B * ctx / t_prefill, 1),
                         "tflops": round(2 * params * B * ctx / t_prefill / 1e12, 1),
                         "path": "tcgen05 GEMM (INT4 fragment tiles dequantised to fp16 in shared memory, TMEM "
@@ -656,14 +672,15 @@ def run_tp(a):
         e1.record(st)
         barrier()
     t = e0.elapsed_time(e1) / 1000.0
-    # e2e: host token ids in, host logits (all-gathered over the ranks) out, through the C ABI
+    # e2e: host token ids in, next ids sampled on the GPU out (every rank samples the all-gathered
+    # logits with the same draws, so all ranks agree), through the C ABI
     host_tok = np.random.default_rng(3).integers(0, shape.vocab, B).astype(np.int32)
-    eng.decode(host_tok)
+    host_tok = eng.decode_sample(host_tok, 0.7, 0.9, 1234)
     barrier()
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2.record(st)
     for _ in range(a.steps):
-        eng.decode(host_tok)
+        host_tok = eng.decode_sample(host_tok, 0.7, 0.9, 1234)
     e3.record(st)
     barrier()
     t_e2e = e2.elapsed_time(e3) / 1000.0
@@ -696,7 +713,7 @@ def run_tp(a):
                           "plan_mismatch": info["tp_plan_mismatch"],
                           "l2": f"no flush: {step_bytes / 1e9:.2f} GB per rank stream from HBM every step (L2 126 MB)"},
                "e2e": {"value": round(B * a.steps / t_e2e, 3), "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
-                       "d2h_bytes_per_step": 4 * B * shape.vocab},
+                       "d2h_bytes_per_step": 8 * B, "call": "n730_model_decode_sample"},
                "roofline": {"bound": "hbm", "achieved": round(step_bytes / (t / a.steps) / 1e9, 1), "peak": peak,
                             "unit": "GB/s per GPU", "frac": round(step_bytes / (t / a.steps) / 1e9 / peak, 4),
                             "traffic": None, "kernel": "whole decode step, per-rank bytes", "peak_source": kind},

@@ -135,6 +135,15 @@ int n730_qlinear(void* qw, const float* d_x, int ldx, int batch, float* d_y, int
 int n730_qgemm(void* qw, const float* d_x, int ldx, int tokens, float* d_y, int ldy, const float* d_bias,
                const float* d_residual, int ldr, const float* d_norm_w, float eps, int swiglu, float* d_ws,
                void* stream);
+/* Next-token sampling on the GPU (replaces the host sampler, inference.py:674-682): for each
+ * of `batch` rows of d_logits (row stride ld >= vocab), temperature <= 0 gives the first index
+ * of the largest logit; otherwise temperature + nucleus (top_p) sampling with u uniform in
+ * [0, 1) from a hash of (seed, counter, row): tokens ordered by probability (ties by index),
+ * the nucleus the shortest prefix whose mass reaches top_p, the token the first whose
+ * cumulative mass exceeds u times the nucleus mass.  d_tokens [batch] int32 out; d_u [batch]
+ * receives u (may be null).  Asynchronous on `stream`. */
+int n730_sample(const float* d_logits, int batch, int vocab, int ld, float temperature, float top_p,
+                uint64_t seed, uint64_t counter, int32_t* d_tokens, float* d_u, void* stream);
 /* Group-wise quantiser on the GPU (the converter's per-group rule):
  * d_w fp32 [rows, cols] -> packed codes, fp16 scales and zeros [rows, cols/group]. */
 int n730_quantize_grouped(const float* d_w, int rows, int cols, int bits, int group, uint8_t* d_codes,
@@ -198,6 +207,11 @@ int n730_model_set_seq_len(void* model, int seq, int len);
 int n730_model_forward(void* model, int seq, const int32_t* host_tokens, int n, float* host_logits);
 /* One decode step for sequences [0, batch): host ids in, host logits [batch][vocab] out. */
 int n730_model_decode(void* model, const int32_t* host_tokens, int batch, float* host_logits);
+/* The same step followed by GPU sampling (n730_sample with counter = the number of sampled
+ * steps so far): host ids in, host next-token ids [batch] out (4 bytes per sequence cross
+ * the bus instead of the logits).  host_u [batch] receives the uniform draws (may be null). */
+int n730_model_decode_sample(void* model, const int32_t* host_tokens, int batch, float temperature, float top_p,
+                             uint64_t seed, int32_t* host_next, float* host_u);
 /* Same step with device-resident ids/logits, asynchronous on `stream`. */
 int n730_model_decode_device(void* model, const int32_t* d_tokens, int batch, float* d_logits, void* stream);
 /* info[16]: weight bytes, KV bytes per position, KV capacity bytes, splits, qkv dim, pages/seq, finalized,

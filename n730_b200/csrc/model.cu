@@ -102,6 +102,8 @@ struct Model {
   // persistent batch-1 decode (decode_persist.cu)
   bool pd_ok = false;
   bool plan_mismatch = false;
+  int32_t* d_next = nullptr;      // GPU sampling: [max_batch] next-token ids, then [max_batch] u draws
+  unsigned long long sample_steps = 0;  // sampled decode steps (the counter of the draws)
   std::vector<int8_t> pd_kinds;   // the persistent plan's phase kinds (PD_GEMV / PD_ATTN / PD_FFN), host copy
   unsigned long long* pd_trace = nullptr;  // per-phase timing buffer (n730_model_trace_step)    // tensor parallel: the ranks' persistent plans differed (per-op path)
   bool pd_ffn_fused = false;     // the persistent step runs each FFN as one phase
@@ -1111,6 +1113,46 @@ N730_API int n730_model_decode(void* p, const int32_t* host_tokens, int batch, f
   N730_CUDA(cudaStreamSynchronize(m->st));
   if (host_logits) memcpy(host_logits, m->h_logits, (size_t)batch * m->c.vocab * 4);
   for (int b = 0; b < batch; ++b) m->h_seq[b] += 1;
+  return step_status(m);
+}
+
+namespace n730 {
+int sample_launch(const float* d_logits, int batch, int vocab, int ld, float temp, float top_p,
+                  unsigned long long seed, unsigned long long counter, int32_t* d_tokens, float* d_u,
+                  cudaStream_t st);
+}
+
+// Decode one token for each of sequences [0, batch) and sample the next tokens
+// on the GPU (temperature + top-p, or greedy): host ids in, host ids out.
+N730_API int n730_model_decode_sample(void* p, const int32_t* host_tokens, int batch, float temperature,
+                                      float top_p, uint64_t seed, int32_t* host_next, float* host_u) {
+  MODEL(p);
+  N730_REQUIRE(m->finalized, N730_STATE, "model: not finalized");
+  N730_REQUIRE(host_tokens && host_next && batch >= 1 && batch <= m->c.max_batch, N730_BAD_ARG,
+               "decode_sample: batch %d", batch);
+  for (int b = 0; b < batch; ++b) {
+    N730_REQUIRE(host_tokens[b] >= 0 && host_tokens[b] < m->c.vocab, N730_BAD_ARG, "decode: token id %d out of range",
+                 host_tokens[b]);
+    if (int rc = check_capacity(m, b, 1)) return rc;
+  }
+  if (!m->d_next) {
+    if (int rc = m->alloc(&m->d_next, (size_t)2 * m->c.max_batch)) return rc;
+  }
+  memcpy(m->h_tok, host_tokens, (size_t)batch * 4);
+  N730_CUDA(cudaMemcpyAsync(m->d_tokens, m->h_tok, (size_t)batch * 4, cudaMemcpyHostToDevice, m->st));
+  if (int rc = run_decode(m, batch)) return rc;
+  float* d_u = reinterpret_cast<float*>(m->d_next + m->c.max_batch);
+  if (int rc = sample_launch(m->logits, batch, m->c.vocab, m->c.vocab, temperature, top_p, seed, m->sample_steps,
+                             m->d_next, d_u, m->st))
+    return rc;
+  // tokens and u to the pinned staging buffer (the logits staging is large enough)
+  N730_CUDA(cudaMemcpyAsync(m->h_logits, m->d_next, (size_t)batch * 4, cudaMemcpyDeviceToHost, m->st));
+  N730_CUDA(cudaMemcpyAsync(m->h_logits + batch, d_u, (size_t)batch * 4, cudaMemcpyDeviceToHost, m->st));
+  N730_CUDA(cudaStreamSynchronize(m->st));
+  memcpy(host_next, m->h_logits, (size_t)batch * 4);
+  if (host_u) memcpy(host_u, m->h_logits + batch, (size_t)batch * 4);
+  for (int b = 0; b < batch; ++b) m->h_seq[b] += 1;
+  ++m->sample_steps;
   return step_status(m);
 }
 

@@ -58,6 +58,8 @@ def _sigs(lib):
     lib.n730_model_forward.restype = i32
     lib.n730_model_decode.argtypes = [vp, vp, i32, vp]
     lib.n730_model_decode.restype = i32
+    lib.n730_model_decode_sample.argtypes = [vp, vp, i32, C.c_float, C.c_float, C.c_uint64, vp, vp]
+    lib.n730_model_decode_sample.restype = i32
     lib.n730_model_decode_device.argtypes = [vp, vp, i32, vp, vp]
     lib.n730_model_decode_device.restype = i32
     lib.n730_model_info.argtypes = [vp, i64p]
@@ -181,6 +183,18 @@ class Engine:
         _lib.check(self.lib.n730_model_decode(self.h, ids.ctypes.data_as(C.c_void_p), B,
                                               self._logits.ctypes.data_as(C.c_void_p)), "model_decode")
         return self._logits[:B]
+
+    def decode_sample(self, tokens, temperature: float = 0.7, top_p: float = 0.9, seed: int = 0,
+                      return_u: bool = False):
+        """One decode step for sequences [0, len(tokens)) with the next tokens sampled on the GPU
+        (n730_model_decode_sample): host ids in, next ids out (4 bytes per sequence)."""
+        ids = np.ascontiguousarray(tokens, np.int32).reshape(-1)
+        nxt = np.empty(ids.size, np.int32)
+        u = np.empty(ids.size, np.float32)
+        _lib.check(self.lib.n730_model_decode_sample(self.h, ids.ctypes.data_as(C.c_void_p), ids.size, temperature,
+                                                     top_p, seed, nxt.ctypes.data_as(C.c_void_p),
+                                                     u.ctypes.data_as(C.c_void_p)), "model_decode_sample")
+        return (nxt, u) if return_u else nxt
 
     def decode_device(self, d_tokens: int, batch: int, d_logits: int, stream: int = 0):
         _lib.check(self.lib.n730_model_decode_device(self.h, C.c_void_p(d_tokens) if d_tokens else None, batch,

@@ -195,6 +195,11 @@ class N730CudaTransformer:
         """Append ``token_ids`` to the sequence; float32 logits of the last position."""
         return self.engine.forward(np.asarray(token_ids, np.int32), seq=0)
 
+    def forward_sample(self, token: int, temp: float = 0.7, top_p: float = 0.9, seed: int = 0) -> int:
+        """Append one token and sample the next on the GPU (``n730_sample``): only the token id
+        crosses back to the host, not the logits."""
+        return int(self.engine.decode_sample([token], temp, top_p, seed)[0])
+
     def close(self):
         self.engine.close()
 
@@ -254,16 +259,23 @@ class N730Generator:
         self.verbose = verbose
         self.last_stats = {}
 
-    def generate(self, prompt, max_tokens=200, temp=0.7, top_p=0.9, rng=None):
+    def generate(self, prompt, max_tokens=200, temp=0.7, top_p=0.9, rng=None, gpu_sampling=True):
+        """With ``gpu_sampling`` (default) every decode step samples on the GPU (the draws are
+        seeded from ``rng``, or at random); ``gpu_sampling=False`` samples the logits on the host
+        with ``sample`` (reproducible with a numpy ``rng``)."""
         self.transformer.kv.clear()
         ids = self.tok.encode_chat(prompt)
         t0 = time.perf_counter()
         tok = sample(self.transformer.forward(ids), temp, top_p, rng)
         out = [tok]
         prefill_s = time.perf_counter() - t0
+        seed = int(rng.integers(0, 2**62)) if hasattr(rng, "integers") else int(np.random.randint(0, 2**31))
         t1 = time.perf_counter()
         while len(out) < max_tokens and tok != self.tok.eos:
-            tok = sample(self.transformer.forward([tok]), temp, top_p, rng)
+            if gpu_sampling:
+                tok = self.transformer.forward_sample(tok, temp, top_p, seed)
+            else:
+                tok = sample(self.transformer.forward([tok]), temp, top_p, rng)
             out.append(tok)
         n = max(len(out) - 1, 1)
         tps = n / max(time.perf_counter() - t1, 1e-6)
