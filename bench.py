@@ -13,11 +13,10 @@ decode steps run at context 2048.. with the fp16 paged KV cache.
 * ``value``: tok/s with token ids and logits resident in HBM (device-side
   decode graph), CUDA events on the model's stream.  Weights (3.76 GB) exceed
   L2 (126 MB), so every step streams them from HBM; no L2 flush is needed.
-* ``e2e``: the same through the host C-ABI call ``n730_model_decode_sample``:
-  host token ids in, the next ids sampled on the GPU (temperature 0.7, top-p
-  0.9, the reference's defaults) out, copies inside the timed region;
-  ``e2e.logits_out`` times ``n730_model_decode`` (host fp32 logits out, the
-  reference's forward() contract) beside it.
+* ``e2e``: the same through the host C-ABI call ``n730_model_decode`` with host
+  token ids in and host fp32 logits out (copies inside the timed region);
+  ``e2e.sampled_ids_out`` times ``n730_model_decode_sample`` (the next ids
+  sampled on the GPU, temperature 0.7 / top-p 0.9) beside it.
 * ``roofline``: the dominant kernel, the persistent decode kernel (one
   cooperative launch runs all 28 layers and the lm_head of a batch-1 step),
   timed alone with CUDA events on the model's stream; algorithmic bytes per
@@ -424,28 +423,28 @@ def run_ours(a):
         e1.record(st)
         barrier()
     t_dev = e0.elapsed_time(e1) / 1000.0
-    # ---- e2e: host ids in, sampled next ids out (GPU temperature 0.7 / top-p 0.9 sampling), C ABI ----
+    # ---- e2e: host ids in, host fp32 logits out (the reference's forward() contract), C ABI ----
     host_tok = rng.integers(0, shape.vocab, B).astype(np.int32)
     for _ in range(2):
-        host_tok = eng.decode_sample(host_tok, 0.7, 0.9, 1234)
+        eng.decode(host_tok)
     barrier()
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2.record(st)
     for _ in range(a.steps):
-        host_tok = eng.decode_sample(host_tok, 0.7, 0.9, 1234)
+        eng.decode(host_tok)
     e3.record(st)
     barrier()
     t_e2e = e2.elapsed_time(e3) / 1000.0
-    # the same with host fp32 logits out (the reference's forward() contract), for comparison
+    # the same with the next ids sampled on the GPU (temperature 0.7 / top-p 0.9) instead of logits out
     for _ in range(2):
-        eng.decode(host_tok)
+        host_tok = eng.decode_sample(host_tok, 0.7, 0.9, 1234)
     barrier()
     e2.record(st)
     for _ in range(a.steps):
-        eng.decode(host_tok)
+        host_tok = eng.decode_sample(host_tok, 0.7, 0.9, 1234)
     e3.record(st)
     barrier()
-    t_e2e_logits = e2.elapsed_time(e3) / 1000.0
+    t_e2e_sampled = e2.elapsed_time(e3) / 1000.0
     # ---- roofline: the dominant kernel alone ----
     persistent = B == 1 and info["persistent_decode"]
     kv_read = info["kv_bytes_per_pos"] * (eng.seq_len(0) + 1)  # K and V of every layer, cached + new position
@@ -485,9 +484,9 @@ def run_ours(a):
 
     # max over ranks
     if world > 1:
-        tt = torch.tensor([t_dev, t_e2e, t_kern, t_e2e_logits], device="cuda", dtype=torch.float64)
+        tt = torch.tensor([t_dev, t_e2e, t_kern, t_e2e_sampled], device="cuda", dtype=torch.float64)
         torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
-        t_dev, t_e2e, t_kern, t_e2e_logits = tt.tolist()
+        t_dev, t_e2e, t_kern, t_e2e_sampled = tt.tolist()
     if rank == 0:
         peak, peak_kind = _peaks()
         achieved = kern_bytes / t_kern / 1e9
@@ -520,9 +519,10 @@ def run_ours(a):
                        "l2": f"no flush: {info['weight_bytes'] / 1e9:.2f} GB of weights stream from HBM every step "
                              "(L2 126 MB)"},
             "e2e": {"value": round(toks / t_e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
-                    "d2h_bytes_per_step": 8 * B, "call": "n730_model_decode_sample (next ids + draws back)",
-                    "logits_out": {"value": round(toks / t_e2e_logits, 2), "call": "n730_model_decode",
-                                   "d2h_bytes_per_step": 4 * B * shape.vocab}},
+                    "d2h_bytes_per_step": 4 * B * shape.vocab, "call": "n730_model_decode (host logits out)",
+                    "sampled_ids_out": {"value": round(toks / t_e2e_sampled, 2),
+                                        "call": "n730_model_decode_sample (GPU temperature 0.7 / top-p 0.9)",
+                                        "d2h_bytes_per_step": 8 * B}},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic, "kernel": kern_name,
                          "bytes_per_launch": kern_bytes, "ms_per_launch": round(t_kern * 1000, 4),
@@ -672,15 +672,14 @@ def run_tp(a):
         e1.record(st)
         barrier()
     t = e0.elapsed_time(e1) / 1000.0
-    # e2e: host token ids in, next ids sampled on the GPU out (every rank samples the all-gathered
-    # logits with the same draws, so all ranks agree), through the C ABI
+    # e2e: host token ids in, host logits (all-gathered over the ranks) out, through the C ABI
     host_tok = np.random.default_rng(3).integers(0, shape.vocab, B).astype(np.int32)
-    host_tok = eng.decode_sample(host_tok, 0.7, 0.9, 1234)
+    eng.decode(host_tok)
     barrier()
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2.record(st)
     for _ in range(a.steps):
-        host_tok = eng.decode_sample(host_tok, 0.7, 0.9, 1234)
+        eng.decode(host_tok)
     e3.record(st)
     barrier()
     t_e2e = e2.elapsed_time(e3) / 1000.0
@@ -713,7 +712,7 @@ def run_tp(a):
                           "plan_mismatch": info["tp_plan_mismatch"],
                           "l2": f"no flush: {step_bytes / 1e9:.2f} GB per rank stream from HBM every step (L2 126 MB)"},
                "e2e": {"value": round(B * a.steps / t_e2e, 3), "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
-                       "d2h_bytes_per_step": 8 * B, "call": "n730_model_decode_sample"},
+                       "d2h_bytes_per_step": 4 * B * shape.vocab, "call": "n730_model_decode (host logits out)"},
                "roofline": {"bound": "hbm", "achieved": round(step_bytes / (t / a.steps) / 1e9, 1), "peak": peak,
                             "unit": "GB/s per GPU", "frac": round(step_bytes / (t / a.steps) / 1e9 / peak, 4),
                             "traffic": None, "kernel": "whole decode step, per-rank bytes", "peak_source": kind},

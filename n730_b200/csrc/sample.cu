@@ -17,13 +17,16 @@
 //
 // One CTA of 1024 threads per row, no full sort: masses are summed in 32.40
 // fixed point (order-independent, deterministic) into 4096 bins of
-// t = -64 (l - max) / temp (bin floor(t); the last bin also takes t >= 4095,
-// masses below 2^-41 round to 0); a scan over the bins finds the bin where the
-// cumulative mass crosses the cut (and later the sample point); only that
-// bin's elements are gathered and bitonic-sorted in shared memory.  A bin with
-// more than SP_CAP elements is split into 4096 finer bins once; elements that
-// still fall together (equal to ~4e-6 relative) are taken in index order.
-// Every pass reads the row from global memory (L2: the lm_head just wrote it).
+// t = -64 (l - max) / temp spread over the row's own range (its smallest logit,
+// capped where masses fall below 2^-43), so a near-flat row uses all bins; a
+// scan over the bins finds the bin where the cumulative mass crosses the cut
+// (and later the sample point); only that bin's elements are gathered and
+// bitonic-sorted in shared memory.  A bin with more than SP_CAP elements is
+// split into 4096 finer bins once; elements that still fall together (equal
+// to a few 1e-7 relative) are taken in index order, as are rows of equal
+// logits.  Four passes read the row (L2: the lm_head just wrote it).  The
+// temperature is applied as a multiplication by its reciprocal, so p can
+// differ from exp((l - max) / temp) by an ulp or two.
 #include <cmath>
 
 #include "common.cuh"
@@ -33,25 +36,27 @@ namespace n730 {
 constexpr int SP_THREADS = 1024;
 constexpr int SP_BINS = 4096;
 constexpr int SP_CAP = 4096;
-constexpr double SP_ONE = 1099511627776.0;  // 2^40: fixed-point unit of probability mass
+constexpr float SP_ONE = 1099511627776.f;  // 2^40: fixed-point unit of probability mass
+constexpr float SP_TMAX = 1920.f;          // bin range cap: t = 1920 is z = -30 (p < 2^-43)
 
 struct SpSmem {
   unsigned long long mass[SP_BINS];
-  unsigned int cnt[SP_BINS];
   float key[SP_CAP];
   int idx[SP_CAP];
   unsigned long long wsum[32];
   float wmax[32];
+  float wmin[32];
   int widx[32];
   int n_gather;
   int first;
+  int first_member;
   unsigned long long res_cum;
   int res_idx;
 };
 
-__device__ __forceinline__ unsigned long long sp_mass(float p) {
-  return (unsigned long long)((double)p * SP_ONE + 0.5);
-}
+// p in [0, 1] in 32.40 fixed point: p * 2^40 is exact in fp32 (an exponent shift),
+// so the conversion rounds the exact value
+__device__ __forceinline__ unsigned long long sp_mass(float p) { return __float2ull_rn(p * SP_ONE); }
 
 // splitmix64 finaliser of (seed, counter, row): 24 random bits -> u in [0, 1)
 __device__ __forceinline__ float sp_uniform(unsigned long long seed, unsigned long long counter, int row) {
@@ -61,6 +66,23 @@ __device__ __forceinline__ float sp_uniform(unsigned long long seed, unsigned lo
   x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
   x ^= x >> 31;
   return (float)(x >> 40) * (1.0f / 16777216.0f);
+}
+
+// Row geometry: p(l) = exp((l - m) / temp) (by the reciprocal), and the bin
+// coordinate x = (m - l) * sx: 4096 bins of width 1 over the row's spread
+// [0, min(64 (m - min l) / temp, SP_TMAX)) scaled to [0, 4096); the last bin also
+// takes everything beyond.  Sized to the row, so a near-flat row spreads over
+// all bins instead of piling into a few.
+struct SpGeom { float m, inv_temp, sx; };
+__device__ __forceinline__ float sp_p(float l, const SpGeom& g) { return expf((l - g.m) * g.inv_temp); }
+__device__ __forceinline__ float sp_x(float l, const SpGeom& g) { return (g.m - l) * g.sx; }
+__device__ __forceinline__ int sp_bin_of(float x) {
+  return x < (float)(SP_BINS - 1) ? max(0, (int)x) : SP_BINS - 1;  // NaN: the last bin
+}
+// finer bin inside bin b (from the same x as the bin, so the two never disagree)
+__device__ __forceinline__ int sp_sub_of(float x, int b) {
+  const float f = (x - (float)b) * (float)SP_BINS;
+  return f < (float)(SP_BINS - 1) ? max(0, (int)f) : SP_BINS - 1;
 }
 
 // Exclusive block scan of one u64 per thread; returns the exclusive prefix, *total the sum.
@@ -92,33 +114,28 @@ __device__ unsigned long long sp_scan(unsigned long long v, SpSmem& s, unsigned 
   return ex;
 }
 
-// t = 64 (max - l) / temp, the bin coordinate (the same expression in every pass)
-__device__ __forceinline__ float sp_t(float l, float m, float temp) {
-  const float z = (l - m) / temp;
-  return -z * 64.f;
-}
-
-// The elements selected by `pred(l, t)`, ordered by p descending and index
-// ascending, gathered (n <= SP_CAP of them), sorted in shared memory and
-// scanned: the first whose cumulative mass from `base` reaches `target`
-// (strict: exceeds it) goes to s.res_idx, its inclusive cumulative mass to
-// s.res_cum (rounding that leaves no crossing picks the last element).
+// The elements selected by `pred(l)`, ordered by p descending and index
+// ascending, gathered into shared memory (false, nothing picked, when there are
+// more than SP_CAP of them), bitonic-sorted and scanned: the first whose
+// cumulative mass from `base` reaches `target` (strict: exceeds it) goes to
+// s.res_idx, its inclusive cumulative mass to s.res_cum (rounding that leaves
+// no crossing picks the last element).
 template <class Pred>
-__device__ void sp_sorted_pick(const float* row, int V, float m, float temp, Pred pred, unsigned long long base,
+__device__ bool sp_sorted_pick(const float* row, int V, const SpGeom& g, Pred pred, unsigned long long base,
                                double target, bool strict, SpSmem& s) {
   const int tid = threadIdx.x;
   if (tid == 0) s.n_gather = 0;
   __syncthreads();
   for (int i = tid; i < V; i += SP_THREADS) {
     const float l = row[i];
-    if (pred(l, sp_t(l, m, temp))) {
+    if (pred(l)) {
       const int k = atomicAdd(&s.n_gather, 1);
-      s.key[k] = expf((l - m) / temp);
-      s.idx[k] = i;
+      if (k < SP_CAP) { s.key[k] = sp_p(l, g); s.idx[k] = i; }
     }
   }
   __syncthreads();
   const int n = s.n_gather;
+  if (n > SP_CAP) return false;
   int np2 = 1;
   while (np2 < n) np2 <<= 1;
   for (int k = n + tid; k < np2; k += SP_THREADS) { s.key[k] = -1.f; s.idx[k] = 0x7fffffff; }
@@ -166,84 +183,61 @@ __device__ void sp_sorted_pick(const float* row, int V, float m, float temp, Pre
     s.res_cum = cc;
   }
   __syncthreads();
+  return true;
 }
 
-// The same pick over the elements of `pred` taken in index order (for values
-// equal to within the finest bin, where the order by value is not resolved).
+// The same pick over the elements of `pred` taken in index order (values equal
+// to within the finest bin, and rows of equal logits): thread t sums the members
+// of its contiguous segment of the row, one block scan places the segments, and
+// the thread whose segment holds the crossing walks it.
 template <class Pred>
-__device__ void sp_index_pick(const float* row, int V, float m, float temp, Pred pred, unsigned long long base,
+__device__ void sp_index_pick(const float* row, int V, const SpGeom& g, Pred pred, unsigned long long base,
                               double target, bool strict, SpSmem& s) {
   const int tid = threadIdx.x;
-  for (int c0 = 0; c0 < V; c0 += SP_THREADS) {
-    const int i = c0 + tid;
-    unsigned long long v = 0;
-    if (i < V) {
-      const float l = row[i];
-      if (pred(l, sp_t(l, m, temp))) v = sp_mass(expf((l - m) / temp));
+  const int seg = (V + SP_THREADS - 1) / SP_THREADS;
+  const int i0 = min(V, tid * seg), i1 = min(V, i0 + seg);
+  auto cross = [strict, target](unsigned long long c) { return strict ? (double)c > target : (double)c >= target; };
+  unsigned long long loc = 0;
+  int first_member = 0x7fffffff;
+  for (int i = i0; i < i1; ++i) {
+    const float l = row[i];
+    if (pred(l)) {
+      loc += sp_mass(sp_p(l, g));
+      first_member = min(first_member, i);
     }
-    unsigned long long tot;
-    const unsigned long long ex = sp_scan(v, s, &tot);
-    if (tid == 0) s.first = 0x7fffffff;
-    __syncthreads();
-    const unsigned long long c = base + ex + v;
-    if (v && (strict ? (double)c > target : (double)c >= target)) atomicMin(&s.first, i);
-    __syncthreads();
-    const int f = s.first;
-    __syncthreads();
-    if (f != 0x7fffffff) {
-      if (i == f) { s.res_idx = f; s.res_cum = c; }
-      __syncthreads();
-      return;
-    }
-    base += tot;
   }
-  if (tid == 0) { s.res_idx = V - 1; s.res_cum = base; }
+  unsigned long long tot;
+  const unsigned long long ex = sp_scan(loc, s, &tot);
+  if (tid == 0) { s.first = 0x7fffffff; s.first_member = 0x7fffffff; }
+  __syncthreads();
+  const unsigned long long c0 = base + ex, c1 = c0 + loc;
+  if (!cross(c0) && cross(c1)) atomicMin(&s.first, tid);
+  if (first_member != 0x7fffffff) atomicMin(&s.first_member, first_member);
+  __syncthreads();
+  if (s.first == 0x7fffffff) {  // crossed before the first member (its first member), or never (the last)
+    if (tid == 0) {
+      const bool before = cross(base);
+      s.res_idx = before ? (s.first_member == 0x7fffffff ? 0 : s.first_member) : V - 1;
+      s.res_cum = base + (before ? 0ull : tot);
+    }
+  } else if (tid == s.first) {
+    unsigned long long c = c0;
+    for (int i = i0; i < i1; ++i) {
+      const float l = row[i];
+      if (pred(l)) {
+        c += sp_mass(sp_p(l, g));
+        if (cross(c)) { s.res_idx = i; s.res_cum = c; break; }
+      }
+    }
+  }
   __syncthreads();
 }
 
-// Among the row's elements with t in [lo, hi) (hi < 0: no upper limit), ordered
-// by p descending and index ascending, the first whose cumulative mass from
-// `base` reaches `target` (strict: exceeds it): s.res_idx, s.res_cum.
-__device__ void sp_find(const float* row, int V, float m, float temp, float lo, float hi, unsigned long long base,
-                        double target, bool strict, SpSmem& s) {
+// First bin (of masses mb[4] per thread, exclusive prefix ex) whose inclusive cumulative mass from
+// `base` reaches `target` (strict: exceeds it); *before = the cumulative mass ahead of it.
+__device__ int sp_cross_bin(const unsigned long long (&mb)[4], unsigned long long ex, unsigned long long base,
+                            double target, bool strict, SpSmem& s, unsigned long long* before) {
   const int tid = threadIdx.x;
-  auto in_range = [lo, hi](float, float t) { return t >= lo && (hi < 0.f || t < hi); };
-  if (tid == 0) s.n_gather = 0;
-  __syncthreads();
-  int cnt = 0;
-  for (int i = tid; i < V; i += SP_THREADS) cnt += in_range(0.f, sp_t(row[i], m, temp));
-  if (cnt) atomicAdd(&s.n_gather, cnt);
-  __syncthreads();
-  const int n = s.n_gather;
-  __syncthreads();
-  if (n <= SP_CAP) {
-    sp_sorted_pick(row, V, m, temp, in_range, base, target, strict, s);
-    return;
-  }
-  if (hi < 0.f) {  // the open last bin (masses ~0): index order
-    sp_index_pick(row, V, m, temp, in_range, base, target, strict, s);
-    return;
-  }
-  // too many elements: 4096 finer bins over [lo, hi), then the one holding the crossing
-  const float w = (hi - lo) / (float)SP_BINS;
-  auto sub = [lo, w](float t) { return min(SP_BINS - 1, max(0, (int)((t - lo) / w))); };
-  for (int b = tid; b < SP_BINS; b += SP_THREADS) { s.mass[b] = 0ull; s.cnt[b] = 0u; }
-  __syncthreads();
-  for (int i = tid; i < V; i += SP_THREADS) {
-    const float l = row[i];
-    const float t = sp_t(l, m, temp);
-    if (in_range(l, t)) {
-      const int b = sub(t);
-      atomicAdd(&s.mass[b], sp_mass(expf((l - m) / temp)));
-      atomicAdd(&s.cnt[b], 1u);
-    }
-  }
-  __syncthreads();
-  unsigned long long mb[4], loc = 0;
-#pragma unroll
-  for (int r = 0; r < 4; ++r) { mb[r] = s.mass[tid * 4 + r]; loc += mb[r]; }
-  unsigned long long tot;
-  const unsigned long long ex = sp_scan(loc, s, &tot);
   if (tid == 0) s.first = 0x7fffffff;
   __syncthreads();
   unsigned long long c = base + ex;
@@ -261,12 +255,40 @@ __device__ void sp_find(const float* row, int V, float m, float temp, float lo, 
     s.res_cum = cc;
   }
   __syncthreads();
-  const unsigned long long before = s.res_cum;
-  const unsigned int nb = s.cnt[b];
+  *before = s.res_cum;
   __syncthreads();
-  auto in_sub = [in_range, sub, b](float l, float t) { return in_range(l, t) && sub(t) == b; };
-  if (nb <= (unsigned)SP_CAP) sp_sorted_pick(row, V, m, temp, in_sub, before, target, strict, s);
-  else sp_index_pick(row, V, m, temp, in_sub, before, target, strict, s);
+  return b;
+}
+
+// Inside bin b (cumulative mass `base` ahead of it): the element where the
+// cumulative mass reaches / exceeds `target` -> s.res_idx, s.res_cum.  A bin of
+// more than SP_CAP elements is split into 4096 finer bins, and a finer bin that
+// is still crowded is walked in index order.
+__device__ void sp_pick_in_bin(const float* row, int V, const SpGeom& g, int b, unsigned long long base,
+                               double target, bool strict, SpSmem& s) {
+  const int tid = threadIdx.x;
+  auto in_bin = [g, b](float l) { return sp_bin_of(sp_x(l, g)) == b; };
+  if (sp_sorted_pick(row, V, g, in_bin, base, target, strict, s)) return;
+  for (int q = tid; q < SP_BINS; q += SP_THREADS) s.mass[q] = 0ull;
+  __syncthreads();
+  for (int i = tid; i < V; i += SP_THREADS) {
+    const float l = row[i];
+    const float x = sp_x(l, g);
+    if (sp_bin_of(x) == b) atomicAdd(&s.mass[sp_sub_of(x, b)], sp_mass(sp_p(l, g)));
+  }
+  __syncthreads();
+  unsigned long long mb[4], loc = 0;
+#pragma unroll
+  for (int r = 0; r < 4; ++r) { mb[r] = s.mass[tid * 4 + r]; loc += mb[r]; }
+  unsigned long long tot, before;
+  const unsigned long long ex = sp_scan(loc, s, &tot);
+  const int q = sp_cross_bin(mb, ex, base, target, strict, s, &before);
+  auto in_sub = [g, b, q](float l) {
+    const float x = sp_x(l, g);
+    return sp_bin_of(x) == b && sp_sub_of(x, b) == q;
+  };
+  if (!sp_sorted_pick(row, V, g, in_sub, before, target, strict, s))
+    sp_index_pick(row, V, g, in_sub, before, target, strict, s);  // values equal to a few 1e-7
 }
 
 __global__ void __launch_bounds__(SP_THREADS, 1)
@@ -276,50 +298,70 @@ sample_kernel(const float* logits, int ld, int V, float temp, float top_p, unsig
   SpSmem& s = *reinterpret_cast<SpSmem*>(sp_raw);
   const int row_i = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const float* row = logits + (int64_t)row_i * ld;
-  // 1. max and its first index
-  float bv = -INFINITY;
+  // 1. the largest logit with its first index, and the smallest logit
+  float bv = -INFINITY, mn = INFINITY;
   int bi = 0x7fffffff;
   for (int i = tid; i < V; i += SP_THREADS) {
     const float v = row[i];
     if (v > bv) { bv = v; bi = i; }  // strided: the first index of this thread's maximum
+    mn = fminf(mn, v);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
     const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
     if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
   }
-  if (lane == 0) { s.wmax[warp] = bv; s.widx[warp] = bi; }
+  if (lane == 0) { s.wmax[warp] = bv; s.widx[warp] = bi; s.wmin[warp] = mn; }
   __syncthreads();
   if (warp == 0) {
     bv = s.wmax[lane];
     bi = s.widx[lane];
+    mn = s.wmin[lane];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
       const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
       if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+      mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
     }
-    if (lane == 0) { s.wmax[0] = bv; s.widx[0] = bi; }
+    if (lane == 0) { s.wmax[0] = bv; s.widx[0] = bi; s.wmin[0] = mn; }
   }
   __syncthreads();
   const float m = s.wmax[0];
   const int amax = s.widx[0];
+  const float lmin = s.wmin[0];
+  __syncthreads();
   const float u = temp > 0.f ? sp_uniform(seed, counter, row_i) : 0.f;
   if (tid == 0 && u_out) u_out[row_i] = u;
   if (!(temp > 0.f)) {
     if (tid == 0) tokens[row_i] = amax;
     return;
   }
+  const float inv_temp = 1.0f / temp;
+  const float R = fminf((m - lmin) * 64.f * inv_temp, SP_TMAX);
+  if (!(R > 0.f)) {
+    // every logit equal: equal probabilities, taken in index order
+    const SpGeom g{m, inv_temp, 0.f};
+    auto all = [](float) { return true; };
+    const unsigned long long total = (unsigned long long)V * sp_mass(1.f);
+    unsigned long long nucleus = total;
+    if (top_p < 1.f) {
+      sp_index_pick(row, V, g, all, 0ull, (double)top_p * (double)total, false, s);
+      nucleus = s.res_cum;
+    }
+    sp_index_pick(row, V, g, all, 0ull, (double)u * (double)nucleus, true, s);
+    if (tid == 0) tokens[row_i] = s.res_idx;
+    return;
+  }
+  const SpGeom g{m, inv_temp, 64.f * inv_temp * ((float)SP_BINS / R)};
   // 2. masses per bin
-  for (int b = tid; b < SP_BINS; b += SP_THREADS) { s.mass[b] = 0ull; s.cnt[b] = 0u; }
+  for (int b = tid; b < SP_BINS; b += SP_THREADS) s.mass[b] = 0ull;
   __syncthreads();
   for (int i = tid; i < V; i += SP_THREADS) {
     const float l = row[i];
-    const float t = sp_t(l, m, temp);
-    const int b = t < (float)(SP_BINS - 1) ? max(0, (int)t) : SP_BINS - 1;  // NaN: the last bin
-    atomicAdd(&s.mass[b], sp_mass(expf((l - m) / temp)));
-    atomicAdd(&s.cnt[b], 1u);
+    atomicAdd(&s.mass[sp_bin_of(sp_x(l, g))], sp_mass(sp_p(l, g)));
   }
   __syncthreads();
   unsigned long long mb[4], loc = 0;
@@ -327,56 +369,21 @@ sample_kernel(const float* logits, int ld, int V, float temp, float top_p, unsig
   for (int r = 0; r < 4; ++r) { mb[r] = s.mass[tid * 4 + r]; loc += mb[r]; }
   unsigned long long total;
   const unsigned long long ex = sp_scan(loc, s, &total);
-  // 3. nucleus: the bin where the cumulative mass reaches top_p of the total, then the element
+  // (mb / ex stay in registers: the finer bins of a crowded bin reuse s.mass)
+  // 3. nucleus: where the cumulative mass reaches top_p of the total
   unsigned long long nucleus = total;
   if (top_p < 1.f) {
     const double target = (double)top_p * (double)total;
-    if (tid == 0) s.first = 0x7fffffff;
-    __syncthreads();
-    unsigned long long c = ex;
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      c += mb[r];
-      if ((double)c >= target) { atomicMin(&s.first, tid * 4 + r); break; }
-    }
-    __syncthreads();
-    const int b = s.first == 0x7fffffff ? SP_BINS - 1 : s.first;
-    __syncthreads();
-    if (tid == b / 4) {
-      unsigned long long cc = ex;
-      for (int r = 0; r < b % 4; ++r) cc += mb[r];
-      s.res_cum = cc;
-    }
-    __syncthreads();
-    const unsigned long long before = s.res_cum;
-    __syncthreads();
-    sp_find(row, V, m, temp, (float)b, b == SP_BINS - 1 ? -1.f : (float)(b + 1), before, target, false, s);
+    unsigned long long before;
+    const int b = sp_cross_bin(mb, ex, 0ull, target, false, s, &before);
+    sp_pick_in_bin(row, V, g, b, before, target, false, s);
     nucleus = s.res_cum;
   }
-  // 4. the sample: first element of the nucleus whose cumulative mass exceeds u * nucleus
+  // 4. the sample: the first element whose cumulative mass exceeds u * nucleus
   const double r = (double)u * (double)nucleus;
-  if (tid == 0) s.first = 0x7fffffff;
-  __syncthreads();
-  {
-    unsigned long long c = ex;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      c += mb[q];
-      if ((double)c > r) { atomicMin(&s.first, tid * 4 + q); break; }
-    }
-  }
-  __syncthreads();
-  const int b = s.first == 0x7fffffff ? SP_BINS - 1 : s.first;
-  __syncthreads();
-  if (tid == b / 4) {
-    unsigned long long cc = ex;
-    for (int q = 0; q < b % 4; ++q) cc += mb[q];
-    s.res_cum = cc;
-  }
-  __syncthreads();
-  const unsigned long long before = s.res_cum;
-  __syncthreads();
-  sp_find(row, V, m, temp, (float)b, b == SP_BINS - 1 ? -1.f : (float)(b + 1), before, r, true, s);
+  unsigned long long before;
+  const int c = sp_cross_bin(mb, ex, 0ull, r, true, s, &before);
+  sp_pick_in_bin(row, V, g, c, before, r, true, s);
   if (tid == 0) tokens[row_i] = s.res_idx;
 }
 
