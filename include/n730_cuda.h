@@ -144,6 +144,16 @@ int n730_qgemm(void* qw, const float* d_x, int ldx, int tokens, float* d_y, int 
  * receives u (may be null).  Asynchronous on `stream`. */
 int n730_sample(const float* d_logits, int batch, int vocab, int ld, float temperature, float top_p,
                 uint64_t seed, uint64_t counter, int32_t* d_tokens, float* d_u, void* stream);
+/* Load packed-weight blocks of a .n730 file onto the current device without an intermediate
+ * host copy (replaces the per-call Python reads of inference.py:355-366 and the read + dequant
+ * of n730core.cpp:192-248): block i at absolute offset offsets[i] becomes out_handles[i] (as
+ * n730_qweight_create).  Blocks are read with pread into two page-aligned pinned buffers, so
+ * the read of one overlaps the copy and conversion of the previous on `stream`.  Per-tensor
+ * ids 2/4/8/16 and group-wise 0x42/0x44/0x48; N730_UNSUPPORTED for a per-tensor block whose
+ * payload is not its packed codes.  bytes_read (may be null): block bytes read.  On error no
+ * handle is left allocated. */
+int n730_qweight_load_blocks(const char* path, int n, const int64_t* offsets, void* stream, void** out_handles,
+                             int64_t* bytes_read);
 /* Group-wise quantiser on the GPU (the converter's per-group rule):
  * d_w fp32 [rows, cols] -> packed codes, fp16 scales and zeros [rows, cols/group]. */
 int n730_quantize_grouped(const float* d_w, int rows, int cols, int bits, int group, uint8_t* d_codes,

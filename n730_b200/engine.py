@@ -13,7 +13,7 @@ from dataclasses import dataclass
 import numpy as np
 
 from . import _lib
-from .formats import RawBlock, GROUPED
+from .formats import RawBlock, GROUPED, read_block, read_header
 
 W_Q, W_K, W_V, W_O, W_GATE, W_UP, W_DOWN, W_EMBED, W_LMHEAD = range(9)
 V_INPUT_NORM, V_POST_NORM, V_Q_BIAS, V_K_BIAS, V_V_BIAS, V_O_BIAS, V_GATE_BIAS, V_UP_BIAS, V_DOWN_BIAS, \
@@ -320,3 +320,65 @@ def load_tensors(engine: Engine, named_blocks, norms: dict | None = None):
             engine.set_vector(int(name.split(".")[2]), V_INPUT_NORM, v)
         elif name.startswith("model.layers.") and name.endswith("post_attention_layernorm.weight"):
             engine.set_vector(int(name.split(".")[2]), V_POST_NORM, v)
+
+def _weight_slot(name: str):
+    """(layer, slot) of a 2-D weight tensor the engine holds, else None."""
+    if name == "model.embed_tokens.weight":
+        return -1, W_EMBED
+    if name == "lm_head.weight":
+        return -1, W_LMHEAD
+    if name.startswith("model.layers.") and name.endswith(".weight"):
+        i, _, tail = name[len("model.layers."):].partition(".")
+        base = tail.rpartition(".")[0]
+        if base in PROJ_SLOTS:
+            return int(i), PROJ_SLOTS[base]
+    return None
+
+
+def qweights_from_file(path, offsets, stream=None):
+    """Packed weights of the blocks at `offsets` through the native loader (n730_qweight_load_blocks:
+    pread into pinned staging, asynchronous copies to HBM); returns handles and bytes read."""
+    lib = _lib.cuda()
+    n = len(offsets)
+    offs = np.ascontiguousarray(offsets, np.int64)
+    out = (C.c_void_p * max(n, 1))()
+    nbytes = C.c_int64()
+    _lib.check(lib.n730_qweight_load_blocks(str(path).encode(), n, offs.ctypes.data_as(C.c_void_p),
+                                            C.c_void_p(stream) if stream else None, out, C.byref(nbytes)),
+               "qweight_load_blocks")
+    return [C.c_void_p(out[i]) for i in range(n)], int(nbytes.value)
+
+
+def load_file(engine: Engine, path, norms: dict | None = None) -> dict:
+    """Hand a ``.n730`` file's tensors to the engine: every 2-D weight through the native block
+    loader in one call, 1-D vectors (q/k/v biases, FP16 norm weights) read in Python.  A
+    per-tensor block the native loader leaves to Python (the reference's odd-length INT4/INT2
+    packing) is read by ``read_block``.  Returns {"native_blocks", "native_bytes", "python_blocks"}."""
+    hdr = read_header(path)
+    big, small = [], []
+    for e in hdr["seek_table"]:
+        slot = _weight_slot(e["layer_name"])
+        (big if slot else small).append((e["layer_name"], e["file_offset"], slot))
+    stats = {"native_blocks": 0, "native_bytes": 0, "python_blocks": len(small)}
+    try:
+        handles, nbytes = qweights_from_file(path, [off for _, off, _ in big])
+        stats.update(native_blocks=len(big), native_bytes=nbytes)
+    except _lib.N730Error as ex:
+        if ex.code != -14:
+            raise
+        handles = []
+        for _, off, _ in big:  # one by one, the blocks the native reader declines through Python
+            try:
+                h, nb = qweights_from_file(path, [off])
+                handles.append(h[0])
+                stats["native_blocks"] += 1
+                stats["native_bytes"] += nb
+            except _lib.N730Error as e2:
+                if e2.code != -14:
+                    raise
+                handles.append(qweight_from_block(read_block(path, off)))
+                stats["python_blocks"] += 1
+    for (_, _, (layer, slot)), h in zip(big, handles):
+        engine.set_qweight(layer, slot, h)
+    load_tensors(engine, [(name, read_block(path, off)) for name, off, _ in small], norms)
+    return stats

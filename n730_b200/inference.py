@@ -20,7 +20,7 @@ from typing import Dict, Optional
 import numpy as np
 
 from . import _lib, model_compat
-from .engine import Engine, ModelShape, load_tensors
+from .engine import Engine, ModelShape, load_file, load_tensors
 from .formats import read_block, read_header
 from .scheduler import N730Scheduler
 
@@ -169,10 +169,8 @@ class N730CudaTransformer:
             self.norm_w = _load_hf_norms(hf_path)
         max_ctx = max_ctx or min(int(cfg.max_position_embeddings), 4096)
         self.engine = Engine(cfg.shape(tie_embeddings=tied), max_ctx=max_ctx, **engine_kw)
-        with open(model_path, "rb") as f:
-            blocks = [(e["layer_name"], read_block(model_path, e["file_offset"], f)) for e in self._seek_table]
-        load_tensors(self.engine, blocks, self.norm_w)
-        del blocks
+        # 2-D weights through the native block loader (pread into pinned staging, async copies)
+        self.load_stats = load_file(self.engine, model_path, self.norm_w)
         self.engine.finalize()
         self.kv = VRAMKVCache(self.engine)
         if verbose:
