@@ -16,6 +16,8 @@ Outputs (small, committed):
 * ``ref_small.npz``        - per tensor: the reference ``read_layer`` output,
                              the reference ``n730core`` ``n730_read_layer``
                              output, rows/cols/prec, and the input weights.
+* ``ref_profiler.npz``     - the reference profiler's sensitivity scores and
+                             statistics on seeded tensors (``profiler_cases``).
 * ``ref_linear4096.npz``   - the single quantised linear W[4096x4096] ~ N(0,0.02)
                              (``default_rng(0)``) converted by the reference to
                              per-tensor INT4: code SHA-256, scale, zero point,
@@ -56,11 +58,44 @@ def _small_tensors():
     return t
 
 
+def profiler_cases():
+    """Seeded tensors for the sensitivity score: (seed, rows, cols, std, outlier share, layer, layers).
+    ``profiler_tensor`` regenerates each one; the tests use the same two functions."""
+    return [(1, 512, 256, 0.02, 0.0, 0, 32), (2, 512, 256, 0.035, 0.0, 16, 32), (3, 512, 256, 0.04, 0.06, 31, 32),
+            (4, 3000, 1500, 0.03, 0.01, 5, 32), (5, 64, 64, 0.0, 0.0, 7, 9)]
+
+
+def profiler_tensor(seed, rows, cols, std, outliers):
+    rng = np.random.default_rng(seed)
+    w = rng.normal(0, std, (rows, cols)).astype(np.float32) if std > 0 else np.full((rows, cols), 0.5, np.float32)
+    if outliers:
+        n = int(w.size * outliers)
+        idx = rng.choice(w.size, n, replace=False)
+        w.flat[idx] = rng.choice([-1, 1], n) * rng.uniform(0.3, 0.8, n)
+    return w
+
+
+def write_profiler_golden(ref: Path):
+    """The reference profiler's own sensitivity scores (src-code/profiler.py:50-89) on seeded tensors."""
+    sys.path.insert(0, str(ref / "src-code"))
+    import profiler  # the reference profiler, unmodified
+    cases = profiler_cases()
+    scores = [profiler.compute_sensitivity(profiler_tensor(*c[:5]), c[5], c[6]) for c in cases]
+    prof = [profiler.profile_weight_tensor(profiler_tensor(*c[:5]), c[5], f"t{i}", c[6]) for i, c in enumerate(cases)]
+    np.savez_compressed(HERE / "ref_profiler.npz", cases=np.array(cases, np.float64), scores=np.array(scores),
+                        std=np.array([p.weight_std for p in prof]), kurtosis=np.array([p.weight_kurtosis for p in prof]),
+                        outlier_ratio=np.array([p.outlier_ratio for p in prof]))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref-root", required=True, help="root of the reference checkout (holds src-code/)")
+    ap.add_argument("--only", choices=["profiler"], help="write one fixture only")
     args = ap.parse_args()
     ref = Path(args.ref_root)
+    if args.only == "profiler":
+        write_profiler_golden(ref)
+        return
     sys.path.insert(0, str(ref / "src-code"))
     import converter  # the reference converter, unmodified
 
@@ -129,6 +164,7 @@ def main():
         sample_idx=idx, sample_dequant=Wd.reshape(-1)[idx].astype(np.float32),
         dequant_sum=np.float64(Wd.astype(np.float64).sum()),
         x=x, y=y.astype(np.float32))
+    write_profiler_golden(ref)
     print("wrote", sorted(p.name for p in HERE.iterdir() if p.suffix in (".n730", ".npz", ".json")))
 
 
