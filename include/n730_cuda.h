@@ -191,6 +191,9 @@ typedef struct N730ModelConfig {
   int32_t tp_allreduce;  /* tensor parallel, decode-sized row-split sums: 0 one-shot over peer memory
                             (CUDA IPC, after n730_model_tp_ipc_open), fused with the residual add;
                             1 NCCL allreduce always */
+  int32_t kv_pool_pages; /* pages in the KV pool shared by the sequences (0: max_batch x pages per
+                            sequence); a sequence takes pages as it grows and returns them when
+                            released (n730_model_seq_release) */
 } N730ModelConfig;
 
 /* weight slots (n730_model_set_qweight); EMBED/LMHEAD take layer = -1 */
@@ -224,6 +227,13 @@ int n730_model_decode_sample(void* model, const int32_t* host_tokens, int batch,
                              uint64_t seed, int32_t* host_next, float* host_u);
 /* Same step with device-resident ids/logits, asynchronous on `stream`. */
 int n730_model_decode_device(void* model, const int32_t* d_tokens, int batch, float* d_logits, void* stream);
+/* Release a sequence (its KV pages return to the pool, its length becomes 0). */
+int n730_model_seq_release(void* model, int seq);
+/* Move sequence src (page ids, length) into the empty slot dst (no KV data moves); src becomes
+ * empty.  Decode steps run slots [0, batch): finished sequences are replaced by the last. */
+int n730_model_seq_move(void* model, int dst, int src);
+/* KV page pool: free and total pages. */
+int n730_model_kv_pages(void* model, int* free_pages, int* total_pages);
 /* info[16]: weight bytes, KV bytes per position, KV capacity bytes, splits, qkv dim, pages/seq, finalized,
  * persistent batch-1 decode, untied embedding bytes, streamed bytes per pass, FFN fused, phase table in
  * global memory, tensor-parallel plan mismatch (every rank fell back to per-op), persistent grid. */

@@ -88,6 +88,12 @@ struct Model {
   int* seq_lens = nullptr;
   std::vector<int> h_seq;
   int max_pages = 0, n_split = 1;
+  // paged KV pool: pages are handed to a sequence as its length grows and returned when it is
+  // released; h_bt mirrors the device block table [max_batch][max_pages]
+  std::vector<int> free_pages;
+  std::vector<std::vector<int>> seq_pages;
+  std::vector<int> h_bt;
+  int pool_pages = 0;
   // decode workspace
   int* d_tokens = nullptr;
   float *x = nullptr, *x2 = nullptr, *qkv = nullptr, *attn = nullptr, *mlp = nullptr, *logits = nullptr;
@@ -636,9 +642,12 @@ static int finalize(Model* m) {
     if (int rc = upload_vec(m, hc, &m->cos_t)) return rc;
     if (int rc = upload_vec(m, hs, &m->sin_t)) return rc;
   }
-  // paged KV: sequence b owns pages [b*max_pages, (b+1)*max_pages)
+  // paged KV: a pool of pages (max_batch x pages per sequence unless kv_pool_pages asks for fewer),
+  // handed to sequences as they grow (ensure_pages) and returned when they are released
   m->max_pages = (c.max_ctx + c.page_size - 1) / c.page_size;
-  const size_t pages = (size_t)c.max_batch * m->max_pages;
+  const size_t table = (size_t)c.max_batch * m->max_pages;
+  const size_t pages = c.kv_pool_pages > 0 ? std::min(table, (size_t)c.kv_pool_pages) : table;
+  m->pool_pages = (int)pages;
   const size_t per_layer = pages * c.kv_heads * c.page_size * c.head_dim;
   if (int rc = m->alloc(&m->k_pool, per_layer * nl)) return rc;
   if (int rc = m->alloc(&m->v_pool, per_layer * nl)) return rc;
@@ -646,10 +655,13 @@ static int finalize(Model* m) {
   N730_CUDA(cudaMemsetAsync(m->v_pool, 0, per_layer * nl * sizeof(__half), m->st));
   for (int l = 0; l < nl; ++l) m->L[l].kv = KVLayer{m->k_pool + per_layer * l, m->v_pool + per_layer * l};
   {
-    std::vector<int> bt(pages);
-    for (size_t i = 0; i < pages; ++i) bt[i] = (int)i;
-    if (int rc = m->alloc(&m->block_table, pages)) return rc;
-    N730_CUDA(cudaMemcpyAsync(m->block_table, bt.data(), pages * 4, cudaMemcpyHostToDevice, m->st));
+    // unassigned entries point at page 0 (in bounds); kernels read entries below a sequence's length only
+    m->h_bt.assign(table, 0);
+    if (int rc = m->alloc(&m->block_table, table)) return rc;
+    N730_CUDA(cudaMemcpyAsync(m->block_table, m->h_bt.data(), table * 4, cudaMemcpyHostToDevice, m->st));
+    m->free_pages.resize(pages);
+    for (size_t i = 0; i < pages; ++i) m->free_pages[i] = (int)(pages - 1 - i);  // page 0 handed out first
+    m->seq_pages.assign(c.max_batch, {});
   }
   if (int rc = m->alloc(&m->seq_lens, c.max_batch)) return rc;
   N730_CUDA(cudaMemsetAsync(m->seq_lens, 0, c.max_batch * 4, m->st));
@@ -841,9 +853,31 @@ static int run_decode(Model* m, int B) {
   return N730_OK;
 }
 
+// Give sequence b pages for positions [0, len) from the pool and upload its new block-table
+// entries (asynchronously on the model stream, ahead of the kernels that read them).
+static int ensure_pages(Model* m, int b, int len) {
+  const int need = (len + m->c.page_size - 1) / m->c.page_size;
+  std::vector<int>& own = m->seq_pages[b];
+  const int have = (int)own.size();
+  if (need <= have) return N730_OK;
+  N730_REQUIRE(need - have <= (int)m->free_pages.size(), N730_STATE,
+               "KV page pool exhausted: sequence %d needs %d more pages, %zu free of %d", b, need - have,
+               m->free_pages.size(), m->pool_pages);
+  for (int k = have; k < need; ++k) {
+    own.push_back(m->free_pages.back());
+    m->free_pages.pop_back();
+    m->h_bt[(size_t)b * m->max_pages + k] = own.back();
+  }
+  const size_t o = (size_t)b * m->max_pages + have;
+  N730_CUDA(cudaMemcpyAsync(m->block_table + o, m->h_bt.data() + o, (size_t)(need - have) * 4, cudaMemcpyHostToDevice,
+                            m->st));
+  return N730_OK;
+}
+
 static int check_capacity(Model* m, int b, int add) {
   N730_REQUIRE(m->h_seq[b] + add <= m->c.max_ctx, N730_STATE,
                "KV cache capacity exceeded: %d tokens requested, maximum is %d", m->h_seq[b] + add, m->c.max_ctx);
+  if (int rc = ensure_pages(m, b, m->h_seq[b] + add)) return rc;
   return N730_OK;
 }
 
@@ -1046,9 +1080,17 @@ N730_API int n730_model_finalize(void* p) {
   return finalize(m);
 }
 
+// Return sequence b's pages to the pool (its length becomes 0).
+static void release_pages(Model* m, int b) {
+  for (int k = (int)m->seq_pages[b].size() - 1; k >= 0; --k) m->free_pages.push_back(m->seq_pages[b][k]);
+  m->seq_pages[b].clear();
+}
+
 N730_API int n730_model_reset(void* p) {
   MODEL(p);
   N730_REQUIRE(m->finalized, N730_STATE, "model: not finalized");
+  N730_CUDA(cudaStreamSynchronize(m->st));
+  for (int b = 0; b < m->c.max_batch; ++b) release_pages(m, b);
   std::fill(m->h_seq.begin(), m->h_seq.end(), 0);
   N730_CUDA(cudaMemsetAsync(m->seq_lens, 0, m->c.max_batch * 4, m->st));
   N730_CUDA(cudaStreamSynchronize(m->st));
@@ -1062,9 +1104,53 @@ N730_API int n730_model_set_seq_len(void* p, int seq, int len) {
   MODEL(p);
   N730_REQUIRE(m->finalized && seq >= 0 && seq < m->c.max_batch && len >= 0 && len <= m->c.max_ctx,
                N730_BAD_ARG, "set_seq_len: bad sequence %d or length %d", seq, len);
+  if (int rc = ensure_pages(m, seq, len)) return rc;
   m->h_seq[seq] = len;
   N730_CUDA(cudaMemcpyAsync(m->seq_lens + seq, &m->h_seq[seq], 4, cudaMemcpyHostToDevice, m->st));
   N730_CUDA(cudaStreamSynchronize(m->st));
+  return N730_OK;
+}
+
+// Release sequence `seq`: its pages go back to the pool and its length becomes 0.
+N730_API int n730_model_seq_release(void* p, int seq) {
+  MODEL(p);
+  N730_REQUIRE(m->finalized && seq >= 0 && seq < m->c.max_batch, N730_BAD_ARG, "seq_release: bad sequence %d", seq);
+  N730_CUDA(cudaStreamSynchronize(m->st));  // no kernel of an earlier step still reads its pages
+  release_pages(m, seq);
+  m->h_seq[seq] = 0;
+  N730_CUDA(cudaMemcpyAsync(m->seq_lens + seq, &m->h_seq[seq], 4, cudaMemcpyHostToDevice, m->st));
+  N730_CUDA(cudaStreamSynchronize(m->st));
+  return N730_OK;
+}
+
+// Move sequence `src` (pages, block-table row, length) into the empty slot `dst`; src becomes empty.
+// Decode steps run sequences [0, batch), so a batch is compacted by moving its last sequence into
+// the slot of one that finished: no KV data moves, only the row of page ids.
+N730_API int n730_model_seq_move(void* p, int dst, int src) {
+  MODEL(p);
+  const int B = m->c.max_batch;
+  N730_REQUIRE(m->finalized && dst >= 0 && dst < B && src >= 0 && src < B && dst != src, N730_BAD_ARG,
+               "seq_move: bad slots %d <- %d", dst, src);
+  N730_REQUIRE(m->seq_pages[dst].empty() && m->h_seq[dst] == 0, N730_STATE, "seq_move: slot %d is not empty", dst);
+  N730_CUDA(cudaStreamSynchronize(m->st));
+  m->seq_pages[dst].swap(m->seq_pages[src]);
+  const size_t P = m->max_pages;
+  for (size_t k = 0; k < P; ++k) m->h_bt[dst * P + k] = m->h_bt[src * P + k];
+  m->h_seq[dst] = m->h_seq[src];
+  m->h_seq[src] = 0;
+  N730_CUDA(cudaMemcpyAsync(m->block_table + dst * P, m->h_bt.data() + dst * P, P * 4, cudaMemcpyHostToDevice, m->st));
+  N730_CUDA(cudaMemcpyAsync(m->seq_lens + dst, &m->h_seq[dst], 4, cudaMemcpyHostToDevice, m->st));
+  N730_CUDA(cudaMemcpyAsync(m->seq_lens + src, &m->h_seq[src], 4, cudaMemcpyHostToDevice, m->st));
+  N730_CUDA(cudaStreamSynchronize(m->st));
+  return N730_OK;
+}
+
+// KV page pool: *free_pages and *total_pages (pages of page_size positions).
+N730_API int n730_model_kv_pages(void* p, int* free_pages, int* total_pages) {
+  MODEL(p);
+  N730_REQUIRE(m->finalized, N730_STATE, "model: not finalized");
+  if (free_pages) *free_pages = (int)m->free_pages.size();
+  if (total_pages) *total_pages = m->pool_pages;
   return N730_OK;
 }
 
@@ -1188,6 +1274,7 @@ N730_API int n730_model_run_step_kernel(void* p, void* stream) {
   N730_REQUIRE(m->finalized, N730_STATE, "model: not finalized");
   N730_REQUIRE(m->pd_ok, N730_UNSUPPORTED, "model: batch-1 decode does not use the persistent kernel");
   N730_REQUIRE(m->h_seq[0] < m->c.max_ctx, N730_STATE, "KV cache capacity exceeded");
+  if (int rc = ensure_pages(m, 0, m->h_seq[0] + 1)) return rc;  // the step writes position h_seq[0]
   return persist_launch(m->pd, stream ? (cudaStream_t)stream : m->st);
 }
 
@@ -1208,6 +1295,7 @@ N730_API int n730_model_trace_step(void* p, void* stream, uint64_t* host_times, 
   N730_REQUIRE(m->finalized, N730_STATE, "model: not finalized");
   N730_REQUIRE(m->pd_ok, N730_UNSUPPORTED, "model: batch-1 decode does not use the persistent kernel");
   N730_REQUIRE(m->h_seq[0] < m->c.max_ctx, N730_STATE, "KV cache capacity exceeded");
+  if (int rc = ensure_pages(m, 0, m->h_seq[0] + 1)) return rc;  // the step writes position h_seq[0]
   const int np = m->pd.a.n_phases, g = m->pd.grid;
   if (n_phases) *n_phases = np;
   if (grid) *grid = g;
@@ -1275,7 +1363,7 @@ N730_API int n730_model_info(void* p, int64_t* info) {
   for (auto& y : m->L) wb += bytes(y.qkv) + bytes(y.o) + bytes(y.gate_up) + bytes(y.down);
   info[0] = wb;
   info[1] = (int64_t)m->c.layers * 2 * m->c.kv_heads * m->c.head_dim * 2;
-  info[2] = info[1] * m->c.max_batch * (int64_t)m->max_pages * m->c.page_size;
+  info[2] = info[1] * (int64_t)m->pool_pages * m->c.page_size;
   info[3] = m->n_split;
   info[4] = m->qkv_dim;
   info[5] = m->max_pages;

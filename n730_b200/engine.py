@@ -32,7 +32,8 @@ class N730ModelConfig(C.Structure):
                [("rms_eps", C.c_float), ("rope_theta", C.c_float)] + \
                [(n, C.c_int32) for n in ("max_ctx", "max_batch", "page_size", "max_prefill", "tie_embeddings",
                                          "tp_rank", "tp_size", "use_graphs", "use_pdl", "exact_gemv",
-                                         "per_op_decode", "stream_depth", "ffn_fuse", "tp_allreduce")]
+                                         "per_op_decode", "stream_depth", "ffn_fuse", "tp_allreduce",
+                                         "kv_pool_pages")]
 
 
 def _sigs(lib):
@@ -80,6 +81,12 @@ def _sigs(lib):
     lib.n730_model_run_linear.restype = i32
     lib.n730_model_linear_bytes.argtypes = [vp, i32, i32, i32]
     lib.n730_model_linear_bytes.restype = C.c_int64
+    lib.n730_model_seq_release.argtypes = [vp, i32]
+    lib.n730_model_seq_release.restype = i32
+    lib.n730_model_seq_move.argtypes = [vp, i32, i32]
+    lib.n730_model_seq_move.restype = i32
+    lib.n730_model_kv_pages.argtypes = [vp, C.POINTER(i32), C.POINTER(i32)]
+    lib.n730_model_kv_pages.restype = i32
     lib.n730_model_trace_step.argtypes = [vp, vp, vp, C.c_int64, vp, C.POINTER(i32), C.POINTER(i32)]
     lib.n730_model_trace_step.restype = i32
     lib._model_sigs = True
@@ -135,14 +142,14 @@ class Engine:
     def __init__(self, shape: ModelShape, max_ctx: int = 4096, max_batch: int = 1, page_size: int = 64,
                  max_prefill: int = 512, use_graphs: bool = True, use_pdl: bool = True,
                  tp_rank: int = 0, tp_size: int = 1, exact_gemv: bool = False, per_op_decode: int = 0,
-                 stream_depth: int = 0, ffn_fuse: int = 0, tp_allreduce: int = 1):
+                 stream_depth: int = 0, ffn_fuse: int = 0, tp_allreduce: int = 1, kv_pool_pages: int = 0):
         self.lib = _sigs(_lib.cuda())
         self.shape = shape
         c = N730ModelConfig(shape.hidden, shape.layers, shape.heads, shape.kv_heads, shape.head_dim, shape.ffn,
                             shape.vocab, shape.rms_eps, shape.rope_theta, max_ctx, max_batch, page_size,
                             max_prefill, int(shape.tie_embeddings), tp_rank, tp_size, int(use_graphs),
                             int(use_pdl), int(exact_gemv), int(per_op_decode), int(stream_depth), int(ffn_fuse),
-                            int(tp_allreduce))
+                            int(tp_allreduce), int(kv_pool_pages))
         self.cfg = c
         self.h = C.c_void_p()
         _lib.check(self.lib.n730_model_create(C.byref(c), C.byref(self.h)), "model_create")
@@ -176,6 +183,18 @@ class Engine:
         _lib.check(self.lib.n730_model_forward(self.h, seq, ids.ctypes.data_as(C.c_void_p), ids.size,
                                                out.ctypes.data_as(C.c_void_p)), "model_forward")
         return out
+
+    def seq_release(self, seq: int):
+        _lib.check(self.lib.n730_model_seq_release(self.h, seq), "model_seq_release")
+
+    def seq_move(self, dst: int, src: int):
+        _lib.check(self.lib.n730_model_seq_move(self.h, dst, src), "model_seq_move")
+
+    def kv_pages(self):
+        """(free, total) pages of the KV pool."""
+        f, t = C.c_int32(), C.c_int32()
+        _lib.check(self.lib.n730_model_kv_pages(self.h, C.byref(f), C.byref(t)), "model_kv_pages")
+        return f.value, t.value
 
     def decode(self, tokens) -> np.ndarray:
         ids = np.ascontiguousarray(tokens, np.int32).reshape(-1)
