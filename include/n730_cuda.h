@@ -227,6 +227,12 @@ int n730_model_decode_sample(void* model, const int32_t* host_tokens, int batch,
                              uint64_t seed, int32_t* host_next, float* host_u);
 /* Same step with device-resident ids/logits, asynchronous on `stream`. */
 int n730_model_decode_device(void* model, const int32_t* d_tokens, int batch, float* d_logits, void* stream);
+/* Self-check of the bounded peer wait of the one-shot allreduce (no counterpart in the
+ * reference): one op as rank 0 of 2 with a local stand-in for rank 1's region.  peer_arrives 0:
+ * the wait runs out after wait_ns and N730_TIMEOUT (-15) comes back through the device error
+ * word, the context stays usable; 1: the peer's slice is present and the op returns 0 with the
+ * sum checked. */
+int n730_tp_wait_check(int64_t wait_ns, int peer_arrives, void* stream);
 /* Release a sequence (its KV pages return to the pool, its length becomes 0). */
 int n730_model_seq_release(void* model, int seq);
 /* Move sequence src (page ids, length) into the empty slot dst (no KV data moves); src becomes

@@ -60,6 +60,7 @@ _CUDA_SIGS = {
     "n730_qgemm": ([vp, vp, i32, i32, vp, i32, vp, vp, i32, vp, f32, i32, vp, vp], i32),
     "n730_sample": ([vp, i32, i32, i32, f32, f32, u64, u64, vp, vp, vp], i32),
     "n730_qweight_load_blocks": ([C.c_char_p, i32, vp, vp, vp, vp], i32),
+    "n730_tp_wait_check": ([i64, i32, vp], i32),
     "n730_attention_forward_noalloc": ([vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, vp], i32),
 }
 

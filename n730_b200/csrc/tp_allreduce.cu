@@ -22,6 +22,8 @@
 #include "common.cuh"
 #include "tp_allreduce.h"
 
+#include <vector>
+
 namespace n730 {
 
 constexpr uint64_t AR_WAIT_NS = 2000000000ull;  // a peer that never arrives: error after 2 s
@@ -58,12 +60,13 @@ __global__ void __launch_bounds__(256) ar_push_reduce_kernel(const ArArgs a) {
   if (tid == 0) {  // every rank's slice s has arrived here
     bool ok = true;
     uint64_t t0 = 0;
+    const uint64_t limit = a.wait_ns ? a.wait_ns : AR_WAIT_NS;
     for (int r = 0; r < a.size && ok; ++r) {
       const int* f = a.local.flags + ((int64_t)par * a.size + r) * AR_SLICES + s;
       while (ar_ld_relaxed_sys(f) < epoch) {
         const uint64_t t = ar_timer();
         if (!t0) t0 = t;
-        else if (t - t0 > AR_WAIT_NS) { atomicExch(a.err, DEV_ERR_TIMEOUT); ok = false; break; }
+        else if (t - t0 > limit) { atomicExch(a.err, DEV_ERR_TIMEOUT); ok = false; break; }
       }
     }
     __threadfence_system();
@@ -117,4 +120,67 @@ int ar_launch(const ArArgs& a, cudaStream_t st) {
   return N730_OK;
 }
 
+int* gemv_err_word();
+int gemv_check_error(bool reset);
+
 }  // namespace n730
+
+using namespace n730;
+
+// Self-check of the bounded peer wait (no counterpart in the reference): one
+// 64-element op of the one-shot allreduce as rank 0 of 2, both regions local
+// buffers of this process.  peer_arrives = 0: nothing ever writes "rank 1"'s
+// flags, so every slice's wait runs out after wait_ns and the op returns
+// N730_TIMEOUT through the device error word (the context stays usable);
+// peer_arrives = 1: rank 1's flags and partial sums are written beforehand, so
+// the op completes and x = part + peer part is checked (N730_BAD_ARG if not).
+N730_API int n730_tp_wait_check(int64_t wait_ns, int peer_arrives, void* stream) {
+  N730_REQUIRE(wait_ns > 0 && wait_ns <= 10000000000ll, N730_BAD_ARG, "tp_wait_check: wait %lld ns", (long long)wait_ns);
+  cudaStream_t st = (cudaStream_t)stream;
+  const int n = 64, size = 2;
+  const size_t rb = ar_region_bytes(size, n);
+  uint8_t* mem = nullptr;
+  const size_t bytes = 2 * rb + 2 * n * sizeof(float) + 2 * sizeof(int);
+  N730_CUDA(cudaMalloc(&mem, bytes));
+  int rc = N730_OK;
+  ArArgs a{};
+  a.local = ar_region_at(mem, size);
+  a.peer[0] = a.local;
+  a.peer[1] = ar_region_at(mem + rb, size);
+  float* part = reinterpret_cast<float*>(mem + 2 * rb);
+  a.part = part;
+  a.x = part + n;
+  a.n = n;
+  a.rank = 0;
+  a.size = size;
+  a.cap = n;
+  a.epoch = reinterpret_cast<int*>(part + 2 * n);
+  a.done = a.epoch + 1;
+  a.err = gemv_err_word();
+  a.wait_ns = (uint64_t)wait_ns;
+  std::vector<float> h(2 * n);
+  for (int i = 0; i < n; ++i) { h[i] = 1.0f; h[n + i] = 0.0f; }
+  std::vector<int> flags(2 * size * AR_SLICES, 0);
+  std::vector<float> peer_part(n, 2.0f);
+  if (!a.err) rc = N730_OOM;
+  if (!rc) rc = cuda_rc(cudaMemsetAsync(mem, 0, bytes, st), __FILE__, __LINE__);
+  if (!rc) rc = cuda_rc(cudaMemcpyAsync(part, h.data(), 2 * n * sizeof(float), cudaMemcpyHostToDevice, st), __FILE__, __LINE__);
+  if (!rc && peer_arrives) {  // rank 1 of epoch 1 (parity 1) has pushed its slice into rank 0's region
+    for (int s = 0; s < AR_SLICES; ++s) flags[(1 * size + 1) * AR_SLICES + s] = 1;
+    rc = cuda_rc(cudaMemcpyAsync(a.local.flags, flags.data(), flags.size() * sizeof(int), cudaMemcpyHostToDevice, st),
+                 __FILE__, __LINE__);
+    if (!rc) rc = cuda_rc(cudaMemcpyAsync(a.local.recv + (1 * size + 1) * n, peer_part.data(), n * sizeof(float),
+                                          cudaMemcpyHostToDevice, st), __FILE__, __LINE__);
+  }
+  if (!rc) rc = ar_launch(a, st);
+  if (!rc) rc = cuda_rc(cudaStreamSynchronize(st), __FILE__, __LINE__);
+  if (!rc) rc = gemv_check_error(true);
+  if (!rc) {
+    rc = cuda_rc(cudaMemcpy(h.data(), part + n, n * sizeof(float), cudaMemcpyDeviceToHost), __FILE__, __LINE__);
+    for (int i = 0; i < n && !rc; ++i)
+      if (h[i] != 3.0f) { set_error("tp_wait_check: sum %g at %d, want 3", h[i], i); rc = N730_BAD_ARG; }
+  }
+  cudaStreamSynchronize(st);
+  cudaFree(mem);
+  return rc;
+}

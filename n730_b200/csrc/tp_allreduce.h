@@ -32,6 +32,7 @@ struct ArArgs {
   int* epoch;                             // this rank's op counter
   int* done;                              // CTAs finished in the current op
   int* err;                               // device error word (DEV_ERR_TIMEOUT when a peer never arrives)
+  uint64_t wait_ns = 0;                   // limit of the wait for a peer's slice (0: AR_WAIT_NS, 2 s)
 };
 
 // Bytes of the shared part of a region for `size` ranks and `cap` floats per slot.
