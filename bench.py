@@ -116,59 +116,95 @@ def _peaks():
 
 
 class ClockSampler:
-    """nvidia-smi sampling (every 20 ms) of clocks and throttle reasons; only the
-    samples that arrive inside the timed region are summarised."""
+    """Clocks and throttle reasons sampled DURING the timed region.
+
+    NVML is polled from a thread every millisecond (a short timed region of a few
+    steps still gets samples; reading clocks changes no setting); where NVML is
+    not importable, ``nvidia-smi -lms 20`` is read instead.  Only samples taken
+    between ``__enter__`` and ``__exit__`` are summarised."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
     def __init__(self, index: int):
         self.index = index
         self.p = None
-        self.lines = []
+        self.th = None
+        self.rows = []        # (time, sm_mhz, sm_max_mhz, [reason names])
+        self.stop = False
 
-    def _read(self):
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        try:
+            import torch
+            uuid = str(torch.cuda.get_device_properties(self.index).uuid)
+            return pynvml, pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.index)
+
+    def _poll_nvml(self, nv, h):
+        bits = [(nv.nvmlClocksEventReasonHwSlowdown, "hw_slowdown"),
+                (nv.nvmlClocksEventReasonHwThermalSlowdown, "hw_thermal_slowdown"),
+                (nv.nvmlClocksEventReasonSwThermalSlowdown, "sw_thermal_slowdown"),
+                (nv.nvmlClocksEventReasonSwPowerCap, "sw_power_cap")]
+        smax = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        while not self.stop:
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.rows.append((time.time(), int(sm), int(smax), [n for b, n in bits if r & b]))
+            except Exception:
+                return
+            time.sleep(0.001)
+
+    def _read_smi(self):
         for line in self.p.stdout:
-            self.lines.append((time.time(), line))
+            f = [x.strip() for x in line.split(",")]
+            if len(f) >= 9 and f[1].isdigit():
+                self.rows.append((time.time(), int(f[1]), int(f[2]),
+                                  [n for n, v in zip(self.NAMES, f[5:9]) if v.lower() == "active"]))
 
     def __enter__(self):
         import threading
         try:
-            self.p = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                                       "--format=csv,noheader,nounits", "-lms", "20"],
-                                      stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.th = threading.Thread(target=self._read, daemon=True)
-            self.th.start()
-            time.sleep(0.3)  # let the sampler start before the timed region
+            nv, h = self._nvml_handle()
+            self.th = threading.Thread(target=self._poll_nvml, args=(nv, h), daemon=True)
         except Exception:
-            self.p = None
+            try:
+                self.p = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                           "--format=csv,noheader,nounits", "-lms", "20"],
+                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                self.th = threading.Thread(target=self._read_smi, daemon=True)
+            except Exception:
+                self.th = None
+        if self.th is not None:
+            self.th.start()
+            time.sleep(0.3 if self.p else 0.01)  # let the sampler start before the timed region
         self.t_start = time.time()
         return self
 
     def __exit__(self, *a):
         self.t_end = time.time()
+        self.stop = True
         if self.p:
             self.p.terminate()
             try:
                 self.p.wait(timeout=5)
             except Exception:
                 self.p.kill()
+        if self.th is not None:
             self.th.join(timeout=2)
 
     def summary(self):
-        rows = []
-        for t, line in self.lines:
-            f = [x.strip() for x in line.split(",")]
-            if self.t_start <= t <= self.t_end and len(f) >= 9 and f[1].isdigit():
-                rows.append(f)
+        rows = [r for r in self.rows if self.t_start <= r[0] <= self.t_end]
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
-        sm = [int(r[1]) for r in rows]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": int(rows[0][2]), "reasons": reasons,
-                "samples": len(rows)}
+        reasons = sorted({n for r in rows for n in r[3]})
+        return {"sm_mhz": statistics.median(r[1] for r in rows), "sm_max_mhz": rows[0][2],
+                "reasons": reasons, "samples": len(rows), "source": "nvml" if self.p is None else "nvidia-smi"}
 
 
 def _dist():
@@ -791,10 +827,10 @@ def run_linear(a):
            "data": "synthetic W ~ N(0, 0.02) seed 0, x ~ N(0, 1) seed 1",
            "config": {"workload": f"one {rows}x{cols} INT4 g128 GEMV per step (n730_qlinear, tensor-core GEMV)",
                       "copies": copies, "l2": f"rotation over {copies} weight copies = "
-                                              f"{copies * bytes_per / 1e6:.0f} MB (> 4x L2)", "graph": True},
+                                              f"{copies * bytes_per / 1e6:.0f} MB (L2 126 MB)", "graph": True},
            "roofline": {"bound": "hbm", "achieved": round(bytes_per / t / 1e9, 1), "peak": peak, "unit": "GB/s",
                         "frac": round(bytes_per / t / 1e9 / peak, 4), "traffic": None,
-                        "kernel": f"gemv_mma2_kernel<8,1,16> ({rows} rows, K {cols})", "bytes_per_launch": bytes_per,
+                        "kernel": f"gemv_mma2_kernel<8,1,WARPS> ({rows} rows, K {cols}; 8 warps per CTA below 32 chunks per SM, else 16)", "bytes_per_launch": bytes_per,
                         "ms_per_launch": round(t * 1e3, 5), "peak_source": kind},
            "clocks": clk.summary(), "gpu_launches": a.steps * copies}
     print(json.dumps(out), flush=True)
