@@ -82,7 +82,8 @@ def _args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (small profiling cases)")
     ap.add_argument("--vocab", type=int, default=0, help="phases workload: override the vocabulary (profiling cases)")
-    ap.add_argument("--linear-shape", default="4096x4096", help="linear workload: rows x cols of W")
+    ap.add_argument("--linear-shape", default="4096x4096", help="linear / gemm workload: rows x cols of W")
+    ap.add_argument("--tokens", type=int, default=512, help="gemm workload: tokens per call")
     ap.add_argument("--copies", type=int, default=0,
                     help="linear workload: weight copies rotated through (default: > 4x L2 of bytes)")
     ap.add_argument("--tp-allreduce", type=int, default=1, choices=[0, 1],
@@ -97,7 +98,7 @@ def _args():
                     help="resident workload: precision map (mixed_05b: INT8 attention, INT4 g128 FFN, fp16 tied "
                          "embedding/lm_head)")
     ap.add_argument("--workload", default="auto",
-                    choices=["auto", "resident", "streamed", "tp72b", "linear", "phases"],
+                    choices=["auto", "resident", "streamed", "tp72b", "linear", "gemm", "phases"],
                     help="auto: tp72b when launched by torchrun (any N), else resident (the 7B headline); "
                          "resident: the model resident in HBM (N ranks: independent replicas); "
                          "streamed: 7B aggressive mixed quant (FFN INT2 g64, attention INT4 g128, lm_head INT8 "
@@ -571,8 +572,9 @@ def run_ours(a):
             "gpu_launches_e2e_per_step": (3 if persistent else 5 * shape.layers + 3) + 1,
             "prefill": {"tokens": B * ctx, "s": round(t_prefill, 4), "tok_per_s": round(B * ctx / t_prefill, 1),
                         "tflops": round(2 * params * B * ctx / t_prefill / 1e12, 1),
-                        "path": "tcgen05 GEMM (INT4 fragment tiles dequantised to fp16 in shared memory, TMEM "
-                                "accumulators) for every linear, 512-token chunks; wall clock incl. host calls"},
+                        "path": "tcgen05 GEMM (INT4 fragment tiles dequantised to fp16 into tensor memory as the "
+                                "MMA's A operand, x from shared memory, TMEM accumulators, 256- or 128-token tiles) for "
+                                "every linear, 512-token chunks; wall clock incl. host calls"},
         }
         if not a.no_cpu_baseline and headline:
             cs = CpuReferenceDecoder(shape, ctx)
@@ -838,6 +840,89 @@ def run_linear(a):
         lib.n730_qweight_destroy(q)
 
 
+def _tensor_peak():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["bf16_tflops"]), "measured (burst)"
+    return 1590.0, "fallback (burst)"
+
+
+def run_gemm(a):
+    """The tcgen05 prefill GEMM alone (n730_qgemm: x packing + the GEMM kernel per call) on one
+    INT4 g128 weight of --linear-shape for --tokens tokens, calls replayed from a CUDA graph over
+    --copies weight copies; TFLOP/s = 2 rows cols tokens per call against the measured burst
+    bf16 tensor peak (the kernel is kind::f16, the same rate)."""
+    import torch
+    from n730_b200 import _lib
+    lib = _lib.cuda()
+    torch.cuda.set_device(0)
+    rows, cols = (int(v) for v in a.linear_shape.lower().split("x"))
+    T = a.tokens
+    g = torch.Generator(device="cuda")
+    g.manual_seed(0)
+    w = torch.randn(rows, cols, generator=g, device="cuda") * 0.02
+    P = lambda t: C.c_void_p(t.data_ptr())
+    copies = a.copies or 2
+    qs = []
+    for _ in range(copies):
+        codes = torch.empty(rows * cols // 2, dtype=torch.uint8, device="cuda")
+        s16 = torch.empty(rows, cols // 128, dtype=torch.float16, device="cuda")
+        z16 = torch.empty_like(s16)
+        _lib.check(lib.n730_quantize_grouped(P(w), rows, cols, 4, 128, P(codes), P(s16), P(z16), None), "quantize")
+        q = C.c_void_p()
+        _lib.check(lib.n730_qweight_create(0x44, rows, cols, 128, 1.0, 0.0, P(codes), P(s16), P(z16), 1, None,
+                                           C.byref(q)), "qweight_create")
+        _lib.check(lib.n730_qweight_set_layout(q, 1, None), "qweight_set_layout")
+        qs.append(q)
+    del w
+    g1 = torch.Generator(device="cuda")
+    g1.manual_seed(1)
+    x = torch.randn(T, cols, generator=g1, device="cuda")
+    y = torch.empty(copies, T, rows, device="cuda")
+    side = torch.cuda.Stream()
+    call = lambda i, st: _lib.check(lib.n730_qgemm(qs[i], P(x), cols, T, P(y[i]), rows, None, None, 0, None, 1e-6, 0,
+                                                   None, C.c_void_p(st)), "qgemm")
+    with torch.cuda.stream(side):
+        for i in range(copies):  # warm-up outside capture (grows the packed-x workspace)
+            call(i, side.cuda_stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        st = torch.cuda.current_stream().cuda_stream
+        for i in range(copies):
+            call(i, st)
+    for _ in range(a.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        e0.record()
+        for _ in range(a.steps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+    t = e0.elapsed_time(e1) / 1000.0 / (a.steps * copies)
+    flops = 2.0 * rows * cols * T
+    peak, kind = _tensor_peak()
+    tf = flops / t / 1e12
+    ntok = 256 if -(-rows // 128) * -(-T // 256) >= torch.cuda.get_device_properties(0).multi_processor_count else 128
+    out = {"metric": f"INT4 g128 prefill GEMM throughput (W {rows}x{cols}, {T} tokens)",
+           "value": round(tf, 1), "unit": "TFLOP/s", "n_gpus": 1, "steps": a.steps, "warmup": a.warmup,
+           "ms_per_step": round(t * 1e3, 5), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "dtype": "int4 weights dequantised to fp16; fp16 x; f32 accumulate (tcgen05 kind::f16)",
+           "data": "synthetic W ~ N(0, 0.02) seed 0, x ~ N(0, 1) seed 1",
+           "config": {"workload": f"one {rows}x{cols} INT4 g128 GEMM of {T} tokens per call (n730_qgemm)",
+                      "copies": copies, "graph": True, "token_tile": ntok},
+           "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peak, "unit": "TFLOP/s",
+                        "frac": round(tf / peak, 4), "traffic": None,
+                        "kernel": f"gemm_tc_kernel<{ntok}> + x16_pack_kernel per call", "ms_per_launch": round(t * 1e3, 5),
+                        "peak_source": kind},
+           "clocks": clk.summary(), "gpu_launches": a.steps * copies * 2}
+    print(json.dumps(out), flush=True)
+    for q in qs:
+        lib.n730_qweight_destroy(q)
+
+
 def run_phases(a):
     """Per-phase timing of the persistent decode kernel (--model, batch 1, context --ctx): --steps
     traced launches (n730_model_trace_step, medians over them).  Per phase kind, averaged over the
@@ -950,6 +1035,8 @@ def main():
         run_phases(a)
     elif _tp_workload(a):
         run_tp(a)
+    elif a.workload == "gemm":
+        run_gemm(a)
     elif a.workload == "linear":
         run_linear(a)
     else:

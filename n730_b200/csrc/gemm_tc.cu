@@ -3,25 +3,30 @@
 // Y[T x N] = X[T x K] . dequant(W)[N x K]^T for INT4 group-wise weights held in
 // the fragment-tiled layout of the decode GEMV (no second copy of the weights),
 // with the decoder's epilogues: bias, residual add (in place), SwiGLU of
-// interleaved gate/up rows, and RMSNorm folded into the A operand.
+// interleaved gate/up rows, and RMSNorm folded into the x operand.
 //
 // A pre-pass packs x once per call (RMS-normalised, rounded to fp16) into
 // 128-token x 64-column blocks already in the K-major, 128-byte-swizzled
 // layout the UMMA shared-memory descriptors read (8-row x 128-byte atoms,
-// 16-byte chunk c of row r at c ^ (r % 8)).  One CTA computes a 128-token x
-// 128-row output tile over K in steps of 128 (one group) through a 3-stage
-// pipeline of specialised warps, with no CTA-wide barrier inside the K loop:
-//  * a producer warp issues, once a stage's previous MMAs have completed, one
-//    bulk copy of the packed A tile and one bulk copy per 16-row tile of W
-//    (the step's whole group blocks: codes and fp16 scale/zero);
-//  * 8 dequant warps turn their row tile's codes into (q - z) * s fp16 values
-//    in the swizzled B tile and arrive on the stage's conversion barrier;
-//  * an MMA warp issues eight tcgen05.mma.kind::f16 (M 128, N 128, K 16,
-//    fp32 accumulate in tensor memory) and a tcgen05.commit to the stage's
-//    empty barrier, which gates that stage's next copies;
-//  * after the last step the accumulator is read back with tcgen05.ld
-//    (32 lanes x 32 columns per warp and instruction) and written with the
-//    epilogue.
+// 16-byte chunk c of row r at c ^ (r % 8)).  One CTA computes a 128-row x
+// NTOK-token output tile (NTOK 256, or 128 when 256-token tiles would leave
+// SMs idle) over K in steps of 128 through a pipeline of specialised warps,
+// with no CTA-wide barrier inside the K loop:
+//  * a producer warp issues, once a stage's previous MMAs have completed, the
+//    bulk copies of the step's x blocks (NTOK x 128 fp16) and, per 16-row tile
+//    of W, of the step's whole group blocks (codes and fp16 scale/zero);
+//  * 8 dequant warps turn the codes into (q - z) * s fp16 and store them
+//    straight into tensor memory (tcgen05.st, one W row per TMEM lane, two
+//    fp16 per 32-bit column): the weights are the MMA's A operand, read from
+//    TMEM, so the converted tile never goes through shared memory, and each
+//    dequantised weight serves NTOK tokens;
+//  * an MMA warp issues eight tcgen05.mma.kind::f16 (A from TMEM, B = x from
+//    shared memory; M 128, N NTOK, K 16; fp32 accumulator in TMEM) and a
+//    tcgen05.commit to the stage's empty barrier, which gates that stage's
+//    next copies and next conversion;
+//  * after the last step the accumulator (TMEM lane = W row, column = token)
+//    is read back with tcgen05.ld and written with the epilogue, each warp
+//    instruction storing 32 consecutive rows of one token.
 // Every mbarrier wait is bounded (%globaltimer, 2 s); a wait that runs out sets
 // the device error word, stops issuing, waits (bounded) for the MMAs in
 // flight, and still frees the tensor memory.
@@ -34,12 +39,26 @@
 
 namespace n730 {
 
-constexpr int TC_BM = 128, TC_BN = 128, TC_BK = 128, TC_STAGES = 3;
-constexpr int TC_SUB = 128 * 64 * 2;        // one 128-row x 64-column fp16 sub-tile (one 128-byte swizzle atom wide)
-constexpr int TC_TILE = 2 * TC_SUB;         // A or B operand of one K-step (two sub-tiles)
+constexpr int TC_BN = 128;                  // W rows per CTA: the MMA's M, one per TMEM lane
+constexpr int TC_BK = 128;                  // K per pipeline step
+constexpr int TC_XT = 128;                  // tokens per packed x sub-tile
+constexpr int TC_SUB = TC_XT * 64 * 2;      // one 128-token x 64-column fp16 sub-tile (one swizzle atom wide)
 constexpr int TC_RAWT = 1152;               // raw codes + scale/zero blocks of one 16-row tile per K-step
-constexpr int TC_STAGE = 2 * TC_TILE + 9216;  // A | B | raw B (8 x TC_RAWT), a multiple of 1024
-constexpr uint32_t TC_TMEM_COLS = 128;      // fp32 accumulator columns (N)
+constexpr int TC_RAW = 8 * TC_RAWT;         // raw W of one step (8 row tiles), a multiple of 1024
+constexpr int TC_ACOLS = TC_BK / 2;         // TMEM columns of one step's A (two fp16 per column)
+constexpr uint32_t TC_TMEM_COLS = 512;      // accumulator (NTOK columns) + one A block per stage
+
+template <int NTOK>
+struct TcCfg {
+  static constexpr int STAGES = NTOK == 256 ? 3 : 4;
+  static constexpr int XB = NTOK * TC_BK * 2;  // x bytes per step: [64-column block][NTOK rows][128 B]
+  static constexpr int STAGE = XB + TC_RAW;    // a multiple of 1024 (swizzle atoms stay aligned)
+  static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE + (3 * STAGES + 1) * 8 + 32;
+  // kind::f16 instruction descriptor: D fp32, A = B = fp16, both K-major, N = NTOK, M = 128
+  static constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(NTOK >> 3) << 17) | ((uint32_t)(TC_BN >> 4) << 24);
+  static_assert(NTOK + STAGES * TC_ACOLS <= (int)TC_TMEM_COLS, "tensor memory budget");
+  static_assert(STAGE % 1024 == 0, "stage alignment");
+};
 
 struct TcArgs {
   const uint8_t* blob;  // fragment tiles: group u = tile*G + g at u * (kpg*128 + 64)
@@ -64,16 +83,16 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
   return d;
 }
 
-// kind::f16 instruction descriptor: D fp32, A = B = fp16, both K-major, N = 128, M = 128.
-constexpr uint32_t TC_IDESC = (1u << 4) | ((uint32_t)(TC_BN >> 3) << 17) | ((uint32_t)(TC_BM >> 4) << 24);
-
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+// D[tmem_d] (+)= A[tmem_a] . B[bdesc]^T with A in tensor memory (lane = row,
+// two fp16 per 32-bit column) and B in shared memory.
+template <uint32_t IDESC>
+__device__ __forceinline__ void tc_mma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t accumulate) {
   asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-               " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}"
-               :: "r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(TC_IDESC), "r"(accumulate) : "memory");
+               " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}"
+               :: "r"(tmem_d), "r"(tmem_a), "l"(bdesc), "r"(IDESC), "r"(accumulate) : "memory");
 }
 
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
@@ -96,21 +115,29 @@ __device__ __forceinline__ void tc_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// byte offset of element (row r, column k) in a K-major 128B-swizzled tile (64 fp16 per row)
-__device__ __forceinline__ uint32_t sw128(int r, int k) {
-  return (uint32_t)(r * 128 + ((((k >> 3) ^ (r & 7)) & 7) << 4) + ((k & 7) << 1));
+// 32 consecutive 32-bit columns of this thread's TMEM lane (the warp's 32 lanes)
+__device__ __forceinline__ void tc_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+               "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+               :: "r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+                  "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+                  "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
+                  "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+               : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
-// A operand packing: x [T][ldx] (RMS-normalised with inv_rms and norm_w when
+// x operand packing: x [T][ldx] (RMS-normalised with inv_rms and norm_w when
 // given) -> fp16 blocks of 128 tokens x 64 columns, each laid out exactly as
-// the GEMM's shared-memory A tile (row r: 128 bytes, 16-byte chunk c at
-// c ^ (r % 8)); tokens >= T are zero.  Grid (K / 64, token tiles).
+// a 128-token slice of the GEMM's shared-memory x block (row r: 128 bytes,
+// 16-byte chunk c at c ^ (r % 8)); tokens >= T are zero.  Grid (K / 64, token
+// sub-tiles).
 __global__ void x16_pack_kernel(const float* x, int ldx, int T, const float* inv_rms, const float* norm_w,
                                 uint8_t* out) {
   const int kb = blockIdx.x, tt = blockIdx.y;
   uint8_t* blk = out + ((size_t)tt * gridDim.x + kb) * TC_SUB;
-  for (int i = threadIdx.x; i < TC_BM * 8; i += blockDim.x) {
-    const int r = i >> 3, c8 = i & 7, tok = tt * TC_BM + r, k = kb * 64 + c8 * 8;
+  for (int i = threadIdx.x; i < TC_XT * 8; i += blockDim.x) {
+    const int r = i >> 3, c8 = i & 7, tok = tt * TC_XT + r, k = kb * 64 + c8 * 8;
     uint4 pk = make_uint4(0u, 0u, 0u, 0u);
     if (tok < T) {
       const float4* src = reinterpret_cast<const float4*>(x + (int64_t)tok * ldx + k);
@@ -144,43 +171,53 @@ __device__ __forceinline__ void mbar_arrive1(uint64_t* bar) {
   asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" :: "r"(smem_u32(bar)) : "memory");
 }
 
-// One CTA per 128-token x 128-row output tile; K in steps of 128 through a
-// 3-stage pipeline with specialised warps and no CTA-wide barrier in the loop:
+// One CTA per 128-row x NTOK-token output tile; K in steps of 128 through a
+// pipeline of specialised warps with no CTA-wide barrier in the loop:
 //  * warp 8 (producer): once a stage's MMAs are done (empty[s]) it issues the
-//    next step's bulk copies into it (the packed A tile, 32 KB; per 16-row tile
-//    of W the step's codes with their scale/zero blocks, one copy when the
-//    step covers whole groups) -> full[s];
-//  * warps 0-7 (dequant, then epilogue): warp w waits for full[s], turns row
-//    tile w's codes into (q - z) * s fp16 in the swizzled B tile and arrives on
-//    conv[s];
-//  * warp 9 (MMA): waits for conv[s], issues four tcgen05.mma.kind::f16 and
-//    commits them to empty[s]; after the last step, to `done`.
+//    next step's bulk copies into it (the x blocks of the step, NTOK x 128
+//    fp16; per 16-row tile of W the step's codes with their scale/zero
+//    blocks, one copy when the step covers whole groups) -> full[s];
+//  * warps 0-7 (dequant, then epilogue): warp w owns TMEM lanes 32(w%4).. (W
+//    rows) and K half w/4 of each step; it waits for full[s], writes its 32
+//    rows x 64 dequantised fp16 into stage s's A columns with one tcgen05.st
+//    and arrives on conv[s];
+//  * warp 9 (MMA): waits for conv[s], issues eight tcgen05.mma.kind::f16 (A in
+//    TMEM, B = x in shared memory) and commits them to empty[s]; after the last
+//    step, to `done`.
+// full[s] of a step is only raised after the producer saw empty[s] of the
+// step that last used stage s, so the dequant warps never overwrite an A block
+// the tensor core is still reading.
 constexpr int TC_WARPS = 10;
 
+template <int NTOK>
 __global__ void __launch_bounds__(TC_WARPS * 32, 1) gemm_tc_kernel(const TcArgs p) {
+  using Cfg = TcCfg<NTOK>;
+  constexpr int S = Cfg::STAGES;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + TC_STAGES * TC_STAGE);  // [STAGES] copies landed
-  uint64_t* conv = full + TC_STAGES;                                           // [STAGES] B tile converted
-  uint64_t* empty = conv + TC_STAGES;                                          // [STAGES] MMAs done
-  uint64_t* done = empty + TC_STAGES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::STAGE);  // [S] copies landed
+  uint64_t* conv = full + S;                                             // [S] A block in TMEM
+  uint64_t* empty = conv + S;                                            // [S] MMAs done
+  uint64_t* done = empty + S;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   volatile int* abortf = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* counts = const_cast<int*>(abortf) + 1;  // [0] steps produced, [1] steps issued, [2] result ok
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int n0 = blockIdx.x * TC_BN, tt = blockIdx.y, m0 = tt * TC_BM;
+  const int n0 = blockIdx.x * TC_BN, m0 = blockIdx.y * NTOK;
+  const int xt0 = blockIdx.y * (NTOK / TC_XT);  // first packed 128-token sub-tile
+  const int KB = p.cols / 64;                   // packed 64-column blocks per sub-tile
   const int GB = p.kpg * 128 + 64;
   const int n_tiles = (p.rows + 15) >> 4, tile0 = n0 >> 4;
-  const int nt_here = min(8, n_tiles - tile0);  // 16-row tiles of W in this CTA's B (>= 1)
+  const int nt_here = min(8, n_tiles - tile0);  // 16-row tiles of W in this CTA (>= 1)
   // per 16-row tile and K-step: whole groups (kpg <= 8: 8/kpg contiguous group
   // blocks) or, for kpg 16, half a group's codes plus its scale/zero block
   const int gps = p.kpg <= 8 ? 8 / p.kpg : 1;                  // groups touched per step
   const uint32_t raw_b = p.kpg <= 8 ? (uint32_t)(gps * GB) : 1088u;
-  const uint32_t stage_tx = (uint32_t)TC_TILE + (uint32_t)nt_here * raw_b;
+  const uint32_t stage_tx = (uint32_t)Cfg::XB + (uint32_t)nt_here * raw_b;
   const int KT = p.cols / TC_BK;
 
   if (tid == 0) {
-    for (int s = 0; s < TC_STAGES; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&conv[s], 8);
       mbar_init(&empty[s], 1);
@@ -198,22 +235,28 @@ __global__ void __launch_bounds__(TC_WARPS * 32, 1) gemm_tc_kernel(const TcArgs 
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem = *tmem_slot;  // accumulator: columns [0, NTOK); A block of stage s at NTOK + s * TC_ACOLS
 
   if (warp == 8) {
     // ---------------- producer ----------------
     if (lane == 0) {
       int kt = 0;
       for (; kt < KT; ++kt) {
-        const int s = kt % TC_STAGES;
-        if (kt >= TC_STAGES && !tc_wait(&empty[s], (uint32_t)(((kt / TC_STAGES) - 1) & 1), abortf)) break;
-        uint8_t* st = smem + s * TC_STAGE;
+        const int s = kt % S;
+        if (kt >= S && !tc_wait(&empty[s], (uint32_t)(((kt / S) - 1) & 1), abortf)) break;
+        uint8_t* st = smem + s * Cfg::STAGE;
         mbar_arrive_expect_tx(&full[s], stage_tx);
-        bulk_g2s(st, p.x16 + ((size_t)tt * KT + kt) * TC_TILE, TC_TILE, &full[s]);
+        // x: 64-column block h of the step holds NTOK rows; sub-tile i fills rows [128 i, 128 i + 128)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int i = 0; i < NTOK / TC_XT; ++i)
+            bulk_g2s(st + h * (NTOK * 128) + i * TC_SUB, p.x16 + ((size_t)(xt0 + i) * KB + 2 * kt + h) * TC_SUB,
+                     TC_SUB, &full[s]);
         const int s0 = kt * 8, gi = s0 / p.kpg;  // first k-step and group of this step
         for (int w = 0; w < nt_here; ++w) {
           const uint8_t* grp = p.blob + ((int64_t)(tile0 + w) * p.G + gi) * GB;
-          uint8_t* dst = st + 2 * TC_TILE + w * TC_RAWT;
+          uint8_t* dst = st + Cfg::XB + w * TC_RAWT;
           if (p.kpg <= 8) {
             bulk_g2s(dst, grp, raw_b, &full[s]);
           } else {  // half of a 16-k-step group: quads 2h, 2h+1, then the group's scale/zero block
@@ -229,14 +272,15 @@ __global__ void __launch_bounds__(TC_WARPS * 32, 1) gemm_tc_kernel(const TcArgs 
     if (lane == 0) {
       int kt = 0;
       for (; kt < KT; ++kt) {
-        const int s = kt % TC_STAGES;
-        if (!tc_wait(&conv[s], (uint32_t)((kt / TC_STAGES) & 1), abortf)) break;
+        const int s = kt % S;
+        if (!tc_wait(&conv[s], (uint32_t)((kt / S) & 1), abortf)) break;
         tc_fence_after();
-        const uint32_t a0 = smem_u32(smem + s * TC_STAGE), b0 = a0 + TC_TILE;
+        const uint32_t b0 = smem_u32(smem + s * Cfg::STAGE);
+        const uint32_t a0 = tmem + (uint32_t)(NTOK + s * TC_ACOLS);
 #pragma unroll
-        for (int j = 0; j < TC_BK / 16; ++j) {  // K = 16 per MMA: 32 bytes along the swizzled row of a sub-tile
-          const uint32_t off = (uint32_t)((j >> 2) * TC_SUB + (j & 3) * 32);
-          tc_mma(tmem, umma_desc_sw128(a0 + off), umma_desc_sw128(b0 + off), (kt > 0 || j > 0) ? 1u : 0u);
+        for (int j = 0; j < TC_BK / 16; ++j) {  // K = 16 per MMA: 8 TMEM columns of A, 32 bytes along x's swizzled rows
+          const uint32_t boff = (uint32_t)((j >> 2) * (NTOK * 128) + (j & 3) * 32);
+          tc_mma_ts<Cfg::IDESC>(tmem, a0 + (uint32_t)(j * 8), umma_desc_sw128(b0 + boff), (kt > 0 || j > 0) ? 1u : 0u);
         }
         tc_commit(&empty[s]);
       }
@@ -250,59 +294,48 @@ __global__ void __launch_bounds__(TC_WARPS * 32, 1) gemm_tc_kernel(const TcArgs 
       }
     }
   } else {
-    // ---------------- dequant warps 0-7: row tile `warp` of the B tile ----------------
-    const int r0 = warp * 16 + (lane >> 2), r1 = r0 + 8;
-    const int kb = 2 * (lane & 3);
+    // ---------------- dequant warps 0-7: W row 32 (w % 4) + lane, K half w / 4 ----------------
+    const int q = warp & 3, h = warp >> 2;
+    const int r = 32 * q + lane, wt = r >> 4, g = r & 7, hi = (r >> 3) & 1;
+    // row g of the 16-row tile sits in the low nibbles of its fragment words, row g + 8 in the high ones
+    const uint32_t msk = hi ? 0x00F000F0u : 0x000F000Fu, mag = hi ? 0x54005400u : 0x64006400u;
+    const __half2 kmag = u2h(mag);  // fp16 64 or 1024: the value the magic bits stand for
+    const int qoff = p.kpg == 4 ? h * 576 : h * 512, zoff = p.kpg == 4 ? h * 576 + 512 : 1024;
+    const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(NTOK + h * 32);
     for (int kt = 0; kt < KT; ++kt) {
-      const int s = kt % TC_STAGES;
+      const int s = kt % S;
       int ok = 1;
-      if (lane == 0) ok = tc_wait(&full[s], (uint32_t)((kt / TC_STAGES) & 1), abortf);
+      if (lane == 0) ok = tc_wait(&full[s], (uint32_t)((kt / S) & 1), abortf);
       if (!__shfl_sync(0xffffffffu, ok, 0)) break;
-      uint8_t* st = smem + s * TC_STAGE;
-      uint8_t* bs = st + TC_TILE;
+      tc_fence_after();
+      const uint8_t* raw = smem + s * Cfg::STAGE + Cfg::XB + wt * TC_RAWT;
+      uint32_t out[32];
+      if (wt < nt_here) {
+        // column c of the half: K pair (16 j + 2 tq (+ 8), +1) for c = 8 j + tq (+ 4), from
+        // word j of fragment lane 4 g + tq (8 nibbles: rows g / g + 8, K 2tq, 2tq+1, 2tq+8, 2tq+9)
+        const uint2 szv = *reinterpret_cast<const uint2*>(raw + zoff + g * 8);
+        const float2 sc = __half22float2(u2h(szv.x)), zp = __half22float2(u2h(szv.y));
+        const float sv = hi ? sc.y : sc.x, zv = hi ? zp.y : zp.x;
+        // (q - z) s in fp16: the nibble ORed into the magic gives magic + q exactly, one
+        // subtraction gives q, one FMA q s - z s (z s rounded to fp16 once)
+        const __half2 s2 = __float2half2_rn(sv), c2 = __float2half2_rn(-zv * sv);
+        const uint4* src = reinterpret_cast<const uint4*>(raw + qoff + g * 64);
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {  // quad h: k-steps 4h..4h+3 of the step -> sub-tile h of B
-        uint8_t* sb = bs + h * TC_SUB;
-        if (warp < nt_here) {
-          const uint8_t* raw = st + 2 * TC_TILE + warp * TC_RAWT;
-          // kpg 4: [quad | sz] per group; kpg 8 and 16: [quad 0 | quad 1 | sz]
-          const int qoff = p.kpg == 4 ? h * 576 : h * 512, zoff = p.kpg == 4 ? h * 576 + 512 : 1024;
-          const uint4 w4 = *reinterpret_cast<const uint4*>(raw + qoff + lane * 16);
-          const uint2 szv = *reinterpret_cast<const uint2*>(raw + zoff + (lane >> 2) * 8);
-          const float2 sc = __half22float2(u2h(szv.x)), zp = __half22float2(u2h(szv.y));
-          // (q - z) s in fp16: the code nibble ORed into fp16 1024 (low nibbles) or 64 (bits 4-7)
-          // gives 1024 + q / 64 + q exactly, one subtraction gives q, one FMA q s - z s (z s
-          // rounded to fp16 once: <= 2^-12 relative of z s per weight)
-          const __half2 s0 = __float2half2_rn(sc.x), s1 = __float2half2_rn(sc.y);
-          const __half2 c0 = __float2half2_rn(-zp.x * sc.x), c1 = __float2half2_rn(-zp.y * sc.y);
-          const __half2 k1024 = u2h(0x64006400u), k64 = u2h(0x54005400u);
+        for (int tq = 0; tq < 4; ++tq) {
+          const uint4 w4 = src[tq];
           const uint32_t wv[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const uint32_t w = wv[j], ws = w >> 8;
-            const int k0 = j * 16 + kb;
-            const __half2 q0 = __hsub2(u2h(lop3_and_or(w, 0x000F000Fu, 0x64006400u)), k1024);   // r0, k0 / k0+1
-            const __half2 q1 = __hsub2(u2h(lop3_and_or(w, 0x00F000F0u, 0x54005400u)), k64);     // r1, k0 / k0+1
-            const __half2 q2 = __hsub2(u2h(lop3_and_or(ws, 0x000F000Fu, 0x64006400u)), k1024);  // r0, k0+8 / +9
-            const __half2 q3 = __hsub2(u2h(lop3_and_or(ws, 0x00F000F0u, 0x54005400u)), k64);    // r1, k0+8 / +9
-            *reinterpret_cast<uint32_t*>(sb + sw128(r0, k0)) = h2u(__hfma2(q0, s0, c0));
-            *reinterpret_cast<uint32_t*>(sb + sw128(r1, k0)) = h2u(__hfma2(q1, s1, c1));
-            *reinterpret_cast<uint32_t*>(sb + sw128(r0, k0 + 8)) = h2u(__hfma2(q2, s0, c0));
-            *reinterpret_cast<uint32_t*>(sb + sw128(r1, k0 + 8)) = h2u(__hfma2(q3, s1, c1));
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int k0 = j * 16 + kb;
-            *reinterpret_cast<uint32_t*>(sb + sw128(r0, k0)) = 0u;
-            *reinterpret_cast<uint32_t*>(sb + sw128(r1, k0)) = 0u;
-            *reinterpret_cast<uint32_t*>(sb + sw128(r0, k0 + 8)) = 0u;
-            *reinterpret_cast<uint32_t*>(sb + sw128(r1, k0 + 8)) = 0u;
+            out[8 * j + tq] = h2u(__hfma2(__hsub2(u2h(lop3_and_or(wv[j], msk, mag)), kmag), s2, c2));
+            out[8 * j + 4 + tq] = h2u(__hfma2(__hsub2(u2h(lop3_and_or(wv[j] >> 8, msk, mag)), kmag), s2, c2));
           }
         }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) out[c] = 0u;
       }
-      // generic-proxy shared-memory writes -> visible to the tensor core's (async proxy) reads
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tc_st32(ta + (uint32_t)(s * TC_ACOLS), out);
+      tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive1(&conv[s]);
     }
@@ -310,42 +343,33 @@ __global__ void __launch_bounds__(TC_WARPS * 32, 1) gemm_tc_kernel(const TcArgs 
   __syncthreads();
   // copies still in flight (abort path) land before the CTA exits
   if (tid == 8 * 32)
-    for (int q = counts[1]; q < counts[0]; ++q)
-      wait_bar(&full[q % TC_STAGES], (uint32_t)((q / TC_STAGES) & 1));
+    for (int qq = counts[1]; qq < counts[0]; ++qq)
+      wait_bar(&full[qq % S], (uint32_t)((qq / S) & 1));
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   if (*abortf && tid == 0) atomicExch(p.err, DEV_ERR_TIMEOUT);
   if (counts[2] && warp < 8) {
-    // ---- epilogue: warp w reads TMEM lanes 32*(w%4).. (tokens), columns 64*(w/4).. (rows) ----
-    const int qd = warp & 3, half = warp >> 2;
-    const int m = qd * 32 + lane, tok = m0 + m;
+    // ---- epilogue: warp w reads TMEM lanes 32 (w % 4).. (W rows), token columns [w / 4 * NTOK / 2, +NTOK / 2) ----
+    const int q = warp & 3, hh = warp >> 2;
+    const int n = n0 + 32 * q + lane;
+    const bool nin = n < p.rows;
+    const float bv = p.bias && nin ? p.bias[n] : 0.f;
 #pragma unroll 1
-    for (int c = 0; c < 2; ++c) {
-      const int col0 = half * 64 + c * 32;
+    for (int c = 0; c < NTOK / 64; ++c) {
+      const int col0 = hh * (NTOK / 2) + c * 32;
       float v[32];
-      tc_ld32(tmem + ((uint32_t)(qd * 32) << 16) + (uint32_t)col0, v);
-      if (tok < p.T) {
-        if (p.swiglu) {
+      tc_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)col0, v);
 #pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            const int n = n0 + col0 + i;
-            if (n + 1 < p.rows) {
-              const float gt = v[i] + (p.bias ? p.bias[n] : 0.f);
-              const float up = v[i + 1] + (p.bias ? p.bias[n + 1] : 0.f);
-              p.y[(int64_t)tok * p.ldy + (n >> 1)] = (gt / (1.0f + expf(-gt))) * up;
-            }
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int n = n0 + col0 + i;
-            if (n < p.rows) {
-              float o = v[i] + (p.bias ? p.bias[n] : 0.f);
-              if (p.residual) o += p.residual[(int64_t)tok * p.ldr + n];
-              p.y[(int64_t)tok * p.ldy + n] = o;
-            }
-          }
+      for (int i = 0; i < 32; ++i) {
+        const int tok = m0 + col0 + i;
+        if (tok >= p.T) break;  // warp-uniform
+        const float o = v[i] + bv;
+        if (p.swiglu) {  // gate row n (even lane), up row n + 1 (the next lane)
+          const float up = __shfl_down_sync(0xffffffffu, o, 1);
+          if (nin && !(lane & 1) && n + 1 < p.rows) p.y[(int64_t)tok * p.ldy + (n >> 1)] = (o / (1.0f + expf(-o))) * up;
+        } else if (nin) {
+          p.y[(int64_t)tok * p.ldy + n] = p.residual ? o + p.residual[(int64_t)tok * p.ldr + n] : o;
         }
       }
     }
@@ -373,11 +397,10 @@ __global__ void inv_rms_kernel(const float* x, int ldx, int T, int K, float eps,
 
 int* gemv_err_word();
 
-constexpr size_t TC_SMEM = 1024 + (size_t)TC_STAGES * TC_STAGE + (3 * TC_STAGES + 1) * 8 + 32;
-
 // One-time kernel attribute set-up (call before any stream capture).
 int gemm_tc_prepare() {
-  return smem_attr_once<gemm_tc_kernel>((int)TC_SMEM);
+  if (int rc = smem_attr_once<gemm_tc_kernel<256>>((int)TcCfg<256>::SMEM)) return rc;
+  return smem_attr_once<gemm_tc_kernel<128>>((int)TcCfg<128>::SMEM);
 }
 
 bool gemm_tc_supported(const QWeight& w, int T) {
@@ -385,7 +408,7 @@ bool gemm_tc_supported(const QWeight& w, int T) {
   return w.layout == 1 && w.bits == 4 && w.cols % TC_BK == 0 && (kpg == 4 || kpg == 8 || kpg == 16) && T >= 1;
 }
 
-// Packed-A workspace of the current device, grown on demand (never inside a stream capture).
+// Packed-x workspace of the current device, grown on demand (never inside a stream capture).
 static int x16_workspace(size_t bytes, cudaStream_t st, uint8_t** out) {
   static uint8_t* buf[64] = {};
   static size_t cap[64] = {};
@@ -396,7 +419,7 @@ static int x16_workspace(size_t bytes, cudaStream_t st, uint8_t** out) {
     cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
     N730_CUDA(cudaStreamIsCapturing(st, &cs));
     N730_REQUIRE(cs == cudaStreamCaptureStatusNone, N730_STATE,
-                 "gemm_tc: packed-A workspace must grow outside stream capture (%zu bytes)", bytes);
+                 "gemm_tc: packed-x workspace must grow outside stream capture (%zu bytes)", bytes);
     N730_CUDA(cudaStreamSynchronize(st));  // a kernel in flight may still read the old buffer
     if (buf[dev]) N730_CUDA(cudaFree(buf[dev]));
     buf[dev] = nullptr;
@@ -418,22 +441,28 @@ int gemm_tc_launch(const GemvArgs& a, float* inv_ws, cudaStream_t st) {
   int* err = gemv_err_word();
   N730_REQUIRE(err, N730_OOM, "gemm_tc: error word allocation failed");
   if (int rc = gemm_tc_prepare()) return rc;
-  const int TT = (a.batch + TC_BM - 1) / TC_BM, KB = w.cols / 64;
+  // 256-token tiles dequantise each weight once per 256 tokens; 128-token tiles
+  // when 256 would leave SMs idle (few row tiles, few tokens)
+  const int RT = (w.rows + TC_BN - 1) / TC_BN, KB = w.cols / 64;
+  const int ntok = (int64_t)RT * ((a.batch + 255) / 256) >= num_sms() ? 256 : 128;
+  const int TT = (a.batch + ntok - 1) / ntok, XT = TT * (ntok / TC_XT);  // output tiles, packed sub-tiles
   uint8_t* x16 = nullptr;
-  if (int rc = x16_workspace((size_t)TT * KB * TC_SUB, st, &x16)) return rc;
+  if (int rc = x16_workspace((size_t)XT * KB * TC_SUB, st, &x16)) return rc;
   if (a.norm_w) {
     inv_rms_kernel<<<(a.batch + 7) / 8, 256, 0, st>>>(a.x, a.ldx, a.batch, w.cols, a.eps, inv_ws);
     N730_CHECK_LAUNCH();
   }
-  x16_pack_kernel<<<dim3(KB, TT), 256, 0, st>>>(a.x, a.ldx, a.batch, a.norm_w ? inv_ws : nullptr, a.norm_w, x16);
+  // every sub-tile a CTA copies is packed (tokens >= T as zeros)
+  x16_pack_kernel<<<dim3(KB, XT), 256, 0, st>>>(a.x, a.ldx, a.batch, a.norm_w ? inv_ws : nullptr, a.norm_w, x16);
   N730_CHECK_LAUNCH();
   TcArgs p = {};
   p.blob = w.codes; p.rows = w.rows; p.cols = w.cols; p.G = w.n_groups; p.kpg = w.group / 16;
   p.x16 = x16; p.T = a.batch;
   p.y = a.y; p.ldy = a.ldy; p.bias = a.bias; p.residual = a.residual; p.ldr = a.ldr; p.swiglu = a.swiglu;
   p.err = err;
-  const dim3 grid((w.rows + TC_BN - 1) / TC_BN, TT);
-  gemm_tc_kernel<<<grid, TC_WARPS * 32, TC_SMEM, st>>>(p);
+  const dim3 grid(RT, TT);
+  if (ntok == 256) gemm_tc_kernel<256><<<grid, TC_WARPS * 32, TcCfg<256>::SMEM, st>>>(p);
+  else gemm_tc_kernel<128><<<grid, TC_WARPS * 32, TcCfg<128>::SMEM, st>>>(p);
   N730_CHECK_LAUNCH();
   return N730_OK;
 }

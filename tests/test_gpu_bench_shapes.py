@@ -171,6 +171,7 @@ def _gpu_weight(rows, cols, seed):
 
 
 @pytest.mark.parametrize("rows,cols,tokens,epi", [(1024, 3584, 512, "plain"), (3584, 18944, 256, "bias_resid"),
+                                                  (19200, 3584, 300, "norm_swiglu"), (37888, 3584, 512, "plain"),
                                                   (2048, 3584, 300, "norm_swiglu"), (640, 8192, 129, "plain")])
 def test_qgemm_matches_oracle(rows, cols, tokens, epi):
     """The tcgen05 GEMM rounds x and the dequantised weights to fp16 and accumulates in fp32:

@@ -1,9 +1,11 @@
 """tcgen05 GEMM (n730_qgemm) against the tensor-core GEMV on the same weights.
 
-Both read INT4 g128 weights in fragment tiles and round x to fp16; the GEMM
-also rounds the dequantised weights to fp16 (one more 2^-11 relative error per
-weight), so the bar is 3e-3 of max|y|.  Covers token counts below, at and
-across the 128-token tile, partial row tiles, and every epilogue.
+Both read INT4 group-wise weights in fragment tiles and round x to fp16; the
+GEMM also rounds the dequantised weights to fp16 (one more 2^-11 relative error
+per weight), so the bar is 3e-3 of max|y|.  Covers token counts below, at and
+across the 128- and 256-token tiles (256-token tiles are taken when there are
+enough row tiles to fill the SMs: 150 x 2 here), partial row tiles, groups of
+64, 128 and 256 columns, and every epilogue.
 """
 import ctypes as C
 
@@ -17,33 +19,35 @@ pytestmark = pytest.mark.gpu
 TOL = 3e-3
 
 
-def _weight(rows, cols, seed):
+def _weight(rows, cols, seed, group=128):
     import torch
     lib = _lib.cuda()
     g = torch.Generator(device="cuda")
     g.manual_seed(seed)
     w = torch.randn(rows, cols, generator=g, device="cuda") * 0.02
     codes = torch.empty(rows * cols // 2, dtype=torch.uint8, device="cuda")
-    s16 = torch.empty(rows, cols // 128, dtype=torch.float16, device="cuda")
+    s16 = torch.empty(rows, cols // group, dtype=torch.float16, device="cuda")
     z16 = torch.empty_like(s16)
     P = lambda t: C.c_void_p(t.data_ptr())
-    _lib.check(lib.n730_quantize_grouped(P(w), rows, cols, 4, 128, P(codes), P(s16), P(z16), None), "quantize")
+    _lib.check(lib.n730_quantize_grouped(P(w), rows, cols, 4, group, P(codes), P(s16), P(z16), None), "quantize")
     q = C.c_void_p()
-    _lib.check(lib.n730_qweight_create(0x44, rows, cols, 128, 1.0, 0.0, P(codes), P(s16), P(z16), 1, None,
+    _lib.check(lib.n730_qweight_create(0x44, rows, cols, group, 1.0, 0.0, P(codes), P(s16), P(z16), 1, None,
                                        C.byref(q)), "create")
     _lib.check(lib.n730_qweight_set_layout(q, 1, None), "layout")
     torch.cuda.synchronize()
     return q
 
 
-@pytest.mark.parametrize("rows,cols,tokens", [(256, 512, 128), (400, 512, 33), (384, 1024, 300), (160, 256, 1),
-                                              (512, 3584, 200)])
+@pytest.mark.parametrize("rows,cols,tokens,group", [(256, 512, 128, 128), (400, 512, 33, 128), (384, 1024, 300, 128),
+                                                    (160, 256, 1, 128), (512, 3584, 200, 128), (19200, 512, 300, 128),
+                                                    (19200, 512, 256, 128), (1024, 1024, 200, 64),
+                                                    (1024, 1024, 200, 256), (19200, 1024, 270, 256)])
 @pytest.mark.parametrize("epi", ["plain", "bias_resid", "norm_swiglu"])
-def test_qgemm_matches_gemv(rows, cols, tokens, epi):
+def test_qgemm_matches_gemv(rows, cols, tokens, group, epi):
     import torch
     lib = _lib.cuda()
     P = lambda t: C.c_void_p(t.data_ptr()) if t is not None else None
-    q = _weight(rows, cols, seed=rows + cols)
+    q = _weight(rows, cols, seed=rows + cols, group=group)
     g = torch.Generator(device="cuda")
     g.manual_seed(tokens)
     x = torch.randn(tokens, cols, generator=g, device="cuda")
