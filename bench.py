@@ -857,6 +857,7 @@ def run_gemm(a):
     INT4 g128 weight of --linear-shape for --tokens tokens, calls replayed from a CUDA graph over
     --copies weight copies; TFLOP/s = 2 rows cols tokens per call against the measured burst
     bf16 tensor peak (the kernel is kind::f16, the same rate)."""
+    import ctypes as C
     import torch
     from n730_b200 import _lib
     lib = _lib.cuda()

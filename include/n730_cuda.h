@@ -16,6 +16,7 @@
  */
 #ifndef N730_CUDA_H
 #define N730_CUDA_H
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -220,6 +221,11 @@ int n730_model_set_seq_len(void* model, int seq, int len);
 int n730_model_forward(void* model, int seq, const int32_t* host_tokens, int n, float* host_logits);
 /* One decode step for sequences [0, batch): host ids in, host logits [batch][vocab] out. */
 int n730_model_decode(void* model, const int32_t* host_tokens, int batch, float* host_logits);
+/* Page-locked host memory (no counterpart in the reference): a logits buffer from here (or
+ * registered with cudaHostRegister) receives n730_model_decode's copy directly, with no
+ * staging copy through the engine's own buffer. */
+int n730_host_alloc(size_t bytes, void** out);
+int n730_host_free(void* ptr);
 /* The same step followed by GPU sampling (n730_sample with counter = the number of sampled
  * steps so far): host ids in, host next-token ids [batch] out (4 bytes per sequence cross
  * the bus instead of the logits).  host_u [batch] receives the uniform draws (may be null). */

@@ -1181,6 +1181,29 @@ static int step_status(Model* m) {
 
 // Decode one token for each of sequences [0, batch): host token ids in,
 // host logits [batch][vocab] out (pinned staging, copies inside the call).
+static bool is_pinned_host(const void* ptr) {
+  cudaPointerAttributes at{};
+  if (cudaPointerGetAttributes(&at, ptr) != cudaSuccess) {
+    cudaGetLastError();  // clear the error this query leaves behind
+    return false;
+  }
+  return at.type == cudaMemoryTypeHost;
+}
+
+// Page-locked host memory (e.g. the logits buffer a caller reuses across
+// n730_model_decode calls: the copy then lands in it directly).
+N730_API int n730_host_alloc(size_t bytes, void** out) {
+  N730_REQUIRE(out && bytes > 0, N730_BAD_ARG, "host_alloc: %zu bytes", bytes);
+  *out = nullptr;
+  N730_CUDA(cudaMallocHost(out, bytes));
+  return N730_OK;
+}
+
+N730_API int n730_host_free(void* ptr) {
+  if (ptr) N730_CUDA(cudaFreeHost(ptr));
+  return N730_OK;
+}
+
 N730_API int n730_model_decode(void* p, const int32_t* host_tokens, int batch, float* host_logits) {
   MODEL(p);
   N730_REQUIRE(m->finalized, N730_STATE, "model: not finalized");
@@ -1193,11 +1216,15 @@ N730_API int n730_model_decode(void* p, const int32_t* host_tokens, int batch, f
   memcpy(m->h_tok, host_tokens, (size_t)batch * 4);
   N730_CUDA(cudaMemcpyAsync(m->d_tokens, m->h_tok, (size_t)batch * 4, cudaMemcpyHostToDevice, m->st));
   if (int rc = run_decode(m, batch)) return rc;
+  // page-locked caller memory (n730_host_alloc, cudaHostRegister) takes the logits directly;
+  // pageable memory gets them through the engine's pinned staging buffer
+  const bool direct = host_logits && is_pinned_host(host_logits);
   if (host_logits) {
-    N730_CUDA(cudaMemcpyAsync(m->h_logits, m->logits, (size_t)batch * m->c.vocab * 4, cudaMemcpyDeviceToHost, m->st));
+    N730_CUDA(cudaMemcpyAsync(direct ? host_logits : m->h_logits, m->logits, (size_t)batch * m->c.vocab * 4,
+                              cudaMemcpyDeviceToHost, m->st));
   }
   N730_CUDA(cudaStreamSynchronize(m->st));
-  if (host_logits) memcpy(host_logits, m->h_logits, (size_t)batch * m->c.vocab * 4);
+  if (host_logits && !direct) memcpy(host_logits, m->h_logits, (size_t)batch * m->c.vocab * 4);
   for (int b = 0; b < batch; ++b) m->h_seq[b] += 1;
   return step_status(m);
 }

@@ -59,6 +59,10 @@ def _sigs(lib):
     lib.n730_model_forward.restype = i32
     lib.n730_model_decode.argtypes = [vp, vp, i32, vp]
     lib.n730_model_decode.restype = i32
+    lib.n730_host_alloc.argtypes = [C.c_size_t, C.POINTER(vp)]
+    lib.n730_host_alloc.restype = i32
+    lib.n730_host_free.argtypes = [vp]
+    lib.n730_host_free.restype = i32
     lib.n730_model_decode_sample.argtypes = [vp, vp, i32, C.c_float, C.c_float, C.c_uint64, vp, vp]
     lib.n730_model_decode_sample.restype = i32
     lib.n730_model_decode_device.argtypes = [vp, vp, i32, vp, vp]
@@ -136,6 +140,32 @@ class ModelShape:
     tie_embeddings: bool = False
 
 
+class _PinnedBlock:
+    """Page-locked host memory from n730_host_alloc, freed when the last array viewing it goes."""
+
+    def __init__(self, lib, nbytes: int):
+        self.lib, self.ptr = lib, C.c_void_p()
+        _lib.check(lib.n730_host_alloc(nbytes, C.byref(self.ptr)), "host_alloc")
+
+    def __del__(self):
+        try:
+            if self.ptr:
+                self.lib.n730_host_free(self.ptr)
+        except Exception:
+            pass
+
+
+def _pinned_f32(lib, n: int) -> np.ndarray:
+    """A float32 array of n zeros in page-locked memory: n730_model_decode copies the logits
+    straight into it.  The array keeps the block alive (numpy base -> ctypes array -> block)."""
+    blk = _PinnedBlock(lib, n * 4)
+    arr = (C.c_float * n).from_address(blk.ptr.value)
+    arr._block = blk
+    out = np.frombuffer(arr, np.float32)
+    out[:] = 0.0
+    return out
+
+
 class Engine:
     """Owns one C model; all methods raise ``N730Error`` on a negative code."""
 
@@ -155,7 +185,7 @@ class Engine:
         _lib.check(self.lib.n730_model_create(C.byref(c), C.byref(self.h)), "model_create")
         self.max_batch = max_batch
         self.max_ctx = max_ctx
-        self._logits = np.zeros((max_batch, shape.vocab), np.float32)
+        self._logits = _pinned_f32(self.lib, max_batch * shape.vocab).reshape(max_batch, shape.vocab)
 
     def set_qweight(self, layer: int, slot: int, qw):
         _lib.check(self.lib.n730_model_set_qweight(self.h, layer, slot, qw), "model_set_qweight")

@@ -192,3 +192,23 @@ def test_streamed_layers_match_resident(model, depth):
         es.run_linear(0, 0, 16, 1, 16)  # rejected before any pointer is used
     es.close()
     er.close()
+
+
+def test_decode_into_pinned_and_pageable_buffers(model):
+    """n730_model_decode copies logits straight into page-locked caller memory (the Engine's
+    own buffer) and through its staging buffer into pageable memory: same values either way."""
+    import ctypes as C
+    shape, blocks, _ = model
+    e = _engine(shape, blocks, max_batch=2)
+    for b in range(2):
+        e.forward(np.arange(5 + b) % shape.vocab, seq=b)
+    L = [e.seq_len(b) for b in range(2)]
+    pinned = e.decode([1, 2]).copy()
+    for b in range(2):
+        e.set_seq_len(b, L[b])
+    pageable = np.full((2, shape.vocab), np.nan, np.float32)
+    rc = e.lib.n730_model_decode(e.h, np.array([1, 2], np.int32).ctypes.data_as(C.c_void_p), 2,
+                                 pageable.ctypes.data_as(C.c_void_p))
+    e.close()
+    assert rc == 0
+    assert np.array_equal(pinned, pageable)
