@@ -909,34 +909,51 @@ __global__ void __launch_bounds__(PD_THREADS, 1) persist_decode_kernel(const PdA
     {
       const int items = nj * KPG * 4;  // (k-step, tq) items of the nj groups
       uint2* xf2 = reinterpret_cast<uint2*>(xf);
-      for (int i = tid; i < items; i += PD_THREADS) {
-        const int s = i >> 2, tqi = i & 3, k = s * 16 + 2 * tqi;
-        xf2[(((s >> 1) * 4 + tqi) << 1) + (s & 1)] =
-            make_uint2(h2u(__floats2half2_rn(mloc[k], mloc[k + 1])), h2u(__floats2half2_rn(mloc[k + 8], mloc[k + 9])));
-      }
-      __syncthreads();
-      for (int grp = tid; grp < nj; grp += PD_THREADS) {
-        const uint4* src = xf + (size_t)grp * (KPG >> 1) * 4;
+      // a group's KPG*4 items sit in one warp (or half-warp) for KPG <= 8: its Sx is a
+      // shuffle reduction of the rounded values (no serial pass over shared memory)
+      for (int i0 = 0; i0 < items; i0 += PD_THREADS) {
+        const int i = i0 + tid;
         float v = 0.f;
-        for (int e = 0; e < KPG * 2; ++e) {
-          const uint4 u = src[e];
-          const float2 f0 = __half22float2(u2h(u.x)), f1 = __half22float2(u2h(u.y));
-          const float2 f2 = __half22float2(u2h(u.z)), f3 = __half22float2(u2h(u.w));
-          v += ((f0.x + f0.y) + (f1.x + f1.y)) + ((f2.x + f2.y) + (f3.x + f3.y));
+        if (i < items) {
+          const int s = i >> 2, tqi = i & 3, k = s * 16 + 2 * tqi;
+          const __half2 h01 = __floats2half2_rn(mloc[k], mloc[k + 1]);
+          const __half2 h23 = __floats2half2_rn(mloc[k + 8], mloc[k + 9]);
+          xf2[(((s >> 1) * 4 + tqi) << 1) + (s & 1)] = make_uint2(h2u(h01), h2u(h23));
+          const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+          v = (f01.x + f01.y) + (f23.x + f23.y);
         }
-        sx[grp] = v;
+        if constexpr (KPG <= 8) {
+#pragma unroll
+          for (int o = KPG * 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+          if ((lane & (KPG * 4 - 1)) == 0 && i < items) sx[i / (KPG * 4)] = v;
+        }
       }
       __syncthreads();
+      if constexpr (KPG > 8) {  // a group spans two warps: sum its fp16 x from shared memory
+        for (int grp = tid; grp < nj; grp += PD_THREADS) {
+          const uint4* src = xf + (size_t)grp * (KPG >> 1) * 4;
+          float v = 0.f;
+          for (int e = 0; e < KPG * 2; ++e) {
+            const uint4 u = src[e];
+            const float2 f0 = __half22float2(u2h(u.x)), f1 = __half22float2(u2h(u.y));
+            const float2 f2 = __half22float2(u2h(u.z)), f3 = __half22float2(u2h(u.w));
+            v += ((f0.x + f0.y) + (f1.x + f1.y)) + ((f2.x + f2.y) + (f3.x + f3.y));
+          }
+          sx[grp] = v;
+        }
+        __syncthreads();
+      }
     }
     const int Td = (P.rows2 + 15) >> 4;
     const int d0 = pd_rng(0, Td, warp, PD_WARPS), d1 = pd_rng(0, Td, warp + 1, PD_WARPS);
     const int per = max(1, GPC / nj);  // whole tiles per chunk
-    auto put_rows = [&](int t, float r_g, float r_g8) {  // fixed-point sums: order-independent
-      const int r = t * 16 + g;
-      if (tq == 0) {
-        if (r < P.rows2) atomicAdd(P.acc + r, (unsigned long long)__float2ll_rn(r_g * PD_FIX));
-        if (r + 8 < P.rows2) atomicAdd(P.acc + r + 8, (unsigned long long)__float2ll_rn(r_g8 * PD_FIX));
-      }
+    // fixed-point sums (order-independent); all 32 lanes call it: lane tq 0 adds row g,
+    // lane tq 1 row g + 8 (handed over by a shuffle), so one conversion and one atomic per lane
+    auto put_rows = [&](int t, float r_g, float r_g8) {
+      const float v8 = __shfl_up_sync(0xffffffffu, r_g8, 1);
+      const int r = t * 16 + g + (tq == 1 ? 8 : 0);
+      if (tq < 2 && r < P.rows2)
+        atomicAdd(P.acc + r, (unsigned long long)__float2ll_rn((tq == 0 ? r_g : v8) * PD_FIX));
     };
     for (int u = d0; u < d1 && !wfail;) {
       const int n = min(per, d1 - u);
