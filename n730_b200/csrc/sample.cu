@@ -15,7 +15,10 @@
 // u comes from a counter-based hash of (seed, counter, row) and is written out
 // when asked, so a checker can replay the choice.
 //
-// One CTA of 1024 threads per row, no full sort: masses are summed in 32.40
+// Three kernels per call, no full sort.  The two passes that touch every logit
+// with arithmetic run on 64 CTAs per row (sp_stats_kernel: max / argmax / min
+// of each slice; sp_hist_kernel: bin masses), the pick on one CTA of 1024
+// threads per row (sample_kernel).  Masses are summed in 32.40
 // fixed point (order-independent, deterministic) into 4096 bins of
 // t = -64 (l - max) / temp spread over the row's own range (its smallest logit,
 // capped where masses fall below 2^-43), so a near-flat row uses all bins; a
@@ -24,10 +27,12 @@
 // bitonic-sorted in shared memory.  A bin with more than SP_CAP elements is
 // split into 4096 finer bins once; elements that still fall together (equal
 // to a few 1e-7 relative) are taken in index order, as are rows of equal
-// logits.  Four passes read the row (L2: the lm_head just wrote it).  The
+// logits.  The pick reads the row two to four more times (L2: the lm_head just
+// wrote it).  The
 // temperature is applied as a multiplication by its reciprocal, so p can
 // differ from exp((l - max) / temp) by an ulp or two.
 #include <cmath>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -291,17 +296,46 @@ __device__ void sp_pick_in_bin(const float* row, int V, const SpGeom& g, int b, 
     sp_index_pick(row, V, g, in_sub, before, target, strict, s);  // values equal to a few 1e-7
 }
 
-__global__ void __launch_bounds__(SP_THREADS, 1)
-sample_kernel(const float* logits, int ld, int V, float temp, float top_p, unsigned long long seed,
-              unsigned long long counter, int32_t* tokens, float* u_out) {
-  extern __shared__ __align__(16) uint8_t sp_raw[];
-  SpSmem& s = *reinterpret_cast<SpSmem*>(sp_raw);
-  const int row_i = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+// ---- row statistics and bin masses on many CTAs per row ----
+// The finishing kernel below runs on one CTA per row; the two passes that touch
+// every logit with real arithmetic (the max / argmax / min scan and the bin
+// masses, one exp per logit) are spread over SP_SLICES CTAs per row first.
+constexpr int SP_SLICES = 64;
+constexpr int SP_PRE_THREADS = 256;
+
+struct SpStat { float mx; int idx; float mn; int pad; };
+
+// Fixed-order combination of a row's slice statistics: the largest logit with
+// its first index (slices are consecutive index ranges), and the smallest.
+__device__ __forceinline__ SpStat sp_combine(const SpStat* st) {
+  SpStat r{-INFINITY, 0x7fffffff, INFINITY, 0};
+  for (int k = 0; k < SP_SLICES; ++k) {
+    const SpStat a = st[k];
+    if (a.mx > r.mx || (a.mx == r.mx && a.idx < r.idx)) { r.mx = a.mx; r.idx = a.idx; }
+    r.mn = fminf(r.mn, a.mn);
+  }
+  return r;
+}
+
+__device__ __forceinline__ void sp_slice(int V, int sl, int* i0, int* i1) {
+  const int per = (V + SP_SLICES - 1) / SP_SLICES;
+  *i0 = min(V, sl * per);
+  *i1 = min(V, *i0 + per);
+}
+
+// grid (SP_SLICES, rows): slice statistics; also zeroes the slice's share of the
+// row's bins for the next kernel
+__global__ void __launch_bounds__(SP_PRE_THREADS)
+sp_stats_kernel(const float* logits, int ld, int V, SpStat* stats, unsigned long long* hist) {
+  __shared__ float wmx[SP_PRE_THREADS / 32], wmn[SP_PRE_THREADS / 32];
+  __shared__ int widx[SP_PRE_THREADS / 32];
+  const int sl = blockIdx.x, row_i = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const float* row = logits + (int64_t)row_i * ld;
-  // 1. the largest logit with its first index, and the smallest logit
+  int i0, i1;
+  sp_slice(V, sl, &i0, &i1);
   float bv = -INFINITY, mn = INFINITY;
   int bi = 0x7fffffff;
-  for (int i = tid; i < V; i += SP_THREADS) {
+  for (int i = i0 + tid; i < i1; i += SP_PRE_THREADS) {
     const float v = row[i];
     if (v > bv) { bv = v; bi = i; }  // strided: the first index of this thread's maximum
     mn = fminf(mn, v);
@@ -313,20 +347,70 @@ sample_kernel(const float* logits, int ld, int V, float temp, float top_p, unsig
     if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
     mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
   }
-  if (lane == 0) { s.wmax[warp] = bv; s.widx[warp] = bi; s.wmin[warp] = mn; }
+  if (lane == 0) { wmx[warp] = bv; widx[warp] = bi; wmn[warp] = mn; }
   __syncthreads();
-  if (warp == 0) {
-    bv = s.wmax[lane];
-    bi = s.widx[lane];
-    mn = s.wmin[lane];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-      mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+  if (tid == 0) {
+    SpStat r{-INFINITY, 0x7fffffff, INFINITY, 0};
+    for (int w = 0; w < SP_PRE_THREADS / 32; ++w) {
+      if (wmx[w] > r.mx || (wmx[w] == r.mx && widx[w] < r.idx)) { r.mx = wmx[w]; r.idx = widx[w]; }
+      r.mn = fminf(r.mn, wmn[w]);
     }
-    if (lane == 0) { s.wmax[0] = bv; s.widx[0] = bi; s.wmin[0] = mn; }
+    stats[(size_t)row_i * SP_SLICES + sl] = r;
+  }
+  unsigned long long* h = hist + (size_t)row_i * SP_BINS;
+  for (int b = sl * (SP_BINS / SP_SLICES) + tid; b < (sl + 1) * (SP_BINS / SP_SLICES); b += SP_PRE_THREADS) h[b] = 0ull;
+}
+
+// Row geometry from the combined statistics (the same arithmetic in every kernel,
+// so every CTA of a row bins identically); false: greedy or a row of equal logits.
+__device__ __forceinline__ bool sp_geom(const SpStat& t, float temp, SpGeom* g) {
+  if (!(temp > 0.f)) return false;
+  const float inv_temp = 1.0f / temp;
+  const float R = fminf((t.mx - t.mn) * 64.f * inv_temp, SP_TMAX);
+  if (!(R > 0.f)) return false;
+  *g = SpGeom{t.mx, inv_temp, 64.f * inv_temp * ((float)SP_BINS / R)};
+  return true;
+}
+
+// grid (SP_SLICES, rows): the slice's bin masses (32.40 fixed point) summed in
+// shared memory, then added into the row's bins (integer sums: order-independent)
+__global__ void __launch_bounds__(SP_PRE_THREADS)
+sp_hist_kernel(const float* logits, int ld, int V, float temp, const SpStat* stats, unsigned long long* hist) {
+  __shared__ unsigned long long hs[SP_BINS];
+  __shared__ SpStat tot;
+  const int sl = blockIdx.x, row_i = blockIdx.y, tid = threadIdx.x;
+  const float* row = logits + (int64_t)row_i * ld;
+  if (tid == 0) tot = sp_combine(stats + (size_t)row_i * SP_SLICES);
+  for (int b = tid; b < SP_BINS; b += SP_PRE_THREADS) hs[b] = 0ull;
+  __syncthreads();
+  SpGeom g;
+  if (!sp_geom(tot, temp, &g)) return;
+  int i0, i1;
+  sp_slice(V, sl, &i0, &i1);
+  for (int i = i0 + tid; i < i1; i += SP_PRE_THREADS) {
+    const float l = row[i];
+    atomicAdd(&hs[sp_bin_of(sp_x(l, g))], sp_mass(sp_p(l, g)));
+  }
+  __syncthreads();
+  unsigned long long* h = hist + (size_t)row_i * SP_BINS;
+  for (int b = tid; b < SP_BINS; b += SP_PRE_THREADS)
+    if (hs[b]) atomicAdd(h + b, hs[b]);
+}
+
+__global__ void __launch_bounds__(SP_THREADS, 1)
+sample_kernel(const float* logits, int ld, int V, float temp, float top_p, unsigned long long seed,
+              unsigned long long counter, int32_t* tokens, float* u_out, const SpStat* stats,
+              const unsigned long long* hist) {
+  extern __shared__ __align__(16) uint8_t sp_raw[];
+  SpSmem& s = *reinterpret_cast<SpSmem*>(sp_raw);
+  const int row_i = blockIdx.x, tid = threadIdx.x;
+  const float* row = logits + (int64_t)row_i * ld;
+  // 1. the largest logit with its first index, and the smallest (from the slice statistics)
+  if (tid == 0) {
+    const SpStat t = sp_combine(stats + (size_t)row_i * SP_SLICES);
+    s.wmax[0] = t.mx;
+    s.widx[0] = t.idx;
+    s.wmin[0] = t.mn;
   }
   __syncthreads();
   const float m = s.wmax[0];
@@ -356,17 +440,11 @@ sample_kernel(const float* logits, int ld, int V, float temp, float top_p, unsig
     return;
   }
   const SpGeom g{m, inv_temp, 64.f * inv_temp * ((float)SP_BINS / R)};
-  // 2. masses per bin
-  for (int b = tid; b < SP_BINS; b += SP_THREADS) s.mass[b] = 0ull;
-  __syncthreads();
-  for (int i = tid; i < V; i += SP_THREADS) {
-    const float l = row[i];
-    atomicAdd(&s.mass[sp_bin_of(sp_x(l, g))], sp_mass(sp_p(l, g)));
-  }
-  __syncthreads();
+  // 2. masses per bin (summed by sp_hist_kernel)
   unsigned long long mb[4], loc = 0;
+  const unsigned long long* hrow = hist + (size_t)row_i * SP_BINS;
 #pragma unroll
-  for (int r = 0; r < 4; ++r) { mb[r] = s.mass[tid * 4 + r]; loc += mb[r]; }
+  for (int r = 0; r < 4; ++r) { mb[r] = hrow[tid * 4 + r]; loc += mb[r]; }
   unsigned long long total;
   const unsigned long long ex = sp_scan(loc, s, &total);
   // (mb / ex stay in registers: the finer bins of a crowded bin reuse s.mass)
@@ -387,6 +465,35 @@ sample_kernel(const float* logits, int ld, int V, float temp, float top_p, unsig
   if (tid == 0) tokens[row_i] = s.res_idx;
 }
 
+// Per-device workspace of the pre-passes (slice statistics + row bins), grown on
+// demand, never inside a stream capture.
+static int sp_workspace(int batch, cudaStream_t st, SpStat** stats, unsigned long long** hist) {
+  static std::mutex mu;
+  static uint8_t* buf[N730_MAX_DEVICES] = {};
+  static int cap[N730_MAX_DEVICES] = {};
+  int dev = 0;
+  N730_CUDA(cudaGetDevice(&dev));
+  N730_REQUIRE(dev >= 0 && dev < N730_MAX_DEVICES, N730_BAD_ARG, "sample: device %d", dev);
+  const size_t hist_off = ((size_t)batch * SP_SLICES * sizeof(SpStat) + 255) / 256 * 256;
+  std::lock_guard<std::mutex> lk(mu);
+  if (cap[dev] < batch) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    N730_CUDA(cudaStreamIsCapturing(st, &cs));
+    N730_REQUIRE(cs == cudaStreamCaptureStatusNone, N730_STATE,
+                 "sample: workspace for %d rows must grow outside stream capture", batch);
+    N730_CUDA(cudaStreamSynchronize(st));  // a kernel in flight may still use the old buffer
+    if (buf[dev]) N730_CUDA(cudaFree(buf[dev]));
+    buf[dev] = nullptr;
+    cap[dev] = 0;
+    N730_CUDA(cudaMalloc(&buf[dev], hist_off + (size_t)batch * SP_BINS * 8));
+    cap[dev] = batch;
+  }
+  const size_t off = ((size_t)cap[dev] * SP_SLICES * sizeof(SpStat) + 255) / 256 * 256;
+  *stats = reinterpret_cast<SpStat*>(buf[dev]);
+  *hist = reinterpret_cast<unsigned long long*>(buf[dev] + off);
+  return N730_OK;
+}
+
 int sample_launch(const float* d_logits, int batch, int vocab, int ld, float temp, float top_p,
                   unsigned long long seed, unsigned long long counter, int32_t* d_tokens, float* d_u,
                   cudaStream_t st) {
@@ -396,8 +503,17 @@ int sample_launch(const float* d_logits, int batch, int vocab, int ld, float tem
   N730_REQUIRE(std::isfinite(temp) && std::isfinite(top_p) && top_p > 0.f, N730_BAD_ARG,
                "sample: temperature %g, top_p %g", temp, top_p);
   if (int rc = smem_attr_once<sample_kernel>((int)sizeof(SpSmem))) return rc;
+  SpStat* stats = nullptr;
+  unsigned long long* hist = nullptr;
+  if (int rc = sp_workspace(batch, st, &stats, &hist)) return rc;
+  sp_stats_kernel<<<dim3(SP_SLICES, batch), SP_PRE_THREADS, 0, st>>>(d_logits, ld, vocab, stats, hist);
+  N730_CHECK_LAUNCH();
+  if (temp > 0.f) {
+    sp_hist_kernel<<<dim3(SP_SLICES, batch), SP_PRE_THREADS, 0, st>>>(d_logits, ld, vocab, temp, stats, hist);
+    N730_CHECK_LAUNCH();
+  }
   sample_kernel<<<batch, SP_THREADS, sizeof(SpSmem), st>>>(d_logits, ld, vocab, temp, top_p, seed, counter, d_tokens,
-                                                           d_u);
+                                                           d_u, stats, hist);
   N730_CHECK_LAUNCH();
   return N730_OK;
 }
