@@ -279,6 +279,9 @@ int n730_model_run_step_kernel(void* model, void* stream);
  * [n_phases] (0 GEMV, 1 attention, 2 FFN).  host_times null: only *n_phases and *grid. */
 int n730_model_trace_step(void* model, void* stream, uint64_t* host_times, int64_t cap, int8_t* host_kinds,
                           int* n_phases, int* grid);
+/* One of the model's linears alone (which: 0 q|k|v, 1 o_proj, 2 gate|up + SwiGLU, 3 down_proj,
+ * 4 lm_head) on `batch` device rows, with the kernel the decode step picks for that batch
+ * (tensor-core GEMV, or the tcgen05 GEMM for wide linears from 17 rows and any from 128). */
 int n730_model_run_linear(void* model, int layer, int which, const float* d_x, int batch, float* d_y,
                           void* stream);
 /* Algorithmic bytes of that linear for `batch` rows: codes + fp16 scale/zero + x + y. */

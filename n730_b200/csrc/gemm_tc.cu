@@ -50,8 +50,10 @@ constexpr uint32_t TC_TMEM_COLS = 512;      // accumulator (NTOK columns) + one 
 
 template <int NTOK>
 struct TcCfg {
-  static constexpr int STAGES = NTOK == 256 ? 3 : 4;
+  // deeper pipelines for narrower token tiles (decode batches), within shared memory and TMEM
+  static constexpr int STAGES = NTOK == 256 ? 3 : NTOK == 128 ? 4 : NTOK == 64 ? 6 : 7;
   static constexpr int XB = NTOK * TC_BK * 2;  // x bytes per step: [64-column block][NTOK rows][128 B]
+  static constexpr int XR = NTOK < TC_XT ? NTOK : TC_XT;  // token rows per x copy (one packed sub-tile at most)
   static constexpr int STAGE = XB + TC_RAW;    // a multiple of 1024 (swizzle atoms stay aligned)
   static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE + (3 * STAGES + 1) * 8 + 32;
   // kind::f16 instruction descriptor: D fp32, A = B = fp16, both K-major, N = NTOK, M = 128
@@ -204,7 +206,6 @@ __global__ void __launch_bounds__(TC_WARPS * 32, 1) gemm_tc_kernel(const TcArgs 
   int* counts = const_cast<int*>(abortf) + 1;  // [0] steps produced, [1] steps issued, [2] result ok
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int n0 = blockIdx.x * TC_BN, m0 = blockIdx.y * NTOK;
-  const int xt0 = blockIdx.y * (NTOK / TC_XT);  // first packed 128-token sub-tile
   const int KB = p.cols / 64;                   // packed 64-column blocks per sub-tile
   const int GB = p.kpg * 128 + 64;
   const int n_tiles = (p.rows + 15) >> 4, tile0 = n0 >> 4;
@@ -246,13 +247,17 @@ __global__ void __launch_bounds__(TC_WARPS * 32, 1) gemm_tc_kernel(const TcArgs 
         if (kt >= S && !tc_wait(&empty[s], (uint32_t)(((kt / S) - 1) & 1), abortf)) break;
         uint8_t* st = smem + s * Cfg::STAGE;
         mbar_arrive_expect_tx(&full[s], stage_tx);
-        // x: 64-column block h of the step holds NTOK rows; sub-tile i fills rows [128 i, 128 i + 128)
+        // x: 64-column block h of the step holds NTOK rows, copied XR rows (<= one packed
+        // sub-tile, row r of a sub-tile at byte 128 r) at a time
 #pragma unroll
         for (int h = 0; h < 2; ++h)
 #pragma unroll
-          for (int i = 0; i < NTOK / TC_XT; ++i)
-            bulk_g2s(st + h * (NTOK * 128) + i * TC_SUB, p.x16 + ((size_t)(xt0 + i) * KB + 2 * kt + h) * TC_SUB,
-                     TC_SUB, &full[s]);
+          for (int i = 0; i < NTOK / Cfg::XR; ++i) {
+            const int tok = m0 + i * Cfg::XR;
+            bulk_g2s(st + h * (NTOK * 128) + i * Cfg::XR * 128,
+                     p.x16 + ((size_t)(tok / TC_XT) * KB + 2 * kt + h) * TC_SUB + (size_t)(tok % TC_XT) * 128,
+                     Cfg::XR * 128, &full[s]);
+          }
         const int s0 = kt * 8, gi = s0 / p.kpg;  // first k-step and group of this step
         for (int w = 0; w < nt_here; ++w) {
           const uint8_t* grp = p.blob + ((int64_t)(tile0 + w) * p.G + gi) * GB;
@@ -350,14 +355,14 @@ __global__ void __launch_bounds__(TC_WARPS * 32, 1) gemm_tc_kernel(const TcArgs 
   tc_fence_after();
   if (*abortf && tid == 0) atomicExch(p.err, DEV_ERR_TIMEOUT);
   if (counts[2] && warp < 8) {
-    // ---- epilogue: warp w reads TMEM lanes 32 (w % 4).. (W rows), token columns [w / 4 * NTOK / 2, +NTOK / 2) ----
+    // ---- epilogue: warp w reads TMEM lanes 32 (w % 4).. (W rows), token columns 32 c.. for c = w / 4, + 2, ... ----
     const int q = warp & 3, hh = warp >> 2;
     const int n = n0 + 32 * q + lane;
     const bool nin = n < p.rows;
     const float bv = p.bias && nin ? p.bias[n] : 0.f;
 #pragma unroll 1
-    for (int c = 0; c < NTOK / 64; ++c) {
-      const int col0 = hh * (NTOK / 2) + c * 32;
+    for (int c = hh; c < NTOK / 32; c += 2) {
+      const int col0 = c * 32;
       float v[32];
       tc_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)col0, v);
 #pragma unroll
@@ -400,12 +405,24 @@ int* gemv_err_word();
 // One-time kernel attribute set-up (call before any stream capture).
 int gemm_tc_prepare() {
   if (int rc = smem_attr_once<gemm_tc_kernel<256>>((int)TcCfg<256>::SMEM)) return rc;
-  return smem_attr_once<gemm_tc_kernel<128>>((int)TcCfg<128>::SMEM);
+  if (int rc = smem_attr_once<gemm_tc_kernel<128>>((int)TcCfg<128>::SMEM)) return rc;
+  if (int rc = smem_attr_once<gemm_tc_kernel<64>>((int)TcCfg<64>::SMEM)) return rc;
+  return smem_attr_once<gemm_tc_kernel<32>>((int)TcCfg<32>::SMEM);
 }
 
 bool gemm_tc_supported(const QWeight& w, int T) {
   const int kpg = w.group / 16;
   return w.layout == 1 && w.bits == 4 && w.cols % TC_BK == 0 && (kpg == 4 || kpg == 8 || kpg == 16) && T >= 1;
+}
+
+// Token tile of a launch: decode batches (< 128 tokens) one tile of 32 / 64 / 128;
+// prefill 256-token tiles (each dequantised weight serves 256 tokens) unless that
+// leaves SMs idle, then 128.
+int gemm_tc_tile(int row_tiles, int tokens) {
+  if (tokens <= 32) return 32;
+  if (tokens <= 64) return 64;
+  if (tokens < 128) return 128;
+  return (int64_t)row_tiles * ((tokens + 255) / 256) >= num_sms() ? 256 : 128;
 }
 
 // Packed-x workspace of the current device, grown on demand (never inside a stream capture).
@@ -431,6 +448,16 @@ static int x16_workspace(size_t bytes, cudaStream_t st, uint8_t** out) {
   return N730_OK;
 }
 
+// Grow the packed-x workspace for calls of up to `tokens` tokens and `cols` columns now,
+// so that calls captured into a CUDA graph later never need to grow it.
+int gemm_tc_reserve(int tokens, int cols, cudaStream_t st) {
+  if (tokens < 1 || cols < 64) return N730_OK;
+  const int KB = (cols + 63) / 64;
+  const int XT = (tokens + 255) / 256 * 2;  // the most sub-tiles any token tile choice packs
+  uint8_t* x16 = nullptr;
+  return x16_workspace((size_t)XT * KB * TC_SUB, st, &x16);
+}
+
 int gemm_tc_launch(const GemvArgs& a, float* inv_ws, cudaStream_t st) {
   const QWeight& w = *a.w;
   N730_REQUIRE(gemm_tc_supported(w, a.batch), N730_UNSUPPORTED, "gemm_tc: needs INT4 fragment tiles, K %% 64 == 0");
@@ -444,8 +471,9 @@ int gemm_tc_launch(const GemvArgs& a, float* inv_ws, cudaStream_t st) {
   // 256-token tiles dequantise each weight once per 256 tokens; 128-token tiles
   // when 256 would leave SMs idle (few row tiles, few tokens)
   const int RT = (w.rows + TC_BN - 1) / TC_BN, KB = w.cols / 64;
-  const int ntok = (int64_t)RT * ((a.batch + 255) / 256) >= num_sms() ? 256 : 128;
-  const int TT = (a.batch + ntok - 1) / ntok, XT = TT * (ntok / TC_XT);  // output tiles, packed sub-tiles
+  const int ntok = gemm_tc_tile(RT, a.batch);
+  const int TT = (a.batch + ntok - 1) / ntok;              // output token tiles
+  const int XT = (TT * ntok + TC_XT - 1) / TC_XT;          // packed 128-token sub-tiles
   uint8_t* x16 = nullptr;
   if (int rc = x16_workspace((size_t)XT * KB * TC_SUB, st, &x16)) return rc;
   if (a.norm_w) {
@@ -462,7 +490,9 @@ int gemm_tc_launch(const GemvArgs& a, float* inv_ws, cudaStream_t st) {
   p.err = err;
   const dim3 grid(RT, TT);
   if (ntok == 256) gemm_tc_kernel<256><<<grid, TC_WARPS * 32, TcCfg<256>::SMEM, st>>>(p);
-  else gemm_tc_kernel<128><<<grid, TC_WARPS * 32, TcCfg<128>::SMEM, st>>>(p);
+  else if (ntok == 128) gemm_tc_kernel<128><<<grid, TC_WARPS * 32, TcCfg<128>::SMEM, st>>>(p);
+  else if (ntok == 64) gemm_tc_kernel<64><<<grid, TC_WARPS * 32, TcCfg<64>::SMEM, st>>>(p);
+  else gemm_tc_kernel<32><<<grid, TC_WARPS * 32, TcCfg<32>::SMEM, st>>>(p);
   N730_CHECK_LAUNCH();
   return N730_OK;
 }

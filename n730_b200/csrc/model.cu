@@ -527,6 +527,7 @@ static int finalize(Model* m) {
   const N730ModelConfig& c = m->c;
   if (int rc = gemv_prepare()) return rc;
   if (int rc = gemm_tc_prepare()) return rc;
+  if (int rc = gemm_tc_reserve(std::max(c.max_batch, c.max_prefill), std::max(c.hidden, c.ffn), m->st)) return rc;
   const int nl = c.layers;
   m->L.assign(nl, Layer{});
   auto W = [&](int l, int s) -> QWeight* {
@@ -703,8 +704,22 @@ static int finalize(Model* m) {
   return N730_OK;
 }
 
-// One linear for `batch` rows of x: the tcgen05 GEMM from GEMM_TC_MIN_TOKENS
-// rows on (weights read once per 128 rows), else the dequant-GEMV.
+// GEMM or GEMV for `batch` rows.  From GEMM_TC_MIN_TOKENS rows on the tcgen05 GEMM
+// (each weight dequantised once per token tile).  Between 17 and 127 rows the GEMV
+// streams the weights once per 16 rows, so the GEMM also wins there when its grid
+// (128-row tiles x token tiles) fills the SMs: measured at 32 rows, gate|up of the 7B
+// shape 73 us against 126 us; with fewer CTAs (o_proj / down_proj, 28 row tiles) or
+// at <= 16 rows the GEMV is faster (the GEMM's per-step dequant latency is exposed
+// when a step holds few tokens).
+static bool use_gemm_tc(const QWeight& w, int batch) {
+  if (!gemm_tc_supported(w, batch)) return false;
+  if (batch >= GEMM_TC_MIN_TOKENS) return true;
+  if (batch <= 16) return false;
+  const int rt = (w.rows + 127) / 128, ntok = gemm_tc_tile(rt, batch);
+  return (int64_t)rt * ((batch + ntok - 1) / ntok) >= num_sms();
+}
+
+// One linear for `batch` rows of x (use_gemm_tc picks the kernel).
 static int gemv(Model* m, const QWeight* w, const float* x, int ldx, int batch, float* y, int ldy,
                 const float* bias, const float* resid, int ldr, const float* norm, int swiglu) {
   GemvArgs a = {};
@@ -712,8 +727,7 @@ static int gemv(Model* m, const QWeight* w, const float* x, int ldx, int batch, 
   a.residual = resid; a.ldr = ldr; a.norm_w = norm; a.eps = m->c.rms_eps; a.swiglu = swiglu;
   a.pdl = m->c.use_pdl;
   if (w->rows <= m->c.hidden) { a.split_ws = m->split_ws; a.split_ws_floats = m->split_ws_floats; }
-  if (batch >= GEMM_TC_MIN_TOKENS && gemm_tc_supported(*w, batch) && !m->c.exact_gemv)
-    return gemm_tc_launch(a, m->rms_ws, m->st);
+  if (use_gemm_tc(*w, batch) && !m->c.exact_gemv) return gemm_tc_launch(a, m->rms_ws, m->st);
   return gemv_launch(a, m->st);
 }
 
@@ -1427,7 +1441,9 @@ N730_API int n730_model_run_linear(void* p, int layer, int which, const float* d
   GemvArgs a = {};
   a.w = w; a.x = d_x; a.ldx = w->cols; a.batch = batch; a.y = d_y;
   a.swiglu = which == 2; a.ldy = which == 2 ? w->rows / 2 : w->rows;
-  return gemv_launch(a, stream ? (cudaStream_t)stream : m->st);
+  cudaStream_t st = stream ? (cudaStream_t)stream : m->st;
+  if (use_gemm_tc(*w, batch) && !m->c.exact_gemv) return gemm_tc_launch(a, m->rms_ws, st);  // as the decode step
+  return gemv_launch(a, st);
 }
 
 // Algorithmic bytes of one linear: packed codes + scale/zero + x + y.

@@ -54,7 +54,12 @@ int gemv_mma_launch(const GemvArgs& a, cudaStream_t stream);
 // tcgen05 GEMM for many tokens (gemm_tc.cu); inv_ws: batch floats of workspace when norm_w is set
 bool gemm_tc_supported(const QWeight& w, int tokens);
 int gemm_tc_prepare();
-constexpr int GEMM_TC_MIN_TOKENS = 128;  // below this the GEMV streams the weights once per 16 tokens
+int gemm_tc_reserve(int tokens, int cols, cudaStream_t stream);
+int gemm_tc_tile(int row_tiles, int tokens);
+// from this many rows of x on, model linears take the tcgen05 GEMM (each weight dequantised
+// once for up to 256 rows); below it the GEMV (weights streamed once per 16 rows), except
+// where the model's rule prefers the GEMM (wide linears at 17-127 rows)
+constexpr int GEMM_TC_MIN_TOKENS = 128;
 int gemm_tc_launch(const GemvArgs& a, float* inv_ws, cudaStream_t stream);
 int qweight_to_mma_layout(QWeight& w, cudaStream_t stream);
 int* gemv_err_word();

@@ -119,6 +119,30 @@ def test_7b_width_auto_plan_long_context():
     e.close()
 
 
+def test_7b_width_batched_decode_gemm():
+    """A decode batch of 24 at 7B width: gate|up (296 row tiles) and the lm_head (1188) take the
+    tcgen05 GEMM with a 32-token tile, q|k|v / o_proj / down_proj the GEMV; two of the
+    sequences are replayed on the oracle."""
+    shape = dataclasses.replace(synthetic.SHAPES["qwen2-7b"], layers=1)
+    B = 24
+    e, w = _build(shape, "int4_g128", seed=11, max_ctx=128, max_batch=B, max_prefill=64)
+    rng = np.random.default_rng(24)
+    picks = (0, 17)
+    orcs = {b: OracleDecoder(shape, w, max_pos=128) for b in picks}
+    for b in range(B):
+        p = rng.integers(0, shape.vocab, 9 + b % 4)
+        y = e.forward(p, seq=b)
+        if b in orcs:
+            assert rel_err(y, orcs[b].forward(p)) <= TOL
+    toks = rng.integers(0, shape.vocab, B)
+    for step in range(2):
+        y = e.decode(toks)
+        for b in picks:
+            assert rel_err(y[b], orcs[b].forward([int(toks[b])])) <= TOL, (step, b)
+        toks = np.argmax(y, axis=1)
+    e.close()
+
+
 def test_72b_width_uneven_fused_ffn():
     shape = dataclasses.replace(synthetic.SHAPES["qwen2-72b"], layers=1, vocab=4096)
     e, w = _build(shape, "int4_g128", seed=9, max_ctx=512, max_batch=1, max_prefill=512)

@@ -212,3 +212,27 @@ def test_decode_into_pinned_and_pageable_buffers(model):
     e.close()
     assert rc == 0
     assert np.array_equal(pinned, pageable)
+
+
+@pytest.mark.parametrize("B", [8, 33, 70])
+def test_large_batch_decode(model, B):
+    """Decode batches of 8 to 70 sequences (GEMV passes of 16 columns, and the tcgen05 GEMM
+    where a linear is wide enough to fill the SMs): every checked sequence within the bar of
+    its oracle."""
+    shape, blocks, w = model
+    e = _engine(shape, blocks, max_batch=B, max_ctx=128)
+    rng = np.random.default_rng(B)
+    picks = [0, B // 2, B - 1]  # sequences checked against an oracle every step
+    oracles = {b: OracleDecoder(shape, w, max_pos=128) for b in picks}
+    for b in range(B):
+        p = rng.integers(0, shape.vocab, 3 + b % 5)
+        y = e.forward(p, seq=b)
+        if b in oracles:
+            assert rel_err(y, oracles[b].forward(p)) <= TOL
+    toks = rng.integers(0, shape.vocab, B)
+    for step in range(3):
+        y = e.decode(toks)
+        for b in picks:
+            assert rel_err(y[b], oracles[b].forward([toks[b]])) <= TOL, (step, b)
+        toks = np.argmax(y, axis=1)
+    e.close()
