@@ -33,6 +33,11 @@
 // Numerics: dequantised weights in fp16 ((q - z) s from an fp16 FMA with the
 // zero-point term z s rounded to fp16), x rounded to fp16, fp32 accumulation.
 #include <algorithm>
+#include <cstring>
+#include <mutex>
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
 
 #include "mma_gemv.cuh"
 #include "qweight.h"
@@ -72,6 +77,7 @@ struct TcArgs {
   const float* residual; int ldr;
   int swiglu;
   int* err;
+  int wtma;             // 1: the step's W blocks of all 8 row tiles come in one 2-D tensor copy (wmap)
 };
 
 // UMMA shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row x 128 B
@@ -127,6 +133,14 @@ __device__ __forceinline__ void tc_st32(uint32_t taddr, const uint32_t (&r)[32])
                   "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
                : "memory");
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// 2-D tiled tensor copy (no multicast) of the box at element coordinates (c0, c1)
+// into shared memory, completing on `bar`
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
+  asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+               :: "r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+               : "memory");
 }
 
 // x operand packing: x [T][ldx] (RMS-normalised with inv_rms and norm_w when
@@ -192,7 +206,8 @@ __device__ __forceinline__ void mbar_arrive1(uint64_t* bar) {
 constexpr int TC_WARPS = 10;
 
 template <int NTOK>
-__global__ void __launch_bounds__(TC_WARPS * 32, 1) gemm_tc_kernel(const TcArgs p) {
+__global__ void __launch_bounds__(TC_WARPS * 32, 1)
+gemm_tc_kernel(const TcArgs p, const __grid_constant__ CUtensorMap wmap) {
   using Cfg = TcCfg<NTOK>;
   constexpr int S = Cfg::STAGES;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -214,7 +229,9 @@ __global__ void __launch_bounds__(TC_WARPS * 32, 1) gemm_tc_kernel(const TcArgs 
   // blocks) or, for kpg 16, half a group's codes plus its scale/zero block
   const int gps = p.kpg <= 8 ? 8 / p.kpg : 1;                  // groups touched per step
   const uint32_t raw_b = p.kpg <= 8 ? (uint32_t)(gps * GB) : 1088u;
-  const uint32_t stage_tx = (uint32_t)Cfg::XB + (uint32_t)nt_here * raw_b;
+  // the tensor copy always delivers its whole 8-row box (rows past the weight read as zeros)
+  const uint32_t stage_tx = (uint32_t)Cfg::XB + (uint32_t)(p.wtma ? 8 : nt_here) * raw_b;
+  const int rstride = p.wtma ? (int)raw_b : TC_RAWT;  // shared-memory bytes per row tile of raw W
   const int KT = p.cols / TC_BK;
 
   if (tid == 0) {
@@ -259,6 +276,9 @@ __global__ void __launch_bounds__(TC_WARPS * 32, 1) gemm_tc_kernel(const TcArgs 
                      Cfg::XR * 128, &full[s]);
           }
         const int s0 = kt * 8, gi = s0 / p.kpg;  // first k-step and group of this step
+        if (p.wtma) {  // one copy: row tiles [tile0, tile0 + 8) x the step's raw_b bytes from group gi
+          tma_load_2d(st + Cfg::XB, &wmap, gi * GB / 8, tile0, &full[s]);
+        } else
         for (int w = 0; w < nt_here; ++w) {
           const uint8_t* grp = p.blob + ((int64_t)(tile0 + w) * p.G + gi) * GB;
           uint8_t* dst = st + Cfg::XB + w * TC_RAWT;
@@ -313,7 +333,7 @@ __global__ void __launch_bounds__(TC_WARPS * 32, 1) gemm_tc_kernel(const TcArgs 
       if (lane == 0) ok = tc_wait(&full[s], (uint32_t)((kt / S) & 1), abortf);
       if (!__shfl_sync(0xffffffffu, ok, 0)) break;
       tc_fence_after();
-      const uint8_t* raw = smem + s * Cfg::STAGE + Cfg::XB + wt * TC_RAWT;
+      const uint8_t* raw = smem + s * Cfg::STAGE + Cfg::XB + wt * rstride;
       uint32_t out[32];
       if (wt < nt_here) {
         // column c of the half: K pair (16 j + 2 tq (+ 8), +1) for c = 8 j + tq (+ 4), from
@@ -448,6 +468,40 @@ static int x16_workspace(size_t bytes, cudaStream_t st, uint8_t** out) {
   return N730_OK;
 }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
+static PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    else
+      cudaGetLastError();
+  });
+  return fn;
+}
+
+// The fragment tiles as a 2-D tensor of 8-byte elements: one row per 16-row tile
+// (n_groups x group-block bytes), box = one step's bytes x 8 row tiles.  Every
+// coordinate the kernel passes is a whole number of group blocks (multiples of
+// 16 bytes), the row pitch and the base are 16-byte aligned.
+static bool encode_wmap(const QWeight& w, uint32_t step_bytes, CUtensorMap* out) {
+  auto enc = tmap_encoder();
+  const int GB = (w.group / 16) * 128 + 64;
+  const uint64_t pitch = (uint64_t)w.n_groups * GB;
+  if (!enc || step_bytes % 16 || step_bytes / 8 > 256 || pitch % 16 || ((uintptr_t)w.codes & 15)) return false;
+  const cuuint64_t dims[2] = {pitch / 8, (cuuint64_t)((w.rows + 15) / 16)};
+  const cuuint64_t strides[1] = {pitch};
+  const cuuint32_t box[2] = {step_bytes / 8, 8};
+  const cuuint32_t es[2] = {1, 1};
+  return enc(out, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t*>(w.codes), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // Grow the packed-x workspace for calls of up to `tokens` tokens and `cols` columns now,
 // so that calls captured into a CUDA graph later never need to grow it.
 int gemm_tc_reserve(int tokens, int cols, cudaStream_t st) {
@@ -489,10 +543,14 @@ int gemm_tc_launch(const GemvArgs& a, float* inv_ws, cudaStream_t st) {
   p.y = a.y; p.ldy = a.ldy; p.bias = a.bias; p.residual = a.residual; p.ldr = a.ldr; p.swiglu = a.swiglu;
   p.err = err;
   const dim3 grid(RT, TT);
-  if (ntok == 256) gemm_tc_kernel<256><<<grid, TC_WARPS * 32, TcCfg<256>::SMEM, st>>>(p);
-  else if (ntok == 128) gemm_tc_kernel<128><<<grid, TC_WARPS * 32, TcCfg<128>::SMEM, st>>>(p);
-  else if (ntok == 64) gemm_tc_kernel<64><<<grid, TC_WARPS * 32, TcCfg<64>::SMEM, st>>>(p);
-  else gemm_tc_kernel<32><<<grid, TC_WARPS * 32, TcCfg<32>::SMEM, st>>>(p);
+  CUtensorMap wmap;
+  std::memset(&wmap, 0, sizeof(wmap));
+  const int kpg = w.group / 16;
+  p.wtma = (kpg == 4 || kpg == 8) && encode_wmap(w, (uint32_t)((8 / kpg) * (kpg * 128 + 64)), &wmap);
+  if (ntok == 256) gemm_tc_kernel<256><<<grid, TC_WARPS * 32, TcCfg<256>::SMEM, st>>>(p, wmap);
+  else if (ntok == 128) gemm_tc_kernel<128><<<grid, TC_WARPS * 32, TcCfg<128>::SMEM, st>>>(p, wmap);
+  else if (ntok == 64) gemm_tc_kernel<64><<<grid, TC_WARPS * 32, TcCfg<64>::SMEM, st>>>(p, wmap);
+  else gemm_tc_kernel<32><<<grid, TC_WARPS * 32, TcCfg<32>::SMEM, st>>>(p, wmap);
   N730_CHECK_LAUNCH();
   return N730_OK;
 }
