@@ -78,6 +78,9 @@ struct TcArgs {
   int swiglu;
   int* err;
   int wtma;             // 1: the step's W blocks of all 8 row tiles come in one 2-D tensor copy (wmap)
+  int kparts;           // K split over blockIdx.z (1: none); with part, raw sums go to part[z][token][row]
+  float* part;
+  int64_t part_stride;
 };
 
 // UMMA shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row x 128 B
@@ -232,7 +235,9 @@ gemm_tc_kernel(const TcArgs p, const __grid_constant__ CUtensorMap wmap) {
   // the tensor copy always delivers its whole 8-row box (rows past the weight read as zeros)
   const uint32_t stage_tx = (uint32_t)Cfg::XB + (uint32_t)(p.wtma ? 8 : nt_here) * raw_b;
   const int rstride = p.wtma ? (int)raw_b : TC_RAWT;  // shared-memory bytes per row tile of raw W
-  const int KT = p.cols / TC_BK;
+  // this CTA's K-part: steps [k0, k0 + KT) of the row (kparts 1: all of them)
+  const int kz = blockIdx.z, KT_all = p.cols / TC_BK;
+  const int k0 = KT_all * kz / p.kparts, KT = KT_all * (kz + 1) / p.kparts - k0;
 
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
@@ -272,10 +277,10 @@ gemm_tc_kernel(const TcArgs p, const __grid_constant__ CUtensorMap wmap) {
           for (int i = 0; i < NTOK / Cfg::XR; ++i) {
             const int tok = m0 + i * Cfg::XR;
             bulk_g2s(st + h * (NTOK * 128) + i * Cfg::XR * 128,
-                     p.x16 + ((size_t)(tok / TC_XT) * KB + 2 * kt + h) * TC_SUB + (size_t)(tok % TC_XT) * 128,
+                     p.x16 + ((size_t)(tok / TC_XT) * KB + 2 * (k0 + kt) + h) * TC_SUB + (size_t)(tok % TC_XT) * 128,
                      Cfg::XR * 128, &full[s]);
           }
-        const int s0 = kt * 8, gi = s0 / p.kpg;  // first k-step and group of this step
+        const int s0 = (k0 + kt) * 8, gi = s0 / p.kpg;  // first k-step and group of this step
         if (p.wtma) {  // one copy: row tiles [tile0, tile0 + 8) x the step's raw_b bytes from group gi
           tma_load_2d(st + Cfg::XB, &wmap, gi * GB / 8, tile0, &full[s]);
         } else
@@ -389,6 +394,10 @@ gemm_tc_kernel(const TcArgs p, const __grid_constant__ CUtensorMap wmap) {
       for (int i = 0; i < 32; ++i) {
         const int tok = m0 + col0 + i;
         if (tok >= p.T) break;  // warp-uniform
+        if (p.part) {  // split K: this part's raw sums (the fold adds bias and residual in part order)
+          if (nin) p.part[(size_t)kz * p.part_stride + (int64_t)tok * p.rows + n] = v[i];
+          continue;
+        }
         const float o = v[i] + bv;
         if (p.swiglu) {  // gate row n (even lane), up row n + 1 (the next lane)
           const float up = __shfl_down_sync(0xffffffffu, o, 1);
@@ -502,14 +511,71 @@ static bool encode_wmap(const QWeight& w, uint32_t step_bytes, CUtensorMap* out)
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// y[t][r] = residual[t][r] + bias[r] + the K-parts' sums part[z][t][r] added in part order
+__global__ void tc_fold_kernel(const float* part, int kparts, int64_t stride, int T, int rows, float* y, int ldy,
+                               const float* residual, int ldr, const float* bias) {
+  const int64_t n = (int64_t)T * rows;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int t = (int)(i / rows), r = (int)(i - (int64_t)t * rows);
+    float v = 0.f;
+    for (int z = 0; z < kparts; ++z) v += __ldcg(part + z * stride + i);
+    if (bias) v += bias[r];
+    if (residual) v += residual[(int64_t)t * ldr + r];
+    y[(int64_t)t * ldy + r] = v;
+  }
+}
+
+constexpr int TC_MAX_KPARTS = 8;
+
+// Split-K partial sums of the current device, grown on demand (never inside a stream capture).
+static int part_workspace(size_t floats, cudaStream_t st, float** out) {
+  static std::mutex mu;
+  static float* buf[N730_MAX_DEVICES] = {};
+  static size_t cap[N730_MAX_DEVICES] = {};
+  int dev = 0;
+  N730_CUDA(cudaGetDevice(&dev));
+  N730_REQUIRE(dev >= 0 && dev < N730_MAX_DEVICES, N730_BAD_ARG, "gemm_tc: device %d", dev);
+  std::lock_guard<std::mutex> lk(mu);
+  if (cap[dev] < floats) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    N730_CUDA(cudaStreamIsCapturing(st, &cs));
+    N730_REQUIRE(cs == cudaStreamCaptureStatusNone, N730_STATE,
+                 "gemm_tc: split-K workspace must grow outside stream capture (%zu floats)", floats);
+    N730_CUDA(cudaStreamSynchronize(st));
+    if (buf[dev]) N730_CUDA(cudaFree(buf[dev]));
+    buf[dev] = nullptr;
+    cap[dev] = 0;
+    N730_CUDA(cudaMalloc(&buf[dev], floats * sizeof(float)));
+    cap[dev] = floats;
+  }
+  *out = buf[dev];
+  return N730_OK;
+}
+
+// K-parts of a launch: decode-sized calls (< 128 tokens) whose grid of row and token tiles
+// leaves SMs idle split K over blockIdx.z (each part >= 2 steps; SwiGLU outputs never split)
+static int gemm_tc_kparts(int row_tiles, int token_tiles, int ksteps, int tokens, bool swiglu) {
+  const int ctas = row_tiles * token_tiles;
+  if (tokens >= 128 || swiglu || ctas >= num_sms()) return 1;
+  return std::max(1, std::min({TC_MAX_KPARTS, (num_sms() + ctas - 1) / ctas, ksteps / 2}));
+}
+
+// CTAs of a launch (row tiles x token tiles x K-parts)
+int gemm_tc_ctas(int rows, int cols, int tokens, bool swiglu) {
+  const int rt = (rows + TC_BN - 1) / TC_BN, ntok = gemm_tc_tile(rt, tokens), tt = (tokens + ntok - 1) / ntok;
+  return rt * tt * gemm_tc_kparts(rt, tt, cols / TC_BK, tokens, swiglu);
+}
+
 // Grow the packed-x workspace for calls of up to `tokens` tokens and `cols` columns now,
 // so that calls captured into a CUDA graph later never need to grow it.
-int gemm_tc_reserve(int tokens, int cols, cudaStream_t st) {
+int gemm_tc_reserve(int tokens, int cols, int rows, cudaStream_t st) {
   if (tokens < 1 || cols < 64) return N730_OK;
   const int KB = (cols + 63) / 64;
   const int XT = (tokens + 255) / 256 * 2;  // the most sub-tiles any token tile choice packs
   uint8_t* x16 = nullptr;
-  return x16_workspace((size_t)XT * KB * TC_SUB, st, &x16);
+  if (int rc = x16_workspace((size_t)XT * KB * TC_SUB, st, &x16)) return rc;
+  float* part = nullptr;
+  return part_workspace((size_t)TC_MAX_KPARTS * std::min(tokens, 127) * std::max(rows, 1), st, &part);
 }
 
 int gemm_tc_launch(const GemvArgs& a, float* inv_ws, cudaStream_t st) {
@@ -542,7 +608,12 @@ int gemm_tc_launch(const GemvArgs& a, float* inv_ws, cudaStream_t st) {
   p.x16 = x16; p.T = a.batch;
   p.y = a.y; p.ldy = a.ldy; p.bias = a.bias; p.residual = a.residual; p.ldr = a.ldr; p.swiglu = a.swiglu;
   p.err = err;
-  const dim3 grid(RT, TT);
+  p.kparts = gemm_tc_kparts(RT, TT, w.cols / TC_BK, a.batch, a.swiglu != 0);
+  if (p.kparts > 1) {
+    p.part_stride = (int64_t)a.batch * w.rows;
+    if (int rc = part_workspace((size_t)p.kparts * p.part_stride, st, &p.part)) return rc;
+  }
+  const dim3 grid(RT, TT, p.kparts);
   CUtensorMap wmap;
   std::memset(&wmap, 0, sizeof(wmap));
   const int kpg = w.group / 16;
@@ -552,6 +623,13 @@ int gemm_tc_launch(const GemvArgs& a, float* inv_ws, cudaStream_t st) {
   else if (ntok == 64) gemm_tc_kernel<64><<<grid, TC_WARPS * 32, TcCfg<64>::SMEM, st>>>(p, wmap);
   else gemm_tc_kernel<32><<<grid, TC_WARPS * 32, TcCfg<32>::SMEM, st>>>(p, wmap);
   N730_CHECK_LAUNCH();
+  if (p.kparts > 1) {
+    const int64_t n = (int64_t)a.batch * w.rows;
+    const int fg = (int)std::min<int64_t>((n + 255) / 256, (int64_t)num_sms() * 4);
+    tc_fold_kernel<<<fg, 256, 0, st>>>(p.part, p.kparts, p.part_stride, a.batch, w.rows, a.y, a.ldy, a.residual,
+                                       a.ldr, a.bias);
+    N730_CHECK_LAUNCH();
+  }
   return N730_OK;
 }
 

@@ -527,7 +527,9 @@ static int finalize(Model* m) {
   const N730ModelConfig& c = m->c;
   if (int rc = gemv_prepare()) return rc;
   if (int rc = gemm_tc_prepare()) return rc;
-  if (int rc = gemm_tc_reserve(std::max(c.max_batch, c.max_prefill), std::max(c.hidden, c.ffn), m->st)) return rc;
+  if (int rc = gemm_tc_reserve(std::max(c.max_batch, c.max_prefill), std::max(c.hidden, c.ffn),
+                               std::max(c.hidden, (c.heads + 2 * c.kv_heads) * c.head_dim), m->st))
+    return rc;
   const int nl = c.layers;
   m->L.assign(nl, Layer{});
   auto W = [&](int l, int s) -> QWeight* {
@@ -705,18 +707,20 @@ static int finalize(Model* m) {
 }
 
 // GEMM or GEMV for `batch` rows.  From GEMM_TC_MIN_TOKENS rows on the tcgen05 GEMM
-// (each weight dequantised once per token tile).  Between 17 and 127 rows the GEMV
-// streams the weights once per 16 rows, so the GEMM also wins there when its grid
-// (128-row tiles x token tiles) fills the SMs: measured at 32 rows, gate|up of the 7B
-// shape 73 us against 126 us; with fewer CTAs (o_proj / down_proj, 28 row tiles) or
-// at <= 16 rows the GEMV is faster (the GEMM's per-step dequant latency is exposed
-// when a step holds few tokens).
-static bool use_gemm_tc(const QWeight& w, int batch) {
+// (each weight dequantised once per token tile).  From 9 to 127 rows the GEMV streams
+// the weights once per 16 rows with twice the tensor-core work of 8, so the GEMM
+// (32- to 128-token tile, K split over CTAs for narrow linears) wins when its grid
+// fills the SMs; measured on the 7B shape at 32 rows: gate|up 44 us against 126 us for
+// the GEMV, down_proj 41 us split 6 ways; at <= 8 rows the GEMV is faster (gate|up 27
+// us against 44), and at 9-16 rows only for narrow linears (decode steps of 12 and 16
+// sequences were faster with their down_proj / q|k|v / o_proj on the GEMV).
+static bool use_gemm_tc(const QWeight& w, int batch, bool swiglu) {
   if (!gemm_tc_supported(w, batch)) return false;
   if (batch >= GEMM_TC_MIN_TOKENS) return true;
-  if (batch <= 16) return false;
-  const int rt = (w.rows + 127) / 128, ntok = gemm_tc_tile(rt, batch);
-  return (int64_t)rt * ((batch + ntok - 1) / ntok) >= num_sms();
+  if (batch <= 8) return false;
+  if (batch <= 16)  // only linears wide enough to fill the SMs without splitting K (7B: gate|up 43 vs 60 us)
+    return (int64_t)((w.rows + 127) / 128) * ((batch + 31) / 32) >= num_sms();
+  return gemm_tc_ctas(w.rows, w.cols, batch, swiglu) >= num_sms();
 }
 
 // One linear for `batch` rows of x (use_gemm_tc picks the kernel).
@@ -727,7 +731,7 @@ static int gemv(Model* m, const QWeight* w, const float* x, int ldx, int batch, 
   a.residual = resid; a.ldr = ldr; a.norm_w = norm; a.eps = m->c.rms_eps; a.swiglu = swiglu;
   a.pdl = m->c.use_pdl;
   if (w->rows <= m->c.hidden) { a.split_ws = m->split_ws; a.split_ws_floats = m->split_ws_floats; }
-  if (use_gemm_tc(*w, batch) && !m->c.exact_gemv) return gemm_tc_launch(a, m->rms_ws, m->st);
+  if (use_gemm_tc(*w, batch, swiglu != 0) && !m->c.exact_gemv) return gemm_tc_launch(a, m->rms_ws, m->st);
   return gemv_launch(a, m->st);
 }
 
@@ -1442,7 +1446,7 @@ N730_API int n730_model_run_linear(void* p, int layer, int which, const float* d
   a.w = w; a.x = d_x; a.ldx = w->cols; a.batch = batch; a.y = d_y;
   a.swiglu = which == 2; a.ldy = which == 2 ? w->rows / 2 : w->rows;
   cudaStream_t st = stream ? (cudaStream_t)stream : m->st;
-  if (use_gemm_tc(*w, batch) && !m->c.exact_gemv) return gemm_tc_launch(a, m->rms_ws, st);  // as the decode step
+  if (use_gemm_tc(*w, batch, a.swiglu != 0) && !m->c.exact_gemv) return gemm_tc_launch(a, m->rms_ws, st);  // as the decode step
   return gemv_launch(a, st);
 }
 

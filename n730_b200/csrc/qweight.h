@@ -54,8 +54,10 @@ int gemv_mma_launch(const GemvArgs& a, cudaStream_t stream);
 // tcgen05 GEMM for many tokens (gemm_tc.cu); inv_ws: batch floats of workspace when norm_w is set
 bool gemm_tc_supported(const QWeight& w, int tokens);
 int gemm_tc_prepare();
-int gemm_tc_reserve(int tokens, int cols, cudaStream_t stream);
+// workspaces for calls of up to `tokens` tokens, `cols` columns and `rows` rows (before any capture)
+int gemm_tc_reserve(int tokens, int cols, int rows, cudaStream_t stream);
 int gemm_tc_tile(int row_tiles, int tokens);
+int gemm_tc_ctas(int rows, int cols, int tokens, bool swiglu);
 // from this many rows of x on, model linears take the tcgen05 GEMM (each weight dequantised
 // once for up to 256 rows); below it the GEMV (weights streamed once per 16 rows), except
 // where the model's rule prefers the GEMM (wide linears at 17-127 rows)

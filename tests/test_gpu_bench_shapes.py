@@ -196,10 +196,14 @@ def _gpu_weight(rows, cols, seed):
 
 @pytest.mark.parametrize("rows,cols,tokens,epi", [(1024, 3584, 512, "plain"), (3584, 18944, 256, "bias_resid"),
                                                   (19200, 3584, 300, "norm_swiglu"), (37888, 3584, 512, "plain"),
+                                                  (3584, 18944, 32, "bias_resid"), (4608, 3584, 40, "plain"),
+                                                  (37888, 3584, 24, "norm_swiglu"),
                                                   (2048, 3584, 300, "norm_swiglu"), (640, 8192, 129, "plain")])
 def test_qgemm_matches_oracle(rows, cols, tokens, epi):
     """The tcgen05 GEMM rounds x and the dequantised weights to fp16 and accumulates in fp32:
-    within 5e-3 of max|y| of the oracle's fp32 product of the exact dequantised weights."""
+    within 5e-3 of max|y| of the oracle's fp32 product of the exact dequantised weights.
+    Decode-sized calls (< 128 tokens) of the narrow down_proj / q|k|v shapes split K over
+    CTAs and fold the parts; the wide SwiGLU one does not split."""
     import torch
     lib = _lib.cuda()
     P = lambda t: C.c_void_p(t.data_ptr()) if t is not None else None
