@@ -132,6 +132,9 @@ int n730_qlinear(void* qw, const float* d_x, int ldx, int batch, float* d_y, int
 /* Many-token linear on the tcgen05 tensor cores (TMEM accumulators): the same epilogues as
  * n730_qlinear for `tokens` rows of x; weights must be INT4 in tensor-core fragment tiles
  * (n730_qweight_set_layout 1).  d_ws: `tokens` floats of device workspace when d_norm_w is set.
+ * Any token count: 256- / 128-token tiles for prefill, 32 / 64 / 128 for decode batches, K split
+ * over CTAs (fixed-order fold) when a decode-sized call would leave SMs idle.  Its internal
+ * workspaces grow on the first call of a size (not inside a stream capture).
  * Replaces the per-layer cuBLAS Sgemm of prefill (n730_cuda.cu:549-579, 847-870). */
 int n730_qgemm(void* qw, const float* d_x, int ldx, int tokens, float* d_y, int ldy, const float* d_bias,
                const float* d_residual, int ldr, const float* d_norm_w, float eps, int swiglu, float* d_ws,
