@@ -155,6 +155,8 @@ __global__ void x16_pack_kernel(const float* x, int ldx, int T, const float* inv
                                 uint8_t* out) {
   const int kb = blockIdx.x, tt = blockIdx.y;
   uint8_t* blk = out + ((size_t)tt * gridDim.x + kb) * TC_SUB;
+  pdl_wait();  // x (and inv_rms) come from the previous kernels
+  pdl_launch_dependents();
   for (int i = threadIdx.x; i < TC_XT * 8; i += blockDim.x) {
     const int r = i >> 3, c8 = i & 7, tok = tt * TC_XT + r, k = kb * 64 + c8 * 8;
     uint4 pk = make_uint4(0u, 0u, 0u, 0u);
@@ -263,14 +265,10 @@ gemm_tc_kernel(const TcArgs p, const __grid_constant__ CUtensorMap wmap) {
   if (warp == 8) {
     // ---------------- producer ----------------
     if (lane == 0) {
-      int kt = 0;
-      for (; kt < KT; ++kt) {
-        const int s = kt % S;
-        if (kt >= S && !tc_wait(&empty[s], (uint32_t)(((kt / S) - 1) & 1), abortf)) break;
+      // step kt's x blocks: 64-column block h holds NTOK rows, copied XR rows (<= one packed
+      // sub-tile, row r of a sub-tile at byte 128 r) at a time
+      auto issue_x = [&](int s, int kt) {
         uint8_t* st = smem + s * Cfg::STAGE;
-        mbar_arrive_expect_tx(&full[s], stage_tx);
-        // x: 64-column block h of the step holds NTOK rows, copied XR rows (<= one packed
-        // sub-tile, row r of a sub-tile at byte 128 r) at a time
 #pragma unroll
         for (int h = 0; h < 2; ++h)
 #pragma unroll
@@ -280,10 +278,15 @@ gemm_tc_kernel(const TcArgs p, const __grid_constant__ CUtensorMap wmap) {
                      p.x16 + ((size_t)(tok / TC_XT) * KB + 2 * (k0 + kt) + h) * TC_SUB + (size_t)(tok % TC_XT) * 128,
                      Cfg::XR * 128, &full[s]);
           }
+      };
+      // step kt's weight blocks of the CTA's row tiles
+      auto issue_w = [&](int s, int kt) {
+        uint8_t* st = smem + s * Cfg::STAGE;
         const int s0 = (k0 + kt) * 8, gi = s0 / p.kpg;  // first k-step and group of this step
         if (p.wtma) {  // one copy: row tiles [tile0, tile0 + 8) x the step's raw_b bytes from group gi
           tma_load_2d(st + Cfg::XB, &wmap, gi * GB / 8, tile0, &full[s]);
-        } else
+          return;
+        }
         for (int w = 0; w < nt_here; ++w) {
           const uint8_t* grp = p.blob + ((int64_t)(tile0 + w) * p.G + gi) * GB;
           uint8_t* dst = st + Cfg::XB + w * TC_RAWT;
@@ -294,6 +297,24 @@ gemm_tc_kernel(const TcArgs p, const __grid_constant__ CUtensorMap wmap) {
             bulk_g2s(dst + 1024, grp + 16 * 128, 64, &full[s]);
           }
         }
+      };
+      // weights do not depend on the previous kernel (programmatic dependent launch): the first
+      // stages' weight copies go out before the grid-dependency wait, their x copies after it
+      const int pre = min(S, KT);
+      for (int j = 0; j < pre; ++j) {
+        mbar_arrive_expect_tx(&full[j], stage_tx);
+        issue_w(j, j);
+      }
+      pdl_wait();
+      int kt = 0;
+      for (; kt < KT; ++kt) {
+        const int s = kt % S;
+        if (kt >= S) {
+          if (!tc_wait(&empty[s], (uint32_t)(((kt / S) - 1) & 1), abortf)) break;
+          mbar_arrive_expect_tx(&full[s], stage_tx);
+          issue_w(s, kt);
+        }
+        issue_x(s, kt);
       }
       counts[0] = kt;
     }
@@ -370,6 +391,7 @@ gemm_tc_kernel(const TcArgs p, const __grid_constant__ CUtensorMap wmap) {
       if (lane == 0) mbar_arrive1(&conv[s]);
     }
   }
+  pdl_launch_dependents();  // the next kernel may launch; it waits for this grid before reading y
   __syncthreads();
   // copies still in flight (abort path) land before the CTA exits
   if (tid == 8 * 32)
@@ -380,6 +402,7 @@ gemm_tc_kernel(const TcArgs p, const __grid_constant__ CUtensorMap wmap) {
   tc_fence_after();
   if (*abortf && tid == 0) atomicExch(p.err, DEV_ERR_TIMEOUT);
   if (counts[2] && warp < 8) {
+    pdl_wait();  // y / residual may be in use by the kernels before this one until they complete
     // ---- epilogue: warp w reads TMEM lanes 32 (w % 4).. (W rows), token columns 32 c.. for c = w / 4, + 2, ... ----
     const int q = warp & 3, hh = warp >> 2;
     const int n = n0 + 32 * q + lane;
@@ -418,6 +441,8 @@ gemm_tc_kernel(const TcArgs p, const __grid_constant__ CUtensorMap wmap) {
 // per-token 1/rms of x [T][ldx] over K columns: one warp per token
 __global__ void inv_rms_kernel(const float* x, int ldx, int T, int K, float eps, float* out) {
   const int tok = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  pdl_wait();
+  pdl_launch_dependents();
   if (tok >= T) return;
   const float* r = x + (int64_t)tok * ldx;
   float ss = 0.f;
@@ -442,6 +467,24 @@ int gemm_tc_prepare() {
 bool gemm_tc_supported(const QWeight& w, int T) {
   const int kpg = w.group / 16;
   return w.layout == 1 && w.bits == 4 && w.cols % TC_BK == 0 && (kpg == 4 || kpg == 8 || kpg == 16) && T >= 1;
+}
+
+// Launch on `st`, with programmatic dependent launch when `pdl` (every kernel of the GEMM
+// chain waits for its predecessor before reading what that one wrote).
+template <typename... KArgs, typename... Args>
+static cudaError_t tc_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
+                             Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
 // Token tile of a launch: decode batches (< 128 tokens) one tile of 32 / 64 / 128;
@@ -515,6 +558,8 @@ static bool encode_wmap(const QWeight& w, uint32_t step_bytes, CUtensorMap* out)
 __global__ void tc_fold_kernel(const float* part, int kparts, int64_t stride, int T, int rows, float* y, int ldy,
                                const float* residual, int ldr, const float* bias) {
   const int64_t n = (int64_t)T * rows;
+  pdl_wait();  // the GEMM's parts, and a residual an earlier kernel wrote
+  pdl_launch_dependents();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     const int t = (int)(i / rows), r = (int)(i - (int64_t)t * rows);
     float v = 0.f;
@@ -596,13 +641,13 @@ int gemm_tc_launch(const GemvArgs& a, float* inv_ws, cudaStream_t st) {
   const int XT = (TT * ntok + TC_XT - 1) / TC_XT;          // packed 128-token sub-tiles
   uint8_t* x16 = nullptr;
   if (int rc = x16_workspace((size_t)XT * KB * TC_SUB, st, &x16)) return rc;
-  if (a.norm_w) {
-    inv_rms_kernel<<<(a.batch + 7) / 8, 256, 0, st>>>(a.x, a.ldx, a.batch, w.cols, a.eps, inv_ws);
-    N730_CHECK_LAUNCH();
-  }
+  const bool pdl = a.pdl != 0;
+  if (a.norm_w)
+    N730_CUDA(tc_launch(inv_rms_kernel, dim3((a.batch + 7) / 8), 256, 0, st, pdl, a.x, a.ldx, a.batch, w.cols, a.eps,
+                        inv_ws));
   // every sub-tile a CTA copies is packed (tokens >= T as zeros)
-  x16_pack_kernel<<<dim3(KB, XT), 256, 0, st>>>(a.x, a.ldx, a.batch, a.norm_w ? inv_ws : nullptr, a.norm_w, x16);
-  N730_CHECK_LAUNCH();
+  N730_CUDA(tc_launch(x16_pack_kernel, dim3(KB, XT), 256, 0, st, pdl, a.x, a.ldx, a.batch,
+                      (const float*)(a.norm_w ? inv_ws : nullptr), a.norm_w, x16));
   TcArgs p = {};
   p.blob = w.codes; p.rows = w.rows; p.cols = w.cols; p.G = w.n_groups; p.kpg = w.group / 16;
   p.x16 = x16; p.T = a.batch;
@@ -618,17 +663,16 @@ int gemm_tc_launch(const GemvArgs& a, float* inv_ws, cudaStream_t st) {
   std::memset(&wmap, 0, sizeof(wmap));
   const int kpg = w.group / 16;
   p.wtma = (kpg == 4 || kpg == 8) && encode_wmap(w, (uint32_t)((8 / kpg) * (kpg * 128 + 64)), &wmap);
-  if (ntok == 256) gemm_tc_kernel<256><<<grid, TC_WARPS * 32, TcCfg<256>::SMEM, st>>>(p, wmap);
-  else if (ntok == 128) gemm_tc_kernel<128><<<grid, TC_WARPS * 32, TcCfg<128>::SMEM, st>>>(p, wmap);
-  else if (ntok == 64) gemm_tc_kernel<64><<<grid, TC_WARPS * 32, TcCfg<64>::SMEM, st>>>(p, wmap);
-  else gemm_tc_kernel<32><<<grid, TC_WARPS * 32, TcCfg<32>::SMEM, st>>>(p, wmap);
+  if (ntok == 256) N730_CUDA(tc_launch(gemm_tc_kernel<256>, grid, TC_WARPS * 32, TcCfg<256>::SMEM, st, pdl, p, wmap));
+  else if (ntok == 128) N730_CUDA(tc_launch(gemm_tc_kernel<128>, grid, TC_WARPS * 32, TcCfg<128>::SMEM, st, pdl, p, wmap));
+  else if (ntok == 64) N730_CUDA(tc_launch(gemm_tc_kernel<64>, grid, TC_WARPS * 32, TcCfg<64>::SMEM, st, pdl, p, wmap));
+  else N730_CUDA(tc_launch(gemm_tc_kernel<32>, grid, TC_WARPS * 32, TcCfg<32>::SMEM, st, pdl, p, wmap));
   N730_CHECK_LAUNCH();
   if (p.kparts > 1) {
     const int64_t n = (int64_t)a.batch * w.rows;
     const int fg = (int)std::min<int64_t>((n + 255) / 256, (int64_t)num_sms() * 4);
-    tc_fold_kernel<<<fg, 256, 0, st>>>(p.part, p.kparts, p.part_stride, a.batch, w.rows, a.y, a.ldy, a.residual,
-                                       a.ldr, a.bias);
-    N730_CHECK_LAUNCH();
+    N730_CUDA(tc_launch(tc_fold_kernel, dim3(fg), 256, 0, st, pdl, (const float*)p.part, p.kparts, p.part_stride,
+                        a.batch, w.rows, a.y, a.ldy, a.residual, a.ldr, a.bias));
   }
   return N730_OK;
 }
