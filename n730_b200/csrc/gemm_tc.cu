@@ -9,12 +9,17 @@
 // 128-token x 64-column blocks already in the K-major, 128-byte-swizzled
 // layout the UMMA shared-memory descriptors read (8-row x 128-byte atoms,
 // 16-byte chunk c of row r at c ^ (r % 8)).  One CTA computes a 128-row x
-// NTOK-token output tile (NTOK 256, or 128 when 256-token tiles would leave
-// SMs idle) over K in steps of 128 through a pipeline of specialised warps,
-// with no CTA-wide barrier inside the K loop:
+// NTOK-token output tile (NTOK 256 for prefill, or 128 when 256-token tiles
+// would leave SMs idle; 32 / 64 / 128 for decode batches, with K split over
+// blockIdx.z and a fold kernel when the grid would leave SMs idle) over K in
+// steps of 128 through a pipeline of specialised warps, with no CTA-wide
+// barrier inside the K loop:
 //  * a producer warp issues, once a stage's previous MMAs have completed, the
-//    bulk copies of the step's x blocks (NTOK x 128 fp16) and, per 16-row tile
-//    of W, of the step's whole group blocks (codes and fp16 scale/zero);
+//    bulk copies of the step's x blocks (NTOK x 128 fp16) and one 2-D tensor
+//    copy of the step's whole group blocks (codes and fp16 scale/zero) of all
+//    8 row tiles (the per-copy cost of 8 small copies bounded the step rate);
+//    the first stages' weight copies go out before the programmatic
+//    dependent-launch wait, since weights do not depend on the previous kernel;
 //  * 8 dequant warps turn the codes into (q - z) * s fp16 and store them
 //    straight into tensor memory (tcgen05.st, one W row per TMEM lane, two
 //    fp16 per 32-bit column): the weights are the MMA's A operand, read from
