@@ -41,7 +41,8 @@ __device__ __forceinline__ const __half* page_ptr(const __half* pages, const int
 // Decode attention, one thread-block cluster per (sequence, KV head): CTA r
 // of the cluster owns context positions [r*chunk, (r+1)*chunk).  Per tile of
 // DEC_TILE positions the CTA stages K and V with cp.async into XOR-swizzled
-// shared memory; each of its 8 warps takes 16 positions and computes
+// shared memory, two buffers deep (the next tile loads while this one
+// computes); each of its 8 warps takes 16 positions and computes
 //   S = Q K^T   with mma.m16n8k16 (f16 in, f32 accumulate): the G <= 8 query
 //               heads of the group are rows 0..G-1 of the A tile, K feeds B
 //               through ldmatrix,
@@ -83,11 +84,10 @@ __device__ __forceinline__ uint32_t swz(int r, int c) {
 
 template <int HD>
 struct DecSmem {
-  __half k[DEC_TILE * HD];
-  __half v[DEC_TILE * HD];
+  __half k[2][DEC_TILE * HD];         // two tile buffers: the next tile loads while this one computes;
+  __half v[2][DEC_TILE * HD];         // after the loop k holds the per-warp outputs (wo)
   float q[MAX_G][HD];                 // RoPE'd, scaled queries (fp32)
   float wm[DEC_WARPS][MAX_G], wl[DEC_WARPS][MAX_G];
-  float wo[DEC_WARPS][MAX_G][HD];     // per-warp unnormalised outputs
   float m[MAX_G], l[MAX_G];           // this CTA's split
   float o[MAX_G][HD];
   float sw[MAX_G][16], den[MAX_G];    // cluster merge: weight e^(m_r - M) of each split, denominator
@@ -159,19 +159,32 @@ __global__ void __launch_bounds__(DEC_THREADS) attn_decode_kernel(const DecodeAt
 #pragma unroll
   for (int n = 0; n < HD / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
   float m_run = -INFINITY, l_run = 0.f;  // for head row lane>>2 (replicated over the 4 lanes of a row)
-  const uint32_t ks_base = smem_u32(sm.k), vs_base = smem_u32(sm.v);
-
-  for (int tile = t0; tile < t1; tile += DEC_TILE) {
+  // ---- stage K and V rows [tile, tile + DEC_TILE) into buffer `buf` (swizzled; rows past t1 zero) ----
+  auto stage = [&](int tile, int buf) {
     const int np = min(DEC_TILE, t1 - tile);
-    // ---- stage K and V rows [tile, tile+np) into swizzled smem ----
+    const uint32_t kb = smem_u32(sm.k[buf]), vb = smem_u32(sm.v[buf]);
     for (int i = tid; i < DEC_TILE * NCH; i += DEC_THREADS) {
       const int r = i / NCH, c = i % NCH;
       const bool ok = r < np;
       const int p = ok ? tile + r : tile;
-      cp_async16(ks_base + swz<HD>(r, c), page_ptr(a.kv.k_pages, bt, p, d, kvh) + c * 8, ok);
-      cp_async16(vs_base + swz<HD>(r, c), page_ptr(a.kv.v_pages, bt, p, d, kvh) + c * 8, ok);
+      cp_async16(kb + swz<HD>(r, c), page_ptr(a.kv.k_pages, bt, p, d, kvh) + c * 8, ok);
+      cp_async16(vb + swz<HD>(r, c), page_ptr(a.kv.v_pages, bt, p, d, kvh) + c * 8, ok);
     }
-    asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  if (t0 < t1) stage(t0, 0);
+
+  for (int tile = t0, it = 0; tile < t1; tile += DEC_TILE, ++it) {
+    const int np = min(DEC_TILE, t1 - tile), buf = it & 1;
+    const uint32_t ks_base = smem_u32(sm.k[buf]), vs_base = smem_u32(sm.v[buf]);
+    // the next tile's copies go out before this one is waited for (its buffer was last read
+    // two tiles ago, before the loop's closing barrier)
+    if (tile + DEC_TILE < t1) {
+      stage(tile + DEC_TILE, buf ^ 1);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
     __syncthreads();
     if (owns_new && pos >= tile && pos < tile + DEC_TILE) {  // the row just appended, from registers' values
       const int r = pos - tile;
@@ -182,8 +195,8 @@ __global__ void __launch_bounds__(DEC_THREADS) attn_decode_kernel(const DecodeAt
         const float x0 = kh[j0], x1 = kh[j0 + H2], c = cs[j0], s = sn[j0];
         const float kv = j < H2 ? x0 * c - x1 * s : x1 * c + x0 * s;
         const uint32_t off = swz<HD>(r, j / 8) + (j % 8) * 2;
-        *reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(sm.k) + off) = __float2half_rn(kv);
-        *reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(sm.v) + off) = __float2half_rn(vh[j]);
+        *reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(sm.k[buf]) + off) = __float2half_rn(kv);
+        *reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(sm.v[buf]) + off) = __float2half_rn(vh[j]);
       }
       __syncthreads();
     }
@@ -246,13 +259,15 @@ __global__ void __launch_bounds__(DEC_THREADS) attn_decode_kernel(const DecodeAt
     __syncthreads();  // tile buffers are reused
   }
 
-  // ---- merge the 8 warps of this CTA ----
+  // ---- merge the 8 warps of this CTA (per-warp outputs in the first K buffer: the loop is done) ----
+  float (*wo)[MAX_G][HD] = reinterpret_cast<float (*)[MAX_G][HD]>(&sm.k[0][0]);
+  static_assert(sizeof(float) * DEC_WARPS * MAX_G * HD <= sizeof(sm.k), "per-warp outputs fit the K buffers");
   {
     const int r = lane >> 2, cb = (lane & 3) * 2;
     if ((lane & 3) == 0 && r < MAX_G) { sm.wm[warp][r] = m_run; sm.wl[warp][r] = l_run; }
     if (r < MAX_G)
 #pragma unroll
-      for (int n = 0; n < HD / 8; ++n) { sm.wo[warp][r][n * 8 + cb] = o[n][0]; sm.wo[warp][r][n * 8 + cb + 1] = o[n][1]; }
+      for (int n = 0; n < HD / 8; ++n) { wo[warp][r][n * 8 + cb] = o[n][0]; wo[warp][r][n * 8 + cb + 1] = o[n][1]; }
   }
   __syncthreads();
   for (int i = tid; i < G * HD; i += DEC_THREADS) {
@@ -266,7 +281,7 @@ __global__ void __launch_bounds__(DEC_THREADS) attn_decode_kernel(const DecodeAt
       const float mw = sm.wm[w][g];
       if (mw == -INFINITY) continue;
       const float e = __expf(mw - M);
-      num = fmaf(e, sm.wo[w][g][dd], num);
+      num = fmaf(e, wo[w][g][dd], num);
       den = fmaf(e, sm.wl[w][g], den);
     }
     sm.o[g][dd] = num;
@@ -363,9 +378,10 @@ int attn_decode_launch(const DecodeAttnArgs& a, cudaStream_t st) {
     if (cl_max < 0) slot = 0;  // set-up failed: try again on the next call
   }
   if (cl_max < 0) return cl_max;
-  // splits per (sequence, KV head): about two CTAs per SM in all, at least 2
+  // splits per (sequence, KV head): about one CTA per SM in all (a CTA's two tile buffers take
+  // most of an SM's shared memory, and its loads overlap its own compute)
   int cl = cl_max;
-  while (cl > 2 && (int64_t)a.batch * d.n_kv * cl > 2 * (int64_t)num_sms()) cl >>= 1;
+  while (cl > 1 && (int64_t)a.batch * d.n_kv * cl > (int64_t)num_sms()) cl >>= 1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(cl, d.n_kv, a.batch);
   cfg.blockDim = dim3(DEC_THREADS);
