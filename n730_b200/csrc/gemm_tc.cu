@@ -56,19 +56,22 @@ constexpr int TC_SUB = TC_XT * 64 * 2;      // one 128-token x 64-column fp16 su
 constexpr int TC_RAWT = 1152;               // raw codes + scale/zero blocks of one 16-row tile per K-step
 constexpr int TC_RAW = 8 * TC_RAWT;         // raw W of one step (8 row tiles), a multiple of 1024
 constexpr int TC_ACOLS = TC_BK / 2;         // TMEM columns of one step's A (two fp16 per column)
-constexpr uint32_t TC_TMEM_COLS = 512;      // accumulator (NTOK columns) + one A block per stage
+// TMEM per CTA: the accumulator (NTOK columns) + one A block per stage, rounded to 256 or 512
 
 template <int NTOK>
 struct TcCfg {
-  // deeper pipelines for narrower token tiles (decode batches), within shared memory and TMEM
-  static constexpr int STAGES = NTOK == 256 ? 3 : NTOK == 128 ? 4 : NTOK == 64 ? 6 : 7;
+  // pipeline depth within shared memory and TMEM; 32- and 64-token tiles (decode batches) take
+  // 3 stages in 256 TMEM columns, so two CTAs (two pipelines) share an SM: measured at 32 tokens,
+  // 7 stages in 512 columns (one CTA per SM) ran gate|up in 46 us, this 37 us
+  static constexpr int STAGES = NTOK == 256 ? 3 : NTOK == 128 ? 4 : 3;
+  static constexpr uint32_t TMEM = NTOK + STAGES * TC_ACOLS <= 256 ? 256u : 512u;  // columns allocated
   static constexpr int XB = NTOK * TC_BK * 2;  // x bytes per step: [64-column block][NTOK rows][128 B]
   static constexpr int XR = NTOK < TC_XT ? NTOK : TC_XT;  // token rows per x copy (one packed sub-tile at most)
   static constexpr int STAGE = XB + TC_RAW;    // a multiple of 1024 (swizzle atoms stay aligned)
   static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE + (3 * STAGES + 1) * 8 + 32;
   // kind::f16 instruction descriptor: D fp32, A = B = fp16, both K-major, N = NTOK, M = 128
   static constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(NTOK >> 3) << 17) | ((uint32_t)(TC_BN >> 4) << 24);
-  static_assert(NTOK + STAGES * TC_ACOLS <= (int)TC_TMEM_COLS, "tensor memory budget");
+  static_assert(NTOK + STAGES * TC_ACOLS <= (int)TMEM, "tensor memory budget");
   static_assert(STAGE % 1024 == 0, "stage alignment");
 };
 
@@ -216,7 +219,7 @@ __device__ __forceinline__ void mbar_arrive1(uint64_t* bar) {
 constexpr int TC_WARPS = 10;
 
 template <int NTOK>
-__global__ void __launch_bounds__(TC_WARPS * 32, 1)
+__global__ void __launch_bounds__(TC_WARPS * 32, NTOK <= 64 ? 2 : 1)
 gemm_tc_kernel(const TcArgs p, const __grid_constant__ CUtensorMap wmap) {
   using Cfg = TcCfg<NTOK>;
   constexpr int S = Cfg::STAGES;
@@ -259,7 +262,7 @@ gemm_tc_kernel(const TcArgs p, const __grid_constant__ CUtensorMap wmap) {
   }
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
-                 :: "r"(smem_u32(tmem_slot)), "r"(TC_TMEM_COLS) : "memory");
+                 :: "r"(smem_u32(tmem_slot)), "r"(Cfg::TMEM) : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   tc_fence_before();
@@ -440,7 +443,7 @@ gemm_tc_kernel(const TcArgs p, const __grid_constant__ CUtensorMap wmap) {
   __syncthreads();
   tc_fence_after();
   if (warp == 0)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(TC_TMEM_COLS) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(Cfg::TMEM) : "memory");
 }
 
 // per-token 1/rms of x [T][ldx] over K columns: one warp per token
