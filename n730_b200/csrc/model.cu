@@ -709,17 +709,14 @@ static int finalize(Model* m) {
 // GEMM or GEMV for `batch` rows.  From GEMM_TC_MIN_TOKENS rows on the tcgen05 GEMM
 // (each weight dequantised once per token tile).  From 9 to 127 rows the GEMV streams
 // the weights once per 16 rows with twice the tensor-core work of 8, so the GEMM
-// (32- to 128-token tile, K split over CTAs for narrow linears) wins when its grid
-// fills the SMs; measured on the 7B shape at 32 rows: gate|up 44 us against 126 us for
-// the GEMV, down_proj 41 us split 6 ways; at <= 8 rows the GEMV is faster (gate|up 27
-// us against 44), and at 9-16 rows only for narrow linears (decode steps of 12 and 16
-// sequences were faster with their down_proj / q|k|v / o_proj on the GEMV).
+// (32- to 128-token tile, K split over CTAs for narrow linears) takes every linear whose
+// grid (with the split) fills the SMs; measured on the 7B shape: gate|up at 32 rows 37 us
+// against 126 us for the GEMV, decode steps of 16 sequences 4381 against 4202 tok/s with
+// the narrow linears on the GEMV; at <= 8 rows the GEMV is faster (gate|up 27 us).
 static bool use_gemm_tc(const QWeight& w, int batch, bool swiglu) {
   if (!gemm_tc_supported(w, batch)) return false;
   if (batch >= GEMM_TC_MIN_TOKENS) return true;
   if (batch <= 8) return false;
-  if (batch <= 16)  // only linears wide enough to fill the SMs without splitting K (7B: gate|up 43 vs 60 us)
-    return (int64_t)((w.rows + 127) / 128) * ((batch + 31) / 32) >= num_sms();
   return gemm_tc_ctas(w.rows, w.cols, batch, swiglu) >= num_sms();
 }
 
