@@ -488,7 +488,7 @@ def run_ours(a):
         t_kern = e4.elapsed_time(e5) / 1000.0 / (reps * shape.layers)
         kern_bytes = eng.linear_bytes(0, 2, B)
         kern_name = (f"gemm_tc_kernel (tcgen05, {32 if B <= 32 else 64 if B <= 64 else 128}-token tile, + x packing) "
-                     if B > 16 else "gemv_mma2_kernel ") + \
+                     if B > 8 else "gemv_mma2_kernel ") + \
             f"on gate|up {2 * shape.ffn}x{shape.hidden} INT4 g128 (+SwiGLU), batch {B}"
         traffic_file = "gemv_gateup_traffic.txt" if headline else "none"
 

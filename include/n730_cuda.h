@@ -284,7 +284,7 @@ int n730_model_trace_step(void* model, void* stream, uint64_t* host_times, int64
                           int* n_phases, int* grid);
 /* One of the model's linears alone (which: 0 q|k|v, 1 o_proj, 2 gate|up + SwiGLU, 3 down_proj,
  * 4 lm_head) on `batch` device rows, with the kernel the decode step picks for that batch
- * (tensor-core GEMV, or the tcgen05 GEMM for wide linears from 17 rows and any from 128). */
+ * (tensor-core GEMV, or the tcgen05 GEMM from 9 rows for linears whose grid fills the SMs, any from 128). */
 int n730_model_run_linear(void* model, int layer, int which, const float* d_x, int batch, float* d_y,
                           void* stream);
 /* Algorithmic bytes of that linear for `batch` rows: codes + fp16 scale/zero + x + y. */
