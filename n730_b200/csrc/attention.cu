@@ -41,7 +41,7 @@ __device__ __forceinline__ const __half* page_ptr(const __half* pages, const int
 // Decode attention, one thread-block cluster per (sequence, KV head): CTA r
 // of the cluster owns context positions [r*chunk, (r+1)*chunk).  Per tile of
 // DEC_TILE positions the CTA stages K and V with cp.async into XOR-swizzled
-// shared memory, two buffers deep (the next tile loads while this one
+// shared memory, three buffers deep (the next two tiles load while this one
 // computes); each of its 8 warps takes 16 positions and computes
 //   S = Q K^T   with mma.m16n8k16 (f16 in, f32 accumulate): the G <= 8 query
 //               heads of the group are rows 0..G-1 of the A tile, K feeds B
@@ -54,6 +54,7 @@ __device__ __forceinline__ const __half* page_ptr(const __half* pages, const int
 constexpr int DEC_THREADS = 256;
 constexpr int DEC_WARPS = DEC_THREADS / 32;
 constexpr int DEC_TILE = 16 * DEC_WARPS;  // 128 positions per tile
+constexpr int DEC_STAGES = 3;             // tile buffers (two tiles in flight while one computes)
 
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   __half2 h = __floats2half2_rn(lo, hi);
@@ -84,8 +85,8 @@ __device__ __forceinline__ uint32_t swz(int r, int c) {
 
 template <int HD>
 struct DecSmem {
-  __half k[2][DEC_TILE * HD];         // two tile buffers: the next tile loads while this one computes;
-  __half v[2][DEC_TILE * HD];         // after the loop k holds the per-warp outputs (wo)
+  __half k[DEC_STAGES][DEC_TILE * HD];  // tile buffers: the next two tiles load while one computes;
+  __half v[DEC_STAGES][DEC_TILE * HD];  // after the loop k holds the per-warp outputs (wo)
   float q[MAX_G][HD];                 // RoPE'd, scaled queries (fp32)
   float wm[DEC_WARPS][MAX_G], wl[DEC_WARPS][MAX_G];
   float m[MAX_G], l[MAX_G];           // this CTA's split
@@ -160,27 +161,43 @@ __global__ void __launch_bounds__(DEC_THREADS) attn_decode_kernel(const DecodeAt
   for (int n = 0; n < HD / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
   float m_run = -INFINITY, l_run = 0.f;  // for head row lane>>2 (replicated over the 4 lanes of a row)
   // ---- stage K and V rows [tile, tile + DEC_TILE) into buffer `buf` (swizzled; rows past t1 zero) ----
+  // Thread tid copies 16-byte chunk tid % NCH of rows tid / NCH + j * RSTEP; the block-table
+  // reads for its rows go out first, independent of one another, then the copies.
+  constexpr int RSTEP = DEC_THREADS / NCH, NIT = DEC_TILE / RSTEP;
+  static_assert(DEC_THREADS % NCH == 0 && DEC_TILE % RSTEP == 0, "staging covers the tile exactly");
+  const int sr0 = tid / NCH, sc = tid % NCH, ps = d.page_size;
   auto stage = [&](int tile, int buf) {
     const int np = min(DEC_TILE, t1 - tile);
     const uint32_t kb = smem_u32(sm.k[buf]), vb = smem_u32(sm.v[buf]);
-    for (int i = tid; i < DEC_TILE * NCH; i += DEC_THREADS) {
-      const int r = i / NCH, c = i % NCH;
-      const bool ok = r < np;
-      const int p = ok ? tile + r : tile;
-      cp_async16(kb + swz<HD>(r, c), page_ptr(a.kv.k_pages, bt, p, d, kvh) + c * 8, ok);
-      cp_async16(vb + swz<HD>(r, c), page_ptr(a.kv.v_pages, bt, p, d, kvh) + c * 8, ok);
+    int64_t off[NIT];
+#pragma unroll
+    for (int j = 0; j < NIT; ++j) {
+      const int r = sr0 + j * RSTEP;
+      const int p = r < np ? tile + r : tile;  // rows past the end: a valid address, zero bytes read
+      off[j] = (((int64_t)bt[p / ps] * d.n_kv + kvh) * ps + p % ps) * HD + sc * 8;
+    }
+#pragma unroll
+    for (int j = 0; j < NIT; ++j) {
+      const int r = sr0 + j * RSTEP;
+      cp_async16(kb + swz<HD>(r, sc), a.kv.k_pages + off[j], r < np);
+      cp_async16(vb + swz<HD>(r, sc), a.kv.v_pages + off[j], r < np);
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
   if (t0 < t1) stage(t0, 0);
+  if (t0 + DEC_TILE < t1) stage(t0 + DEC_TILE, 1);
 
   for (int tile = t0, it = 0; tile < t1; tile += DEC_TILE, ++it) {
-    const int np = min(DEC_TILE, t1 - tile), buf = it & 1;
+    const int np = min(DEC_TILE, t1 - tile), buf = it % DEC_STAGES;
     const uint32_t ks_base = smem_u32(sm.k[buf]), vs_base = smem_u32(sm.v[buf]);
-    // the next tile's copies go out before this one is waited for (its buffer was last read
-    // two tiles ago, before the loop's closing barrier)
-    if (tile + DEC_TILE < t1) {
-      stage(tile + DEC_TILE, buf ^ 1);
+    // the tile two ahead goes out before this one is waited for (its buffer was last read
+    // in the previous iteration, before the loop's closing barrier); then wait until at most
+    // the copies of the tiles after this one are pending
+    static_assert(DEC_STAGES == 3, "the wait_group counts below assume three buffers");
+    if (tile + 2 * DEC_TILE < t1) {
+      stage(tile + 2 * DEC_TILE, (it + 2) % DEC_STAGES);
+      asm volatile("cp.async.wait_group 2;" ::: "memory");
+    } else if (tile + DEC_TILE < t1) {
       asm volatile("cp.async.wait_group 1;" ::: "memory");
     } else {
       asm volatile("cp.async.wait_group 0;" ::: "memory");
@@ -378,7 +395,7 @@ int attn_decode_launch(const DecodeAttnArgs& a, cudaStream_t st) {
     if (cl_max < 0) slot = 0;  // set-up failed: try again on the next call
   }
   if (cl_max < 0) return cl_max;
-  // splits per (sequence, KV head): about one CTA per SM in all (a CTA's two tile buffers take
+  // splits per (sequence, KV head): about one CTA per SM in all (a CTA's three tile buffers take
   // most of an SM's shared memory, and its loads overlap its own compute)
   int cl = cl_max;
   while (cl > 1 && (int64_t)a.batch * d.n_kv * cl > (int64_t)num_sms()) cl >>= 1;

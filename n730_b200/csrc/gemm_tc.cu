@@ -446,20 +446,33 @@ gemm_tc_kernel(const TcArgs p, const __grid_constant__ CUtensorMap wmap) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(Cfg::TMEM) : "memory");
 }
 
-// per-token 1/rms of x [T][ldx] over K columns: one warp per token
-__global__ void inv_rms_kernel(const float* x, int ldx, int T, int K, float eps, float* out) {
-  const int tok = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+// per-token 1/rms of x [T][ldx] over K columns (K % 4 == 0): one CTA of RMS_THREADS per
+// token, so a decode batch's rows are read by as many SMs as it has tokens, each thread's
+// float4 loads independent of one another
+constexpr int RMS_THREADS = 128;
+__global__ void __launch_bounds__(RMS_THREADS) inv_rms_kernel(const float* x, int ldx, int T, int K, float eps,
+                                                              float* out) {
+  __shared__ float red[RMS_THREADS / 32];
+  const int tok = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   pdl_wait();
   pdl_launch_dependents();
   if (tok >= T) return;
-  const float* r = x + (int64_t)tok * ldx;
+  const float4* r = reinterpret_cast<const float4*>(x + (int64_t)tok * ldx);
   float ss = 0.f;
-  for (int k = lane * 4; k < K; k += 128) {
-    const float4 v = *reinterpret_cast<const float4*>(r + k);
+#pragma unroll 4
+  for (int i = threadIdx.x; i < K / 4; i += RMS_THREADS) {
+    const float4 v = r[i];
     ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
   }
   ss = warp_sum(ss);
-  if (lane == 0) out[tok] = rsqrtf(ss / K + eps);
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < RMS_THREADS / 32; ++w) t += red[w];
+    out[tok] = rsqrtf(t / K + eps);
+  }
 }
 
 int* gemv_err_word();
@@ -651,7 +664,7 @@ int gemm_tc_launch(const GemvArgs& a, float* inv_ws, cudaStream_t st) {
   if (int rc = x16_workspace((size_t)XT * KB * TC_SUB, st, &x16)) return rc;
   const bool pdl = a.pdl != 0;
   if (a.norm_w)
-    N730_CUDA(tc_launch(inv_rms_kernel, dim3((a.batch + 7) / 8), 256, 0, st, pdl, a.x, a.ldx, a.batch, w.cols, a.eps,
+    N730_CUDA(tc_launch(inv_rms_kernel, dim3(a.batch), RMS_THREADS, 0, st, pdl, a.x, a.ldx, a.batch, w.cols, a.eps,
                         inv_ws));
   // every sub-tile a CTA copies is packed (tokens >= T as zeros)
   N730_CUDA(tc_launch(x16_pack_kernel, dim3(KB, XT), 256, 0, st, pdl, a.x, a.ldx, a.batch,
