@@ -154,25 +154,37 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
                : "memory");
 }
 
-// x operand packing: x [T][ldx] (RMS-normalised with inv_rms and norm_w when
-// given) -> fp16 blocks of 128 tokens x 64 columns, each laid out exactly as
-// a 128-token slice of the GEMM's shared-memory x block (row r: 128 bytes,
-// 16-byte chunk c at c ^ (r % 8)); tokens >= T are zero.  Grid (K / 64, token
-// sub-tiles).
-__global__ void x16_pack_kernel(const float* x, int ldx, int T, const float* inv_rms, const float* norm_w,
-                                uint8_t* out) {
+// x operand packing: x [T][ldx] (RMS-normalised with norm_w when given, 1/rms
+// from inv_rms or from ss: ss_parts sums of squares per token that the split-K
+// fold which wrote x left behind, added in order) -> fp16 blocks of 128 tokens
+// x 64 columns, each laid out exactly as a 128-token slice of the GEMM's
+// shared-memory x block (row r: 128 bytes, 16-byte chunk c at c ^ (r % 8));
+// tokens >= T are zero.  Grid (K / 64, token sub-tiles).
+__global__ void x16_pack_kernel(const float* x, int ldx, int T, const float* inv_rms, const float* ss, int ss_parts,
+                                int K, float eps, const float* norm_w, uint8_t* out) {
+  __shared__ float siv[TC_XT];
   const int kb = blockIdx.x, tt = blockIdx.y;
   uint8_t* blk = out + ((size_t)tt * gridDim.x + kb) * TC_SUB;
-  pdl_wait();  // x (and inv_rms) come from the previous kernels
+  pdl_wait();  // x (and inv_rms / ss) come from the previous kernels
   pdl_launch_dependents();
+  if (ss) {
+    for (int r = threadIdx.x; r < TC_XT; r += blockDim.x) {
+      const int tok = tt * TC_XT + r;
+      float t = 0.f;
+      if (tok < T)
+        for (int j = 0; j < ss_parts; ++j) t += ss[(int64_t)tok * ss_parts + j];
+      siv[r] = rsqrtf(t / K + eps);
+    }
+    __syncthreads();
+  }
   for (int i = threadIdx.x; i < TC_XT * 8; i += blockDim.x) {
     const int r = i >> 3, c8 = i & 7, tok = tt * TC_XT + r, k = kb * 64 + c8 * 8;
     uint4 pk = make_uint4(0u, 0u, 0u, 0u);
     if (tok < T) {
       const float4* src = reinterpret_cast<const float4*>(x + (int64_t)tok * ldx + k);
       float4 a = src[0], b = src[1];
-      if (inv_rms) {
-        const float iv = inv_rms[tok];
+      if (norm_w) {
+        const float iv = ss ? siv[r] : inv_rms[tok];
         const float4* nw = reinterpret_cast<const float4*>(norm_w + k);
         const float4 na = nw[0], nb = nw[1];
         a.x *= iv * na.x; a.y *= iv * na.y; a.z *= iv * na.z; a.w *= iv * na.w;
@@ -591,6 +603,35 @@ __global__ void tc_fold_kernel(const float* part, int kparts, int64_t stride, in
   }
 }
 
+// tc_fold_kernel for one token per blockIdx.y and TC_SS_ROWS rows per blockIdx.x, which also
+// writes the sum of squares of its outputs to ss[t][blockIdx.x] (fixed-order reductions): the
+// next RMSNorm of y then needs no pass over y of its own
+__global__ void __launch_bounds__(TC_SS_ROWS) tc_fold_ss_kernel(const float* part, int kparts, int64_t stride,
+                                                                int rows, float* y, int ldy, const float* residual,
+                                                                int ldr, const float* bias, float* ss) {
+  __shared__ float red[TC_SS_ROWS / 32];
+  const int t = blockIdx.y, r = blockIdx.x * TC_SS_ROWS + threadIdx.x;
+  pdl_wait();  // the GEMM's parts, and a residual an earlier kernel wrote
+  pdl_launch_dependents();
+  float v = 0.f;
+  if (r < rows) {
+    const int64_t i = (int64_t)t * rows + r;
+    for (int z = 0; z < kparts; ++z) v += __ldcg(part + z * stride + i);
+    if (bias) v += bias[r];
+    if (residual) v += residual[(int64_t)t * ldr + r];
+    y[(int64_t)t * ldy + r] = v;
+  }
+  const float sq = warp_sum(v * v);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sq;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < TC_SS_ROWS / 32; ++w) tot += red[w];
+    ss[(int64_t)t * gridDim.x + blockIdx.x] = tot;
+  }
+}
+
 constexpr int TC_MAX_KPARTS = 8;
 
 // Split-K partial sums of the current device, grown on demand (never inside a stream capture).
@@ -632,6 +673,12 @@ int gemm_tc_ctas(int rows, int cols, int tokens, bool swiglu) {
   return rt * tt * gemm_tc_kparts(rt, tt, cols / TC_BK, tokens, swiglu);
 }
 
+bool gemm_tc_folds(const QWeight& w, int tokens, bool swiglu) {
+  if (!gemm_tc_supported(w, tokens)) return false;
+  const int rt = (w.rows + TC_BN - 1) / TC_BN, ntok = gemm_tc_tile(rt, tokens), tt = (tokens + ntok - 1) / ntok;
+  return gemm_tc_kparts(rt, tt, w.cols / TC_BK, tokens, swiglu) > 1;
+}
+
 // Grow the packed-x workspace for calls of up to `tokens` tokens and `cols` columns now,
 // so that calls captured into a CUDA graph later never need to grow it.
 int gemm_tc_reserve(int tokens, int cols, int rows, cudaStream_t st) {
@@ -649,8 +696,8 @@ int gemm_tc_launch(const GemvArgs& a, float* inv_ws, cudaStream_t st) {
   N730_REQUIRE(gemm_tc_supported(w, a.batch), N730_UNSUPPORTED, "gemm_tc: needs INT4 fragment tiles, K %% 64 == 0");
   N730_REQUIRE(!a.swiglu || w.rows % 2 == 0, N730_BAD_ARG, "gemm_tc: swiglu needs even rows");
   N730_REQUIRE(((uintptr_t)a.x & 15) == 0 && a.ldx % 4 == 0, N730_BAD_ARG, "gemm_tc: x must be 16-byte aligned");
-  N730_REQUIRE(!a.norm_w || (inv_ws && ((uintptr_t)a.norm_w & 15) == 0), N730_BAD_ARG,
-               "gemm_tc: RMSNorm needs a workspace of batch floats and 16-byte aligned weights");
+  N730_REQUIRE(!a.norm_w || ((inv_ws || a.ss_in) && ((uintptr_t)a.norm_w & 15) == 0), N730_BAD_ARG,
+               "gemm_tc: RMSNorm needs a workspace of batch floats (or sums of squares) and 16-byte aligned weights");
   int* err = gemv_err_word();
   N730_REQUIRE(err, N730_OOM, "gemm_tc: error word allocation failed");
   if (int rc = gemm_tc_prepare()) return rc;
@@ -660,21 +707,25 @@ int gemm_tc_launch(const GemvArgs& a, float* inv_ws, cudaStream_t st) {
   const int ntok = gemm_tc_tile(RT, a.batch);
   const int TT = (a.batch + ntok - 1) / ntok;              // output token tiles
   const int XT = (TT * ntok + TC_XT - 1) / TC_XT;          // packed 128-token sub-tiles
+  const int kparts = gemm_tc_kparts(RT, TT, w.cols / TC_BK, a.batch, a.swiglu != 0);
+  N730_REQUIRE(!a.ss_out || kparts > 1, N730_BAD_ARG, "gemm_tc: sums of squares come from the split-K fold only");
   uint8_t* x16 = nullptr;
   if (int rc = x16_workspace((size_t)XT * KB * TC_SUB, st, &x16)) return rc;
   const bool pdl = a.pdl != 0;
-  if (a.norm_w)
+  const float* ss_in = a.norm_w ? a.ss_in : nullptr;
+  if (a.norm_w && !ss_in)
     N730_CUDA(tc_launch(inv_rms_kernel, dim3(a.batch), RMS_THREADS, 0, st, pdl, a.x, a.ldx, a.batch, w.cols, a.eps,
                         inv_ws));
   // every sub-tile a CTA copies is packed (tokens >= T as zeros)
   N730_CUDA(tc_launch(x16_pack_kernel, dim3(KB, XT), 256, 0, st, pdl, a.x, a.ldx, a.batch,
-                      (const float*)(a.norm_w ? inv_ws : nullptr), a.norm_w, x16));
+                      (const float*)(a.norm_w && !ss_in ? inv_ws : nullptr), ss_in,
+                      (w.cols + TC_SS_ROWS - 1) / TC_SS_ROWS, w.cols, a.eps, a.norm_w, x16));
   TcArgs p = {};
   p.blob = w.codes; p.rows = w.rows; p.cols = w.cols; p.G = w.n_groups; p.kpg = w.group / 16;
   p.x16 = x16; p.T = a.batch;
   p.y = a.y; p.ldy = a.ldy; p.bias = a.bias; p.residual = a.residual; p.ldr = a.ldr; p.swiglu = a.swiglu;
   p.err = err;
-  p.kparts = gemm_tc_kparts(RT, TT, w.cols / TC_BK, a.batch, a.swiglu != 0);
+  p.kparts = kparts;
   if (p.kparts > 1) {
     p.part_stride = (int64_t)a.batch * w.rows;
     if (int rc = part_workspace((size_t)p.kparts * p.part_stride, st, &p.part)) return rc;
@@ -689,7 +740,11 @@ int gemm_tc_launch(const GemvArgs& a, float* inv_ws, cudaStream_t st) {
   else if (ntok == 64) N730_CUDA(tc_launch(gemm_tc_kernel<64>, grid, TC_WARPS * 32, TcCfg<64>::SMEM, st, pdl, p, wmap));
   else N730_CUDA(tc_launch(gemm_tc_kernel<32>, grid, TC_WARPS * 32, TcCfg<32>::SMEM, st, pdl, p, wmap));
   N730_CHECK_LAUNCH();
-  if (p.kparts > 1) {
+  if (p.kparts > 1 && a.ss_out) {
+    N730_CUDA(tc_launch(tc_fold_ss_kernel, dim3((w.rows + TC_SS_ROWS - 1) / TC_SS_ROWS, a.batch), TC_SS_ROWS, 0, st,
+                        pdl, (const float*)p.part, p.kparts, p.part_stride, w.rows, a.y, a.ldy, a.residual, a.ldr,
+                        a.bias, a.ss_out));
+  } else if (p.kparts > 1) {
     const int64_t n = (int64_t)a.batch * w.rows;
     const int fg = (int)std::min<int64_t>((n + 255) / 256, (int64_t)num_sms() * 4);
     N730_CUDA(tc_launch(tc_fold_kernel, dim3(fg), 256, 0, st, pdl, (const float*)p.part, p.kparts, p.part_stride,

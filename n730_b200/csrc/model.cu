@@ -135,6 +135,13 @@ struct Model {
   float* logits_all = nullptr;   // [tp][max_batch][vocab / tp]
   int vocab_l = 0;               // lm_head rows on this rank
   float* rms_ws = nullptr;       // [max(max_batch, max_prefill)] per-token 1/rms for the tcgen05 GEMM
+  // sums of squares of the residual stream left by the split-K fold of the o_proj / down_proj GEMM
+  // that last wrote it ([max(max_batch, max_prefill)][ceil(hidden / TC_SS_ROWS)]); the next
+  // RMSNorm'd GEMM reads them instead of a pass over x.  ss_of / ss_rows name the x and the rows
+  // they describe while a forward is enqueued; any other launch clears ss_of.
+  float* ss_ws = nullptr;
+  const float* ss_of = nullptr;
+  int ss_rows = 0;
   float* split_ws = nullptr;     // split-K partial sums of batched GEMVs [16][min(max_batch, 16)][hidden]
   int64_t split_ws_floats = 0;
   unsigned long long* ffn_acc = nullptr;  // persistent decode, fused FFN: [hidden] down_proj sums (fixed point)
@@ -679,6 +686,8 @@ static int finalize(Model* m) {
   if (int rc = m->alloc(&m->mlp, (size_t)B * c.ffn)) return rc;
   if (int rc = m->alloc(&m->logits, (size_t)B * c.vocab)) return rc;
   if (int rc = m->alloc(&m->rms_ws, (size_t)std::max(B, c.max_prefill))) return rc;
+  if (int rc = m->alloc(&m->ss_ws, (size_t)std::max(B, c.max_prefill) * ((c.hidden + TC_SS_ROWS - 1) / TC_SS_ROWS)))
+    return rc;
   if (B > 1) {  // split-K partials of batched GEMVs whose x does not fit shared memory (down_proj)
     m->split_ws_floats = (int64_t)16 * std::min(B, 16) * c.hidden;
     if (int rc = m->alloc(&m->split_ws, (size_t)m->split_ws_floats)) return rc;
@@ -720,16 +729,27 @@ static bool use_gemm_tc(const QWeight& w, int batch, bool swiglu) {
   return gemm_tc_ctas(w.rows, w.cols, batch, swiglu) >= num_sms();
 }
 
-// One linear for `batch` rows of x (use_gemm_tc picks the kernel).
+// One linear for `batch` rows of x (use_gemm_tc picks the kernel).  `sums`: y is the
+// residual stream; a split-K GEMM's fold then also leaves its sums of squares for the
+// next RMSNorm'd GEMM of y, which reads them instead of a pass over y.
 static int gemv(Model* m, const QWeight* w, const float* x, int ldx, int batch, float* y, int ldy,
-                const float* bias, const float* resid, int ldr, const float* norm, int swiglu) {
+                const float* bias, const float* resid, int ldr, const float* norm, int swiglu, bool sums = false) {
   GemvArgs a = {};
   a.w = w; a.x = x; a.ldx = ldx; a.batch = batch; a.y = y; a.ldy = ldy; a.bias = bias;
   a.residual = resid; a.ldr = ldr; a.norm_w = norm; a.eps = m->c.rms_eps; a.swiglu = swiglu;
   a.pdl = m->c.use_pdl;
   if (w->rows <= m->c.hidden) { a.split_ws = m->split_ws; a.split_ws_floats = m->split_ws_floats; }
-  if (use_gemm_tc(*w, batch, swiglu != 0) && !m->c.exact_gemv) return gemm_tc_launch(a, m->rms_ws, m->st);
-  return gemv_launch(a, m->st);
+  const int h = m->c.hidden;
+  const bool tc = use_gemm_tc(*w, batch, swiglu != 0) && !m->c.exact_gemv;
+  if (tc && norm && m->ss_of == x && m->ss_rows == batch && ldx == h && w->cols == h) a.ss_in = m->ss_ws;
+  m->ss_of = nullptr;
+  const bool ss_out = tc && sums && w->rows == h && ldy == h && batch <= std::max(m->c.max_batch, m->c.max_prefill) &&
+                      gemm_tc_folds(*w, batch, swiglu != 0);
+  if (ss_out) a.ss_out = m->ss_ws;
+  if (!tc) return gemv_launch(a, m->st);
+  if (int rc = gemm_tc_launch(a, m->rms_ws, m->st)) return rc;
+  if (ss_out) { m->ss_of = y; m->ss_rows = batch; }
+  return N730_OK;
 }
 
 static int launch_add(Model* m, float* x, const float* d, int64_t n) {
@@ -751,7 +771,7 @@ static int launch_add(Model* m, float* x, const float* d, int64_t n) {
 // summed across ranks by one allreduce, then added to the residual stream.
 static int rowsplit_linear(Model* m, const QWeight* w, const float* a, int lda, int B, float* x, int ldx,
                            const float* bias) {
-  if (m->c.tp_size <= 1) return gemv(m, w, a, lda, B, x, ldx, bias, x, ldx, nullptr, 0);
+  if (m->c.tp_size <= 1) return gemv(m, w, a, lda, B, x, ldx, bias, x, ldx, nullptr, 0, true);
   const int h = m->c.hidden;
   if (int rc = gemv(m, w, a, lda, B, m->delta, h, bias, nullptr, 0, nullptr, 0)) return rc;
   if (m->ar_ok && !m->ar_off && m->c.tp_allreduce == 0 && (int64_t)B * h <= m->ar.cap && ldx == h) {  // one-shot
@@ -809,6 +829,7 @@ static AttnDims dims(const Model* m) {
 static int enqueue_decode(Model* m, int B) {
   const N730ModelConfig& c = m->c;
   const int h = c.hidden, ad = c.heads * c.head_dim;
+  m->ss_of = nullptr;  // x is rewritten by the embedding
   if (int rc = embed_launch(*m->embed, m->d_tokens, B, m->x, m->st)) return rc;
   const bool persistent = B == 1 && m->pd_ok;
   if (persistent) {
@@ -903,6 +924,7 @@ static int prefill(Model* m, int seq, const int32_t* d_tok, int T, float* d_logi
   while (done < T) {
     const int n = std::min(c.max_prefill, T - done);
     const int pos0 = m->h_seq[seq] + done;
+    m->ss_of = nullptr;  // px is rewritten by the embedding
     if (int rc = embed_launch(*m->embed, d_tok + done, n, m->px, m->st)) return rc;
     if (int rc = stream_begin(m)) return rc;
     for (int l = 0; l < c.layers; ++l) {

@@ -31,6 +31,9 @@ struct QWeight {
   int device = 0;
 };
 
+// rows per sum of squares that a split-K fold hands to the next RMSNorm (GemvArgs::ss_out / ss_in)
+constexpr int TC_SS_ROWS = 256;
+
 struct GemvArgs {
   const QWeight* w;
   const float* x;        // [batch][ldx] fp32 activations
@@ -47,6 +50,11 @@ struct GemvArgs {
   int pdl;               // launched with programmatic dependent launch
   float* split_ws;       // tensor-core GEMV: workspace for split-K partial sums (null: one K pass per
   int64_t split_ws_floats;  //   batch chunk that fits shared memory)
+  // tcgen05 GEMM only (null elsewhere):
+  float* ss_out;         // with split K (gemm_tc_folds): the fold also writes the sums of squares of y,
+                         //   [batch][ceil(rows / TC_SS_ROWS)], one per 256-row slice of each token
+  const float* ss_in;    // with norm_w: 1/rms of x from such sums ([batch][ceil(cols / TC_SS_ROWS)])
+                         //   instead of a pass over x of its own
 };
 
 int gemv_launch(const GemvArgs& a, cudaStream_t stream);
@@ -57,6 +65,8 @@ int gemm_tc_prepare();
 // workspaces for calls of up to `tokens` tokens, `cols` columns and `rows` rows (before any capture)
 int gemm_tc_reserve(int tokens, int cols, int rows, cudaStream_t stream);
 int gemm_tc_tile(int row_tiles, int tokens);
+// true when a call of `tokens` tokens splits K and folds the parts (the fold can write ss_out)
+bool gemm_tc_folds(const QWeight& w, int tokens, bool swiglu);
 int gemm_tc_ctas(int rows, int cols, int tokens, bool swiglu);
 // from this many rows of x on, model linears take the tcgen05 GEMM (each weight dequantised
 // once for up to 256 rows); below it the GEMV (weights streamed once per 16 rows), except

@@ -120,9 +120,10 @@ def test_7b_width_auto_plan_long_context():
 
 
 def test_7b_width_batched_decode_gemm():
-    """A decode batch of 24 at 7B width: gate|up (296 row tiles) and the lm_head (1188) take the
-    tcgen05 GEMM with a 32-token tile, q|k|v / o_proj / down_proj the GEMV; two of the
-    sequences are replayed on the oracle."""
+    """A decode batch of 24 at 7B width: every linear takes the tcgen05 GEMM with a 32-token
+    tile, K split over CTAs for q|k|v / o_proj / down_proj, whose folds hand the sums of
+    squares of the residual stream to the next RMSNorm (gate|up, the final norm); two of the
+    sequences are replayed on the oracle, and the steps replay bit-identically."""
     shape = dataclasses.replace(synthetic.SHAPES["qwen2-7b"], layers=1)
     B = 24
     e, w = _build(shape, "int4_g128", seed=11, max_ctx=128, max_batch=B, max_prefill=64)
@@ -135,11 +136,19 @@ def test_7b_width_batched_decode_gemm():
         if b in orcs:
             assert rel_err(y, orcs[b].forward(p)) <= TOL
     toks = rng.integers(0, shape.vocab, B)
+    lens = [e.seq_len(b) for b in range(B)]
+    steps = []
     for step in range(2):
         y = e.decode(toks)
+        steps.append((toks.copy(), y.copy()))
         for b in picks:
             assert rel_err(y[b], orcs[b].forward([int(toks[b])])) <= TOL, (step, b)
         toks = np.argmax(y, axis=1)
+    # split-K folds and the per-slice sums of squares are reduced in a fixed order
+    for b in range(B):
+        e.set_seq_len(b, lens[b])
+    for t, y0 in steps:
+        assert np.array_equal(e.decode(t), y0)
     e.close()
 
 
