@@ -119,13 +119,14 @@ def test_7b_width_auto_plan_long_context():
     e.close()
 
 
-def test_7b_width_batched_decode_gemm():
-    """A decode batch of 24 at 7B width: every linear takes the tcgen05 GEMM with a 32-token
-    tile, K split over CTAs for q|k|v / o_proj / down_proj, whose folds hand the sums of
-    squares of the residual stream to the next RMSNorm (gate|up, the final norm); two of the
-    sequences are replayed on the oracle, and the steps replay bit-identically."""
+@pytest.mark.parametrize("B", [24, 32])
+def test_7b_width_batched_decode_gemm(B):
+    """Decode batches at 7B width: every linear takes the tcgen05 GEMM with a 32-token tile,
+    K split over CTAs for q|k|v / o_proj / down_proj; at 32 sequences their folds also hand
+    the sums of squares of the residual stream to the next RMSNorm (gate|up, the final norm),
+    at 24 a 1/rms kernel runs.  Two of the sequences are replayed on the oracle, and the
+    steps replay bit-identically."""
     shape = dataclasses.replace(synthetic.SHAPES["qwen2-7b"], layers=1)
-    B = 24
     e, w = _build(shape, "int4_g128", seed=11, max_ctx=128, max_batch=B, max_prefill=64)
     rng = np.random.default_rng(24)
     picks = (0, 17)
